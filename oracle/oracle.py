@@ -1,0 +1,279 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes access to the CPU checkers.
+
+Two libraries are bound here, both built by ``oracle/Makefile``:
+
+* ``liboracle.so`` -- our C restatement of the reference's CPU algorithm
+  (``u15_oracle.c``), the checker every GPU parity test compares against;
+* ``_ref/libu15ref.so`` -- the reference's own ``src/u15-ref.cc`` compiled
+  unchanged (plus ``ref_shim.cc``), used to generate the golden fixtures that
+  pin the restatement. It exists only where the reference tree does.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg may import this module, and only as the checker.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libu15ref.so")
+
+BIDIR, CAUSAL, BLOCK_CAUSAL = 0, 1, 2
+
+_f32p = C.POINTER(C.c_float)
+_i32p = C.POINTER(C.c_int)
+_i8p = C.POINTER(C.c_int8)
+
+
+def build(ref: bool = False) -> None:
+    """Build the restatement (and, if asked and present, the reference)."""
+    target = ["all"] if ref else ["oracle"]
+    subprocess.run(["make", "-s", "-C", HERE] + target, check=True)
+
+
+def _fp(a):
+    return a.ctypes.data_as(_f32p) if a is not None else None
+
+
+def _ip(a):
+    return a.ctypes.data_as(_i32p) if a is not None else None
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class _Expert(C.Structure):
+    _fields_ = [(n, _f32p) for n in (
+        "input_layernorm", "post_attention_layernorm", "q_proj", "k_proj",
+        "v_proj", "o_proj", "q_norm", "k_norm", "q_norm_hw", "k_norm_hw",
+        "gate_proj", "up_proj", "down_proj")]
+
+
+class _Dims(C.Structure):
+    _fields_ = [("hidden", C.c_long), ("heads", C.c_long),
+                ("kv_heads", C.c_long), ("head_dim", C.c_long),
+                ("inter", C.c_long), ("eps", C.c_double),
+                ("theta_t", C.c_double), ("theta_hw", C.c_double)]
+
+
+EXPERT_KEYS = [n for n, _ in _Expert._fields_]
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO):
+            build()
+        L = C.CDLL(ORACLE_SO)
+        L.orc_rms_norm.argtypes = [_f32p, _f32p, C.c_float, C.c_long, C.c_long, _f32p]
+        L.orc_linear.argtypes = [_f32p, _f32p, _f32p, C.c_long, C.c_long, C.c_long, _f32p]
+        L.orc_swiglu.argtypes = [_f32p, _f32p, _f32p, C.c_long]
+        L.orc_rope_tables.argtypes = [_i32p, _i32p, _i32p, C.c_long, C.c_int, C.c_int,
+                                      C.c_int, C.c_double, C.c_double, C.c_int, _f32p, _f32p]
+        L.orc_split_qk_norm.argtypes = [_f32p, _f32p, _f32p, C.c_long, C.c_long, C.c_long,
+                                        C.c_float]
+        L.orc_split_rope.argtypes = [_f32p, _f32p, _f32p, C.c_long, C.c_long, C.c_long,
+                                     C.c_int, C.c_int]
+        L.orc_attention.argtypes = [_f32p, _f32p, _f32p] + [C.c_long] * 6 + [
+            C.c_int, C.c_long, _i32p, _f32p]
+        L.orc_mot_layer.argtypes = [_f32p, C.c_long, C.c_int, _i32p, _i32p,
+                                    C.POINTER(_Expert), C.POINTER(_Dims), _i32p, _i32p,
+                                    _i32p, C.c_long, _f32p, _f32p, C.c_int, _i32p, _f32p,
+                                    _f32p, _f32p]
+        L.orc_quant_rows_i8.argtypes = [_f32p, C.c_long, C.c_long, _i8p, _f32p]
+        L.orc_gemm_i8.argtypes = [_i8p, _i8p, C.c_long, C.c_long, C.c_long, _i32p]
+        L.orc_dequant_i8.argtypes = [_i32p, _f32p, _f32p, C.c_long, C.c_long, _f32p]
+        L.orc_sage_attention.argtypes = [_f32p, _f32p, _f32p] + [C.c_long] * 8 + [_f32p]
+        L.orc_time_schedule.argtypes = [C.c_int, C.c_double, _f32p]
+        _lib = L
+    return _lib
+
+
+# ---------------------------------------------------------------------------
+# restatement wrappers (numpy in, numpy out)
+# ---------------------------------------------------------------------------
+
+def rms_norm(x, w, eps=1e-6):
+    x = _f32(x); w = _f32(w)
+    out = np.empty_like(x)
+    rows, dim = x.reshape(-1, x.shape[-1]).shape
+    lib().orc_rms_norm(_fp(x), _fp(w), eps, rows, dim, _fp(out))
+    return out
+
+
+def linear(x, w, b=None):
+    x = _f32(x); w = _f32(w)
+    b = _f32(b) if b is not None else None
+    rows = x.shape[0]
+    out = np.empty((rows, w.shape[0]), np.float32)
+    lib().orc_linear(_fp(x), _fp(w), _fp(b), rows, x.shape[1], w.shape[0], _fp(out))
+    return out
+
+
+def swiglu(g, u):
+    g = _f32(g); u = _f32(u)
+    y = np.empty_like(g)
+    lib().orc_swiglu(_fp(g), _fp(u), _fp(y), g.size)
+    return y
+
+
+def rope_tables(pos_t, pos_h, pos_w, head_dim=128, theta_t=5e6, theta_hw=1e4,
+                inv_freq_f32=False):
+    pt, ph, pw = (np.ascontiguousarray(p, np.int32) for p in (pos_t, pos_h, pos_w))
+    T = pt.size
+    c = np.empty((T, head_dim), np.float32)
+    s = np.empty((T, head_dim), np.float32)
+    lib().orc_rope_tables(_ip(pt), _ip(ph), _ip(pw), T, head_dim, head_dim // 2,
+                          head_dim // 4, theta_t, theta_hw, int(inv_freq_f32),
+                          _fp(c), _fp(s))
+    return c, s
+
+
+def split_qk_norm(x, w_t, w_hw, heads, eps=1e-6):
+    """Token-major [T][heads*hd]; returns a new array."""
+    x = _f32(x).copy()
+    T = x.shape[0]
+    hd = x.shape[1] // heads
+    lib().orc_split_qk_norm(_fp(x), _fp(_f32(w_t)), _fp(_f32(w_hw)), heads, T, hd, eps)
+    return x
+
+
+def split_rope(x, cos, sin, heads):
+    x = _f32(x).copy()
+    T = x.shape[0]
+    hd = x.shape[1] // heads
+    lib().orc_split_rope(_fp(x), _fp(_f32(cos)), _fp(_f32(sin)), heads, T, hd,
+                         hd // 2, hd // 4)
+    return x
+
+
+def attention(q, k, v, tk=None, mode=BIDIR, q_offset=0, t_index=None):
+    """q [hq][tq][d]; k/v [hkv][cap][d] (cap >= tk); out [tq][hq*d]."""
+    q = _f32(q); k = _f32(k); v = _f32(v)
+    hq, tq, d = q.shape
+    hkv, cap, _ = k.shape
+    tk = cap if tk is None else tk
+    ti = np.ascontiguousarray(t_index, np.int32) if t_index is not None else None
+    out = np.empty((tq, hq * d), np.float32)
+    lib().orc_attention(_fp(q), _fp(k), _fp(v), hq, hkv, tq, tk, d, cap, mode,
+                        q_offset, _ip(ti), _fp(out))
+    return out
+
+
+def sage_attention(q, k, v, tk=None, bq=64, bk=64):
+    q = _f32(q); k = _f32(k); v = _f32(v)
+    hq, tq, d = q.shape
+    hkv, cap, _ = k.shape
+    tk = cap if tk is None else tk
+    out = np.empty((tq, hq * d), np.float32)
+    lib().orc_sage_attention(_fp(q), _fp(k), _fp(v), hq, hkv, tq, tk, d, cap, bq, bk,
+                             _fp(out))
+    return out
+
+
+def mot_layer(x, segments, experts, dims, pos_t, pos_h, pos_w, k_prefix=None,
+              v_prefix=None, mode=BIDIR, t_index=None):
+    """The joint MoT layer. segments: list of (start, end, expert_id).
+    experts: list of two dicts keyed by EXPERT_KEYS (fp32 arrays).
+    dims: dict(hidden, heads, kv_heads, head_dim, inter, eps, theta_t, theta_hw).
+    Returns (out [T][H], k_new [hkv][T][hd], v_new [hkv][T][hd])."""
+    x = _f32(x)
+    T = x.shape[0]
+    keep = []
+    E = (_Expert * len(experts))()
+    for i, e in enumerate(experts):
+        for n in EXPERT_KEYS:
+            a = _f32(e[n]); keep.append(a)
+            setattr(E[i], n, _fp(a))
+    D = _Dims(dims["hidden"], dims["heads"], dims["kv_heads"], dims["head_dim"],
+              dims["inter"], dims.get("eps", 1e-6), dims.get("theta_t", 5e6),
+              dims.get("theta_hw", 1e4))
+    off = np.array([s[0] for s in segments] + [segments[-1][1]], np.int32)
+    ex = np.array([s[2] for s in segments], np.int32)
+    pt, ph, pw = (np.ascontiguousarray(p, np.int32) for p in (pos_t, pos_h, pos_w))
+    npre = 0 if k_prefix is None else k_prefix.shape[1]
+    kp = _f32(k_prefix) if k_prefix is not None else None
+    vp = _f32(v_prefix) if v_prefix is not None else None
+    ti = np.ascontiguousarray(t_index, np.int32) if t_index is not None else None
+    out = np.empty_like(x)
+    hkv, hd = dims["kv_heads"], dims["head_dim"]
+    kn = np.empty((hkv, T, hd), np.float32)
+    vn = np.empty((hkv, T, hd), np.float32)
+    lib().orc_mot_layer(_fp(x), T, len(segments), _ip(off), _ip(ex), E, C.byref(D),
+                        _ip(pt), _ip(ph), _ip(pw), npre, _fp(kp), _fp(vp), mode,
+                        _ip(ti), _fp(out), _fp(kn), _fp(vn))
+    return out, kn, vn
+
+
+def quant_rows_i8(x):
+    x = _f32(x)
+    rows, cols = x.shape
+    q = np.empty((rows, cols), np.int8)
+    s = np.empty(rows, np.float32)
+    lib().orc_quant_rows_i8(_fp(x), rows, cols, q.ctypes.data_as(_i8p), _fp(s))
+    return q, s
+
+
+def gemm_i8(a, w):
+    a = np.ascontiguousarray(a, np.int8); w = np.ascontiguousarray(w, np.int8)
+    M, K = a.shape
+    N = w.shape[0]
+    acc = np.empty((M, N), np.int32)
+    lib().orc_gemm_i8(a.ctypes.data_as(_i8p), w.ctypes.data_as(_i8p), M, K, N, _ip(acc))
+    return acc
+
+
+def dequant_i8(acc, s_tok, s_ch):
+    acc = np.ascontiguousarray(acc, np.int32)
+    M, N = acc.shape
+    y = np.empty((M, N), np.float32)
+    lib().orc_dequant_i8(_ip(acc), _fp(_f32(s_tok)), _fp(_f32(s_ch)), M, N, _fp(y))
+    return y
+
+
+def time_schedule(n, shift):
+    out = np.empty(n + 1, np.float32)
+    lib().orc_time_schedule(n, shift, _fp(out))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# the reference's own CPU code (fixture generation and pinning only)
+# ---------------------------------------------------------------------------
+
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref():
+    """The reference's u15::ref through oracle/ref_shim.cc."""
+    global _ref
+    if _ref is None:
+        L = C.CDLL(REF_SO)
+        L.refx_rms_norm.argtypes = [_f32p, _f32p, C.c_float, C.c_long, C.c_long, _f32p]
+        L.refx_linear.argtypes = [_f32p, _f32p, _f32p, C.c_long, C.c_long, C.c_long, _f32p]
+        L.refx_rope_inv_freq.argtypes = [C.c_int, C.c_double, _f32p]
+        L.refx_split_rope_project.argtypes = [
+            _f32p, _f32p, _f32p, _f32p, _i32p, _i32p, _i32p, C.c_long, C.c_long, C.c_int,
+            C.c_int, C.c_double, C.c_double, C.c_double, _f32p]
+        L.refx_attention.argtypes = [_f32p, _f32p, _f32p, _f32p] + [C.c_long] * 5 + [_f32p]
+        L.refx_block_causal_mask.argtypes = [_i32p, C.c_long, _f32p]
+        L.refx_decoder_layer.argtypes = [
+            _f32p, C.POINTER(_f32p)] + [C.c_long] * 5 + [C.c_double] * 3 + [
+            _i32p, _i32p, _i32p, _f32p, C.c_long, _f32p]
+        L.refx_time_schedule.argtypes = [C.c_int, C.c_double, _f32p]
+        L.refx_optimized_scale.argtypes = [_f32p, _f32p, C.c_long]
+        L.refx_optimized_scale.restype = C.c_double
+        _ref = L
+    return _ref

@@ -1,0 +1,553 @@
+/*
+ * TEST INFRASTRUCTURE ONLY -- the CPU checker for the CUDA path. See
+ * u15_oracle.h for the conventions. Paths in the citations are relative to
+ * the reference project's root.
+ *
+ * Parity is pinned by tests/test_oracle_golden.py: every routine that has a
+ * counterpart in the reference's u15::ref is compared against fixtures the
+ * reference itself produced (tests/golden/gen_golden.py, run against the
+ * reference compiled by oracle/Makefile). The W8A8 and Sage routines have
+ * no reference CPU counterpart and are restated from their published
+ * definitions; see their comments.
+ */
+#include "u15_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ */
+/* primitives                                                          */
+/* ------------------------------------------------------------------ */
+
+/* src/u15-ref.cc:15-31 -- row RMSNorm with gain, mean of squares in
+ * double. */
+void orc_rms_norm(const float* x, const float* w, float eps, long rows,
+                  long dim, float* out)
+{
+#pragma omp parallel for schedule(static)
+  for (long r = 0; r < rows; ++r) {
+    const float* xr = x + r * dim;
+    float* o = out + r * dim;
+    double acc = 0.0;
+    for (long c = 0; c < dim; ++c) acc += (double)xr[c] * (double)xr[c];
+    const double inv = 1.0 / sqrt(acc / (double)dim + (double)eps);
+    for (long c = 0; c < dim; ++c)
+      o[c] = (float)((double)xr[c] * inv * (double)w[c]);
+  }
+}
+
+/* src/u15-ref.cc:33-49 -- y = x W^T (+ b), W [out][in], double dot. */
+void orc_linear(const float* x, const float* w, const float* b, long rows,
+                long in_dim, long out_dim, float* out)
+{
+#pragma omp parallel for collapse(2) schedule(static)
+  for (long r = 0; r < rows; ++r) {
+    for (long oc = 0; oc < out_dim; ++oc) {
+      const float* xr = x + r * in_dim;
+      const float* wr = w + oc * in_dim;
+      double acc = 0.0;
+#pragma omp simd reduction(+ : acc)
+      for (long ic = 0; ic < in_dim; ++ic)
+        acc += (double)xr[ic] * (double)wr[ic];
+      if (b) acc += (double)b[oc];
+      out[r * out_dim + oc] = (float)acc;
+    }
+  }
+}
+
+/* src/u15-ref.cc:51-58 */
+void orc_silu(float* x, long n)
+{
+  for (long i = 0; i < n; ++i) {
+    const double v = (double)x[i];
+    x[i] = (float)(v / (1.0 + exp(-v)));
+  }
+}
+
+/* silu(g) * u, the MLP body of src/u15-ref.cc:292-299 */
+void orc_swiglu(const float* g, const float* u, float* y, long n)
+{
+#pragma omp parallel for schedule(static)
+  for (long i = 0; i < n; ++i) {
+    const double v = (double)g[i];
+    y[i] = (float)((v / (1.0 + exp(-v))) * (double)u[i]);
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* split-3 RoPE                                                        */
+/* ------------------------------------------------------------------ */
+
+/* src/u15-metal-ops.cc:547-605 -- [tokens][head_dim] cos/sin tables, each
+ * of the three ranges (t: [0,d_t), h: [d_t,d_t+d_h), w: [d_t+d_h, hd))
+ * filled with its own ladder, doubled cat(freqs, freqs)-style, angles
+ * formed in double and narrowed once.
+ *
+ * inv_freq_f32 = 1 narrows the inverse frequencies to float first, the way
+ * src/u15-ref.cc:64-74 (rope_inv_freq) does; 0 keeps them in double as the
+ * GPU path's table builder does. */
+void orc_rope_tables(const int* pos_t, const int* pos_h, const int* pos_w,
+                     long tokens, int head_dim, int d_t, int d_h,
+                     double theta_t, double theta_hw, int inv_freq_f32,
+                     float* cos_tab, float* sin_tab)
+{
+  const int offs[3] = {0, d_t, d_t + d_h};
+  const int width[3] = {d_t, d_h, d_h};
+  const double theta[3] = {theta_t, theta_hw, theta_hw};
+  const int* pos[3] = {pos_t, pos_h, pos_w};
+  for (int r = 0; r < 3; ++r) {
+    const int half = width[r] / 2;
+    for (long t = 0; t < tokens; ++t) {
+      const double p = (double)pos[r][t];
+      for (int i = 0; i < half; ++i) {
+        double inv = 1.0 / pow(theta[r], (double)(2 * i) / (double)width[r]);
+        if (inv_freq_f32) inv = (double)(float)inv;
+        const double a = p * inv;
+        const float cv = (float)cos(a), sv = (float)sin(a);
+        const long base = t * head_dim + offs[r];
+        cos_tab[base + i] = cv;
+        sin_tab[base + i] = sv;
+        cos_tab[base + i + half] = cv;
+        sin_tab[base + i + half] = sv;
+      }
+    }
+  }
+}
+
+/* src/u15-kernels.metal:50-87 (and src/u15-ref.cc:136-160) -- per
+ * (token, head) row of head_dim: one RMS reduction over [0, hd/2) with w_t
+ * and one over [hd/2, hd) with w_hw. Token-major [tokens][heads*hd], in
+ * place. */
+void orc_split_qk_norm(float* x, const float* w_t, const float* w_hw,
+                       long heads, long tokens, long head_dim, float eps)
+{
+  const long half = head_dim / 2;
+#pragma omp parallel for schedule(static)
+  for (long row = 0; row < tokens * heads; ++row) {
+    float* r = x + row * head_dim;
+    double at = 0.0, ah = 0.0;
+    for (long i = 0; i < half; ++i) {
+      at += (double)r[i] * (double)r[i];
+      ah += (double)r[i + half] * (double)r[i + half];
+    }
+    const double it = 1.0 / sqrt(at / (double)half + (double)eps);
+    const double ih = 1.0 / sqrt(ah / (double)half + (double)eps);
+    for (long i = 0; i < half; ++i) {
+      r[i] = (float)((double)r[i] * it * (double)w_t[i]);
+      r[i + half] = (float)((double)r[i + half] * ih * (double)w_hw[i]);
+    }
+  }
+}
+
+/* src/u15-kernels.metal:118-157 -- rotate_half within each of the three
+ * ranges, reading the first half of each range's table entries. */
+void orc_split_rope(float* x, const float* cos_tab, const float* sin_tab,
+                    long heads, long tokens, long head_dim, int d_t, int d_h)
+{
+  const int offs[3] = {0, d_t, d_t + d_h};
+  const int width[3] = {d_t, d_h, d_h};
+#pragma omp parallel for schedule(static)
+  for (long row = 0; row < tokens * heads; ++row) {
+    const long t = row / heads;
+    float* r = x + row * head_dim;
+    for (int g = 0; g < 3; ++g) {
+      const int half = width[g] / 2;
+      for (int i = 0; i < half; ++i) {
+        const long ti = t * head_dim + offs[g] + i;
+        const double c = (double)cos_tab[ti], s = (double)sin_tab[ti];
+        const double a = (double)r[offs[g] + i];
+        const double b = (double)r[offs[g] + i + half];
+        r[offs[g] + i] = (float)(a * c - b * s);
+        r[offs[g] + i + half] = (float)(b * c + a * s);
+      }
+    }
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* attention                                                           */
+/* ------------------------------------------------------------------ */
+
+/* src/u15-ref.cc:184-230 (GQA attention in double) with the mask rules of
+ * src/u15-ref.cc:169-182 and src/u15-kernels.metal:186-252, evaluated from
+ * the rule instead of a materialised mask:
+ *   ORC_BIDIR         every key j < tk
+ *   ORC_CAUSAL        j <= q_offset + i
+ *   ORC_BLOCK_CAUSAL  t[j] == t[q_offset + i]  or  j <= q_offset + i
+ * q [hq][tq][d]; k/v [hkv][kv_stride][d]; out [tq][hq*d]. */
+void orc_attention(const float* q, const float* k, const float* v, long hq,
+                   long hkv, long tq, long tk, long d, long kv_stride,
+                   int mode, long q_offset, const int* t_index, float* out)
+{
+  const double scale = 1.0 / sqrt((double)d);
+  const long group = hq / hkv;
+#pragma omp parallel
+  {
+    double* row = (double*)malloc(sizeof(double) * (size_t)tk);
+    double* acc = (double*)malloc(sizeof(double) * (size_t)d);
+#pragma omp for collapse(2) schedule(static)
+    for (long h = 0; h < hq; ++h) {
+      for (long i = 0; i < tq; ++i) {
+        const long hk = h / group;
+        const long qpos = q_offset + i;
+        const float* qi = q + (h * tq + i) * d;
+        double mx = -INFINITY;
+        for (long j = 0; j < tk; ++j) {
+          int ok = 1;
+          if (mode == ORC_CAUSAL) ok = (j <= qpos);
+          else if (mode == ORC_BLOCK_CAUSAL)
+            ok = (t_index[j] == t_index[qpos]) || (j <= qpos);
+          if (!ok) { row[j] = -INFINITY; continue; }
+          const float* kj = k + (hk * kv_stride + j) * d;
+          double s = 0.0;
+          for (long c = 0; c < d; ++c) s += (double)qi[c] * (double)kj[c];
+          row[j] = s * scale;
+          if (row[j] > mx) mx = row[j];
+        }
+        double sum = 0.0;
+        for (long j = 0; j < tk; ++j) {
+          row[j] = (row[j] == -INFINITY) ? 0.0 : exp(row[j] - mx);
+          sum += row[j];
+        }
+        const double inv = sum > 0.0 ? 1.0 / sum : 0.0;
+        for (long c = 0; c < d; ++c) acc[c] = 0.0;
+        for (long j = 0; j < tk; ++j) {
+          if (row[j] == 0.0) continue;
+          const double p = row[j] * inv;
+          const float* vj = v + (hk * kv_stride + j) * d;
+          for (long c = 0; c < d; ++c) acc[c] += p * (double)vj[c];
+        }
+        float* o = out + i * (hq * d) + h * d;
+        for (long c = 0; c < d; ++c) o[c] = (float)acc[c];
+      }
+    }
+    free(row);
+    free(acc);
+  }
+}
+
+/* ------------------------------------------------------------------ */
+/* the joint MoT layer                                                 */
+/* ------------------------------------------------------------------ */
+
+/* One MoT decoder layer over `tokens` rows split into contiguous segments,
+ * each routed to expert seg_expert[s] (0 = und, 1 = _mot_gen). The body is
+ * the single-expert src/u15-ref.cc:236-308 (decoder_layer) applied per
+ * segment for every per-token step (norms, projections, split norm, MLP),
+ * with ONE shared attention over [prefix || this block] -- the order of
+ * src/u15-backbone.cc:173-257, where K/V go to the cache before attention
+ * and queries attend the cache. The prefix K/V, when n_prefix > 0, are
+ * already normed and roped (what a cache holds): [hkv][n_prefix][hd].
+ *
+ * The rope tables use the GPU path's double inverse frequencies
+ * (src/u15-metal-ops.cc:547-605).
+ *
+ * Outputs: out [tokens][hidden]; k_new/v_new (optional) [hkv][tokens][hd],
+ * the block this layer appended to the cache. */
+void orc_mot_layer(const float* x, long T, int nseg, const int* seg_off,
+                   const int* seg_expert, const orc_expert* E,
+                   const orc_dims* d, const int* pos_t, const int* pos_h,
+                   const int* pos_w, long n_prefix, const float* k_prefix,
+                   const float* v_prefix, int mode, const int* t_index,
+                   float* out, float* k_new, float* v_new)
+{
+  const long H = d->hidden, NH = d->heads, KV = d->kv_heads,
+             HD = d->head_dim, I = d->inter;
+  const float eps = (float)d->eps;
+  const int d_t = (int)(HD / 2), d_h = (int)(HD / 4);
+  const long TK = n_prefix + T;
+
+  float* normed = malloc(sizeof(float) * T * H);
+  float* q = malloc(sizeof(float) * T * NH * HD);
+  float* kk = malloc(sizeof(float) * T * KV * HD);
+  float* vv = malloc(sizeof(float) * T * KV * HD);
+  float* qh = malloc(sizeof(float) * T * NH * HD);
+  float* kc = malloc(sizeof(float) * TK * KV * HD);
+  float* vc = malloc(sizeof(float) * TK * KV * HD);
+  float* att = malloc(sizeof(float) * T * NH * HD);
+  float* proj = malloc(sizeof(float) * T * H);
+  float* g = malloc(sizeof(float) * T * I);
+  float* u = malloc(sizeof(float) * T * I);
+  float* ctab = malloc(sizeof(float) * T * HD);
+  float* stab = malloc(sizeof(float) * T * HD);
+
+  orc_rope_tables(pos_t, pos_h, pos_w, T, (int)HD, d_t, d_h, d->theta_t,
+                  d->theta_hw, 0, ctab, stab);
+
+  /* attention half */
+  for (int s = 0; s < nseg; ++s) {
+    const long r0 = seg_off[s], n = seg_off[s + 1] - seg_off[s];
+    if (n <= 0) continue;
+    const orc_expert* w = &E[seg_expert[s]];
+    orc_rms_norm(x + r0 * H, w->input_layernorm, eps, n, H,
+                 normed + r0 * H);
+    orc_linear(normed + r0 * H, w->q_proj, NULL, n, H, NH * HD,
+               q + r0 * NH * HD);
+    orc_linear(normed + r0 * H, w->k_proj, NULL, n, H, KV * HD,
+               kk + r0 * KV * HD);
+    orc_linear(normed + r0 * H, w->v_proj, NULL, n, H, KV * HD,
+               vv + r0 * KV * HD);
+    orc_split_qk_norm(q + r0 * NH * HD, w->q_norm, w->q_norm_hw, NH, n, HD,
+                      eps);
+    orc_split_qk_norm(kk + r0 * KV * HD, w->k_norm, w->k_norm_hw, KV, n, HD,
+                      eps);
+  }
+  orc_split_rope(q, ctab, stab, NH, T, HD, d_t, d_h);
+  orc_split_rope(kk, ctab, stab, KV, T, HD, d_t, d_h);
+
+  /* head-major q; the cache holds [prefix || block] per kv head */
+  for (long t = 0; t < T; ++t)
+    for (long h = 0; h < NH; ++h)
+      memcpy(qh + (h * T + t) * HD, q + (t * NH + h) * HD,
+             sizeof(float) * HD);
+  for (long h = 0; h < KV; ++h) {
+    if (n_prefix > 0) {
+      memcpy(kc + h * TK * HD, k_prefix + h * n_prefix * HD,
+             sizeof(float) * n_prefix * HD);
+      memcpy(vc + h * TK * HD, v_prefix + h * n_prefix * HD,
+             sizeof(float) * n_prefix * HD);
+    }
+    for (long t = 0; t < T; ++t) {
+      memcpy(kc + (h * TK + n_prefix + t) * HD, kk + (t * KV + h) * HD,
+             sizeof(float) * HD);
+      memcpy(vc + (h * TK + n_prefix + t) * HD, vv + (t * KV + h) * HD,
+             sizeof(float) * HD);
+    }
+  }
+  if (k_new && v_new) {
+    for (long h = 0; h < KV; ++h) {
+      memcpy(k_new + h * T * HD, kc + (h * TK + n_prefix) * HD,
+             sizeof(float) * T * HD);
+      memcpy(v_new + h * T * HD, vc + (h * TK + n_prefix) * HD,
+             sizeof(float) * T * HD);
+    }
+  }
+  orc_attention(qh, kc, vc, NH, KV, T, TK, HD, TK, mode, n_prefix, t_index,
+                att);
+
+  /* o_proj + residual, then the MLP half, per segment */
+  for (int s = 0; s < nseg; ++s) {
+    const long r0 = seg_off[s], n = seg_off[s + 1] - seg_off[s];
+    if (n <= 0) continue;
+    const orc_expert* w = &E[seg_expert[s]];
+    orc_linear(att + r0 * NH * HD, w->o_proj, NULL, n, NH * HD, H,
+               proj + r0 * H);
+    for (long i = 0; i < n * H; ++i) proj[r0 * H + i] += x[r0 * H + i];
+    orc_rms_norm(proj + r0 * H, w->post_attention_layernorm, eps, n, H,
+                 normed + r0 * H);
+    orc_linear(normed + r0 * H, w->gate_proj, NULL, n, H, I, g + r0 * I);
+    orc_linear(normed + r0 * H, w->up_proj, NULL, n, H, I, u + r0 * I);
+    orc_swiglu(g + r0 * I, u + r0 * I, g + r0 * I, n * I);
+    orc_linear(g + r0 * I, w->down_proj, NULL, n, I, H, out + r0 * H);
+    for (long i = 0; i < n * H; ++i) out[r0 * H + i] += proj[r0 * H + i];
+  }
+
+  free(normed); free(q); free(kk); free(vv); free(qh); free(kc); free(vc);
+  free(att); free(proj); free(g); free(u); free(ctab); free(stab);
+}
+
+/* ------------------------------------------------------------------ */
+/* W8A8                                                                */
+/* ------------------------------------------------------------------ */
+
+/* Symmetric per-row int8 quantization, the rule the BASELINE W8A8 config
+ * states (the reference's own i8_gemm uses per-512-group scales inside a
+ * host library whose source is not in the tree, src/u15-metal-ops.h:71-98,
+ * so this is restated from that spec):
+ *   scale = absmax(row) / 127         (fp32 division)
+ *   q     = round_half_even(x / scale) (fp32 division), clamped to +-127
+ *   an all-zero row has scale 0 and codes 0.
+ * Every step is one IEEE fp32 operation, so the GPU kernel reproduces the
+ * codes bit for bit. Used per token for activations and per output
+ * channel for weights. */
+void orc_quant_rows_i8(const float* x, long rows, long cols, int8_t* q,
+                       float* scale)
+{
+#pragma omp parallel for schedule(static)
+  for (long r = 0; r < rows; ++r) {
+    const float* xr = x + r * cols;
+    float amax = 0.0f;
+    for (long c = 0; c < cols; ++c) {
+      const float a = fabsf(xr[c]);
+      if (a > amax) amax = a;
+    }
+    const float s = amax / 127.0f;
+    scale[r] = s;
+    for (long c = 0; c < cols; ++c) {
+      int v = 0;
+      if (s > 0.0f) {
+        const float t = xr[c] / s;
+        v = (int)rintf(t);
+        if (v > 127) v = 127;
+        if (v < -127) v = -127;
+      }
+      q[r * cols + c] = (int8_t)v;
+    }
+  }
+}
+
+/* acc[m][n] = sum_k a[m][k] * w[n][k], exact (int64 sums, |acc| < 2^31 for
+ * K <= 2^17 at |code| <= 127). */
+void orc_gemm_i8(const int8_t* a, const int8_t* w, long M, long K, long N,
+                 int32_t* acc)
+{
+#pragma omp parallel for collapse(2) schedule(static)
+  for (long m = 0; m < M; ++m) {
+    for (long n = 0; n < N; ++n) {
+      const int8_t* ar = a + m * K;
+      const int8_t* wr = w + n * K;
+      long long s = 0;
+#pragma omp simd reduction(+ : s)
+      for (long k = 0; k < K; ++k) s += (long long)ar[k] * (long long)wr[k];
+      acc[m * N + n] = (int32_t)s;
+    }
+  }
+}
+
+/* y = ((float)acc * s_tok[m]) * s_ch[n], in fp32, in that order -- the
+ * dequant the GPU epilogue applies before its bf16 rounding. */
+void orc_dequant_i8(const int32_t* acc, const float* s_tok, const float* s_ch,
+                    long M, long N, float* y)
+{
+#pragma omp parallel for schedule(static)
+  for (long m = 0; m < M; ++m)
+    for (long n = 0; n < N; ++n)
+      y[m * N + n] = ((float)acc[m * N + n] * s_tok[m]) * s_ch[n];
+}
+
+/* ------------------------------------------------------------------ */
+/* Sage int8-QK attention                                              */
+/* ------------------------------------------------------------------ */
+
+/* The SageAttention method (Zhang et al., "SageAttention: Accurate 8-bit
+ * attention for plug-and-play inference acceleration", 2024) as the
+ * reference describes its use (src/u15-metal-ops.h:294-315,
+ * src/u15-metal-ops.cc:789-833): QK^T in int8 with one scale per attention
+ * block, the key side smoothed as K - mean_tokens(K) per kv head and
+ * channel (exact under softmax: it shifts each score row by a constant),
+ * and P.V kept in floating point. The reference's own kernels are not in
+ * its tree, so this is restated from the method:
+ *   kmean[hk][c]  = (sum over the tk keys of K[hk][j][c]) / tk
+ *   ks            = K - kmean
+ *   Q blocks of bq query rows per head, K blocks of bk key rows per kv
+ *   head, each quantized with orc_quant_rows_i8's rule over the whole
+ *   block (one scale per block);
+ *   s_ij = int_dot(q8_i, k8_j) * sq * sk / sqrt(d), then softmax and P.V. */
+void orc_sage_attention(const float* q, const float* k, const float* v,
+                        long hq, long hkv, long tq, long tk, long d,
+                        long kv_stride, long bq, long bk, float* out)
+{
+  const long group = hq / hkv;
+  const double scale = 1.0 / sqrt((double)d);
+  float* ks = malloc(sizeof(float) * hkv * tk * d);
+  int8_t* k8 = malloc((size_t)(hkv * tk * d));
+  int8_t* q8 = malloc((size_t)(hq * tq * d));
+  const long nqb = (tq + bq - 1) / bq, nkb = (tk + bk - 1) / bk;
+  float* sq = malloc(sizeof(float) * hq * nqb);
+  float* sk = malloc(sizeof(float) * hkv * nkb);
+
+  for (long h = 0; h < hkv; ++h) {
+    for (long c = 0; c < d; ++c) {
+      double s = 0.0;
+      for (long j = 0; j < tk; ++j) s += (double)k[(h * kv_stride + j) * d + c];
+      const float mean = (float)(s / (double)tk);
+      for (long j = 0; j < tk; ++j)
+        ks[(h * tk + j) * d + c] = k[(h * kv_stride + j) * d + c] - mean;
+    }
+  }
+  /* block quantization: a block is rows x d values sharing one scale */
+  for (long h = 0; h < hq; ++h) {
+    for (long b = 0; b < nqb; ++b) {
+      const long r0 = b * bq, n = (r0 + bq <= tq) ? bq : tq - r0;
+      float s;
+      float amax = 0.0f;
+      const float* src = q + (h * tq + r0) * d;
+      for (long i = 0; i < n * d; ++i)
+        if (fabsf(src[i]) > amax) amax = fabsf(src[i]);
+      s = amax / 127.0f;
+      sq[h * nqb + b] = s;
+      for (long i = 0; i < n * d; ++i) {
+        int vq = 0;
+        if (s > 0.0f) {
+          vq = (int)rintf(src[i] / s);
+          if (vq > 127) vq = 127;
+          if (vq < -127) vq = -127;
+        }
+        q8[(h * tq + r0) * d + i] = (int8_t)vq;
+      }
+    }
+  }
+  for (long h = 0; h < hkv; ++h) {
+    for (long b = 0; b < nkb; ++b) {
+      const long r0 = b * bk, n = (r0 + bk <= tk) ? bk : tk - r0;
+      float amax = 0.0f;
+      const float* src = ks + (h * tk + r0) * d;
+      for (long i = 0; i < n * d; ++i)
+        if (fabsf(src[i]) > amax) amax = fabsf(src[i]);
+      const float s = amax / 127.0f;
+      sk[h * nkb + b] = s;
+      for (long i = 0; i < n * d; ++i) {
+        int vq = 0;
+        if (s > 0.0f) {
+          vq = (int)rintf(src[i] / s);
+          if (vq > 127) vq = 127;
+          if (vq < -127) vq = -127;
+        }
+        k8[(h * tk + r0) * d + i] = (int8_t)vq;
+      }
+    }
+  }
+
+#pragma omp parallel
+  {
+    double* row = malloc(sizeof(double) * (size_t)tk);
+    double* acc = malloc(sizeof(double) * (size_t)d);
+#pragma omp for collapse(2) schedule(static)
+    for (long h = 0; h < hq; ++h) {
+      for (long i = 0; i < tq; ++i) {
+        const long hk = h / group;
+        const int8_t* qi = q8 + (h * tq + i) * d;
+        const double sqv = (double)sq[h * nqb + i / bq];
+        double mx = -INFINITY;
+        for (long j = 0; j < tk; ++j) {
+          const int8_t* kj = k8 + (hk * tk + j) * d;
+          long long dot = 0;
+          for (long c = 0; c < d; ++c) dot += (long long)qi[c] * kj[c];
+          row[j] = (double)dot * sqv * (double)sk[hk * nkb + j / bk] * scale;
+          if (row[j] > mx) mx = row[j];
+        }
+        double sum = 0.0;
+        for (long j = 0; j < tk; ++j) {
+          row[j] = exp(row[j] - mx);
+          sum += row[j];
+        }
+        for (long c = 0; c < d; ++c) acc[c] = 0.0;
+        for (long j = 0; j < tk; ++j) {
+          const double p = row[j] / sum;
+          const float* vj = v + (hk * kv_stride + j) * d;
+          for (long c = 0; c < d; ++c) acc[c] += p * (double)vj[c];
+        }
+        float* o = out + i * (hq * d) + h * d;
+        for (long c = 0; c < d; ++c) o[c] = (float)acc[c];
+      }
+    }
+    free(row);
+    free(acc);
+  }
+  free(ks); free(k8); free(q8); free(sq); free(sk);
+}
+
+/* ------------------------------------------------------------------ */
+/* sampling                                                            */
+/* ------------------------------------------------------------------ */
+
+/* src/u15-ref.cc:722-733 -- sigma = 1 - i/n, shifted, t = 1 - sigma. */
+void orc_time_schedule(int num_steps, double shift, float* out)
+{
+  for (int i = 0; i <= num_steps; ++i) {
+    double sigma = 1.0 - (double)i / (double)num_steps;
+    sigma = shift * sigma / (1.0 + (shift - 1.0) * sigma);
+    out[i] = (float)(1.0 - sigma);
+  }
+}
