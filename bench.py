@@ -1,0 +1,417 @@
+"""Benchmark: one SenseNova-U1.5 MoT layer at 4096 tokens on B200.
+
+Workload (BASELINE configs 2 and 4 in one layer): 4096 tokens routed 512 to
+the understanding expert and 3584 to the _mot_gen expert (the MoT projection
+GEMMs: QKV 4096x6144, O 4096x4096, gate+up 4096x24576, down 12288x4096),
+joint bidirectional attention of the 4096 queries over a frozen 320-token
+prefix plus themselves (4416 keys, GQA 32/8 x 128) through the paged KV
+cache. Random-init weights N(0, 0.02) (no checkpoint), synthetic inputs
+N(0, 1), all seeded. A step = one layer forward; steps rotate over 4 layers
+with distinct weights (772 MB per layer, far above the 126 MB L2), so every
+step streams its weights from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank runs an independent replica (a CFG branch or seed
+of its own); no collective is on the data path, value = whole-job
+effective ms per layer (max-over-ranks time / layers done by all ranks).
+--impl reference times the reference's own CPU implementation (u15-ref,
+compiled from the reference sources into oracle/_ref) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "vpipe-sensenova-u1.5_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "ms/MoT layer @4096 tok (bf16)"
+UNIT = "ms"
+M_TOK, N_UND, N_PRE = 4096, 512, 320
+H, NH, KV, HD, I = 4096, 32, 8, 128, 12288
+TK = N_PRE + M_TOK
+GEMMS = {"qkv": (H, (NH + 2 * KV) * HD), "o": (NH * HD, H), "gate_up": (H, 2 * I),
+         "down": (I, H)}
+PROJ_FLOP = sum(2.0 * M_TOK * k * n for k, n in GEMMS.values())      # 1.5806e12
+ATTN_FLOP = 4.0 * NH * M_TOK * TK * HD                                  # 2.964e11
+LAYER_FLOP = PROJ_FLOP + ATTN_FLOP
+PUBLISHED_MS = 148.0   # Apple M5, bf16 (README.md:112-114 of the reference)
+WORKLOAD = ("MoT layer @4096 tok: 512 und + 3584 gen routed, frozen 320-token prefix, "
+            "bidirectional GQA 32/8x128 over 4416 keys (paged KV)")
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def positions():
+    pt = np.concatenate([N_PRE + np.arange(N_UND), np.full(M_TOK - N_UND, N_PRE + N_UND)])
+    gh, gw = 56, 64
+    ph = np.concatenate([np.zeros(N_UND), np.repeat(np.arange(gh), gw)])
+    pw = np.concatenate([np.zeros(N_UND), np.tile(np.arange(gw), gh)])
+    return [a.astype(np.int32) for a in (pt, ph, pw)]
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv",
+                                       "-lms", "200", "-i", str(self.dev)],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                      text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        if not getattr(self, "out", ""):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = list(csv.reader(io.StringIO(self.out)))[1:]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1].split()[0]))
+                mx = float(r[2].split()[0])
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if "Active" in v and "Not" not in v:
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def ev_time(fn, n, stream=None):
+    """Average ms of fn() over n runs, CUDA events on the current stream."""
+    import torch
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(n):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / n
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own u15-ref (or the restatement) row-sharded
+# ---------------------------------------------------------------------------
+class CpuLayer:
+    """ms per MoT layer @4096 tok from a bounded sample of rows: ref::linear
+    over the seven projections and ref::attention for the sampled queries,
+    rows sharded over threads (rows are independent, results identical)."""
+
+    def __init__(self, threads, rows):
+        import ctypes as C
+        from oracle import oracle as O
+        self.C = C
+        if O.ref_available():
+            self.kind, L = "reference", O.ref()
+            self.lin, self.att = L.refx_linear, L.refx_attention
+        else:
+            self.kind, L = "port", O.lib()
+            self.lin = L.orc_linear
+            self.att = None
+            self.O = O
+        self.threads, self.rows = threads, rows
+        rng = np.random.default_rng(0)
+        f = lambda *s: (rng.standard_normal(s, dtype=np.float32) * 0.02)  # noqa: E731
+        self.W = {"q": f(NH * HD, H), "k": f(KV * HD, H), "v": f(KV * HD, H), "o": f(H, NH * HD),
+                  "gate": f(I, H), "up": f(I, H), "down": f(H, I)}
+        self.x = rng.standard_normal((rows, max(H, I)), dtype=np.float32)
+        self.q = rng.standard_normal((NH, rows, HD), dtype=np.float32)
+        self.k = rng.standard_normal((KV, TK, HD), dtype=np.float32)
+        self.v = rng.standard_normal((KV, TK, HD), dtype=np.float32)
+
+    def _shard(self, fn):
+        n = self.rows
+        parts = [(i * n // self.threads, (i + 1) * n // self.threads) for i in range(self.threads)]
+        ts = [threading.Thread(target=fn, args=p) for p in parts if p[1] > p[0]]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    def step(self):
+        C = self.C
+        fp = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))  # noqa: E731
+        t0 = time.perf_counter()
+        for name, w in self.W.items():
+            kin = w.shape[1]
+
+            def run(a, b, w=w, kin=kin):
+                xs = np.ascontiguousarray(self.x[a:b, :kin])
+                out = np.empty((b - a, w.shape[0]), np.float32)
+                self.lin(fp(xs), fp(w), None, b - a, kin, w.shape[0], fp(out))
+            self._shard(run)
+
+        def att(a, b):
+            qs = np.ascontiguousarray(self.q[:, a:b])
+            out = np.empty((b - a, NH * HD), np.float32)
+            if self.att is not None:
+                self.att(fp(qs), fp(self.k), fp(self.v), None, NH, KV, b - a, TK, HD, fp(out))
+            else:
+                self.O.lib().orc_attention(fp(qs), fp(self.k), fp(self.v), NH, KV, b - a, TK,
+                                           HD, TK, 0, 0, None, fp(out))
+        self._shard(att)
+        dt = time.perf_counter() - t0
+        return dt * 1e3 * (M_TOK / self.rows)   # extrapolated ms per layer
+
+    def describe(self):
+        return (f"{self.rows} of 4096 token rows through all seven projections and "
+                f"attention over {TK} keys, extrapolated x{M_TOK // self.rows}; "
+                f"u15::ref::linear/attention row-sharded over {self.threads} threads")
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cpu = CpuLayer(threads, rows=max(32, 2 * threads))
+    for _ in range(args.warmup):
+        cpu.step()
+    vals = [cpu.step() for _ in range(args.steps)]
+    v = float(np.median(vals))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": v,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": v / PUBLISHED_MS,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": M_TOK, "seq_len": TK,
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": cpu.kind,
+                             "sample": cpu.describe()},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local):
+    import torch
+    import u15b200
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    n_layers = args.layers
+    m = u15b200.Model(int8=True, n_layers=n_layers)
+    m.bind_random(seed=1234 + rank, std=0.02, norm_mean=1.0, norm_std=0.2)
+    m.finalize()
+    kv = m.make_cache(TK)
+    g = torch.Generator(device="cuda").manual_seed(99 + rank)
+    for li in range(n_layers):
+        kv.write(li, False, torch.randn(KV, N_PRE, HD, device="cuda", generator=g).bfloat16())
+        kv.write(li, True, torch.randn(KV, N_PRE, HD, device="cuda", generator=g).bfloat16())
+    pos = [torch.from_numpy(p).cuda() for p in positions()]
+    segs = [(0, N_UND, 0), (N_UND, M_TOK, 1)]
+    x0 = torch.randn(M_TOK, H, device="cuda", generator=g).bfloat16()
+    x = x0.clone()
+    state = {"i": 0}
+
+    def step(int8=False, sage=False):
+        li = state["i"] % n_layers
+        state["i"] += 1
+        m.layer_forward(li, x, kv, N_PRE, TK, *pos, segments=segs, int8=int8, sage=sage)
+
+    ops = u15b200.CudaOps(local)
+    for _ in range(args.warmup):
+        step()
+    ops.sync()
+    x.copy_(x0)
+
+    # ---- timed region: K layer steps, bf16 ----
+    def timed(fn, k):
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(k):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e)
+        if dist is not None:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    with Clocks(local) as clk:
+        total_ms = timed(step, args.steps)
+    ops.sync()
+    ms_step = total_ms / args.steps
+    value = ms_step / world
+    launches_per_layer = 9
+
+    # ---- W8A8 and Sage variants (same loop, same rules) ----
+    for _ in range(args.warmup):
+        step(int8=True)
+    x.copy_(x0)
+    ms_i8 = timed(lambda: step(int8=True), args.steps) / args.steps
+    for _ in range(args.warmup):
+        step(int8=True, sage=True)
+    x.copy_(x0)
+    ms_i8_sage = timed(lambda: step(int8=True, sage=True), args.steps) / args.steps
+    ops.sync()
+
+    # ---- e2e through the C ABI with host buffers (H2D + layer + D2H) ----
+    xh = x0.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+
+    def e2e_step():
+        li = state["i"] % n_layers
+        state["i"] += 1
+        m.layer_forward_host(li, xh, oh, kv, N_PRE, TK, *pos, segments=segs)
+    for _ in range(args.warmup):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps) / args.steps
+
+    # ---- per-kernel timing on the launching stream (dominant: gate_up) ----
+    hbm, bf16_peak, peak_kind = peaks()
+    kern = {}
+    if rank == 0:
+        xa = torch.randn(M_TOK, I, device="cuda").bfloat16()
+        for name, (K, N) in GEMMS.items():
+            w = (torch.randn(2, N, K, device="cuda") * 0.02).bfloat16()
+            epi = {"gate_up": 2, "o": 1, "down": 1}.get(name, 0)
+            y = torch.empty(M_TOK, N // 2 if epi == 2 else N, device="cuda").bfloat16()
+            xin = xa[:, :K].contiguous()
+            fn = lambda: ops.mot_linear(xin, w, segs, y, M_TOK, K, N, epilogue=epi,  # noqa
+                                        resid=y if epi == 1 else None)
+            for _ in range(3):
+                fn()
+            t = ev_time(fn, max(5, args.steps))
+            kern[name] = {"ms": t, "tflops": 2.0 * M_TOK * K * N / t / 1e9}
+            del w, y, xin
+        q = torch.randn(NH, M_TOK, HD, device="cuda").bfloat16()
+        kc = torch.randn(KV, TK, HD, device="cuda").bfloat16()
+        vc = torch.randn(KV, TK, HD, device="cuda").bfloat16()
+        o = torch.empty(M_TOK, NH * HD, device="cuda").bfloat16()
+        fn = lambda: ops.attention(q, kc, vc, o, NH, KV, M_TOK, TK, cap=TK)  # noqa: E731
+        fn()
+        t = ev_time(fn, max(5, args.steps))
+        kern["attention"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
+        ws = ops.sage_workspace(NH, KV, M_TOK, TK)
+        fn = lambda: ops.attention(q, kc, vc, o, NH, KV, M_TOK, TK, cap=TK, sage_ws=ws)  # noqa
+        fn()
+        t = ev_time(fn, max(5, args.steps))
+        kern["attention_sage"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
+        torch.cuda.empty_cache()
+
+    # ---- CPU baseline (rank 0, N=1 only): bounded sample, ~10-30 s ----
+    cpu_line = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        cpu = CpuLayer(threads, rows=max(32, 2 * threads))
+        cpu.step()
+        vals = [cpu.step() for _ in range(3)]
+        cpu_line = {"value": float(np.median(vals)), "unit": UNIT, "cores": threads,
+                    "kind": cpu.kind, "sample": cpu.describe() + "; median of 3"}
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    gu = kern.get("gate_up", {})
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        try:
+            traffic = json.load(open(tf)).get("gemm_gate_up_bytes_per_launch")
+        except Exception:
+            traffic = None
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_MS, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": M_TOK * world, "seq_len": TK,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: 4 layers x 772 MB of weights rotated per step"},
+        "tflops_per_gpu": LAYER_FLOP / ms_step / 1e9,
+        "i8": {"ms_per_layer": ms_i8 / world, "ms_per_step": ms_i8,
+               "sage_ms_per_step": ms_i8_sage},
+        "e2e": {"value": ms_e2e / world, "unit": UNIT,
+                "h2d_bytes_per_step": M_TOK * H * 2, "d2h_bytes_per_step": M_TOK * H * 2},
+        "gpu_launches": launches_per_layer * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "gemm_tc (gate_up, routed, SwiGLU epilogue)",
+                     "achieved": gu.get("tflops"), "peak": bf16_peak, "unit": "TFLOP/s",
+                     "frac": (gu.get("tflops") or 0) / bf16_peak, "traffic": traffic,
+                     "peak_kind": f"{peak_kind} burst bf16"},
+        "kernels": kern,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu_line,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

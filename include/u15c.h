@@ -1,0 +1,339 @@
+/*
+ * u15c.h -- C ABI of libu15c.so, the B200 (sm_100a) implementation of the
+ * SenseNova-U1.5 Mixture-of-Transformers backbone layer.
+ *
+ * The entry points replace the operator surface the reference's backbone
+ * calls (class MetalOps, src/u15-metal-ops.h:59-403 of the reference), the
+ * backbone itself (class U15Backbone, src/u15-backbone.h:67-170) and the
+ * weight bind step (U15Weights::load, src/u15-weights.h:152-197). Each
+ * declaration names the reference interface it replaces.
+ *
+ * Conventions (as the reference's):
+ *   - weights [out][in]; activations token-major [tokens][dim]; bf16 unless
+ *     a name says i8/f32; every pointer argument is a DEVICE pointer unless
+ *     documented as host;
+ *   - attention q is head-major [heads][tokens][128]; the K/V cache is either
+ *     the reference's contiguous [kv_heads][capacity][128] (page_table ==
+ *     NULL, `cap` = capacity in tokens) or a paged pool
+ *     [num_pages][kv_heads][64][128] addressed through a device int32 page
+ *     table of logical page -> physical page (64 tokens per page);
+ *   - head_dim is 128 (the model's); the split RoPE ranges are t [0,64),
+ *     h [64,96), w [96,128);
+ *   - every call returns U15C_OK (0) or an error code; u15c_last_error()
+ *     gives this thread's message for the last failure. Calls that launch
+ *     work are asynchronous on `stream` and allocate nothing.
+ *   - a device-side wait that runs out (a kernel-internal watchdog, about
+ *     2 s) writes a code into the device status word instead of hanging;
+ *     u15c_sync() and u15c_device_status() report it.
+ */
+#ifndef U15C_H
+#define U15C_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* u15c_stream; /* a cudaStream_t (NULL: the legacy default stream) */
+
+#define U15C_OK 0
+#define U15C_EINVAL 1   /* bad argument, refused before any launch */
+#define U15C_ECUDA 2    /* a CUDA runtime/driver call failed */
+#define U15C_ENOMEM 3   /* device allocation failed */
+#define U15C_EDEVICE 4  /* a kernel's bounded wait ran out (device status word) */
+#define U15C_ESTOPPED 5 /* the cooperative stop fired (U15Backbone::kStopped) */
+
+#define U15C_EPI_STORE 0    /* y = acc (+ bias) */
+#define U15C_EPI_RESIDUAL 1 /* y = resid + acc (o_proj / down_proj + add) */
+#define U15C_EPI_SWIGLU 2   /* gate|up rows interleaved in 128-row blocks: y = silu(g)*u */
+
+#define U15C_ATTN_BIDIRECTIONAL 0 /* Attn::Bidirectional, src/u15-backbone.h:48-57 */
+#define U15C_ATTN_CAUSAL 1        /* Attn::Causal */
+#define U15C_ATTN_BLOCK_CAUSAL 2  /* Attn::BlockCausal */
+
+#define U15C_EXPERT_UND 0 /* Expert::Und, src/u15-backbone.h:46 */
+#define U15C_EXPERT_GEN 1 /* Expert::Gen (the _mot_gen weight set) */
+
+/* ------------------------------------------------------------------ */
+/* library                                                             */
+/* ------------------------------------------------------------------ */
+
+/* Message of this thread's last failed call ("" if none). */
+const char* u15c_last_error(void);
+const char* u15c_version(void);
+
+/* Prepare `device` (makes it current, reads its SM count, allocates the
+ * device status word). Replaces MetalOps::init (src/u15-metal-ops.cc:39-245),
+ * which validates every kernel: here every kernel is compiled in, so init
+ * checks the device is sm_100 and records its properties. Other calls
+ * initialise the current device on first use. */
+int u15c_init(int device, unsigned flags);
+
+/* Read and clear the device status word of `device` (0 = no watchdog fired). */
+int u15c_device_status(int device, unsigned* code);
+
+/* cudaStreamSynchronize + the status word: U15C_EDEVICE if a watchdog fired. */
+int u15c_sync(u15c_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* GEMMs                                                               */
+/* ------------------------------------------------------------------ */
+
+/* MetalOps::linear (src/u15-metal-ops.h:102-108, .cc:448-468):
+ * y[M][N] = x[M][K] w[N][K]^T (+ bias[N]). K must be a multiple of 8. */
+int u15c_linear_bf16(u15c_stream stream, const void* x, const void* w, const void* bias,
+                     void* y, int M, int K, int N);
+
+/* The MoT token-routed projection (the reference selects the expert per
+ * pass at src/u15-backbone.cc:189; here one launch routes per segment).
+ * w_stack: [n_experts][N][K]; rows [seg_off[i], seg_off[i+1]) use expert
+ * seg_expert[i] (host arrays, nseg <= 8, segments cover [0, M)).
+ * epilogue: U15C_EPI_STORE (y [M][N], optional bias [n_experts][N]),
+ * U15C_EPI_RESIDUAL (y = resid + acc; y may equal resid), U15C_EPI_SWIGLU
+ * (N = 2*inter rows interleaved [gate 128 | up 128]..., y [M][N/2]; the
+ * layout MetalOps::swiglu_fused expects, src/u15-metal-ops.h:121-135, with
+ * 128-row blocks instead of single rows). */
+int u15c_mot_linear_bf16(u15c_stream stream, const void* x, const void* w_stack,
+                         int n_experts, const int* seg_off, const int* seg_expert, int nseg,
+                         int epilogue, const void* bias, const void* resid, void* y, int M,
+                         int K, int N);
+
+/* Symmetric per-row int8 quantisation (per token for activations, per
+ * output channel for weights): scale = absmax/127, q = rn_even(x/scale)
+ * clamped to +-127. The activation half of i8_gemm
+ * (src/u15-metal-ops.h:71-98; BASELINE's W8A8 rule). */
+int u15c_quant_rows_i8(u15c_stream stream, const void* x, int8_t* q, float* scale, int rows,
+                       int cols);
+
+/* i8_gemm W8A8 (src/u15-metal-ops.cc:291-306, I8GemmContext::gemm):
+ * acc = xq[M][K] . wq[N][K]^T in int32 (exact), y = bf16(acc*s_tok[m]*s_ch[n]
+ * (+ bias)). acc_dump, when non-NULL, receives the raw int32 [M][N]. */
+int u15c_linear_i8(u15c_stream stream, const int8_t* xq, const float* s_tok, const int8_t* wq,
+                   const float* s_ch, const void* bias, void* y, int32_t* acc_dump, int M, int K,
+                   int N);
+
+/* The routed W8A8 projection: wq_stack [n_experts][N][K], s_ch_stack
+ * [n_experts][N]; segments and epilogues as u15c_mot_linear_bf16. */
+int u15c_mot_linear_i8(u15c_stream stream, const int8_t* xq, const float* s_tok,
+                       const int8_t* wq_stack, const float* s_ch_stack, int n_experts,
+                       const int* seg_off, const int* seg_expert, int nseg, int epilogue,
+                       const void* resid, void* y, int32_t* acc_dump, int M, int K, int N);
+
+/* ------------------------------------------------------------------ */
+/* norms, RoPE, layout                                                 */
+/* ------------------------------------------------------------------ */
+
+/* MetalOps::rms_norm (src/u15-metal-ops.h:146-154). dim % 8 == 0. */
+int u15c_rms_norm(u15c_stream stream, const void* x, const void* w, void* y, int rows, int dim,
+                  float eps);
+/* The same with one gain row per expert, w_stack [n_experts][dim]. */
+int u15c_mot_rms_norm(u15c_stream stream, const void* x, const void* w_stack, int n_experts,
+                      const int* seg_off, const int* seg_expert, int nseg, void* y, int rows,
+                      int dim, float eps);
+
+/* MetalOps::split_qk_norm (src/u15-metal-ops.h:156-161,
+ * src/u15-kernels.metal:50-87): in place on token-major [tokens][heads*128]. */
+int u15c_split_qk_norm(u15c_stream stream, void* x, const void* w_t, const void* w_hw,
+                       int heads, int tokens, int head_dim, float eps);
+
+/* MetalOps::split_rope (src/u15-metal-ops.h:163-169,
+ * src/u15-kernels.metal:118-157): in place; cos/sin f32 [tokens][128]. */
+int u15c_split_rope(u15c_stream stream, void* x, const float* cos_tab, const float* sin_tab,
+                    int heads, int tokens, int head_dim, int d_t, int d_h);
+
+/* MetalOps::build_rope_tables (src/u15-metal-ops.h:171-185, .cc:547-605),
+ * on the device with fp64 angles. pos_* are device int32 [tokens]. */
+int u15c_build_rope_tables(u15c_stream stream, const int32_t* pos_t, const int32_t* pos_h,
+                           const int32_t* pos_w, int tokens, int head_dim, int d_t, int d_h,
+                           double theta_t, double theta_hw, float* cos_tab, float* sin_tab);
+
+/* The QKV post-processing of one layer, fused: split q/k norm (per-expert
+ * gains, norms_stack [n_experts][4][64] = q_norm, q_norm_hw, k_norm,
+ * k_norm_hw), split RoPE, q -> head-major q_out [heads][T][128], k/v
+ * appended to the cache at token kv_off. Replaces split_qk_norm x2,
+ * split_rope x2, transpose_thd and transpose_into_cache x2
+ * (src/u15-backbone.cc:199-214). qkv is token-major [T][(heads+2*kv_heads)*128]. */
+int u15c_qkv_post(u15c_stream stream, const void* qkv, const void* norms_stack, int n_experts,
+                  const int* seg_off, const int* seg_expert, int nseg, const float* cos_tab,
+                  const float* sin_tab, void* q_out, void* k_cache, void* v_cache,
+                  const int32_t* page_table, int cap, int heads, int kv_heads, int T, int kv_off,
+                  float eps);
+
+/* MetalOps::transpose_thd / transpose_htd (src/u15-metal-ops.h:332-342). */
+int u15c_transpose_thd(u15c_stream stream, const void* in, void* out, int T, int H, int D);
+int u15c_transpose_htd(u15c_stream stream, const void* in, void* out, int T, int H, int D);
+
+/* MetalOps::transpose_into_cache (src/u15-metal-ops.h:344-348): [T][H*128]
+ * -> contiguous cache [H][cap][128] at token `offset` (the KV append). */
+int u15c_transpose_into_cache(u15c_stream stream, const void* in, void* cache, int T, int H,
+                              int D, int cap, int offset);
+/* The same into a paged pool [pages][H][64][128] through `page_table`. */
+int u15c_kv_append(u15c_stream stream, const void* in, void* pages, const int32_t* page_table,
+                   int T, int H, int offset);
+
+/* ------------------------------------------------------------------ */
+/* elementwise (src/u15-metal-ops.h:207-212, 359-370)                   */
+/* ------------------------------------------------------------------ */
+int u15c_swiglu(u15c_stream stream, const void* gate, const void* up, void* y, int rows,
+                int inter);
+int u15c_add(u15c_stream stream, void* dst, const void* src, long n);
+int u15c_add_row(u15c_stream stream, void* dst, const void* row, int rows, int dim);
+int u15c_silu(u15c_stream stream, void* x, long n);
+
+/* ------------------------------------------------------------------ */
+/* attention                                                           */
+/* ------------------------------------------------------------------ */
+
+/* Bytes of device workspace the Sage int8-QK path needs at this geometry
+ * (the role of MetalOps::sage_lend's arena, src/u15-metal-ops.h:316-318). */
+size_t u15c_sage_workspace_bytes(int hq, int hkv, int tq, int tk);
+
+/* Grouped-query flash attention, head_dim 128.
+ * q [hq][tq][128]; K/V as described at the top (contiguous when page_table
+ * is NULL, then `cap` is the capacity); out token-major [tq][hq*128].
+ * mode: U15C_ATTN_*; q_offset places the queries in the key range (causal
+ * rules); t_index: device int32 [tk] (block-causal). sage_ws non-NULL
+ * selects the Sage int8-QK path (bidirectional only; size from
+ * u15c_sage_workspace_bytes). Replaces MetalOps::sdpa, ::sdpa_steel and
+ * ::sdpa_block_causal (src/u15-metal-ops.h:214-331). */
+int u15c_attention(u15c_stream stream, const void* q, const void* k, const void* v,
+                   const int32_t* page_table, int cap, void* out, int hq, int hkv, int tq,
+                   int tk, int head_dim, int mode, int q_offset, const int32_t* t_index,
+                   void* sage_ws);
+
+/* The reference's three attention entry points with their own argument
+ * order, over the contiguous cache (kv stride = cap tokens):
+ * MetalOps::sdpa (src/u15-metal-ops.h:214-232): full or causal. */
+int u15c_sdpa(u15c_stream stream, const void* q, const void* k, const void* v, void* out,
+              int hq, int hkv, int tq, int tk, int d, int cap, int causal, int q_offset);
+/* MetalOps::sdpa_steel (src/u15-metal-ops.h:282-289): bidirectional; Sage
+ * when sage_ws is non-NULL. */
+int u15c_sdpa_steel(u15c_stream stream, const void* q, const void* k, const void* v, void* out,
+                    int hq, int hkv, int tq, int tk, int d, int cap, void* sage_ws);
+/* MetalOps::sdpa_block_causal (src/u15-metal-ops.h:320-331). */
+int u15c_sdpa_block_causal(u15c_stream stream, const void* q, const void* k, const void* v,
+                           void* out, const int32_t* t_index, int hq, int hkv, int tq, int tk,
+                           int d, int cap, int q_offset);
+
+/* ------------------------------------------------------------------ */
+/* model: weights, KV cache, backbone                                   */
+/* ------------------------------------------------------------------ */
+
+typedef struct u15c_model u15c_model; /* U15Weights + U15Backbone */
+typedef struct u15c_kv u15c_kv;       /* KvCache, src/u15-backbone.h:60-66 (paged) */
+
+typedef struct u15c_config {
+  int n_layers;   /* 42 */
+  int hidden;     /* 4096 */
+  int heads;      /* 32 */
+  int kv_heads;   /* 8 */
+  int head_dim;   /* 128 */
+  int inter;      /* 12288 */
+  int n_experts;  /* 2: und, _mot_gen */
+  double eps;     /* 1e-6 */
+  double theta_t; /* 5e6 */
+  double theta_hw;/* 1e4 */
+} u15c_config;
+
+#define U15C_MODEL_INT8 1u /* also bind the W8A8 twin of every projection */
+
+/* tensor ids for u15c_model_bind, the 13 per-expert tensors of
+ * src/u15-weights.cc:539-578 */
+#define U15C_T_INPUT_LN 0
+#define U15C_T_POST_LN 1
+#define U15C_T_Q 2
+#define U15C_T_K 3
+#define U15C_T_V 4
+#define U15C_T_O 5
+#define U15C_T_Q_NORM 6
+#define U15C_T_K_NORM 7
+#define U15C_T_Q_NORM_HW 8
+#define U15C_T_K_NORM_HW 9
+#define U15C_T_GATE 10
+#define U15C_T_UP 11
+#define U15C_T_DOWN 12
+#define U15C_T_FINAL_NORM 13 /* trunk: `norm` (und) / `norm_mot_gen`; layer ignored */
+
+#define U15C_DT_F32 0
+#define U15C_DT_F16 1
+#define U15C_DT_BF16 2
+
+/* U15Weights::load + U15Backbone::create: allocate the bound layout for
+ * cfg (all layers, all experts). */
+int u15c_model_create(const u15c_config* cfg, unsigned flags, u15c_model** out);
+void u15c_model_destroy(u15c_model* m);
+
+/* U15Weights bind_bf16_/bind_matrix_ (src/u15-weights.cc:102-151,
+ * 516-603): convert one tensor (f32/f16/bf16, host or device) to bf16 with
+ * round-to-nearest-even and place it in the bound layout (q|k|v fused,
+ * gate|up interleaved, experts stacked). */
+int u15c_model_bind(u15c_model* m, u15c_stream stream, int layer, int expert, int tensor,
+                    const void* src, int dtype, int src_on_host);
+/* Seeded synthetic weights (no checkpoint): projections N(0, std), norm
+ * gains N(norm_mean, norm_std). */
+int u15c_model_bind_random(u15c_model* m, u15c_stream stream, uint64_t seed, float std,
+                           float norm_mean, float norm_std);
+/* Build the W8A8 twins (per-output-channel int8) from the bound bf16. */
+int u15c_model_finalize(u15c_model* m, u15c_stream stream);
+
+size_t u15c_model_weight_bytes(const u15c_model* m);
+/* U15Backbone::scratch_bytes (src/u15-backbone.cc:150-165) of this layout. */
+size_t u15c_model_scratch_bytes(const u15c_model* m, int n);
+/* U15Backbone::kv_bytes (src/u15-backbone.cc:54-61), rounded to pages. */
+size_t u15c_model_kv_bytes(const u15c_model* m, int capacity);
+
+/* U15Backbone::make_cache (src/u15-backbone.cc:63-90): a paged bf16 cache of
+ * `capacity` tokens for every layer. */
+int u15c_kv_create(u15c_model* m, int capacity, u15c_kv** out);
+void u15c_kv_destroy(u15c_kv* kv);
+int u15c_kv_capacity(const u15c_kv* kv);
+/* Replace the logical->physical page map (host int32[n], a permutation of
+ * the cache's pages); the paged layout is then exercised non-contiguously. */
+int u15c_kv_set_page_table(u15c_kv* kv, const int32_t* pages_host, int n);
+/* Read one layer's K or V for tokens [0, n) into a contiguous
+ * [kv_heads][n][128] buffer (tests, diagnostics). */
+int u15c_kv_read(u15c_kv* kv, u15c_stream stream, int layer, int which_v, void* out, int n);
+/* Write a prefix of one layer's K or V from a contiguous [kv_heads][n][128]
+ * buffer at tokens [0, n) (a frozen prefix prepared elsewhere). */
+int u15c_kv_write(u15c_kv* kv, u15c_stream stream, int layer, int which_v, const void* in,
+                  int n);
+
+#define U15C_FWD_INT8 1u /* W8A8 projections (i8_gemm) */
+#define U15C_FWD_SAGE 2u /* Sage int8-QK on the bidirectional pass */
+
+/* One MoT layer for one branch: U15Backbone::layer_step_
+ * (src/u15-backbone.cc:173-257), x [n][hidden] updated in place, tokens
+ * routed per segment (host seg arrays), K/V written at kv_off, attention
+ * over kv_len keys by rule `attn`. pos_* are device int32 [n]; t_index is
+ * device int32 [kv_len] (block-causal). */
+int u15c_layer_forward(u15c_model* m, u15c_stream stream, int layer, void* x, int n,
+                       const int* seg_off, const int* seg_expert, int nseg, u15c_kv* kv,
+                       int kv_off, int kv_len, const int32_t* pos_t, const int32_t* pos_h,
+                       const int32_t* pos_w, int attn, const int32_t* t_index, unsigned flags);
+
+/* U15Backbone::forward (src/u15-backbone.cc:259-277): every layer, with a
+ * cooperative stop polled before each layer (stop(ctx) != 0 returns
+ * U15C_ESTOPPED, src/u15-backbone.cc:386-397). stop may be NULL. */
+int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* seg_off,
+                 const int* seg_expert, int nseg, u15c_kv* kv, int kv_off, int kv_len,
+                 const int32_t* pos_t, const int32_t* pos_h, const int32_t* pos_w, int attn,
+                 const int32_t* t_index, unsigned flags, int (*stop)(void*), void* stop_ctx);
+
+/* U15Backbone::final_norm (src/u15-backbone.cc:140-148). */
+int u15c_final_norm(u15c_model* m, u15c_stream stream, void* x, int n, int expert);
+
+/* End to end through host memory: copy x_host [n][hidden] bf16 to the
+ * device, run u15c_layer_forward, copy the result back to out_host (both
+ * should be pinned for full speed). Synchronous. */
+int u15c_layer_forward_host(u15c_model* m, u15c_stream stream, int layer, const void* x_host,
+                            void* out_host, int n, const int* seg_off, const int* seg_expert,
+                            int nseg, u15c_kv* kv, int kv_off, int kv_len, const int32_t* pos_t,
+                            const int32_t* pos_h, const int32_t* pos_w, int attn,
+                            const int32_t* t_index, unsigned flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* U15C_H */

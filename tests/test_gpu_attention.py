@@ -1,0 +1,136 @@
+"""GPU parity of the flash attention against the CPU restatement.
+
+Geometry from the reference's steel test (tests/u15-kernels-test.cc:737-828:
+hq 8 / hkv 2 at head_dim 128, tq 48, tk 67, cache capacity 88 > tk) and its
+negative controls (GQA factor 1 must differ, plain causal must differ from
+block-causal, the kv stride is the capacity), plus the BASELINE attention
+shape (4096 queries over a 320-token prefix + 4096) on sampled heads, the
+paged cache with a permuted page table, and the Sage int8-QK path against its
+own restatement and against exact attention.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import bf16_round, dev_bf16, dev_i32, host, randn, rel_l2, torch
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+BAR = 4e-3
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import u15b200
+    return u15b200.CudaOps(0)
+
+
+def qkv(hq, hkv, tq, cap, seed, k_mean=0.0):
+    q = bf16_round(randn((hq, tq, 128), seed))
+    k = bf16_round(randn((hkv, cap, 128), seed + 1, 1.0, k_mean))
+    v = bf16_round(randn((hkv, cap, 128), seed + 2))
+    return q, k, v
+
+
+def run(ops, q, k, v, tk, mode=0, q_offset=0, t_index=None, sage=False, page_table=None):
+    hq, tq, _ = q.shape
+    hkv, cap, _ = k.shape
+    out = torch.empty(tq, hq * 128, dtype=torch.bfloat16, device="cuda")
+    ws = ops.sage_workspace(hq, hkv, tq, tk) if sage else None
+    if page_table is None:
+        ops.attention(dev_bf16(q), dev_bf16(k), dev_bf16(v), out, hq, hkv, tq, tk, cap=cap,
+                      mode=mode, q_offset=q_offset,
+                      t_index=dev_i32(t_index) if t_index is not None else None, sage_ws=ws)
+    else:
+        kp, vp = to_pages(k, page_table), to_pages(v, page_table)
+        ops.attention(dev_bf16(q), dev_bf16(kp), dev_bf16(vp), out, hq, hkv, tq, tk,
+                      page_table=dev_i32(page_table), mode=mode, q_offset=q_offset,
+                      t_index=dev_i32(t_index) if t_index is not None else None, sage_ws=ws)
+    ops.sync()
+    return host(out)
+
+
+def to_pages(kc, table):
+    """[hkv][cap][128] -> pool [pages][hkv][64][128] under a logical->physical table."""
+    hkv, cap, _ = kc.shape
+    n = len(table)
+    pool = np.zeros((n, hkv, 64, 128), np.float32)
+    for lp in range(n):
+        seg = kc[:, lp * 64:(lp + 1) * 64]
+        pool[table[lp], :, :seg.shape[1]] = seg
+    return pool
+
+
+def test_steel_geometry_bidirectional(ops):
+    q, k, v = qkv(8, 2, 48, 88, 1)
+    got = run(ops, q, k, v, 67)
+    ref = O.attention(q, k, v, tk=67)
+    assert rel_l2(got, ref) < BAR
+    # negative control: GQA factor 1 (query head h reads kv head h % 2)
+    wrong = O.attention(q, np.concatenate([k] * 4)[:8], np.concatenate([v] * 4)[:8], tk=67)
+    assert rel_l2(got, wrong) > 1e-2
+    # negative control: the stride is the capacity, not the key length
+    packed_k = np.ascontiguousarray(k[:, :67])
+    assert rel_l2(run(ops, q, packed_k, np.ascontiguousarray(v[:, :67]), 67), ref) < BAR
+
+
+def test_causal_with_offset(ops):
+    q, k, v = qkv(4, 1, 40, 100, 4)
+    got = run(ops, q, k, v, 90, mode=1, q_offset=50)
+    ref = O.attention(q, k, v, tk=90, mode=O.CAUSAL, q_offset=50)
+    assert rel_l2(got, ref) < BAR
+
+
+def test_block_causal(ops):
+    # the reference's t pattern, extended: a text run, an image block sharing
+    # one t, more text (tests/u15-kernels-test.cc:612)
+    t = np.array([0, 1, 2] + [3] * 70 + [4, 5, 6], np.int32)
+    T = t.size
+    q, k, v = qkv(8, 2, T, T + 4, 7)
+    got = run(ops, q, k, v, T, mode=2, t_index=t)
+    ref = O.attention(q, k, v, tk=T, mode=O.BLOCK_CAUSAL, t_index=t)
+    assert rel_l2(got, ref) < BAR
+    causal = O.attention(q, k, v, tk=T, mode=O.CAUSAL)
+    assert rel_l2(got, causal) > 1e-2
+
+
+def test_paged_permuted(ops):
+    q, k, v = qkv(32, 8, 100, 320, 9)
+    table = np.array([3, 0, 4, 1, 2], np.int32)   # 5 pages of 64
+    got = run(ops, q, k, v, 300, page_table=table)
+    ref = O.attention(q, k, v, tk=300)
+    assert rel_l2(got, ref) < BAR
+
+
+def test_baseline_shape_sampled_heads(ops):
+    """4096 generation queries over [320 prefix || 4096], GQA 32/8."""
+    tq, tk = 4096, 4416
+    torch.manual_seed(11)
+    qd = torch.randn(32, tq, 128, device="cuda").to(torch.bfloat16)
+    kd = torch.randn(8, tk, 128, device="cuda").to(torch.bfloat16)
+    vd = torch.randn(8, tk, 128, device="cuda").to(torch.bfloat16)
+    out = torch.empty(tq, 32 * 128, dtype=torch.bfloat16, device="cuda")
+    ops.attention(qd, kd, vd, out, 32, 8, tq, tk, cap=tk)
+    ops.sync()
+    rows = np.sort(np.random.default_rng(12).choice(tq, 48, replace=False))
+    for h in (0, 13, 31):
+        hk = h // 4
+        q = host(qd[h:h + 1, torch.from_numpy(rows).cuda()])
+        ref = O.attention(q, host(kd[hk:hk + 1]), host(vd[hk:hk + 1]))
+        got = host(out[torch.from_numpy(rows).cuda(), h * 128:(h + 1) * 128])
+        assert rel_l2(got, ref) < BAR
+
+
+def test_sage_matches_restatement(ops):
+    q, k, v = qkv(8, 2, 130, 200, 13, k_mean=0.7)
+    got = run(ops, q, k, v, 170, sage=True)
+    sage_ref = O.sage_attention(q, k, v, tk=170, bq=64, bk=64)
+    exact = O.attention(q, k, v, tk=170)
+    assert rel_l2(got, sage_ref) < 1e-2
+    assert rel_l2(got, exact) < 3e-2
+
+
+def test_sage_refuses_masked(ops):
+    import u15b200
+    q, k, v = qkv(4, 1, 16, 64, 14)
+    with pytest.raises(u15b200.U15Error):
+        run(ops, q, k, v, 64, mode=1, sage=True)

@@ -1,0 +1,184 @@
+"""GPU parity of the tcgen05 projection GEMMs.
+
+bf16: the CPU restatement's double-accumulated product of the same
+bf16-rounded inputs, bar kBf16Bar = 4e-3 rel-L2 (tests/u15-kernels-test.cc:55
+in the reference). Full BASELINE shapes (M = 4096 routed 512 und / 3584 gen,
+the four projections) are checked on a seeded sample of rows: the GPU
+computes every row, the oracle the sampled ones.
+
+int8 (BASELINE's W8A8 config): quantised inputs equal bit for bit, the int32
+accumulators equal the exact integer product bit for bit, the dequantised
+bf16 output within one bf16 rounding of the restatement.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import bf16_round, dev_bf16, host, randn, rel_l2, torch
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+BAR = 4e-3
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import u15b200
+    return u15b200.CudaOps(0)
+
+
+def sample_rows(M, n, seed):
+    if M <= n:
+        return np.arange(M)
+    return np.sort(np.random.default_rng(seed).choice(M, n, replace=False))
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 64, 256), (1, 64, 8), (200, 136, 48), (333, 4096, 1024),
+                                   (130, 12288, 512)])
+def test_linear_bf16(ops, M, K, N):
+    x = bf16_round(randn((M, K), 1))
+    w = bf16_round(randn((N, K), 2, 0.02))
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.linear(dev_bf16(x), dev_bf16(w), None, y, M, K, N)
+    ops.sync()
+    assert rel_l2(host(y), O.linear(x, w)) < BAR
+
+
+def test_linear_bias(ops):
+    M, K, N = 100, 256, 300
+    x = bf16_round(randn((M, K), 3))
+    w = bf16_round(randn((N, K), 4, 0.02))
+    b = bf16_round(randn(N, 5, 0.5))
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.linear(dev_bf16(x), dev_bf16(w), dev_bf16(b), y, M, K, N)
+    assert rel_l2(host(y), O.linear(x, w, b)) < BAR
+
+
+def routed_ref(x, w, segs, rows):
+    out = []
+    for r in rows:
+        e = [s[2] for s in segs if s[0] <= r < s[1]][0]
+        out.append(O.linear(x[r:r + 1], w[e])[0])
+    return np.stack(out)
+
+
+@pytest.mark.parametrize("segs", [[(0, 64, 0), (64, 256, 1)],
+                                  [(0, 100, 1), (100, 101, 0), (101, 300, 1)],
+                                  [(0, 300, 0)]])
+def test_mot_routing(ops, segs):
+    M, K, N = segs[-1][1], 512, 768
+    x = bf16_round(randn((M, K), 6))
+    w = bf16_round(randn((2, N, K), 7, 0.02))
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.mot_linear(dev_bf16(x), dev_bf16(w), segs, y, M, K, N)
+    rows = np.arange(M)
+    assert rel_l2(host(y), routed_ref(x, w, segs, rows)) < BAR
+    if len(segs) > 1:   # negative control: the experts differ
+        assert rel_l2(host(y), O.linear(x, w[segs[0][2]])) > 1e-2
+
+
+def test_residual_epilogue_in_place(ops):
+    M, K, N = 256, 1024, 512
+    x = bf16_round(randn((M, K), 8))
+    w = bf16_round(randn((2, N, K), 9, 0.02))
+    r = bf16_round(randn((M, N), 10))
+    segs = [(0, 64, 0), (64, M, 1)]
+    rd = dev_bf16(r)
+    ops.mot_linear(dev_bf16(x), dev_bf16(w), segs, rd, M, K, N, epilogue=EPI_RESIDUAL, resid=rd)
+    ref = r + routed_ref(x, w, segs, np.arange(M))
+    assert rel_l2(host(rd), ref) < BAR
+
+
+def interleave_gate_up(g, u):
+    """[gate_j | up_j] 128-row blocks, the SwiGLU epilogue's bound layout."""
+    I, K = g.shape
+    out = np.empty((2 * I, K), np.float32)
+    for j in range(I // 128):
+        out[256 * j:256 * j + 128] = g[128 * j:128 * j + 128]
+        out[256 * j + 128:256 * j + 256] = u[128 * j:128 * j + 128]
+    return out
+
+
+def test_swiglu_epilogue(ops):
+    M, K, I = 200, 512, 384
+    x = bf16_round(randn((M, K), 11))
+    g = bf16_round(randn((I, K), 12, 0.05))
+    u = bf16_round(randn((I, K), 13, 0.05))
+    w = interleave_gate_up(g, u)[None]
+    y = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    ops.mot_linear(dev_bf16(x), dev_bf16(w), None, y, M, K, 2 * I, epilogue=EPI_SWIGLU)
+    ref = O.swiglu(O.linear(x, g), O.linear(x, u))
+    assert rel_l2(host(y), ref) < BAR
+
+
+# the four projections at M = 4096, routed 512 / 3584
+SHAPES = {"qkv": (4096, 6144), "o": (4096, 4096), "gate_up": (4096, 24576),
+          "down": (12288, 4096)}
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+def test_baseline_shapes_routed(ops, name):
+    K, N = SHAPES[name]
+    M = 4096
+    segs = [(0, 512, 0), (512, 4096, 1)]
+    torch.manual_seed(17)
+    xd = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    wd = (torch.randn(2, N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.mot_linear(xd, wd, segs, y, M, K, N)
+    ops.sync()
+    rows = sample_rows(M, 24, 18)
+    rows = np.union1d(rows, [0, 511, 512, 4095])
+    x = host(xd[torch.from_numpy(rows).cuda()])
+    got = host(y[torch.from_numpy(rows).cuda()])
+    ref = np.stack([O.linear(x[i:i + 1], host(wd[0 if r < 512 else 1]))[0]
+                    for i, r in enumerate(rows)])
+    assert rel_l2(got, ref) < BAR
+
+
+# ---------------------------------------------------------------- W8A8
+def quantised(ops, x):
+    rows, cols = x.shape
+    q = torch.empty(rows, cols, dtype=torch.int8, device="cuda")
+    s = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ops.quant_rows_i8(dev_bf16(x), q, s, rows, cols)
+    return q, s
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 128, 256), (77, 4096, 1000), (256, 12288, 512)])
+def test_linear_i8_bit_exact(ops, M, K, N):
+    x = bf16_round(randn((M, K), 20))
+    w = bf16_round(randn((N, K), 21, 0.02))
+    xq, xs = quantised(ops, x)
+    wq, ws = quantised(ops, w)
+    rxq, rxs = O.quant_rows_i8(x)
+    rwq, rws = O.quant_rows_i8(w)
+    assert np.array_equal(host(xq), rxq) and np.array_equal(host(wq), rwq)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+    ops.linear_i8(xq, xs, wq, ws, y, M, K, N, acc_dump=acc)
+    ops.sync()
+    racc = O.gemm_i8(rxq, rwq)
+    assert np.array_equal(host(acc), racc)          # int32 accumulators: bit-exact
+    ry = bf16_round(O.dequant_i8(racc, rxs, rws))
+    assert rel_l2(host(y), ry) < 2e-3
+    # and the W8A8 product stays close to the bf16 one
+    assert rel_l2(host(y), O.linear(x, w)) < 3e-2
+
+
+def test_mot_linear_i8_routed_full_k(ops):
+    M, K, N = 640, 4096, 1536
+    segs = [(0, 512, 0), (512, 640, 1)]
+    x = bf16_round(randn((M, K), 22))
+    w = bf16_round(randn((2, N, K), 23, 0.02))
+    xq, xs = quantised(ops, x)
+    wq, ws = quantised(ops, w.reshape(2 * N, K))
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+    ops.mot_linear_i8(xq, xs, wq.view(2, N, K), ws.view(2, N), segs, y, M, K, N, acc_dump=acc)
+    ops.sync()
+    rxq, _ = O.quant_rows_i8(x)
+    rwq, _ = O.quant_rows_i8(w.reshape(2 * N, K))
+    rwq = rwq.reshape(2, N, K)
+    ref = np.concatenate([O.gemm_i8(rxq[a:b], rwq[e]) for a, b, e in segs])
+    assert np.array_equal(host(acc), ref)

@@ -1,0 +1,245 @@
+"""The MoT layer and backbone on the GPU against the CPU restatement.
+
+Bars from the north star: max-abs/rel 2e-2 per layer, 5e-2 after 42 layers.
+Because the residual stream dominates the output, the layer's own
+contribution (out - x) is also held to rel-L2 2e-2. Inputs are bf16-rounded
+once on the host and both sides start from the same values.
+
+The full-width case is BASELINE config 1: hidden 4096, 32/8 heads x 128,
+SwiGLU 12288, 64 und tokens + 192 gen tokens on a 16x12 grid, joint
+bidirectional attention, both experts N(0, 0.02) with norm gains N(1, 0.2)
+(the reference kernel test's gains, so a skipped gain shows).
+"""
+import numpy as np
+import pytest
+
+from gpu_util import bf16_round, dev_bf16, dev_i32, host, max_rel, randn, rel_l2, torch
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(n_layers=2, hidden=512, heads=4, kv_heads=1, head_dim=128, inter=1024,
+             n_experts=2)
+
+
+def expert_weights(cfg, seed, norm_mean=1.0, norm_std=0.2):
+    H, NH, KV, I = cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["inter"]
+    rng = np.random.default_rng(seed)
+    g = lambda *s: bf16_round(rng.normal(0, 0.02, s).astype(np.float32))  # noqa: E731
+    n = lambda *s: bf16_round(rng.normal(norm_mean, norm_std, s).astype(np.float32))  # noqa
+    return {"input_layernorm": n(H), "post_attention_layernorm": n(H),
+            "q_proj": g(NH * 128, H), "k_proj": g(KV * 128, H), "v_proj": g(KV * 128, H),
+            "o_proj": g(H, NH * 128), "q_norm": n(64), "k_norm": n(64), "q_norm_hw": n(64),
+            "k_norm_hw": n(64), "gate_proj": g(I, H), "up_proj": g(I, H), "down_proj": g(H, I)}
+
+
+def build(cfg, seed, int8=False, **kw):
+    import u15b200
+    m = u15b200.Model(int8=int8, **cfg)
+    W = [[expert_weights(cfg, seed + 100 * li + e, **kw) for e in range(cfg["n_experts"])]
+         for li in range(cfg["n_layers"])]
+    for li in range(cfg["n_layers"]):
+        for e in range(cfg["n_experts"]):
+            m.bind_expert_layer(li, e, W[li][e])
+    for e in range(cfg["n_experts"]):
+        m.bind(0, e, "final_norm", np.ones(cfg["hidden"], np.float32))
+    m.finalize()
+    torch.cuda.synchronize()
+    return m, W
+
+
+def grid_positions(n_und, gh, gw, t_img):
+    pt = np.concatenate([np.arange(n_und), np.full(gh * gw, t_img)]).astype(np.int32)
+    ph = np.concatenate([np.zeros(n_und), np.repeat(np.arange(gh), gw)]).astype(np.int32)
+    pw = np.concatenate([np.zeros(n_und), np.tile(np.arange(gw), gh)]).astype(np.int32)
+    return pt, ph, pw
+
+
+def dims_of(cfg):
+    return dict(hidden=cfg["hidden"], heads=cfg["heads"], kv_heads=cfg["kv_heads"],
+                head_dim=128, inter=cfg["inter"])
+
+
+def check_layer(out, x, ref, bar=2e-2):
+    assert max_rel(out, ref) < bar
+    assert rel_l2(out - x, ref - x) < bar
+
+
+@pytest.fixture(scope="module")
+def small():
+    return build(SMALL, 1)
+
+
+def test_layer_joint_small(small):
+    m, W = small
+    n_und, gh, gw = 32, 8, 8
+    T = n_und + gh * gw
+    segs = [(0, n_und, 0), (n_und, T, 1)]
+    pos = grid_positions(n_und, gh, gw, n_und)
+    x = bf16_round(randn((T, SMALL["hidden"]), 2))
+    kv = m.make_cache(T)
+    xd = dev_bf16(x)
+    m.layer_forward(0, xd, kv, 0, T, *(dev_i32(p) for p in pos), segments=segs)
+    torch.cuda.synchronize()
+    ref, kn, vn = O.mot_layer(x, segs, W[0], dims_of(SMALL), *pos)
+    check_layer(host(xd), x, ref)
+    # the K/V the layer appended to the paged cache
+    assert rel_l2(host(kv.read(0, False, T)), kn) < 1e-2
+    assert rel_l2(host(kv.read(0, True, T)), vn) < 1e-2
+
+
+def test_layer_frozen_prefix_paged(small):
+    """The denoise form: gen tokens over [prefix || block] with a permuted page table."""
+    m, W = small
+    npre, gh, gw = 70, 6, 10
+    T = gh * gw
+    pt = np.full(T, npre, np.int32)
+    ph = np.repeat(np.arange(gh), gw).astype(np.int32)
+    pw = np.tile(np.arange(gw), gh).astype(np.int32)
+    x = bf16_round(randn((T, SMALL["hidden"]), 3))
+    kpre = bf16_round(randn((1, npre, 128), 4))
+    vpre = bf16_round(randn((1, npre, 128), 5))
+    kv = m.make_cache(npre + T)
+    kv.set_page_table([2, 0, 1])
+    for layer in range(SMALL["n_layers"]):
+        kv.write(layer, False, dev_bf16(kpre))
+        kv.write(layer, True, dev_bf16(vpre))
+    xd = dev_bf16(x)
+    m.layer_forward(1, xd, kv, npre, npre + T, dev_i32(pt), dev_i32(ph), dev_i32(pw),
+                    segments=[(0, T, 1)])
+    torch.cuda.synchronize()
+    ref, _, _ = O.mot_layer(x, [(0, T, 1)], W[1], dims_of(SMALL), pt, ph, pw,
+                            k_prefix=kpre, v_prefix=vpre)
+    check_layer(host(xd), x, ref)
+    # the prefix is frozen: still exactly what was written
+    assert np.array_equal(host(kv.read(1, False, npre)), kpre)
+
+
+def test_layer_causal_prefill(small):
+    m, W = small
+    T = 45
+    pt = np.arange(T, dtype=np.int32)
+    z = np.zeros(T, np.int32)
+    x = bf16_round(randn((T, SMALL["hidden"]), 6))
+    kv = m.make_cache(T)
+    xd = dev_bf16(x)
+    m.layer_forward(0, xd, kv, 0, T, dev_i32(pt), dev_i32(z), dev_i32(z), segments=[(0, T, 0)],
+                    attn=1)
+    torch.cuda.synchronize()
+    ref, _, _ = O.mot_layer(x, [(0, T, 0)], W[0], dims_of(SMALL), pt, z, z, mode=O.CAUSAL)
+    check_layer(host(xd), x, ref)
+
+
+def test_layer_block_causal_prefill(small):
+    m, W = small
+    t = np.array([0, 1, 2] + [3] * 30 + [4, 5], np.int32)
+    T = t.size
+    ph = np.concatenate([[0, 0, 0], np.repeat(np.arange(5), 6), [0, 0]]).astype(np.int32)
+    pw = np.concatenate([[0, 0, 0], np.tile(np.arange(6), 5), [0, 0]]).astype(np.int32)
+    x = bf16_round(randn((T, SMALL["hidden"]), 7))
+    kv = m.make_cache(T)
+    xd = dev_bf16(x)
+    m.layer_forward(0, xd, kv, 0, T, dev_i32(t), dev_i32(ph), dev_i32(pw), segments=[(0, T, 0)],
+                    attn=2, t_index=dev_i32(t))
+    torch.cuda.synchronize()
+    ref, _, _ = O.mot_layer(x, [(0, T, 0)], W[0], dims_of(SMALL), t, ph, pw,
+                            mode=O.BLOCK_CAUSAL, t_index=t)
+    check_layer(host(xd), x, ref)
+
+
+def test_int8_and_sage_layers_close(small):
+    import u15b200
+    cfg = dict(SMALL)
+    m, W = build(cfg, 1, int8=True)
+    n_und, gh, gw = 16, 8, 8
+    T = n_und + gh * gw
+    segs = [(0, n_und, 0), (n_und, T, 1)]
+    pos = grid_positions(n_und, gh, gw, n_und)
+    x = bf16_round(randn((T, cfg["hidden"]), 8))
+    ref, _, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos)
+    for int8, sage in ((True, False), (False, True), (True, True)):
+        kv = m.make_cache(T)
+        xd = dev_bf16(x)
+        m.layer_forward(0, xd, kv, 0, T, *(dev_i32(p) for p in pos), segments=segs, int8=int8,
+                        sage=sage)
+        torch.cuda.synchronize()
+        assert rel_l2(host(xd) - x, ref - x) < 6e-2, (int8, sage)
+    assert isinstance(m, u15b200.Model)
+
+
+def test_stop_and_determinism(small):
+    import u15b200
+    m, _ = small
+    T = 64
+    pos = grid_positions(0, 8, 8, 0)
+    x = bf16_round(randn((T, SMALL["hidden"]), 9))
+    kv = m.make_cache(T)
+    calls = []
+
+    def stop():
+        calls.append(1)
+        return len(calls) > 1
+
+    with pytest.raises(u15b200.U15Error) as ei:
+        m.forward(dev_bf16(x), kv, 0, T, *(dev_i32(p) for p in pos), stop=stop)
+    assert ei.value.code == 5 and len(calls) == 2
+    outs = []
+    for _ in range(2):
+        xd = dev_bf16(x)
+        m.forward(xd, kv, 0, T, *(dev_i32(p) for p in pos))
+        torch.cuda.synchronize()
+        outs.append(host(xd))
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_layer_forward_host_matches_device(small):
+    m, _ = small
+    T = 64
+    pos = [dev_i32(p) for p in grid_positions(0, 8, 8, 0)]
+    x = bf16_round(randn((T, SMALL["hidden"]), 10))
+    kv = m.make_cache(T)
+    xd = dev_bf16(x)
+    m.layer_forward(0, xd, kv, 0, T, *pos)
+    torch.cuda.synchronize()
+    xh = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    m.layer_forward_host(0, xh, oh, kv, 0, T, *pos)
+    assert np.array_equal(oh.float().numpy(), host(xd))
+
+
+def test_42_layer_drift():
+    cfg = dict(SMALL, n_layers=42)
+    m, W = build(cfg, 50)
+    n_und, gh, gw = 16, 6, 8
+    T = n_und + gh * gw
+    segs = [(0, n_und, 0), (n_und, T, 1)]
+    pos = grid_positions(n_und, gh, gw, n_und)
+    x = bf16_round(randn((T, cfg["hidden"]), 11))
+    kv = m.make_cache(T)
+    xd = dev_bf16(x)
+    m.forward(xd, kv, 0, T, *(dev_i32(p) for p in pos), segments=segs)
+    torch.cuda.synchronize()
+    ref = x
+    for li in range(42):
+        ref, _, _ = O.mot_layer(ref, segs, W[li], dims_of(cfg), *pos)
+    assert max_rel(host(xd), ref) < 5e-2
+    assert rel_l2(host(xd) - x, ref - x) < 5e-2
+
+
+def test_full_width_c1_layer():
+    """BASELINE config 1 at full width (one layer, both experts)."""
+    cfg = dict(n_layers=1, hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=12288,
+               n_experts=2)
+    m, W = build(cfg, 70)
+    n_und, gh, gw = 64, 16, 12
+    T = n_und + gh * gw
+    segs = [(0, n_und, 0), (n_und, T, 1)]
+    pos = grid_positions(n_und, gh, gw, n_und)
+    x = bf16_round(randn((T, cfg["hidden"]), 12))
+    kv = m.make_cache(T)
+    xd = dev_bf16(x)
+    m.layer_forward(0, xd, kv, 0, T, *(dev_i32(p) for p in pos), segments=segs)
+    torch.cuda.synchronize()
+    ref, _, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos)
+    check_layer(host(xd), x, ref)
+    m.close()

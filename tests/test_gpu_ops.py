@@ -1,0 +1,161 @@
+"""GPU parity of the bandwidth kernels against the CPU restatement.
+
+Shapes follow the reference's kernel test (tests/u15-kernels-test.cc in the
+reference: seeded inputs, norm gains around 1 so that a skipped gain shows,
+tolerance kBf16Bar = 4e-3 rel-L2) at the model's head_dim of 128, with the
+reference's negative controls: one whole-head norm is not two half norms, the
+h and w ranges are not interchangeable, the cache stride is the capacity.
+The int8 quantiser must match bit for bit.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import (bf16_round, dev_bf16, dev_f32, dev_i32, host, randn, rel_l2, torch)
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+BAR = 4e-3
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import u15b200
+    return u15b200.CudaOps(0)
+
+
+def positions(T, seed):
+    rng = np.random.default_rng(seed)
+    pt = np.sort(rng.integers(0, 4416, T)).astype(np.int32)
+    ph = rng.integers(0, 64, T).astype(np.int32)
+    pw = rng.integers(0, 64, T).astype(np.int32)
+    return pt, ph, pw
+
+
+@pytest.mark.parametrize("rows,dim", [(7, 64), (300, 4096), (33, 12288)])
+def test_rms_norm(ops, rows, dim):
+    x = bf16_round(randn((rows, dim), 1))
+    w = bf16_round(randn(dim, 2, 0.2, 1.0))
+    y = torch.empty(rows, dim, dtype=torch.bfloat16, device="cuda")
+    ops.rms_norm(dev_bf16(x), dev_bf16(w), y, rows, dim, 1e-6)
+    assert rel_l2(host(y), O.rms_norm(x, w)) < BAR
+
+
+def test_mot_rms_norm_routes_gains(ops):
+    rows, dim = 200, 512
+    x = bf16_round(randn((rows, dim), 3))
+    w = bf16_round(randn((2, dim), 4, 0.2, 1.0))
+    segs = [(0, 64, 0), (64, 150, 1), (150, 200, 0)]
+    y = torch.empty(rows, dim, dtype=torch.bfloat16, device="cuda")
+    ops.mot_rms_norm(dev_bf16(x), dev_bf16(w), segs, y, rows, dim, 1e-6)
+    ref = np.concatenate([O.rms_norm(x[a:b], w[e]) for a, b, e in segs])
+    assert rel_l2(host(y), ref) < BAR
+    wrong = O.rms_norm(x, w[0])
+    assert rel_l2(host(y), wrong) > 1e-2
+
+
+def test_rope_tables_fp64(ops):
+    T = 257
+    pt, ph, pw = positions(T, 5)
+    c, s = ops.build_rope_tables(dev_i32(pt), dev_i32(ph), dev_i32(pw))
+    rc, rs = O.rope_tables(pt, ph, pw)
+    # angles in fp64 on both sides, narrowed once: equal to the last bit
+    # or within one float ulp where the two libms round differently
+    assert np.abs(host(c) - rc).max() < 2e-7
+    assert np.abs(host(s) - rs).max() < 2e-7
+
+
+@pytest.mark.parametrize("heads,T", [(4, 12), (32, 100), (8, 333)])
+def test_split_qk_norm_and_rope(ops, heads, T):
+    x = bf16_round(randn((T, heads * 128), 7))
+    wt = bf16_round(randn(64, 8, 0.2, 1.0))
+    wh = bf16_round(randn(64, 9, 0.2, 1.0))
+    pt, ph, pw = positions(T, 10)
+    xd = dev_bf16(x)
+    ops.split_qk_norm(xd, dev_bf16(wt), dev_bf16(wh), heads, T, 128, 1e-6)
+    normed = O.split_qk_norm(x, wt, wh, heads)
+    assert rel_l2(host(xd), normed) < BAR
+    # negative control: one reduction over the whole head is different
+    whole = O.rms_norm(x.reshape(-1, 128), np.concatenate([wt, wh])).reshape(x.shape)
+    assert rel_l2(host(xd), whole) > 1e-2
+
+    c, s = O.rope_tables(pt, ph, pw)
+    before = host(xd)
+    ops.split_rope(xd, dev_f32(c), dev_f32(s), heads, T, 128, 64, 32)
+    ref = O.split_rope(before, c, s, heads)
+    assert rel_l2(host(xd), ref) < BAR
+    # negative control: swapping the h and w position vectors
+    c2, s2 = O.rope_tables(pt, pw, ph)
+    assert rel_l2(host(xd), O.split_rope(normed, c2, s2, heads)) > 1e-2
+
+
+def test_transposes_and_cache(ops):
+    T, H = 37, 8
+    x = bf16_round(randn((T, H * 128), 11))
+    xd = dev_bf16(x)
+    hm = torch.empty(H, T, 128, dtype=torch.bfloat16, device="cuda")
+    ops.transpose_thd(xd, hm, T, H, 128)
+    assert np.array_equal(host(hm), x.reshape(T, H, 128).transpose(1, 0, 2))
+    back = torch.empty_like(xd)
+    ops.transpose_htd(hm, back, T, H, 128)
+    assert np.array_equal(host(back), x)
+    cap, off = 100, 29
+    cache = torch.zeros(H, cap, 128, dtype=torch.bfloat16, device="cuda")
+    ops.transpose_into_cache(xd, cache, T, H, 128, cap, off)
+    ref = np.zeros((H, cap, 128), np.float32)
+    ref[:, off:off + T] = x.reshape(T, H, 128).transpose(1, 0, 2)
+    assert np.array_equal(host(cache), ref)
+
+
+def test_paged_kv_append_permuted(ops):
+    T, H, off = 150, 8, 70
+    pages = 4
+    perm = np.array([2, 0, 3, 1], np.int32)
+    x = bf16_round(randn((T, H * 128), 12))
+    pool = torch.zeros(pages, H, 64, 128, dtype=torch.bfloat16, device="cuda")
+    ops.kv_append(dev_bf16(x), pool, dev_i32(perm), T, H, off)
+    p = host(pool)
+    xt = x.reshape(T, H, 128)
+    for t in range(T):
+        j = off + t
+        assert np.array_equal(p[perm[j // 64], :, j % 64], xt[t])
+
+
+def test_elementwise(ops):
+    rows, inter = 50, 1024
+    g = bf16_round(randn((rows, inter), 13))
+    u = bf16_round(randn((rows, inter), 14))
+    y = torch.empty(rows, inter, dtype=torch.bfloat16, device="cuda")
+    ops.swiglu(dev_bf16(g), dev_bf16(u), y, rows, inter)
+    assert rel_l2(host(y), O.swiglu(g, u)) < BAR
+    d = dev_bf16(g)
+    ops.add(d, dev_bf16(u), rows * inter)
+    assert rel_l2(host(d), g + u) < BAR
+    r = bf16_round(randn(inter, 15))
+    d = dev_bf16(g)
+    ops.add_row(d, dev_bf16(r), rows, inter)
+    assert rel_l2(host(d), g + r[None]) < BAR
+    d = dev_bf16(g)
+    ops.silu(d, rows * inter)
+    assert rel_l2(host(d), g / (1 + np.exp(-g.astype(np.float64)))) < BAR
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 8), (77, 4096), (300, 12288)])
+def test_quant_rows_bit_exact(ops, rows, cols):
+    x = bf16_round(randn((rows, cols), 16))
+    if rows > 5:
+        x[5] = 0.0
+    q = torch.empty(rows, cols, dtype=torch.int8, device="cuda")
+    s = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ops.quant_rows_i8(dev_bf16(x), q, s, rows, cols)
+    rq, rs = O.quant_rows_i8(x)
+    assert np.array_equal(host(s), rs)
+    assert np.array_equal(host(q), rq)
+
+
+def test_invalid_shapes_refused(ops):
+    import u15b200
+    x = torch.zeros(4, 96, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(u15b200.U15Error):
+        ops.split_qk_norm(x, x, x, 1, 4, 96, 1e-6)   # head_dim must be 128
+    with pytest.raises(u15b200.U15Error):
+        ops.transpose_into_cache(x, x, 4, 1, 128, 3, 0)   # cache too small

@@ -1,0 +1,507 @@
+// Flash attention for the MoT layer, head_dim 128, GQA.
+//
+//   out[i][h*128 + :] = softmax_j(q_h[i] . k_{h/G}[j] / sqrt(128) + mask) v_{h/G}[j]
+//
+// q head-major [hq][tq][128] (what the QKV epilogue writes), K/V read from
+// a paged or contiguous cache through KvView (the reference reads its
+// contiguous [hkv][cap][128] cache with cap as the head stride,
+// src/u15-metal-ops.cc:687-787), out token-major [tq][hq*128] -- the
+// reference's transpose_htd is folded into the store.
+//
+// One CTA serves the G query heads of one kv-head group for R = 128/G query
+// rows (128 rows total, 8 warps x 16), so each K/V tile is read once for
+// all G heads. K/V tiles are 64 keys (one cache page), double-buffered with
+// cp.async; S = QK^T and O += PV on mma.sync m16n8k16 (bf16) with online
+// softmax in registers. Masks are evaluated per element from the rule:
+//   0 bidirectional   every key j < tk                (denoise)
+//   1 causal          j <= q_offset + i               (text prefill)
+//   2 block-causal    t[j] == t[q_offset+i] or j <= q_offset + i   (edit prefill)
+// The causal form skips KV tiles past the CTA's last query.
+//
+// The Sage variant (bidirectional only) computes QK^T with mma.sync
+// m16n8k32 s8 x s8 -> s32 from int8 Q and smoothed int8 K prepared by
+// sage_prepare(), with one scale per 64-row Q block and per 64-key K
+// block; P.V stays bf16.
+#include "u15_common.cuh"
+#include "u15_kernels.h"
+
+#include <cmath>
+
+namespace u15 {
+
+namespace {
+
+constexpr int kRows = 128;      // query rows per CTA (all heads of the group)
+constexpr int kKeys = 64;       // keys per tile (= one cache page)
+constexpr int kThreads = 256;
+
+struct AttnP {
+  const __nv_bfloat16* q;
+  KvView kv;
+  __nv_bfloat16* out;
+  int hq, hkv, tq, tk, mode, q_offset, G, R;
+  const int32_t* t_index;
+  float scale_log2;
+  const int8_t* q8;
+  const int8_t* k8;
+  const float* sq;
+  const float* sk;
+  int nqb, nkb;
+  long k8_stride;   // rows per kv head in k8
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid)
+{
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3)
+{
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3)
+{
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1)
+{
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                             uint32_t b1)
+{
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Swizzled shared-memory offsets: 16-byte chunk c of row r is stored at
+// chunk (c ^ (r & 7)), so the 8 rows an ldmatrix reads hit 8 bank groups.
+__device__ __forceinline__ uint32_t swz256(int r, int c) { return r * 256 + ((c ^ (r & 7)) << 4); }
+__device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ const __nv_bfloat16* kv_row(const KvView& kv, const void* base, int h,
+                                                       int j)
+{
+  const long page = kv.page_table ? (long)kv.page_table[j >> 6] : (long)(j >> 6);
+  return reinterpret_cast<const __nv_bfloat16*>(base) + page * kv.page_stride +
+         (long)h * kv.head_stride + (long)(j & 63) * 128;
+}
+
+template <bool SAGE>
+__global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant__ AttnP p)
+{
+  extern __shared__ __align__(128) uint8_t sm[];
+  // bf16: Q 32 KB | K 2 x 16 KB | V 2 x 16 KB.  Sage: Q8 16 KB | K8 2 x 8 KB | V 2 x 16 KB
+  constexpr int kQBytes = SAGE ? kRows * 128 : kRows * 256;
+  constexpr int kKBytes = SAGE ? kKeys * 128 : kKeys * 256;
+  constexpr int kVBytes = kKeys * 256;
+  uint8_t* sQ = sm;
+  uint8_t* sK = sm + kQBytes;
+  uint8_t* sV = sK + 2 * kKBytes;
+  const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+
+  const int hk = blockIdx.y;
+  const int q0 = blockIdx.x * p.R;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+
+  // ---- Q tile: row r -> head hk*G + r/R, query q0 + r%R ----
+  if constexpr (SAGE) {
+    for (int i = tid; i < kRows * 8; i += kThreads) {
+      const int r = i >> 3, c = i & 7;
+      const int h = hk * p.G + r / p.R, qi = q0 + r % p.R;
+      const bool ok = qi < p.tq;
+      const int8_t* src = p.q8 + ((long)h * p.tq + (ok ? qi : 0)) * 128 + c * 16;
+      cp_async16(aQ + swz128(r, c), src, ok);
+    }
+  } else {
+    for (int i = tid; i < kRows * 16; i += kThreads) {
+      const int r = i >> 4, c = i & 15;
+      const int h = hk * p.G + r / p.R, qi = q0 + r % p.R;
+      const bool ok = qi < p.tq;
+      const __nv_bfloat16* src = p.q + ((long)h * p.tq + (ok ? qi : 0)) * 128 + c * 8;
+      cp_async16(aQ + swz256(r, c), src, ok);
+    }
+  }
+
+  // ---- which KV tiles this CTA needs ----
+  int n_tiles = (p.tk + kKeys - 1) / kKeys;
+  if (p.mode == 1) {
+    const int last_q = p.q_offset + min(q0 + p.R, p.tq) - 1;
+    n_tiles = min(n_tiles, last_q / kKeys + 1);
+  }
+
+  auto load_kv = [&](int tile, int buf) {
+    const int j0 = tile * kKeys;
+    if constexpr (SAGE) {
+      for (int i = tid; i < kKeys * 8; i += kThreads) {
+        const int r = i >> 3, c = i & 7;
+        const int j = j0 + r;
+        const bool ok = j < p.tk;
+        const int8_t* src = p.k8 + ((long)hk * p.k8_stride + (ok ? j : 0)) * 128 + c * 16;
+        cp_async16(aK + buf * kKBytes + swz128(r, c), src, ok);
+      }
+    } else {
+      for (int i = tid; i < kKeys * 16; i += kThreads) {
+        const int r = i >> 4, c = i & 15;
+        const int j = j0 + r;
+        const bool ok = j < p.tk;
+        const __nv_bfloat16* src = kv_row(p.kv, p.kv.k, hk, ok ? j : 0) + c * 8;
+        cp_async16(aK + buf * kKBytes + swz256(r, c), src, ok);
+      }
+    }
+    for (int i = tid; i < kKeys * 16; i += kThreads) {
+      const int r = i >> 4, c = i & 15;
+      const int j = j0 + r;
+      const bool ok = j < p.tk;
+      const __nv_bfloat16* src = kv_row(p.kv, p.kv.v, hk, ok ? j : 0) + c * 8;
+      cp_async16(aV + buf * kVBytes + swz256(r, c), src, ok);
+    }
+  };
+
+  if (n_tiles > 0) load_kv(0, 0);
+  cp_async_commit();
+
+  // per-thread rows: r0 = w*16 + l/4, r1 = r0 + 8
+  const int r0 = w * 16 + (l >> 2), r1 = r0 + 8;
+  const int h0 = hk * p.G + r0 / p.R, h1 = hk * p.G + r1 / p.R;
+  const int qi0 = q0 + r0 % p.R, qi1 = q0 + r1 % p.R;
+  const int qp0 = p.q_offset + qi0, qp1 = p.q_offset + qi1;
+  int tq0 = 0, tq1 = 0;
+  if (p.mode == 2) {
+    tq0 = qi0 < p.tq ? p.t_index[qp0] : 0;
+    tq1 = qi1 < p.tq ? p.t_index[qp1] : 0;
+  }
+  float sq0 = 1.0f, sq1 = 1.0f;
+  if constexpr (SAGE) {
+    sq0 = qi0 < p.tq ? p.sq[(long)h0 * p.nqb + qi0 / 64] : 0.0f;
+    sq1 = qi1 < p.tq ? p.sq[(long)h1 * p.nqb + qi1 / 64] : 0.0f;
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+
+  for (int t = 0; t < n_tiles; ++t) {
+    cp_async_wait_all();
+    __syncthreads();
+    if (t + 1 < n_tiles) load_kv(t + 1, (t + 1) & 1);
+    cp_async_commit();
+    const int buf = t & 1;
+    const int j0 = t * kKeys;
+
+    // ---- S = Q K^T, 16 rows x 64 keys per warp ----
+    float s[8][4];
+    if constexpr (SAGE) {
+      int si[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; ++n) si[n][0] = si[n][1] = si[n][2] = si[n][3] = 0;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t a[4];
+        const int ar = w * 16 + (l & 7) + ((l >> 3) & 1) * 8;
+        ldsm_x4(aQ + swz128(ar, 2 * kk + (l >> 4)), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int br = np * 16 + (l & 7) + (l >> 4) * 8;
+          ldsm_x4(aK + buf * kKBytes + swz128(br, 2 * kk + ((l >> 3) & 1)), b0, b1, b2, b3);
+          mma_s8_16832(si[2 * np], a, b0, b1);
+          mma_s8_16832(si[2 * np + 1], a, b2, b3);
+        }
+      }
+      const float skv = p.sk[(long)hk * p.nkb + t] * p.scale_log2;
+      const float f0 = sq0 * skv, f1 = sq1 * skv;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        s[n][0] = (float)si[n][0] * f0;
+        s[n][1] = (float)si[n][1] * f0;
+        s[n][2] = (float)si[n][2] * f1;
+        s[n][3] = (float)si[n][3] * f1;
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4];
+        const int ar = w * 16 + (l & 7) + ((l >> 3) & 1) * 8;
+        ldsm_x4(aQ + swz256(ar, 2 * kk + (l >> 4)), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int br = np * 16 + (l & 7) + (l >> 4) * 8;
+          ldsm_x4(aK + buf * kKBytes + swz256(br, 2 * kk + ((l >> 3) & 1)), b0, b1, b2, b3);
+          mma_bf16_16816(s[2 * np], a, b0, b1);
+          mma_bf16_16816(s[2 * np + 1], a, b2, b3);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[n][e] *= p.scale_log2;
+    }
+
+    // ---- mask ----
+    const bool tail = j0 + kKeys > p.tk;
+    if (tail || p.mode != 0) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = j0 + n * 8 + (l & 3) * 2 + (e & 1);
+          const int qp = e < 2 ? qp0 : qp1;
+          bool ok = j < p.tk;
+          if (p.mode == 1) ok = ok && (j <= qp);
+          else if (p.mode == 2) ok = ok && ((j <= qp) || (p.t_index[j] == (e < 2 ? tq0 : tq1)));
+          if (!ok) s[n][e] = -INFINITY;
+        }
+      }
+    }
+
+    // ---- online softmax (base 2) ----
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      mx0 = fmaxf(mx0, fmaxf(s[n][0], s[n][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[n][2], s[n][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float use0 = mx0 == -INFINITY ? 0.0f : mx0;
+    const float use1 = mx1 == -INFINITY ? 0.0f : mx1;
+    const float c0 = exp2f(m0 - use0), c1 = exp2f(m1 - use1);   // exp2(-inf) = 0
+    m0 = mx0;
+    m1 = mx1;
+    l0 *= c0;
+    l1 *= c1;
+#pragma unroll
+    for (int d = 0; d < 16; ++d) {
+      o[d][0] *= c0; o[d][1] *= c0;
+      o[d][2] *= c1; o[d][3] *= c1;
+    }
+    uint32_t pa[4][4];   // P as the A operand of 4 k-steps of 16 keys
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float p0 = exp2f(s[n][0] - use0), p1 = exp2f(s[n][1] - use0);
+      const float p2 = exp2f(s[n][2] - use1), p3 = exp2f(s[n][3] - use1);
+      l0 += p0 + p1;
+      l1 += p2 + p3;
+      const int kk = n >> 1, hi = n & 1;
+      pa[kk][hi * 2 + 0] = pack_bf2(p0, p1);
+      pa[kk][hi * 2 + 1] = pack_bf2(p2, p3);
+    }
+
+    // ---- O += P V ----
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t a[4] = {pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3]};
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        const int vr = kk * 16 + (l & 7) + ((l >> 3) & 1) * 8;
+        ldsm_x4_t(aV + buf * kVBytes + swz256(vr, 2 * dp + (l >> 4)), b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * dp], a, b0, b1);
+        mma_bf16_16816(o[2 * dp + 1], a, b2, b3);
+      }
+    }
+  }
+  cp_async_wait_all();
+
+  // ---- normalise and store token-major through shared memory ----
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+  __syncthreads();
+  uint8_t* sO = SAGE ? sV : sQ;   // 32 KB of bf16 staging
+  const uint32_t aO = smem_u32(sO);
+#pragma unroll
+  for (int d = 0; d < 16; ++d) {
+    const int col = d * 8 + (l & 3) * 2;
+    const uint32_t v0 = pack_bf2(o[d][0] * inv0, o[d][1] * inv0);
+    const uint32_t v1 = pack_bf2(o[d][2] * inv1, o[d][3] * inv1);
+    *reinterpret_cast<uint32_t*>(sO + swz256(r0, col >> 3) + (col & 7) * 2) = v0;
+    *reinterpret_cast<uint32_t*>(sO + swz256(r1, col >> 3) + (col & 7) * 2) = v1;
+  }
+  (void)aO;
+  __syncthreads();
+  for (int i = tid; i < kRows * 16; i += kThreads) {
+    const int r = i >> 4, c = i & 15;
+    const int h = hk * p.G + r / p.R, qi = q0 + r % p.R;
+    if (qi >= p.tq) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(sO + swz256(r, c));
+    *reinterpret_cast<uint4*>(p.out + (long)qi * p.hq * 128 + (long)h * 128 + c * 8) = v;
+  }
+}
+
+// ---------------------------------------------------------------------
+// Sage prologue
+// ---------------------------------------------------------------------
+// kmean[hk][c] = sum_j<tk K[hk][j][c] / tk; 1024 threads per kv head,
+// 8 key-strided partial sums per channel combined in a fixed order.
+__global__ void __launch_bounds__(1024) kmean_kernel(KvView kv, int tk, float* kmean)
+{
+  const int hk = blockIdx.x, c = threadIdx.x & 127, part = threadIdx.x >> 7;
+  float acc = 0.0f;
+  for (int j = part; j < tk; j += 8) acc += bf2f(kv_row(kv, kv.k, hk, j)[c]);
+  __shared__ float red[8][128];
+  red[part][c] = acc;
+  __syncthreads();
+  if (part == 0) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += red[i][c];
+    kmean[hk * 128 + c] = s / (float)tk;
+  }
+}
+
+// One CTA per 64-row block: absmax over the block, s = amax/127, codes.
+// K blocks read the smoothed K (K - kmean) from the cache view.
+template <bool IS_K>
+__global__ void __launch_bounds__(256)
+    sage_quant_kernel(const __nv_bfloat16* q, KvView kv, const float* kmean, int rows_valid,
+                      int nblk, int8_t* out, float* scale, long out_stride)
+{
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int r0 = b * 64;
+  __shared__ float red[8];
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < 64 * 128; i += 256) {
+    const int r = r0 + i / 128, c = i % 128;
+    if (r >= rows_valid) continue;
+    float v;
+    if (IS_K) v = bf2f(kv_row(kv, kv.k, h, r)[c]) - kmean[h * 128 + c];
+    else v = bf2f(q[((long)h * rows_valid + r) * 128 + c]);
+    m = fmaxf(m, fabsf(v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  const float s = __fdiv_rn(amax, 127.0f);
+  if (threadIdx.x == 0) scale[(long)h * nblk + b] = s;
+  for (int i = threadIdx.x; i < 64 * 128; i += 256) {
+    const int r = r0 + i / 128, c = i % 128;
+    int k = 0;
+    if (r < rows_valid && s > 0.0f) {
+      float v;
+      if (IS_K) v = bf2f(kv_row(kv, kv.k, h, r)[c]) - kmean[h * 128 + c];
+      else v = bf2f(q[((long)h * rows_valid + r) * 128 + c]);
+      k = max(-127, min(127, __float2int_rn(__fdiv_rn(v, s))));
+    }
+    if (IS_K || r < rows_valid) out[((long)h * out_stride + r) * 128 + c] = (int8_t)k;
+  }
+}
+
+}  // namespace
+
+int attention(const AttnArgs& a, cudaStream_t st, std::string* err)
+{
+  if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv != 0) {
+    *err = "attention: hq must be a positive multiple of hkv";
+    return 1;
+  }
+  const int G = a.hq / a.hkv;
+  if (G > 8 || (kRows % G) != 0) {
+    *err = "attention: GQA group size must divide 128 and be at most 8";
+    return 1;
+  }
+  if (a.tq <= 0 || a.tk <= 0) return 0;
+  if (a.mode == 2 && a.t_index == nullptr) {
+    *err = "attention: block-causal needs the t-index vector";
+    return 1;
+  }
+  const bool sage = a.q8 != nullptr;
+  if (sage && a.mode != 0) {
+    *err = "attention: the int8-QK path serves the bidirectional pass only";
+    return 1;
+  }
+  AttnP p{};
+  p.q = static_cast<const __nv_bfloat16*>(a.q);
+  p.kv = a.kv;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.hq = a.hq;
+  p.hkv = a.hkv;
+  p.tq = a.tq;
+  p.tk = a.tk;
+  p.mode = a.mode;
+  p.q_offset = a.q_offset;
+  p.G = G;
+  p.R = kRows / G;
+  p.t_index = a.t_index;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  p.q8 = a.q8;
+  p.k8 = a.k8;
+  p.sq = a.sq;
+  p.sk = a.sk;
+  p.nqb = (a.tq + 63) / 64;
+  p.nkb = (a.tk + 63) / 64;
+  p.k8_stride = (long)p.nkb * 64;
+  const dim3 grid((a.tq + p.R - 1) / p.R, a.hkv);
+  const int smem = sage ? (kRows * 128 + 2 * kKeys * 128 + 2 * kKeys * 256)
+                        : (kRows * 256 + 2 * kKeys * 256 + 2 * kKeys * 256);
+  static bool set0 = false, set1 = false;
+  if (sage) {
+    if (!set1) {
+      cudaFuncSetAttribute(attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      set1 = true;
+    }
+    attn_kernel<true><<<grid, kThreads, smem, st>>>(p);
+  } else {
+    if (!set0) {
+      cudaFuncSetAttribute(attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      set0 = true;
+    }
+    attn_kernel<false><<<grid, kThreads, smem, st>>>(p);
+  }
+  if (cudaGetLastError() != cudaSuccess) {
+    *err = "attention: kernel launch failed";
+    return 2;
+  }
+  return 0;
+}
+
+int sage_prepare(const void* q, const KvView& kv, int hq, int hkv, int tq, int tk, int8_t* q8,
+                 int8_t* k8, float* sq, float* sk, float* kmean, cudaStream_t st,
+                 std::string* err)
+{
+  if (tq <= 0 || tk <= 0) return 0;
+  const int nqb = (tq + 63) / 64, nkb = (tk + 63) / 64;
+  kmean_kernel<<<hkv, 1024, 0, st>>>(kv, tk, kmean);
+  sage_quant_kernel<false><<<dim3(nqb, hq), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(q), kv, kmean, tq, nqb, q8, sq, tq);
+  sage_quant_kernel<true><<<dim3(nkb, hkv), 256, 0, st>>>(nullptr, kv, kmean, tk, nkb, k8, sk,
+                                                           (long)nkb * 64);
+  if (cudaGetLastError() != cudaSuccess) {
+    *err = "sage_prepare: kernel launch failed";
+    return 2;
+  }
+  return 0;
+}
+
+}  // namespace u15

@@ -1,0 +1,44 @@
+// Shared internals of the C ABI implementation (u15_capi.cu, u15_model.cu).
+#pragma once
+
+#include "../../include/u15c.h"
+#include "u15_kernels.h"
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+namespace u15 {
+
+struct DevState {
+  bool ready = false;
+  int sms = 148;
+  unsigned* err = nullptr;   // device status word (watchdog codes)
+};
+
+// Set this thread's last error and return `code`.
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+int dev_init(int device);
+DevState* dev();   // state of the current device, initialised on first use
+
+bool fill_seg(SegInfo* s, const int* off, const int* ex, int nseg, int rows, int n_experts,
+              std::string* err);
+KvView kv_view(void* k, void* v, const int32_t* page_table, int cap, int hkv);
+
+struct SageWs {
+  int8_t* q8;
+  int8_t* k8;
+  float* sq;
+  float* sk;
+  float* kmean;
+};
+size_t sage_bytes(int hq, int hkv, int tq, int tk);
+SageWs sage_split(void* ws, int hq, int hkv, int tq, int tk);
+
+int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, int hq, int hkv,
+                  int tq, int tk, int mode, int q_offset, const int32_t* t_index, void* sage_ws);
+int run_gemm(GemmArgs& a, cudaStream_t st);
+
+}  // namespace u15

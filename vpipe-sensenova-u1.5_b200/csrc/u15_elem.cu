@@ -1,0 +1,527 @@
+// Bandwidth-bound kernels of the MoT layer: each reads and writes its
+// tensors once with 16-byte vector accesses, coalesced across a warp, and
+// reduces with warp shuffles. Grids are sized from the row count; every
+// kernel is HBM-bound and is reported in GB/s against the copy peak.
+//
+// Rounding points follow the reference's bf16 buffers: every op reads
+// bf16, computes in f32 and writes bf16 once, as the Metal kernels do
+// (src/u15-kernels.metal in the reference).
+#include "u15_common.cuh"
+#include "u15_kernels.h"
+
+#include <algorithm>
+
+namespace u15 {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ int expert_of(int row, const SegInfo& s)
+{
+  int e = s.expert[0];
+#pragma unroll 1
+  for (int i = 1; i < s.nseg; ++i)
+    if (row >= s.off[i]) e = s.expert[i];
+  return e;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8])
+{
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8])
+{
+  uint4 u;
+  u.x = pack_bf2(v[0], v[1]);
+  u.y = pack_bf2(v[2], v[3]);
+  u.z = pack_bf2(v[4], v[5]);
+  u.w = pack_bf2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// ---------------------------------------------------------------------
+// RMSNorm, one CTA per row, gains chosen per expert segment.
+// y = bf16(x * rsqrt(mean(x^2) + eps) * w_e)
+// ---------------------------------------------------------------------
+constexpr int kRmsThreads = 256;
+
+__global__ void __launch_bounds__(kRmsThreads)
+    rms_norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                    __nv_bfloat16* __restrict__ y, int rows, int dim, float eps, SegInfo seg)
+{
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + (long)row * dim;
+  const __nv_bfloat16* wr = w + (long)expert_of(row, seg) * dim;
+  __nv_bfloat16* yr = y + (long)row * dim;
+  __shared__ float red[kRmsThreads / 32];
+  float acc = 0.0f;
+  for (int c = threadIdx.x * 8; c < dim; c += kRmsThreads * 8) {
+    float v[8];
+    load8(xr + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += v[i] * v[i];
+  }
+  acc = warp_sum(acc);
+  if (lane_id() == 0) red[warp_id()] = acc;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kRmsThreads / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / (float)dim + eps);
+  for (int c = threadIdx.x * 8; c < dim; c += kRmsThreads * 8) {
+    float v[8], g[8];
+    load8(xr + c, v);
+    load8(wr + c, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
+    store8(yr + c, v);
+  }
+}
+
+// ---------------------------------------------------------------------
+// Split q/k RMSNorm (src/u15-kernels.metal:50-87): one warp per
+// (token, head) row of 128, lanes 0-15 own the t half [0,64) and lanes
+// 16-31 the hw half [64,128), 4 elements each; two 16-lane reductions.
+// ---------------------------------------------------------------------
+__device__ __forceinline__ float half_sum(float v)
+{
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void split_qk_norm_kernel(__nv_bfloat16* __restrict__ x,
+                                     const __nv_bfloat16* __restrict__ w_t,
+                                     const __nv_bfloat16* __restrict__ w_hw, long nrows,
+                                     float eps)
+{
+  const long row = (long)blockIdx.x * (blockDim.x / 32) + warp_id();
+  if (row >= nrows) return;
+  const int l = lane_id();
+  __nv_bfloat16* r = x + row * 128 + l * 4;
+  const uint2 u = *reinterpret_cast<const uint2*>(r);
+  const float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y);
+  float v[4] = {a.x, a.y, b.x, b.y};
+  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+  ss = half_sum(ss);
+  const float inv = rsqrtf(ss / 64.0f + eps);
+  const __nv_bfloat16* g = (l < 16 ? w_t : w_hw) + (l & 15) * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = v[i] * inv * bf2f(g[i]);
+  uint2 o;
+  o.x = pack_bf2(v[0], v[1]);
+  o.y = pack_bf2(v[2], v[3]);
+  *reinterpret_cast<uint2*>(r) = o;
+}
+
+// ---------------------------------------------------------------------
+// Split-3 RoPE (src/u15-kernels.metal:118-157), same warp-per-row layout:
+// pairs (i, i+32) of the t range sit 8 lanes apart, pairs (64+i, 80+i)
+// and (96+i, 112+i) of h and w sit 4 lanes apart, so each lane fetches its
+// partner's values with one shuffle. Tables are [T][128] f32, doubled, so
+// both members of a pair read the same angle at their own column.
+// ---------------------------------------------------------------------
+__device__ __forceinline__ void rope4(float (&v)[4], const float* cs, const float* sn, int l)
+{
+  const int m = l < 16 ? 8 : 4;
+  const bool first = l < 16 ? (l < 8) : ((l & 7) < 4);
+  float p[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, v[i], m);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float c = cs[i], s = sn[i];
+    v[i] = first ? (v[i] * c - p[i] * s) : (v[i] * c + p[i] * s);
+  }
+}
+
+__global__ void split_rope_kernel(__nv_bfloat16* __restrict__ x, const float* __restrict__ cosf_,
+                                  const float* __restrict__ sinf_, long nrows, int heads)
+{
+  const long row = (long)blockIdx.x * (blockDim.x / 32) + warp_id();
+  if (row >= nrows) return;
+  const int l = lane_id();
+  const long t = row / heads;
+  __nv_bfloat16* r = x + row * 128 + l * 4;
+  const uint2 u = *reinterpret_cast<const uint2*>(r);
+  const float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y);
+  float v[4] = {a.x, a.y, b.x, b.y};
+  const float4 c4 = *reinterpret_cast<const float4*>(cosf_ + t * 128 + l * 4);
+  const float4 s4 = *reinterpret_cast<const float4*>(sinf_ + t * 128 + l * 4);
+  const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+  rope4(v, cs, sn, l);
+  uint2 o;
+  o.x = pack_bf2(v[0], v[1]);
+  o.y = pack_bf2(v[2], v[3]);
+  *reinterpret_cast<uint2*>(r) = o;
+}
+
+// ---------------------------------------------------------------------
+// RoPE tables on the device, angles in fp64 (src/u15-metal-ops.cc:547-605):
+// one thread per (token, column), column c in range [off, off + width).
+// ---------------------------------------------------------------------
+__global__ void rope_tables_kernel(const int32_t* __restrict__ pt, const int32_t* __restrict__ ph,
+                                   const int32_t* __restrict__ pw, int tokens, int d_t, int d_h,
+                                   double theta_t, double theta_hw, float* __restrict__ cos_out,
+                                   float* __restrict__ sin_out)
+{
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)tokens * 128) return;
+  const int t = (int)(idx / 128), c = (int)(idx % 128);
+  int off, width;
+  double theta;
+  const int32_t* pos;
+  if (c < d_t) { off = 0; width = d_t; theta = theta_t; pos = pt; }
+  else if (c < d_t + d_h) { off = d_t; width = d_h; theta = theta_hw; pos = ph; }
+  else { off = d_t + d_h; width = d_h; theta = theta_hw; pos = pw; }
+  const int half = width / 2;
+  const int i = (c - off) % half;
+  const double inv = 1.0 / pow(theta, (double)(2 * i) / (double)width);
+  const double ang = (double)pos[t] * inv;
+  cos_out[idx] = (float)cos(ang);
+  sin_out[idx] = (float)sin(ang);
+}
+
+// ---------------------------------------------------------------------
+// Fused QKV post-processing of the token-major GEMM output
+// qkv [T][(NH + 2*KV) * 128]: per (token, head) warp,
+//   q heads: split norm (q_norm, q_norm_hw of the row's expert) -> bf16 ->
+//            split rope -> bf16 -> q_out [NH][T][128]      (transpose_thd)
+//   k heads: the same with k_norm / k_norm_hw -> K cache @ kv_off (append)
+//   v heads: copied -> V cache @ kv_off                    (append)
+// The reference runs these as split_qk_norm, split_rope, transpose_thd and
+// transpose_into_cache (src/u15-backbone.cc:199-214); the bf16 rounding
+// after the norm and after the rope is kept.
+// norms: [E][4][64] bf16 = q_t, q_hw, k_t, k_hw per expert.
+// ---------------------------------------------------------------------
+__global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                const __nv_bfloat16* __restrict__ norms,
+                                const float* __restrict__ cosf_, const float* __restrict__ sinf_,
+                                __nv_bfloat16* __restrict__ q_out, KvView kv, int T, int nh,
+                                int nkv, int kv_off, float eps, SegInfo seg)
+{
+  const int heads = nh + 2 * nkv;
+  const long row = (long)blockIdx.x * (blockDim.x / 32) + warp_id();
+  if (row >= (long)T * heads) return;
+  const int l = lane_id();
+  const int t = (int)(row / heads), h = (int)(row % heads);
+  const __nv_bfloat16* src = qkv + row * 128 + l * 4;
+  const uint2 u = *reinterpret_cast<const uint2*>(src);
+  const float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y);
+  float v[4] = {a.x, a.y, b.x, b.y};
+  __nv_bfloat16* dst;
+  if (h < nh + nkv) {
+    const int e = expert_of(t, seg);
+    const __nv_bfloat16* nw = norms + (long)e * 256 + (h < nh ? 0 : 128) + (l < 16 ? 0 : 64) +
+                              (l & 15) * 4;
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = half_sum(ss);
+    const float inv = rsqrtf(ss / 64.0f + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = bfround(v[i] * inv * bf2f(nw[i]));
+    const float4 c4 = *reinterpret_cast<const float4*>(cosf_ + (long)t * 128 + l * 4);
+    const float4 s4 = *reinterpret_cast<const float4*>(sinf_ + (long)t * 128 + l * 4);
+    const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+    rope4(v, cs, sn, l);
+    if (h < nh) {
+      dst = q_out + ((long)h * T + t) * 128;
+    } else {
+      const int j = kv_off + t;
+      const long page = kv.page_table ? kv.page_table[j >> 6] : (j >> 6);
+      dst = reinterpret_cast<__nv_bfloat16*>(kv.k) + page * kv.page_stride +
+            (long)(h - nh) * kv.head_stride + (long)(j & 63) * 128;
+    }
+  } else {
+    const int j = kv_off + t;
+    const long page = kv.page_table ? kv.page_table[j >> 6] : (j >> 6);
+    dst = reinterpret_cast<__nv_bfloat16*>(kv.v) + page * kv.page_stride +
+          (long)(h - nh - nkv) * kv.head_stride + (long)(j & 63) * 128;
+  }
+  uint2 o;
+  o.x = pack_bf2(v[0], v[1]);
+  o.y = pack_bf2(v[2], v[3]);
+  *reinterpret_cast<uint2*>(dst + l * 4) = o;
+}
+
+// ---------------------------------------------------------------------
+// Layout moves (src/u15-kernels.metal:544-600), 16 bytes per thread.
+// ---------------------------------------------------------------------
+// [T][H*D] -> [H][T][D]
+__global__ void transpose_thd_kernel(const __nv_bfloat16* __restrict__ in,
+                                     __nv_bfloat16* __restrict__ out, int T, int H, int D)
+{
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;   // 8-element chunk
+  const int cpr = D / 8;
+  if (idx >= (long)T * H * cpr) return;
+  const int c = (int)(idx % cpr);
+  const long th = idx / cpr;
+  const int h = (int)(th % H);
+  const long t = th / H;
+  const uint4 v = *reinterpret_cast<const uint4*>(in + (t * H + h) * D + c * 8);
+  *reinterpret_cast<uint4*>(out + ((long)h * T + t) * D + c * 8) = v;
+}
+// [H][T][D] -> [T][H*D]
+__global__ void transpose_htd_kernel(const __nv_bfloat16* __restrict__ in,
+                                     __nv_bfloat16* __restrict__ out, int T, int H, int D)
+{
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cpr = D / 8;
+  if (idx >= (long)T * H * cpr) return;
+  const int c = (int)(idx % cpr);
+  const long th = idx / cpr;
+  const int h = (int)(th % H);
+  const long t = th / H;
+  const uint4 v = *reinterpret_cast<const uint4*>(in + ((long)h * T + t) * D + c * 8);
+  *reinterpret_cast<uint4*>(out + (t * H + h) * D + c * 8) = v;
+}
+// [T][H*128] -> KV view (paged or contiguous) at token offset `off`.
+__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ in, void* cache,
+                                 const int32_t* __restrict__ page_table, long page_stride,
+                                 long head_stride, int T, int H, int off)
+{
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)T * H * 16) return;
+  const int c = (int)(idx % 16);
+  const long th = idx / 16;
+  const int h = (int)(th % H);
+  const int t = (int)(th / H);
+  const int j = off + t;
+  const long page = page_table ? page_table[j >> 6] : (j >> 6);
+  const uint4 v = *reinterpret_cast<const uint4*>(in + ((long)t * H + h) * 128 + c * 8);
+  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(cache) + page * page_stride +
+                            h * head_stride + (long)(j & 63) * 128 + c * 8) = v;
+}
+
+// ---------------------------------------------------------------------
+// Elementwise
+// ---------------------------------------------------------------------
+__global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ u,
+                              __nv_bfloat16* __restrict__ y, long n8)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float a[8], b[8];
+  load8(g + i * 8, a);
+  load8(u + i * 8, b);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = (a[k] / (1.0f + expf(-a[k]))) * b[k];
+  store8(y + i * 8, a);
+}
+__global__ void add_kernel(__nv_bfloat16* __restrict__ d, const __nv_bfloat16* __restrict__ s,
+                           long n8)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float a[8], b[8];
+  load8(d + i * 8, a);
+  load8(s + i * 8, b);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] += b[k];
+  store8(d + i * 8, a);
+}
+__global__ void add_row_kernel(__nv_bfloat16* __restrict__ d, const __nv_bfloat16* __restrict__ r,
+                               long rows, int dim8)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * dim8) return;
+  float a[8], b[8];
+  load8(d + i * 8, a);
+  load8(r + (i % dim8) * 8, b);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] += b[k];
+  store8(d + i * 8, a);
+}
+__global__ void silu_kernel(__nv_bfloat16* __restrict__ x, long n8)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float a[8];
+  load8(x + i * 8, a);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = a[k] / (1.0f + expf(-a[k]));
+  store8(x + i * 8, a);
+}
+
+// ---------------------------------------------------------------------
+// Symmetric per-row int8 quantisation, one CTA per row:
+//   s = absmax / 127 (IEEE fp32 division), q = rn_even(x / s), clamp +-127
+// Every step is a single correctly-rounded fp32 operation, so the codes
+// equal the CPU restatement's bit for bit.
+// ---------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ q,
+                      float* __restrict__ scale, int cols)
+{
+  const long row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * cols;
+  __shared__ float red[8];
+  float m = 0.0f;
+  for (int c = threadIdx.x * 8; c < cols; c += 256 * 8) {
+    float v[8];
+    load8(xr + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+  }
+  m = warp_max(m);
+  if (lane_id() == 0) red[warp_id()] = m;
+  __syncthreads();
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  const float s = __fdiv_rn(amax, 127.0f);
+  if (threadIdx.x == 0) scale[row] = s;
+  for (int c = threadIdx.x * 8; c < cols; c += 256 * 8) {
+    float v[8];
+    load8(xr + c, v);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int k = 0;
+      if (s > 0.0f) k = max(-127, min(127, __float2int_rn(__fdiv_rn(v[i], s))));
+      const uint32_t b = (uint32_t)(k & 0xff);
+      if (i < 4) lo |= b << (8 * i); else hi |= b << (8 * (i - 4));
+    }
+    *reinterpret_cast<uint2*>(q + row * cols + c) = make_uint2(lo, hi);
+  }
+}
+
+inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+}  // namespace
+
+// ---------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------
+int launch_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,
+                    const SegInfo& seg, cudaStream_t st)
+{
+  if (rows <= 0) return 0;
+  rms_norm_kernel<<<rows, kRmsThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                static_cast<const __nv_bfloat16*>(w),
+                                                static_cast<__nv_bfloat16*>(y), rows, dim, eps, seg);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_split_qk_norm(void* x, const void* w_t, const void* w_hw, int heads, int tokens,
+                         float eps, cudaStream_t st)
+{
+  const long rows = (long)heads * tokens;
+  if (rows <= 0) return 0;
+  split_qk_norm_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(
+      static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w_t),
+      static_cast<const __nv_bfloat16*>(w_hw), rows, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_split_rope(void* x, const float* c, const float* s, int heads, int tokens,
+                      cudaStream_t st)
+{
+  const long rows = (long)heads * tokens;
+  if (rows <= 0) return 0;
+  split_rope_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(static_cast<__nv_bfloat16*>(x), c, s,
+                                                          rows, heads);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_rope_tables(const int32_t* pt, const int32_t* ph, const int32_t* pw, int tokens,
+                       int d_t, int d_h, double theta_t, double theta_hw, float* c, float* s,
+                       cudaStream_t st)
+{
+  if (tokens <= 0) return 0;
+  rope_tables_kernel<<<blocks_for((long)tokens * 128, 256), 256, 0, st>>>(
+      pt, ph, pw, tokens, d_t, d_h, theta_t, theta_hw, c, s);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_qkv_post(const void* qkv, const void* norms, const float* c, const float* s,
+                    void* q_out, const KvView& kv, int T, int nh, int nkv, int kv_off, float eps,
+                    const SegInfo& seg, cudaStream_t st)
+{
+  const long rows = (long)T * (nh + 2 * nkv);
+  if (rows <= 0) return 0;
+  qkv_post_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(norms), c, s,
+      static_cast<__nv_bfloat16*>(q_out), kv, T, nh, nkv, kv_off, eps, seg);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_transpose(const void* in, void* out, int T, int H, int D, bool to_head_major,
+                     cudaStream_t st)
+{
+  const long n = (long)T * H * (D / 8);
+  if (n <= 0) return 0;
+  if (to_head_major)
+    transpose_thd_kernel<<<blocks_for(n, 256), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), T, H, D);
+  else
+    transpose_htd_kernel<<<blocks_for(n, 256), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), T, H, D);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_kv_append(const void* in, void* cache, const int32_t* page_table, long page_stride,
+                     long head_stride, int T, int H, int off, cudaStream_t st)
+{
+  const long n = (long)T * H * 16;
+  if (n <= 0) return 0;
+  kv_append_kernel<<<blocks_for(n, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(in),
+                                                        cache, page_table, page_stride,
+                                                        head_stride, T, H, off);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_swiglu(const void* g, const void* u, void* y, long n, cudaStream_t st)
+{
+  if (n <= 0) return 0;
+  swiglu_kernel<<<blocks_for(n / 8, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(g),
+                                                         static_cast<const __nv_bfloat16*>(u),
+                                                         static_cast<__nv_bfloat16*>(y), n / 8);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_add(void* d, const void* s, long n, cudaStream_t st)
+{
+  if (n <= 0) return 0;
+  add_kernel<<<blocks_for(n / 8, 256), 256, 0, st>>>(static_cast<__nv_bfloat16*>(d),
+                                                      static_cast<const __nv_bfloat16*>(s), n / 8);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_add_row(void* d, const void* r, long rows, int dim, cudaStream_t st)
+{
+  if (rows <= 0) return 0;
+  add_row_kernel<<<blocks_for(rows * (dim / 8), 256), 256, 0, st>>>(
+      static_cast<__nv_bfloat16*>(d), static_cast<const __nv_bfloat16*>(r), rows, dim / 8);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_silu(void* x, long n, cudaStream_t st)
+{
+  if (n <= 0) return 0;
+  silu_kernel<<<blocks_for(n / 8, 256), 256, 0, st>>>(static_cast<__nv_bfloat16*>(x), n / 8);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_quant_rows(const void* x, int8_t* q, float* s, int rows, int cols, cudaStream_t st)
+{
+  if (rows <= 0) return 0;
+  quant_rows_kernel<<<rows, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), q, s, cols);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+}  // namespace u15

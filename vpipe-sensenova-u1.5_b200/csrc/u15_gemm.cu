@@ -1,0 +1,520 @@
+// The projection GEMM of the MoT layer on sm_100a tensor cores.
+//
+//   y[m][n] = epilogue( sum_k x[m][k] * W_e[n][k] ),  e = expert of row m
+//
+// One persistent kernel per call, one CTA per SM, warp-specialised:
+//   warp 0      TMA producer: 128x(BK) A tile + 256x(BK) B tile per stage,
+//               128-byte swizzle, 4-stage ring in shared memory
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256)
+//               into one of two TMEM accumulators (2 x 256 f32 columns)
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (one row per thread),
+//               apply the fused epilogue, store bf16 to global
+// The two TMEM accumulators let the epilogue of tile i overlap the
+// main loop of tile i+1.
+//
+// MoT routing (the reference selects ONE expert per pass,
+// src/u15-backbone.cc:189; here one launch serves every segment): the host
+// splits the M axis into "units" -- a 128-row block intersected with one
+// contiguous token segment -- and each unit names the expert whose weight
+// rows (W stacked as [E][N][K]) its B tiles come from. A block that
+// straddles a segment boundary appears once per segment and each pass
+// stores only its own rows.
+//
+// bf16: kind::f16, BK = 64 elements (128 bytes), 4 MMAs of K=16 per stage.
+// int8: kind::i8, BK = 128 elements (128 bytes), 4 MMAs of K=32 per stage,
+//       s32 accumulators, dequantised in the epilogue by the per-token and
+//       per-channel scales (acc * s_tok[m] * s_ch[n]).
+//
+// Epilogues (the reference's separate passes, src/u15-backbone.cc:229-256,
+// with their bf16 rounding points kept):
+//   STORE   y = bf16(acc [+ bias])
+//   RESID   y = bf16(resid + bf16(acc))                       o_proj / down
+//   SWIGLU  B rows interleaved in 128-row blocks [gate_j | up_j]:
+//           y[:, 128j + c] = bf16(silu(bf16(g)) * bf16(u))    gate|up
+#include "u15_common.cuh"
+#include "u15_kernels.h"
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+namespace u15 {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kStages = 4, kThreads = 192;
+constexpr int kAStage = kBM * 128;   // bytes per A stage (128 rows x 128 B)
+constexpr int kBStage = kBN * 128;   // bytes per B stage
+constexpr int kSmemBytes = kStages * (kAStage + kBStage) + 1024 /*align*/ + 256 /*bars*/;
+
+struct Unit {
+  int m0, row_lo, row_hi, expert;
+};
+
+constexpr int kMaxUnits = 200;
+
+struct Params {
+  int M, N, K;          // N: weight rows per expert (SWIGLU: 2x the output width)
+  int n_units, n_nblk, n_kblk;
+  void* y;
+  long ldy;             // output row stride, elements
+  const __nv_bfloat16* resid;
+  long ldr;
+  const __nv_bfloat16* bias;   // [E][N] or null
+  const float* s_tok;          // int8: [M]
+  const float* s_ch;           // int8: [E][N]
+  int32_t* acc_dump;           // int8 debug: [M][N] raw accumulators, or null
+  unsigned* err;
+  Unit units[kMaxUnits];
+};
+
+template <bool I8>
+__device__ __forceinline__ void chunk_values(uint32_t taddr, float (&v)[32], const Params& p,
+                                             int row, bool row_ok, int col0, int expert)
+{
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_ld_wait();
+  if constexpr (I8) {
+    const float st = row_ok ? p.s_tok[row] : 0.0f;
+    if (p.acc_dump != nullptr && row_ok) {
+      int32_t* d = p.acc_dump + (long)row * p.N + col0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.N) d[i] = (int32_t)r[i];
+    }
+    const float* sc = p.s_ch + (long)expert * p.N + col0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float s = (col0 + i < p.N) ? sc[i] : 0.0f;
+      v[i] = ((float)(int32_t)r[i] * st) * s;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  }
+}
+
+// Store 32 bf16 values of one row at columns [col0, col0 + 32) with
+// columns >= ncols dropped.
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)[32], int col0,
+                                            int ncols)
+{
+  if (col0 + 32 <= ncols && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 o;
+      o.x = pack_bf2(v[q * 8 + 0], v[q * 8 + 1]);
+      o.y = pack_bf2(v[q * 8 + 2], v[q * 8 + 3]);
+      o.z = pack_bf2(v[q * 8 + 4], v[q * 8 + 5]);
+      o.w = pack_bf2(v[q * 8 + 6], v[q * 8 + 7]);
+      d4[q] = o;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < ncols) dst[i] = f2bf(v[i]);
+  }
+}
+
+__device__ __forceinline__ void load_row32(const __nv_bfloat16* src, float (&v)[32], int col0,
+                                           int ncols)
+{
+  if (col0 + 32 <= ncols && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 u = s4[q];
+      float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
+      v[q * 8 + 0] = a.x; v[q * 8 + 1] = a.y; v[q * 8 + 2] = b.x; v[q * 8 + 3] = b.y;
+      v[q * 8 + 4] = c.x; v[q * 8 + 5] = c.y; v[q * 8 + 6] = d.x; v[q * 8 + 7] = d.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (col0 + i < ncols) ? bf2f(src[i]) : 0.0f;
+  }
+}
+
+template <bool I8, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ Params p)
+{
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kAStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBStage);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = full0 + 8 * kStages;
+  const uint32_t accf0 = empty0 + 8 * kStages;
+  const uint32_t acce0 = accf0 + 16;
+  const uint32_t drain = acce0 + 16;
+
+  const uint32_t w = warp_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf0 + 8 * a, 1);
+      mbar_init(acce0 + 8 * a, 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (w == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = p.n_units * p.n_nblk;
+  constexpr int kBK = I8 ? 128 : 64;   // elements per 128-byte row
+
+  if (w == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane_id() == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        const Unit u = p.units[t % p.n_units];
+        const int nb = t / p.n_units;
+        const int brow = u.expert * p.N + nb * kBN;
+        for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1;
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full0 + 8 * s, kAStage + kBStage);
+          tma_load_2d(smem_u32(sA + s * kAStage), &tmA, kb * kBK, u.m0, full0 + 8 * s);
+          tma_load_2d(smem_u32(sB + s * kBStage), &tmB, kb * kBK, brow, full0 + 8 * s);
+        }
+      }
+      // Unwind: every stage's last fill must land before the CTA may exit.
+      for (uint32_t s = 0; s < kStages; ++s) {
+        if (it > s) {
+          const uint32_t last = ((it - 1 - s) / kStages) * kStages + s;
+          mbar_wait(full0 + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
+        }
+      }
+    }
+  } else if (w == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane_id() == 0) {
+      const uint32_t idesc = I8 ? idesc_s8(kBM, kBN) : idesc_bf16(kBM, kBN);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++lt) {
+        const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+        if (!mbar_wait(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1;
+          if (!mbar_wait(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * kAStage);
+          const uint32_t b0 = smem_u32(sB + s * kBStage);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = smem_desc_sw128(a0 + k * 32);
+            const uint64_t bd = smem_desc_sw128(b0 + k * 32);
+            if constexpr (I8)
+              mma_i8(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            else
+              mma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          mma_commit(empty0 + 8 * s);
+        }
+        if (!ok) break;
+        mma_commit(accf0 + 8 * acc);
+      }
+      // Unwind: all MMAs this thread issued complete before TMEM is freed.
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.err, kDevWaitDrain);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int wq = (int)(w & 3);   // TMEM lane quadrant this warp may access
+    const int r_in = wq * 32 + (int)lane_id();
+    int lt = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
+      const Unit u = p.units[t % p.n_units];
+      const int nb = t / p.n_units;
+      const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+      if (!mbar_wait(accf0 + 8 * acc, aph, p.err, kDevWaitAccFull)) break;
+      tc_fence_after();
+      const int row = u.m0 + r_in;
+      const bool row_ok = row >= u.row_lo && row < u.row_hi;
+      const uint32_t tb = tmem_base + acc * kBN + ((uint32_t)(wq * 32) << 16);
+      const int n0 = nb * kBN;
+      if constexpr (EPI == kEpiSwiglu) {
+        const int nout = p.N / 2;
+        __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.y) + (long)row * p.ldy;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float g[32], v[32];
+          chunk_values<I8>(tb + c * 32, g, p, row, row_ok, n0 + c * 32, u.expert);
+          chunk_values<I8>(tb + 128 + c * 32, v, p, row, row_ok, n0 + 128 + c * 32, u.expert);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gg = bfround(g[i]), uu = bfround(v[i]);
+            g[i] = (gg / (1.0f + expf(-gg))) * uu;
+          }
+          const int oc = nb * 128 + c * 32;
+          if (row_ok) store_row32(yrow + oc, g, oc, nout);
+        }
+      } else {
+        __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.y) + (long)row * p.ldy;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          const int col0 = n0 + c * 32;
+          chunk_values<I8>(tb + c * 32, v, p, row, row_ok, col0, u.expert);
+          if (!row_ok || col0 >= p.N) continue;
+          if (p.bias != nullptr) {
+            const __nv_bfloat16* b = p.bias + (long)u.expert * p.N + col0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.N) v[i] += bf2f(b[i]);
+          }
+          if constexpr (EPI == kEpiResid) {
+            float rr[32];
+            load_row32(p.resid + (long)row * p.ldr + col0, rr, col0, p.N);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = rr[i] + bfround(v[i]);
+          }
+          store_row32(yrow + col0, v, col0, p.N);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce0 + 8 * acc);
+    }
+  }
+
+  __syncthreads();
+  if (w == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  uint64_t rows, cols;
+  uint32_t box_rows;
+  int elsize;
+  bool operator==(const MapKey& o) const
+  {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+           elsize == o.elsize;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const
+  {
+    return std::hash<const void*>()(k.ptr) ^ (k.rows * 1315423911ull) ^ (k.cols << 7) ^
+           ((uint64_t)k.box_rows << 40) ^ ((uint64_t)k.elsize << 56);
+  }
+};
+
+// A 2-D [rows][cols] row-major tensor (elsize 2 = bf16, 1 = int8), box of
+// 128 bytes x box_rows, 128-byte swizzle, zero fill out of bounds. Cached:
+// encoding costs microseconds and a layer calls the same maps every pass.
+int make_map(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+             int elsize, std::string* err)
+{
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{ptr, rows, cols, box_rows, elsize};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return 0;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    *err = "cuTensorMapEncodeTiled is unavailable (driver too old?)";
+    return 1;
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * (cuuint64_t)elsize};
+  const cuuint32_t box[2] = {(cuuint32_t)(128 / elsize), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      fn(out, elsize == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+         const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+    return 1;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *out);
+  return 0;
+}
+
+template <bool I8, int EPI>
+int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid,
+               cudaStream_t st)
+{
+  static bool attr_set = false;   // per instantiation; benign race (idempotent)
+  auto k = gemm_tc_kernel<I8, EPI>;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+        cudaSuccess)
+      return 2;
+    attr_set = true;
+  }
+  k<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+}  // namespace
+
+int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
+{
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) {
+    *err = "gemm: M, N and K must be positive";
+    return 1;
+  }
+  const int es = a.int8 ? 1 : 2;
+  if ((a.K * es) % 16 != 0) {
+    *err = "gemm: K * element size must be a multiple of 16 bytes (TMA row stride)";
+    return 1;
+  }
+  if (a.epilogue == kEpiSwiglu && (a.N % 256) != 0) {
+    *err = "gemm: the SwiGLU epilogue needs N (gate+up rows) to be a multiple of 256";
+    return 1;
+  }
+  if (a.int8 && (a.s_tok == nullptr || a.s_ch == nullptr)) {
+    *err = "gemm: int8 needs the per-token and per-channel scales";
+    return 1;
+  }
+  if (a.epilogue == kEpiResid && a.resid == nullptr) {
+    *err = "gemm: the residual epilogue needs a residual input";
+    return 1;
+  }
+  Params p{};
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.y = a.y;
+  p.ldy = a.ldy > 0 ? a.ldy : (a.epilogue == kEpiSwiglu ? a.N / 2 : a.N);
+  p.resid = static_cast<const __nv_bfloat16*>(a.resid);
+  p.ldr = a.ldr > 0 ? a.ldr : a.N;
+  p.bias = static_cast<const __nv_bfloat16*>(a.bias);
+  p.s_tok = a.s_tok;
+  p.s_ch = a.s_ch;
+  p.acc_dump = a.acc_dump;
+  p.err = a.dev_err;
+
+  // Units: 128-row blocks intersected with the routing segments.
+  int nseg = a.nseg;
+  int off1[2] = {0, a.M}, ex1[1] = {0};
+  const int* off = a.seg_off;
+  const int* ex = a.seg_expert;
+  if (nseg <= 0 || off == nullptr || ex == nullptr) {
+    nseg = 1;
+    off = off1;
+    ex = ex1;
+  }
+  if (off[0] != 0 || off[nseg] != a.M) {
+    *err = "gemm: segments must cover [0, M)";
+    return 1;
+  }
+  int n_units = 0;
+  for (int m0 = 0; m0 < a.M; m0 += kBM) {
+    const int m1 = std::min(m0 + kBM, a.M);
+    for (int s = 0; s < nseg; ++s) {
+      if (off[s + 1] < off[s]) {
+        *err = "gemm: segment offsets must be non-decreasing";
+        return 1;
+      }
+      if (ex[s] < 0 || ex[s] >= a.n_experts) {
+        *err = "gemm: segment expert out of range";
+        return 1;
+      }
+      const int lo = std::max(m0, off[s]), hi = std::min(m1, off[s + 1]);
+      if (lo >= hi) continue;
+      if (n_units >= kMaxUnits) {
+        *err = "gemm: too many row blocks for one launch (M too large)";
+        return 1;
+      }
+      p.units[n_units++] = Unit{m0, lo, hi, ex[s]};
+    }
+  }
+  p.n_units = n_units;
+  p.n_nblk = (a.N + kBN - 1) / kBN;
+  const int bk = a.int8 ? 128 : 64;
+  p.n_kblk = (a.K + bk - 1) / bk;
+
+  CUtensorMap ma, mb;
+  if (make_map(&ma, a.x, (uint64_t)a.M, (uint64_t)a.K, kBM, es, err)) return 2;
+  if (make_map(&mb, a.w, (uint64_t)a.N * a.n_experts, (uint64_t)a.K, kBN, es, err)) return 2;
+
+  const int tiles = p.n_units * p.n_nblk;
+  const int grid = std::min(tiles, a.num_sms > 0 ? a.num_sms : 148);
+  int rc;
+  if (a.int8) {
+    rc = a.epilogue == kEpiResid    ? launch_one<true, kEpiResid>(ma, mb, p, grid, st)
+         : a.epilogue == kEpiSwiglu ? launch_one<true, kEpiSwiglu>(ma, mb, p, grid, st)
+                                    : launch_one<true, kEpiStore>(ma, mb, p, grid, st);
+  } else {
+    rc = a.epilogue == kEpiResid    ? launch_one<false, kEpiResid>(ma, mb, p, grid, st)
+         : a.epilogue == kEpiSwiglu ? launch_one<false, kEpiSwiglu>(ma, mb, p, grid, st)
+                                    : launch_one<false, kEpiStore>(ma, mb, p, grid, st);
+  }
+  if (rc) *err = "gemm: kernel launch failed";
+  return rc;
+}
+
+}  // namespace u15

@@ -1,0 +1,110 @@
+// Internal launcher interface between the C ABI (u15_capi.cu) and the
+// kernel files. Not installed; the public surface is include/u15c.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace u15 {
+
+enum Epilogue { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2 };
+
+// Token segments routed to experts: rows [off[i], off[i+1]) use expert[i].
+constexpr int kMaxSeg = 8;
+struct SegInfo {
+  int nseg = 1;
+  int off[kMaxSeg + 1] = {0};
+  int expert[kMaxSeg] = {0};
+};
+
+struct GemmArgs {
+  bool int8 = false;
+  const void* x = nullptr;       // [M][K] bf16 or int8
+  const void* w = nullptr;       // [n_experts][N][K] bf16 or int8
+  int n_experts = 1;
+  int M = 0, N = 0, K = 0;
+  const int* seg_off = nullptr;  // host, nseg + 1 entries (null: one segment, expert 0)
+  const int* seg_expert = nullptr;
+  int nseg = 0;
+  int epilogue = kEpiStore;
+  void* y = nullptr;             // bf16 [M][ldy]
+  long ldy = 0;                  // 0: N (SwiGLU: N / 2)
+  const void* resid = nullptr;   // bf16 [M][ldr]
+  long ldr = 0;
+  const void* bias = nullptr;    // bf16 [n_experts][N]
+  const float* s_tok = nullptr;  // int8
+  const float* s_ch = nullptr;   // int8 [n_experts][N]
+  int32_t* acc_dump = nullptr;   // int8 debug [M][N]
+  unsigned* dev_err = nullptr;
+  int num_sms = 148;
+};
+
+int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err);
+
+// Paged or contiguous K/V addressing shared by the attention and KV kernels.
+// Token j of kv head h lives at
+//   base + page(j >> 6) * page_stride + h * head_stride + (j & 63) * 128
+// with page(i) = page_table ? page_table[i] : i. The reference's contiguous
+// cache [hkv][cap][128] is page_stride = 64*128, head_stride = cap*128; the
+// paged pool [page][hkv][64][128] is page_stride = hkv*64*128,
+// head_stride = 64*128.
+struct KvView {
+  void* k = nullptr;
+  void* v = nullptr;
+  const int32_t* page_table = nullptr;   // device; null = identity
+  long page_stride = 0;                  // elements
+  long head_stride = 0;                  // elements
+};
+constexpr int kPageTokens = 64;
+constexpr int kHeadDim = 128;
+
+struct AttnArgs {
+  const void* q = nullptr;      // [hq][tq][128] bf16 (head-major, tq rows per head)
+  KvView kv;
+  void* out = nullptr;          // [tq][hq*128] bf16 (token-major)
+  int hq = 0, hkv = 0, tq = 0, tk = 0;
+  int mode = 0;                 // 0 bidirectional, 1 causal, 2 block-causal
+  int q_offset = 0;
+  const int32_t* t_index = nullptr;   // device [tk], block-causal
+  // Sage int8 QK (bidirectional only): prepared by sage_prepare()
+  const int8_t* q8 = nullptr;   // [hq][tq][128]
+  const int8_t* k8 = nullptr;   // [hkv][tk_pad][128]
+  const float* sq = nullptr;    // [hq][ceil(tq/64)]
+  const float* sk = nullptr;    // [hkv][ceil(tk/64)]
+  unsigned* dev_err = nullptr;
+};
+
+int attention(const AttnArgs& a, cudaStream_t st, std::string* err);
+
+// Sage prologue: K smoothing (mean over tk keys per kv head and channel),
+// per-64-row block int8 quantisation of Q and of the smoothed K.
+int sage_prepare(const void* q, const KvView& kv, int hq, int hkv, int tq, int tk, int8_t* q8,
+                 int8_t* k8, float* sq, float* sk, float* kmean, cudaStream_t st,
+                 std::string* err);
+
+// bandwidth kernels (u15_elem.cu); all bf16 unless stated
+int launch_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,
+                    const SegInfo& seg, cudaStream_t st);
+int launch_split_qk_norm(void* x, const void* w_t, const void* w_hw, int heads, int tokens,
+                         float eps, cudaStream_t st);
+int launch_split_rope(void* x, const float* c, const float* s, int heads, int tokens,
+                      cudaStream_t st);
+int launch_rope_tables(const int32_t* pt, const int32_t* ph, const int32_t* pw, int tokens,
+                       int d_t, int d_h, double theta_t, double theta_hw, float* c, float* s,
+                       cudaStream_t st);
+int launch_qkv_post(const void* qkv, const void* norms, const float* c, const float* s,
+                    void* q_out, const KvView& kv, int T, int nh, int nkv, int kv_off, float eps,
+                    const SegInfo& seg, cudaStream_t st);
+int launch_transpose(const void* in, void* out, int T, int H, int D, bool to_head_major,
+                     cudaStream_t st);
+int launch_kv_append(const void* in, void* cache, const int32_t* page_table, long page_stride,
+                     long head_stride, int T, int H, int off, cudaStream_t st);
+int launch_swiglu(const void* g, const void* u, void* y, long n, cudaStream_t st);
+int launch_add(void* d, const void* s, long n, cudaStream_t st);
+int launch_add_row(void* d, const void* r, long rows, int dim, cudaStream_t st);
+int launch_silu(void* x, long n, cudaStream_t st);
+int launch_quant_rows(const void* x, int8_t* q, float* s, int rows, int cols, cudaStream_t st);
+
+}  // namespace u15

@@ -1,0 +1,660 @@
+// The model half of the C ABI: the bound weight layout (U15Weights' bind
+// step), the paged KV cache (KvCache) and the backbone layer/stack
+// (U15Backbone::layer_step_ / forward), src/u15-weights.*, u15-backbone.*
+// in the reference.
+//
+// Bound layout, per layer, experts stacked on the outer axis:
+//   qkv   [E][(NH + 2*KV) * HD][H]   q rows, then k rows, then v rows
+//   o     [E][H][NH * HD]
+//   gu    [E][2 * I][H]              128-row blocks [gate_j | up_j] for the
+//                                    SwiGLU epilogue
+//   down  [E][H][I]
+//   ln_in, ln_post [E][H]; norms [E][4][64] = q_norm, q_norm_hw, k_norm, k_norm_hw
+//   (INT8) the same four matrices as per-output-channel int8 plus f32 scales
+// The GEMM's TMA maps tile these row-major buffers into 128-byte-swizzled
+// shared-memory tiles; no further repacking pays at these shapes.
+//
+// Paged KV cache: per layer a K and a V pool [pages][KV][64][128] bf16,
+// one logical->physical page table shared by all layers.
+#include "u15_capi_internal.h"
+#include "u15_common.cuh"
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+using u15::fail;
+using u15::cuda_fail;
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+struct LayerW {
+  bf16* qkv = nullptr;
+  bf16* o = nullptr;
+  bf16* gu = nullptr;
+  bf16* down = nullptr;
+  bf16* ln_in = nullptr;
+  bf16* ln_post = nullptr;
+  bf16* norms = nullptr;
+  int8_t* qkv8 = nullptr;
+  int8_t* o8 = nullptr;
+  int8_t* gu8 = nullptr;
+  int8_t* down8 = nullptr;
+  float* qkv_s = nullptr;
+  float* o_s = nullptr;
+  float* gu_s = nullptr;
+  float* down_s = nullptr;
+};
+
+// ---------------------------------------------------------------------
+// kernels: dtype conversion into the bound layout, seeded init
+// ---------------------------------------------------------------------
+__device__ __forceinline__ float src_value(const void* src, int dtype, long i)
+{
+  if (dtype == U15C_DT_F32) return static_cast<const float*>(src)[i];
+  if (dtype == U15C_DT_F16) return __half2float(static_cast<const __half*>(src)[i]);
+  return __bfloat162float(static_cast<const bf16*>(src)[i]);
+}
+
+// dst row for source row r: base + r, or (interleave >= 0) the gate/up
+// block layout base + (r/128)*256 + interleave*128 + r%128.
+__global__ void bind_kernel(const void* src, int dtype, long rows, long cols, bf16* dst,
+                            int interleave)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * cols) return;
+  const long r = i / cols, c = i % cols;
+  long dr = r;
+  if (interleave >= 0) dr = (r / 128) * 256 + interleave * 128 + r % 128;
+  dst[dr * cols + c] = __float2bfloat16_rn(src_value(src, dtype, i));
+}
+
+__device__ __forceinline__ uint64_t splitmix(uint64_t x)
+{
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+// N(mean, std) by Box-Muller on a counter hash (seed, stream, index).
+__global__ void randn_kernel(bf16* dst, long n, uint64_t seed, uint64_t stream, float mean,
+                             float std)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t h = splitmix(seed ^ splitmix(stream * 0x100000001B3ull + (uint64_t)i));
+  const float u1 = ((float)(h >> 40) + 1.0f) * (1.0f / 16777217.0f);
+  const float u2 = (float)((h >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+  const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+  dst[i] = __float2bfloat16_rn(mean + std * z);
+}
+
+inline unsigned nblk(long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+}  // namespace
+
+struct u15c_model {
+  u15c_config cfg{};
+  unsigned flags = 0;
+  int device = 0;
+  std::vector<LayerW> layers;
+  bf16* final_norm = nullptr;   // [E][H]
+  size_t weight_bytes = 0;
+  std::vector<void*> allocs;
+
+  // grow-only activation arena (U15Backbone::ensure_scratch_)
+  int scratch_n = 0;
+  int scratch_tk = 0;
+  bf16* xn = nullptr;
+  bf16* qkv = nullptr;
+  bf16* qh = nullptr;
+  bf16* attn = nullptr;
+  bf16* h = nullptr;
+  float* rcos = nullptr;
+  float* rsin = nullptr;
+  int8_t* x8 = nullptr;
+  float* s_tok = nullptr;
+  void* sage_ws = nullptr;
+  size_t sage_ws_bytes = 0;
+  bf16* io = nullptr;   // layer_forward_host staging
+  std::vector<void*> scratch_allocs;
+
+  int qkv_n() const { return (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim; }
+  int qd() const { return cfg.heads * cfg.head_dim; }
+
+  template <class T>
+  int alloc(T** p, size_t bytes, std::vector<void*>& list)
+  {
+    const cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), bytes);
+    if (e != cudaSuccess) return fail(U15C_ENOMEM, "out of device memory (" +
+                                                       std::to_string(bytes >> 20) + " MB)");
+    list.push_back(*p);
+    return U15C_OK;
+  }
+
+  void free_scratch()
+  {
+    for (void* p : scratch_allocs) cudaFree(p);
+    scratch_allocs.clear();
+    scratch_n = 0;
+    scratch_tk = 0;
+    sage_ws = nullptr;
+    sage_ws_bytes = 0;
+  }
+
+  int ensure_scratch(int n, int tk)
+  {
+    if (n <= scratch_n && tk <= scratch_tk) return U15C_OK;
+    free_scratch();
+    n = std::max(n, 1);
+    tk = std::max(tk, n);
+    const size_t H = cfg.hidden, I = cfg.inter;
+    const size_t maxk = std::max({H, I, (size_t)qd()});
+    int rc = 0;
+    rc |= alloc(&xn, n * H * 2, scratch_allocs);
+    rc |= alloc(&qkv, (size_t)n * qkv_n() * 2, scratch_allocs);
+    rc |= alloc(&qh, (size_t)n * qd() * 2, scratch_allocs);
+    rc |= alloc(&attn, (size_t)n * qd() * 2, scratch_allocs);
+    rc |= alloc(&h, n * I * 2, scratch_allocs);
+    rc |= alloc(&rcos, (size_t)n * 128 * 4, scratch_allocs);
+    rc |= alloc(&rsin, (size_t)n * 128 * 4, scratch_allocs);
+    rc |= alloc(&x8, n * maxk, scratch_allocs);
+    rc |= alloc(&s_tok, (size_t)n * 4, scratch_allocs);
+    rc |= alloc(&io, n * H * 2, scratch_allocs);
+    sage_ws_bytes = u15::sage_bytes(cfg.heads, cfg.kv_heads, n, tk);
+    rc |= alloc(reinterpret_cast<uint8_t**>(&sage_ws), sage_ws_bytes, scratch_allocs);
+    if (rc) {
+      free_scratch();
+      return U15C_ENOMEM;
+    }
+    scratch_n = n;
+    scratch_tk = tk;
+    return U15C_OK;
+  }
+
+  ~u15c_model()
+  {
+    free_scratch();
+    for (void* p : allocs) cudaFree(p);
+  }
+};
+
+struct u15c_kv {
+  u15c_model* m = nullptr;
+  int capacity = 0;
+  int pages = 0;
+  long layer_elems = 0;   // elements of one layer's K (or V) pool
+  bf16* k = nullptr;      // [layers][pages][KV][64][128]
+  bf16* v = nullptr;
+  int32_t* table = nullptr;   // [pages]
+
+  u15::KvView view(int layer) const
+  {
+    u15::KvView kv;
+    kv.k = k + (long)layer * layer_elems;
+    kv.v = v + (long)layer * layer_elems;
+    kv.page_table = table;
+    kv.page_stride = (long)m->cfg.kv_heads * u15::kPageTokens * 128;
+    kv.head_stride = (long)u15::kPageTokens * 128;
+    return kv;
+  }
+  ~u15c_kv()
+  {
+    cudaFree(k);
+    cudaFree(v);
+    cudaFree(table);
+  }
+};
+
+namespace {
+
+int check_cfg(const u15c_config& c)
+{
+  if (c.n_layers <= 0 || c.hidden <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.inter <= 0 ||
+      c.n_experts <= 0 || c.n_experts > 8)
+    return fail(U15C_EINVAL, "model config: sizes must be positive (experts <= 8)");
+  if (c.head_dim != 128) return fail(U15C_EINVAL, "model config: head_dim must be 128");
+  if (c.heads % c.kv_heads) return fail(U15C_EINVAL, "model config: heads % kv_heads != 0");
+  if (c.hidden % 64 || c.inter % 128)
+    return fail(U15C_EINVAL, "model config: hidden % 64 and inter % 128 must be 0");
+  return U15C_OK;
+}
+
+// Sequence the layer's steps on `st`. rcos/rsin already hold the tables.
+int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15::SegInfo& seg,
+               const int* seg_off, const int* seg_expert, int nseg, u15c_kv* kv, int kv_off,
+               int kv_len, int attn, const int32_t* t_index, unsigned flags)
+{
+  const u15c_config& c = m->cfg;
+  const LayerW& L = m->layers[li];
+  const int E = c.n_experts, H = c.hidden, I = c.inter;
+  const bool i8 = (flags & U15C_FWD_INT8) != 0;
+  const bool sage = (flags & U15C_FWD_SAGE) != 0 && attn == U15C_ATTN_BIDIRECTIONAL;
+  if (i8 && L.qkv8 == nullptr)
+    return fail(U15C_EINVAL, "W8A8 requested but the model has no int8 twins "
+                             "(create with U15C_MODEL_INT8 and call u15c_model_finalize)");
+  int rc;
+  auto gemm = [&](const void* in, int K, const bf16* w, const int8_t* w8, const float* ws, int N,
+                  int epi, void* y) -> int {
+    u15::GemmArgs a;
+    a.n_experts = E;
+    a.M = n;
+    a.K = K;
+    a.N = N;
+    a.seg_off = seg_off;
+    a.seg_expert = seg_expert;
+    a.nseg = nseg;
+    a.epilogue = epi;
+    a.y = y;
+    a.resid = epi == u15::kEpiResid ? x : nullptr;
+    if (i8) {
+      if (u15::launch_quant_rows(in, m->x8, m->s_tok, n, K, st))
+        return fail(U15C_ECUDA, "quant_rows launch failed");
+      a.int8 = true;
+      a.x = m->x8;
+      a.w = w8;
+      a.s_tok = m->s_tok;
+      a.s_ch = ws;
+    } else {
+      a.x = in;
+      a.w = w;
+    }
+    return u15::run_gemm(a, st);
+  };
+
+  // ---- attention half (src/u15-backbone.cc:191-235) ----
+  if (u15::launch_rms_norm(x, L.ln_in, m->xn, n, H, (float)c.eps, seg, st))
+    return fail(U15C_ECUDA, "rms_norm launch failed");
+  if ((rc = gemm(m->xn, H, L.qkv, L.qkv8, L.qkv_s, m->qkv_n(), u15::kEpiStore, m->qkv)))
+    return rc;
+  const u15::KvView view = kv->view(li);
+  if (u15::launch_qkv_post(m->qkv, L.norms, m->rcos, m->rsin, m->qh, view, n, c.heads,
+                           c.kv_heads, kv_off, (float)c.eps, seg, st))
+    return fail(U15C_ECUDA, "qkv_post launch failed");
+  if ((rc = u15::run_attention(st, m->qh, view, m->attn, c.heads, c.kv_heads, n, kv_len, attn,
+                               kv_off, t_index, sage ? m->sage_ws : nullptr)))
+    return rc;
+  if ((rc = gemm(m->attn, m->qd(), L.o, L.o8, L.o_s, H, u15::kEpiResid, x))) return rc;
+
+  // ---- MLP half (src/u15-backbone.cc:246-256) ----
+  if (u15::launch_rms_norm(x, L.ln_post, m->xn, n, H, (float)c.eps, seg, st))
+    return fail(U15C_ECUDA, "rms_norm launch failed");
+  if ((rc = gemm(m->xn, H, L.gu, L.gu8, L.gu_s, 2 * I, u15::kEpiSwiglu, m->h))) return rc;
+  if ((rc = gemm(m->h, I, L.down, L.down8, L.down_s, H, u15::kEpiResid, x))) return rc;
+  return U15C_OK;
+}
+
+int validate_pass(u15c_model* m, int n, u15c_kv* kv, int kv_off, int kv_len, int attn,
+                  const int32_t* pos_t, const int32_t* pos_h, const int32_t* pos_w,
+                  const int32_t* t_index)
+{
+  if (m == nullptr || kv == nullptr) return fail(U15C_EINVAL, "no model or KV cache");
+  if (kv->m != m) return fail(U15C_EINVAL, "the KV cache belongs to another model");
+  if (n <= 0) return fail(U15C_EINVAL, "token count must be positive");
+  if (kv_off < 0 || kv_off + n > kv->capacity)
+    return fail(U15C_EINVAL, "KV cache too small: need " + std::to_string(kv_off + n) +
+                                 ", capacity " + std::to_string(kv->capacity));
+  if (kv_len < kv_off + n || kv_len > kv->capacity)
+    return fail(U15C_EINVAL, "kv_len is shorter than the tokens just written");
+  if (pos_t == nullptr || pos_h == nullptr || pos_w == nullptr)
+    return fail(U15C_EINVAL, "position arrays are required");
+  if (attn < 0 || attn > 2) return fail(U15C_EINVAL, "unknown attention rule");
+  if (attn == U15C_ATTN_BLOCK_CAUSAL && t_index == nullptr)
+    return fail(U15C_EINVAL, "Attn::BlockCausal needs the t-index vector");
+  return U15C_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int u15c_model_create(const u15c_config* cfg, unsigned flags, u15c_model** out)
+{
+  if (cfg == nullptr || out == nullptr) return fail(U15C_EINVAL, "null argument");
+  *out = nullptr;
+  int rc = check_cfg(*cfg);
+  if (rc) return rc;
+  if (u15::dev() == nullptr) return U15C_ECUDA;
+  auto* m = new u15c_model();
+  m->cfg = *cfg;
+  m->flags = flags;
+  cudaGetDevice(&m->device);
+  const size_t E = cfg->n_experts, H = cfg->hidden, I = cfg->inter;
+  const size_t QKV = (size_t)m->qkv_n(), QD = (size_t)m->qd();
+  m->layers.resize(cfg->n_layers);
+  for (auto& L : m->layers) {
+    rc |= m->alloc(&L.qkv, E * QKV * H * 2, m->allocs);
+    rc |= m->alloc(&L.o, E * H * QD * 2, m->allocs);
+    rc |= m->alloc(&L.gu, E * 2 * I * H * 2, m->allocs);
+    rc |= m->alloc(&L.down, E * H * I * 2, m->allocs);
+    rc |= m->alloc(&L.ln_in, E * H * 2, m->allocs);
+    rc |= m->alloc(&L.ln_post, E * H * 2, m->allocs);
+    rc |= m->alloc(&L.norms, E * 256 * 2, m->allocs);
+    m->weight_bytes += E * (QKV * H + H * QD + 2 * I * H + H * I + 2 * H + 256) * 2;
+    if (flags & U15C_MODEL_INT8) {
+      rc |= m->alloc(&L.qkv8, E * QKV * H, m->allocs);
+      rc |= m->alloc(&L.o8, E * H * QD, m->allocs);
+      rc |= m->alloc(&L.gu8, E * 2 * I * H, m->allocs);
+      rc |= m->alloc(&L.down8, E * H * I, m->allocs);
+      rc |= m->alloc(&L.qkv_s, E * QKV * 4, m->allocs);
+      rc |= m->alloc(&L.o_s, E * H * 4, m->allocs);
+      rc |= m->alloc(&L.gu_s, E * 2 * I * 4, m->allocs);
+      rc |= m->alloc(&L.down_s, E * H * 4, m->allocs);
+      m->weight_bytes += E * (QKV * H + H * QD + 2 * I * H + H * I) + E * (QKV + 2 * H + 2 * I) * 4;
+    }
+    if (rc) break;
+  }
+  if (!rc) rc |= m->alloc(&m->final_norm, E * H * 2, m->allocs);
+  if (rc) {
+    delete m;
+    return U15C_ENOMEM;
+  }
+  *out = m;
+  return U15C_OK;
+}
+
+void u15c_model_destroy(u15c_model* m) { delete m; }
+
+int u15c_model_bind(u15c_model* m, u15c_stream stream, int layer, int expert, int tensor,
+                    const void* src, int dtype, int src_on_host)
+{
+  if (m == nullptr || src == nullptr) return fail(U15C_EINVAL, "null argument");
+  const u15c_config& c = m->cfg;
+  if (expert < 0 || expert >= c.n_experts) return fail(U15C_EINVAL, "expert out of range");
+  if (tensor != U15C_T_FINAL_NORM && (layer < 0 || layer >= c.n_layers))
+    return fail(U15C_EINVAL, "layer out of range");
+  if (dtype < 0 || dtype > 2) return fail(U15C_EINVAL, "unknown source dtype");
+  const long H = c.hidden, I = c.inter, QD = m->qd(), KD = (long)c.kv_heads * c.head_dim;
+  const long E = c.n_experts;
+  LayerW* L = tensor == U15C_T_FINAL_NORM ? nullptr : &m->layers[layer];
+  bf16* dst = nullptr;
+  long rows = 0, cols = 0;
+  int inter = -1;
+  switch (tensor) {
+    case U15C_T_INPUT_LN: dst = L->ln_in + expert * H; rows = 1; cols = H; break;
+    case U15C_T_POST_LN: dst = L->ln_post + expert * H; rows = 1; cols = H; break;
+    case U15C_T_Q: dst = L->qkv + (long)expert * m->qkv_n() * H; rows = QD; cols = H; break;
+    case U15C_T_K: dst = L->qkv + ((long)expert * m->qkv_n() + QD) * H; rows = KD; cols = H; break;
+    case U15C_T_V:
+      dst = L->qkv + ((long)expert * m->qkv_n() + QD + KD) * H; rows = KD; cols = H; break;
+    case U15C_T_O: dst = L->o + (long)expert * H * QD; rows = H; cols = QD; break;
+    case U15C_T_Q_NORM: dst = L->norms + expert * 256 + 0; rows = 1; cols = 64; break;
+    case U15C_T_Q_NORM_HW: dst = L->norms + expert * 256 + 64; rows = 1; cols = 64; break;
+    case U15C_T_K_NORM: dst = L->norms + expert * 256 + 128; rows = 1; cols = 64; break;
+    case U15C_T_K_NORM_HW: dst = L->norms + expert * 256 + 192; rows = 1; cols = 64; break;
+    case U15C_T_GATE: dst = L->gu + (long)expert * 2 * I * H; rows = I; cols = H; inter = 0; break;
+    case U15C_T_UP: dst = L->gu + (long)expert * 2 * I * H; rows = I; cols = H; inter = 1; break;
+    case U15C_T_DOWN: dst = L->down + (long)expert * H * I; rows = H; cols = I; break;
+    case U15C_T_FINAL_NORM: dst = m->final_norm + expert * H; rows = 1; cols = H; break;
+    default: return fail(U15C_EINVAL, "unknown tensor id");
+  }
+  (void)E;
+  const size_t es = dtype == U15C_DT_F32 ? 4 : 2;
+  const size_t bytes = (size_t)rows * cols * es;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const void* dsrc = src;
+  void* staging = nullptr;
+  if (src_on_host) {
+    cudaError_t e = cudaMalloc(&staging, bytes);
+    if (e != cudaSuccess) return fail(U15C_ENOMEM, "bind: staging allocation failed");
+    e = cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      cudaFree(staging);
+      return cuda_fail(e, "bind: upload");
+    }
+    dsrc = staging;
+  }
+  bind_kernel<<<nblk(rows * cols, 256), 256, 0, st>>>(dsrc, dtype, rows, cols, dst, inter);
+  cudaError_t e = cudaGetLastError();
+  if (staging != nullptr) {
+    cudaStreamSynchronize(st);
+    cudaFree(staging);
+  }
+  return e == cudaSuccess ? U15C_OK : cuda_fail(e, "bind kernel");
+}
+
+int u15c_model_bind_random(u15c_model* m, u15c_stream stream, uint64_t seed, float std,
+                           float norm_mean, float norm_std)
+{
+  if (m == nullptr) return fail(U15C_EINVAL, "null model");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const u15c_config& c = m->cfg;
+  const long E = c.n_experts, H = c.hidden, I = c.inter, QD = m->qd(), QKV = m->qkv_n();
+  uint64_t sid = 0;
+  auto fill = [&](bf16* p, long n, float mean, float sd) {
+    randn_kernel<<<nblk(n, 256), 256, 0, st>>>(p, n, seed, ++sid, mean, sd);
+  };
+  for (auto& L : m->layers) {
+    fill(L.qkv, E * QKV * H, 0.0f, std);
+    fill(L.o, E * H * QD, 0.0f, std);
+    fill(L.gu, E * 2 * I * H, 0.0f, std);
+    fill(L.down, E * H * I, 0.0f, std);
+    fill(L.ln_in, E * H, norm_mean, norm_std);
+    fill(L.ln_post, E * H, norm_mean, norm_std);
+    fill(L.norms, E * 256, norm_mean, norm_std);
+  }
+  fill(m->final_norm, E * H, norm_mean, norm_std);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? U15C_OK : cuda_fail(e, "random init");
+}
+
+int u15c_model_finalize(u15c_model* m, u15c_stream stream)
+{
+  if (m == nullptr) return fail(U15C_EINVAL, "null model");
+  if (!(m->flags & U15C_MODEL_INT8)) return U15C_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const u15c_config& c = m->cfg;
+  const int E = c.n_experts, H = c.hidden, I = c.inter, QD = m->qd(), QKV = m->qkv_n();
+  for (auto& L : m->layers) {
+    int rc = 0;
+    rc |= u15::launch_quant_rows(L.qkv, L.qkv8, L.qkv_s, E * QKV, H, st);
+    rc |= u15::launch_quant_rows(L.o, L.o8, L.o_s, E * H, QD, st);
+    rc |= u15::launch_quant_rows(L.gu, L.gu8, L.gu_s, E * 2 * I, H, st);
+    rc |= u15::launch_quant_rows(L.down, L.down8, L.down_s, E * H, I, st);
+    if (rc) return fail(U15C_ECUDA, "finalize: quantisation launch failed");
+  }
+  return U15C_OK;
+}
+
+size_t u15c_model_weight_bytes(const u15c_model* m) { return m ? m->weight_bytes : 0; }
+
+size_t u15c_model_scratch_bytes(const u15c_model* m, int n)
+{
+  if (m == nullptr || n <= 0) return 0;
+  const size_t H = m->cfg.hidden, I = m->cfg.inter, QD = m->qd(), QKV = m->qkv_n();
+  const size_t maxk = std::max({H, I, QD});
+  return (size_t)n * (2 * (H + QKV + 2 * QD + I + H) + 8 * 128 + maxk + 4);
+}
+
+size_t u15c_model_kv_bytes(const u15c_model* m, int capacity)
+{
+  if (m == nullptr || capacity <= 0) return 0;
+  const size_t pages = (size_t)(capacity + u15::kPageTokens - 1) / u15::kPageTokens;
+  return pages * u15::kPageTokens * (size_t)m->cfg.kv_heads * 128 * 2 * 2 *
+         (size_t)m->cfg.n_layers;
+}
+
+int u15c_kv_create(u15c_model* m, int capacity, u15c_kv** out)
+{
+  if (m == nullptr || out == nullptr) return fail(U15C_EINVAL, "null argument");
+  *out = nullptr;
+  if (capacity <= 0) return fail(U15C_EINVAL, "capacity must be positive");
+  auto* kv = new u15c_kv();
+  kv->m = m;
+  kv->capacity = capacity;
+  kv->pages = (capacity + u15::kPageTokens - 1) / u15::kPageTokens;
+  kv->layer_elems = (long)kv->pages * m->cfg.kv_heads * u15::kPageTokens * 128;
+  const size_t bytes = (size_t)kv->layer_elems * m->cfg.n_layers * 2;
+  if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess ||
+      cudaMalloc(&kv->table, (size_t)kv->pages * 4) != cudaSuccess) {
+    delete kv;
+    return fail(U15C_ENOMEM, "out of memory allocating the KV cache (" +
+                                 std::to_string(2 * bytes >> 20) + " MB)");
+  }
+  cudaMemset(kv->k, 0, bytes);
+  cudaMemset(kv->v, 0, bytes);
+  std::vector<int32_t> ident(kv->pages);
+  for (int i = 0; i < kv->pages; ++i) ident[i] = i;
+  cudaMemcpy(kv->table, ident.data(), ident.size() * 4, cudaMemcpyHostToDevice);
+  *out = kv;
+  return U15C_OK;
+}
+
+void u15c_kv_destroy(u15c_kv* kv) { delete kv; }
+
+int u15c_kv_capacity(const u15c_kv* kv) { return kv ? kv->capacity : 0; }
+
+int u15c_kv_set_page_table(u15c_kv* kv, const int32_t* pages_host, int n)
+{
+  if (kv == nullptr || pages_host == nullptr || n != kv->pages)
+    return fail(U15C_EINVAL, "page table must have exactly one entry per page");
+  std::vector<char> seen(n, 0);
+  for (int i = 0; i < n; ++i) {
+    if (pages_host[i] < 0 || pages_host[i] >= n || seen[pages_host[i]])
+      return fail(U15C_EINVAL, "page table must be a permutation of the cache's pages");
+    seen[pages_host[i]] = 1;
+  }
+  const cudaError_t e = cudaMemcpy(kv->table, pages_host, (size_t)n * 4, cudaMemcpyHostToDevice);
+  return e == cudaSuccess ? U15C_OK : cuda_fail(e, "set_page_table");
+}
+
+int u15c_kv_read(u15c_kv* kv, u15c_stream stream, int layer, int which_v, void* out, int n)
+{
+  if (kv == nullptr || out == nullptr || n <= 0 || n > kv->capacity || layer < 0 ||
+      layer >= kv->m->cfg.n_layers)
+    return fail(U15C_EINVAL, "kv_read: bad argument");
+  std::vector<int32_t> table(kv->pages);
+  cudaError_t e = cudaMemcpy(table.data(), kv->table, table.size() * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "kv_read");
+  const u15::KvView v = kv->view(layer);
+  const bf16* base = static_cast<const bf16*>(which_v ? v.v : v.k);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int h = 0; h < kv->m->cfg.kv_heads; ++h) {
+    for (int p0 = 0; p0 < n; p0 += u15::kPageTokens) {
+      const int cnt = std::min(u15::kPageTokens, n - p0);
+      const bf16* src = base + (long)table[p0 / u15::kPageTokens] * v.page_stride +
+                        (long)h * v.head_stride;
+      e = cudaMemcpyAsync(static_cast<bf16*>(out) + ((long)h * n + p0) * 128, src,
+                          (size_t)cnt * 256, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_fail(e, "kv_read copy");
+    }
+  }
+  return U15C_OK;
+}
+
+int u15c_kv_write(u15c_kv* kv, u15c_stream stream, int layer, int which_v, const void* in, int n)
+{
+  if (kv == nullptr || in == nullptr || n <= 0 || n > kv->capacity || layer < 0 ||
+      layer >= kv->m->cfg.n_layers)
+    return fail(U15C_EINVAL, "kv_write: bad argument");
+  std::vector<int32_t> table(kv->pages);
+  cudaError_t e = cudaMemcpy(table.data(), kv->table, table.size() * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "kv_write");
+  const u15::KvView v = kv->view(layer);
+  bf16* base = static_cast<bf16*>(which_v ? v.v : v.k);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int h = 0; h < kv->m->cfg.kv_heads; ++h) {
+    for (int p0 = 0; p0 < n; p0 += u15::kPageTokens) {
+      const int cnt = std::min(u15::kPageTokens, n - p0);
+      bf16* dst = base + (long)table[p0 / u15::kPageTokens] * v.page_stride +
+                  (long)h * v.head_stride;
+      e = cudaMemcpyAsync(dst, static_cast<const bf16*>(in) + ((long)h * n + p0) * 128,
+                          (size_t)cnt * 256, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_fail(e, "kv_write copy");
+    }
+  }
+  return U15C_OK;
+}
+
+int u15c_layer_forward(u15c_model* m, u15c_stream stream, int layer, void* x, int n,
+                       const int* seg_off, const int* seg_expert, int nseg, u15c_kv* kv,
+                       int kv_off, int kv_len, const int32_t* pos_t, const int32_t* pos_h,
+                       const int32_t* pos_w, int attn, const int32_t* t_index, unsigned flags)
+{
+  int rc = validate_pass(m, n, kv, kv_off, kv_len, attn, pos_t, pos_h, pos_w, t_index);
+  if (rc) return rc;
+  if (layer < 0 || layer >= m->cfg.n_layers) return fail(U15C_EINVAL, "layer out of range");
+  if (x == nullptr) return fail(U15C_EINVAL, "null activations");
+  u15::SegInfo seg;
+  std::string err;
+  if (!u15::fill_seg(&seg, seg_off, seg_expert, nseg, n, m->cfg.n_experts, &err))
+    return fail(U15C_EINVAL, err);
+  if ((rc = m->ensure_scratch(n, kv_len))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (u15::launch_rope_tables(pos_t, pos_h, pos_w, n, 64, 32, m->cfg.theta_t, m->cfg.theta_hw,
+                              m->rcos, m->rsin, st))
+    return fail(U15C_ECUDA, "rope tables launch failed");
+  return layer_impl(m, st, layer, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, kv,
+                    kv_off, kv_len, attn, t_index, flags);
+}
+
+int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* seg_off,
+                 const int* seg_expert, int nseg, u15c_kv* kv, int kv_off, int kv_len,
+                 const int32_t* pos_t, const int32_t* pos_h, const int32_t* pos_w, int attn,
+                 const int32_t* t_index, unsigned flags, int (*stop)(void*), void* stop_ctx)
+{
+  int rc = validate_pass(m, n, kv, kv_off, kv_len, attn, pos_t, pos_h, pos_w, t_index);
+  if (rc) return rc;
+  if (x == nullptr) return fail(U15C_EINVAL, "null activations");
+  u15::SegInfo seg;
+  std::string err;
+  if (!u15::fill_seg(&seg, seg_off, seg_expert, nseg, n, m->cfg.n_experts, &err))
+    return fail(U15C_EINVAL, err);
+  if ((rc = m->ensure_scratch(n, kv_len))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The rope tables depend on the positions only: built once per pass
+  // (src/u15-backbone.cc:340-367), not per layer.
+  if (u15::launch_rope_tables(pos_t, pos_h, pos_w, n, 64, 32, m->cfg.theta_t, m->cfg.theta_hw,
+                              m->rcos, m->rsin, st))
+    return fail(U15C_ECUDA, "rope tables launch failed");
+  for (int li = 0; li < m->cfg.n_layers; ++li) {
+    if (stop != nullptr && stop(stop_ctx) != 0) return fail(U15C_ESTOPPED, "stopped");
+    if ((rc = layer_impl(m, st, li, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, kv,
+                         kv_off, kv_len, attn, t_index, flags)))
+      return rc;
+  }
+  return U15C_OK;
+}
+
+int u15c_final_norm(u15c_model* m, u15c_stream stream, void* x, int n, int expert)
+{
+  if (m == nullptr || x == nullptr || expert < 0 || expert >= m->cfg.n_experts)
+    return fail(U15C_EINVAL, "final_norm: bad argument");
+  u15::SegInfo seg;
+  seg.nseg = 1;
+  seg.off[0] = 0;
+  seg.off[1] = n;
+  seg.expert[0] = 0;
+  const bf16* w = m->final_norm + (long)expert * m->cfg.hidden;
+  if (u15::launch_rms_norm(x, w, x, n, m->cfg.hidden, (float)m->cfg.eps, seg,
+                           static_cast<cudaStream_t>(stream)))
+    return fail(U15C_ECUDA, "final_norm launch failed");
+  return U15C_OK;
+}
+
+int u15c_layer_forward_host(u15c_model* m, u15c_stream stream, int layer, const void* x_host,
+                            void* out_host, int n, const int* seg_off, const int* seg_expert,
+                            int nseg, u15c_kv* kv, int kv_off, int kv_len, const int32_t* pos_t,
+                            const int32_t* pos_h, const int32_t* pos_w, int attn,
+                            const int32_t* t_index, unsigned flags)
+{
+  if (m == nullptr || x_host == nullptr || out_host == nullptr)
+    return fail(U15C_EINVAL, "layer_forward_host: null argument");
+  int rc = m->ensure_scratch(n, kv_len);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t bytes = (size_t)n * m->cfg.hidden * 2;
+  cudaError_t e = cudaMemcpyAsync(m->io, x_host, bytes, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host: upload");
+  rc = u15c_layer_forward(m, stream, layer, m->io, n, seg_off, seg_expert, nseg, kv, kv_off,
+                          kv_len, pos_t, pos_h, pos_w, attn, t_index, flags);
+  if (rc) return rc;
+  e = cudaMemcpyAsync(out_host, m->io, bytes, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host: download");
+  return u15c_sync(stream);
+}
+
+}  // extern "C"

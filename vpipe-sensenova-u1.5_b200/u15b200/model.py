@@ -1,0 +1,152 @@
+"""Model, KV cache and backbone handles over libu15c's C ABI: the Python
+face of U15Weights (bind), KvCache and U15Backbone (src/u15-weights.h,
+src/u15-backbone.h of the reference)."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from ._lib import check, lib
+from .ops import _p, _stream, segments_arrays
+
+FULL = dict(n_layers=42, hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=12288,
+            n_experts=2, eps=1e-6, theta_t=5e6, theta_hw=1e4)
+
+
+class Model:
+    """U15Weights + U15Backbone for one device."""
+
+    def __init__(self, int8: bool = False, **cfg):
+        c = dict(FULL)
+        c.update(cfg)
+        self.cfg = c
+        self._cfg = L.Config(**c)
+        h = C.c_void_p()
+        check(lib().u15c_model_create(C.byref(self._cfg), L.MODEL_INT8 if int8 else 0,
+                                      C.byref(h)))
+        self.h = h
+        self.int8 = int8
+
+    def close(self):
+        if self.h:
+            lib().u15c_model_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- bind (U15Weights::load) --------------------------------------
+    def bind(self, layer: int, expert: int, name: str, array) -> None:
+        """Bind one tensor from a host numpy array (f32/f16) or a CUDA tensor
+        (f32/f16/bf16)."""
+        tid = L.TENSORS.index(name)
+        if isinstance(array, np.ndarray):
+            a = np.ascontiguousarray(array)
+            dt = {np.dtype(np.float32): L.DT_F32, np.dtype(np.float16): L.DT_F16}[a.dtype]
+            check(lib().u15c_model_bind(self.h, _stream(), layer, expert, tid,
+                                        C.c_void_p(a.ctypes.data), dt, 1))
+            torch.cuda.current_stream().synchronize()
+        else:
+            a = array.contiguous()
+            dt = {torch.float32: L.DT_F32, torch.float16: L.DT_F16,
+                  torch.bfloat16: L.DT_BF16}[a.dtype]
+            check(lib().u15c_model_bind(self.h, _stream(), layer, expert, tid, _p(a), dt, 0))
+
+    def bind_expert_layer(self, layer: int, expert: int, weights: dict) -> None:
+        for k, v in weights.items():
+            self.bind(layer, expert, k, v)
+
+    def bind_random(self, seed: int, std: float = 0.02, norm_mean: float = 1.0,
+                    norm_std: float = 0.0) -> None:
+        check(lib().u15c_model_bind_random(self.h, _stream(), seed, std, norm_mean, norm_std))
+
+    def finalize(self) -> None:
+        check(lib().u15c_model_finalize(self.h, _stream()))
+
+    def weight_bytes(self) -> int:
+        return lib().u15c_model_weight_bytes(self.h)
+
+    def scratch_bytes(self, n: int) -> int:
+        return lib().u15c_model_scratch_bytes(self.h, n)
+
+    def kv_bytes(self, capacity: int) -> int:
+        return lib().u15c_model_kv_bytes(self.h, capacity)
+
+    def make_cache(self, capacity: int) -> "KvCache":
+        return KvCache(self, capacity)
+
+    # ---- backbone -----------------------------------------------------
+    def layer_forward(self, layer, x, kv, kv_off, kv_len, pos_t, pos_h, pos_w, segments=None,
+                      attn=L.ATTN_BIDIRECTIONAL, t_index=None, int8=False, sage=False):
+        n = x.shape[0]
+        off, ex, ns = segments_arrays(segments, n)
+        flags = (L.FWD_INT8 if int8 else 0) | (L.FWD_SAGE if sage else 0)
+        check(lib().u15c_layer_forward(self.h, _stream(), layer, _p(x), n, off, ex, ns, kv.h,
+                                       kv_off, kv_len, _p(pos_t), _p(pos_h), _p(pos_w), attn,
+                                       _p(t_index), flags))
+
+    def forward(self, x, kv, kv_off, kv_len, pos_t, pos_h, pos_w, segments=None,
+                attn=L.ATTN_BIDIRECTIONAL, t_index=None, int8=False, sage=False, stop=None):
+        n = x.shape[0]
+        off, ex, ns = segments_arrays(segments, n)
+        flags = (L.FWD_INT8 if int8 else 0) | (L.FWD_SAGE if sage else 0)
+        cb = L.STOP_FN(lambda _ctx: int(bool(stop()))) if stop is not None else L.STOP_FN()
+        check(lib().u15c_forward(self.h, _stream(), _p(x), n, off, ex, ns, kv.h, kv_off, kv_len,
+                                 _p(pos_t), _p(pos_h), _p(pos_w), attn, _p(t_index), flags, cb,
+                                 None))
+
+    def final_norm(self, x, expert):
+        check(lib().u15c_final_norm(self.h, _stream(), _p(x), x.shape[0], expert))
+
+    def layer_forward_host(self, layer, x_host, out_host, kv, kv_off, kv_len, pos_t, pos_h,
+                           pos_w, segments=None, attn=L.ATTN_BIDIRECTIONAL, t_index=None,
+                           int8=False, sage=False):
+        n = x_host.shape[0]
+        off, ex, ns = segments_arrays(segments, n)
+        flags = (L.FWD_INT8 if int8 else 0) | (L.FWD_SAGE if sage else 0)
+        check(lib().u15c_layer_forward_host(self.h, _stream(), layer, _p(x_host), _p(out_host),
+                                            n, off, ex, ns, kv.h, kv_off, kv_len, _p(pos_t),
+                                            _p(pos_h), _p(pos_w), attn, _p(t_index), flags))
+
+
+class KvCache:
+    """Paged bf16 KV cache for every layer of one branch."""
+
+    def __init__(self, model: Model, capacity: int):
+        self.model = model
+        h = C.c_void_p()
+        check(lib().u15c_kv_create(model.h, capacity, C.byref(h)))
+        self.h = h
+        self.capacity = capacity
+        self.pages = (capacity + 63) // 64
+
+    def close(self):
+        if self.h:
+            lib().u15c_kv_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_page_table(self, pages):
+        arr = (C.c_int * len(pages))(*[int(p) for p in pages])
+        check(lib().u15c_kv_set_page_table(self.h, arr, len(pages)))
+
+    def read(self, layer: int, v: bool, n: int) -> torch.Tensor:
+        hkv = self.model.cfg["kv_heads"]
+        out = torch.empty(hkv, n, 128, dtype=torch.bfloat16, device="cuda")
+        check(lib().u15c_kv_read(self.h, _stream(), layer, int(v), _p(out), n))
+        return out
+
+    def write(self, layer: int, v: bool, data: torch.Tensor) -> None:
+        d = data.contiguous()
+        check(lib().u15c_kv_write(self.h, _stream(), layer, int(v), _p(d), d.shape[1]))
