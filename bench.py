@@ -100,10 +100,12 @@ class Clocks:
                 self.p.kill()
 
     def summary(self):
+        """Median SM clock over samples under load (power above 40% of the
+        peak seen), the max clock, and every throttle reason seen active."""
         if not getattr(self, "out", ""):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         rows = list(csv.reader(io.StringIO(self.out)))[1:]
-        sm, mx, reasons = [], None, set()
+        sm, pw, mx, reasons = [], [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             if len(r) < 9:
@@ -111,13 +113,16 @@ class Clocks:
             try:
                 sm.append(float(r[1].split()[0]))
                 mx = float(r[2].split()[0])
-            except ValueError:
+                pw.append(float(r[3].split()[0]))
+            except (ValueError, IndexError):
                 continue
             for n, v in zip(names, r[5:9]):
                 if "Active" in v and "Not" not in v:
                     reasons.add(n)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        load = [c for c, p in zip(sm, pw) if p > 0.4 * max(pw)] if pw else sm
+        return {"sm_mhz": float(np.median(load)) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(load),
+                "window": "whole bench (model set-up, warm-up, every timed loop)"}
 
 
 def ev_time(fn, n, stream=None):
@@ -239,6 +244,7 @@ def run_ours(args, rank, world, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+    clk = Clocks(local).__enter__()
     n_layers = args.layers
     m = u15b200.Model(int8=True, n_layers=n_layers)
     m.bind_random(seed=1234 + rank, std=0.02, norm_mean=1.0, norm_std=0.2)
@@ -284,8 +290,7 @@ def run_ours(args, rank, world, local):
             dist.barrier()
         return ms
 
-    with Clocks(local) as clk:
-        total_ms = timed(step, args.steps)
+    total_ms = timed(step, args.steps)
     ops.sync()
     ms_step = total_ms / args.steps
     value = ms_step / world
@@ -346,6 +351,8 @@ def run_ours(args, rank, world, local):
         kern["attention_sage"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
         torch.cuda.empty_cache()
 
+    clk.__exit__(None, None, None)
+
     # ---- CPU baseline (rank 0, N=1 only): bounded sample, ~10-30 s ----
     cpu_line = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -397,8 +404,8 @@ def run_ours(args, rank, world, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
