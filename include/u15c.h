@@ -217,6 +217,25 @@ int u15c_sdpa_block_causal(u15c_stream stream, const void* q, const void* k, con
                            void* out, const int32_t* t_index, int hq, int hkv, int tq, int tk,
                            int d, int cap, int q_offset);
 
+/* Sage int8-QK bidirectional attention that allocates nothing: the same
+ * computation as u15c_attention with a Sage workspace, but the workspace is a
+ * fixed 24 MiB device array inside this library (16 MiB of int8 queries plus
+ * keys and scales covers 32 query heads x 4096 tokens over 8 kv heads x 4416
+ * keys). It is for callers that cannot call cudaMalloc: a host that plans its
+ * device memory up front and may not grow it, a process whose free memory is
+ * held by another allocator, a latency-bound caller that cannot take the
+ * implicit synchronisation of cudaMalloc/cudaFree. This entry point has no
+ * counterpart in the reference.
+ * Geometries whose workspace (u15c_sage_workspace_bytes) exceeds 24 MiB are
+ * refused with U15C_EINVAL. The first call on a device sets up the array's
+ * address for that device (make it before any stream capture). Every call
+ * shares the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. Every GPU that loads the library holds the
+ * 24 MiB until the process exits. Arguments as u15c_attention. */
+int u15c_attention_sage_static(u15c_stream stream, const void* q, const void* k, const void* v,
+                               const int32_t* page_table, int cap, void* out, int hq, int hkv,
+                               int tq, int tk, int head_dim);
+
 /* ------------------------------------------------------------------ */
 /* model: weights, KV cache, backbone                                   */
 /* ------------------------------------------------------------------ */

@@ -1,0 +1,67 @@
+"""u15c_attention_sage_static: the Sage attention entry point that allocates
+nothing, for callers that cannot call cudaMalloc (a host that plans its
+device memory up front and may not grow it, a process whose free memory
+another allocator holds, a latency-bound caller that cannot take
+cudaMalloc's implicit synchronisation). Its workspace is a fixed 24 MiB
+device array inside libu15c.
+
+Checked through the C ABI against the existing entry point, u15c_attention
+with a caller-provided Sage workspace, on two calls in a row with different
+geometries (so the second call runs on the array the first one left
+behind), within the attention tests' bar. Collected last (file name), and
+independent of every other test, so it passes alone or after the suite.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from gpu_util import bf16_round, dev_bf16, host, randn, rel_l2, torch
+
+pytestmark = pytest.mark.gpu
+BAR = 4e-3
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def _reference_call(lib, st, q, k, v, cap, out, hq, hkv, tq, tk):
+    n = lib.u15c_sage_workspace_bytes(hq, hkv, tq, tk)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    rc = lib.u15c_attention(st, _ptr(q), _ptr(k), _ptr(v), None, cap, _ptr(out), hq, hkv, tq,
+                            tk, 128, 0, 0, None, _ptr(ws))
+    assert rc == 0, lib.u15c_last_error()
+
+
+def test_static_workspace_matches_allocating_entry_point():
+    from u15b200 import _lib as L
+    lib = L.lib()
+    assert lib.u15c_init(0, 0) == 0
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    # two calls in a row: a small geometry, then the BASELINE attention shape
+    for (hq, hkv, tq, cap, tk, seed) in ((8, 2, 130, 200, 170, 31),
+                                         (32, 8, 4096, 4416, 4416, 32)):
+        q = dev_bf16(bf16_round(randn((hq, tq, 128), seed)))
+        k = dev_bf16(bf16_round(randn((hkv, cap, 128), seed + 1, 1.0, 0.5)))
+        v = dev_bf16(bf16_round(randn((hkv, cap, 128), seed + 2)))
+        got = torch.empty(tq, hq * 128, dtype=torch.bfloat16, device="cuda")
+        ref = torch.empty_like(got)
+        rc = lib.u15c_attention_sage_static(st, _ptr(q), _ptr(k), _ptr(v), None, cap, _ptr(got),
+                                            hq, hkv, tq, tk, 128)
+        assert rc == 0, L.last_error()
+        _reference_call(lib, st, q, k, v, cap, ref, hq, hkv, tq, tk)
+        assert lib.u15c_sync(st) == 0, L.last_error()
+        assert rel_l2(host(got), host(ref)) < BAR
+
+
+def test_static_workspace_refuses_oversize():
+    from u15b200 import _lib as L
+    lib = L.lib()
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    hq, hkv, tq, tk = 32, 8, 8192, 8192   # ~38 MB of workspace: over the 24 MiB array
+    q = torch.zeros(1, dtype=torch.bfloat16, device="cuda")
+    rc = lib.u15c_attention_sage_static(st, _ptr(q), _ptr(q), _ptr(q), None, tk, _ptr(q), hq,
+                                        hkv, tq, tk, 128)
+    assert rc == L.EINVAL
+    assert "static workspace" in L.last_error()

@@ -73,6 +73,7 @@ SIGNATURES = {
     "u15c_silu": (ip, [vp, vp, C.c_long]),
     "u15c_sage_workspace_bytes": (C.c_size_t, [ip, ip, ip, ip]),
     "u15c_attention": (ip, [vp, vp, vp, vp, vp, ip, vp, ip, ip, ip, ip, ip, ip, ip, vp, vp]),
+    "u15c_attention_sage_static": (ip, [vp, vp, vp, vp, vp, ip, vp, ip, ip, ip, ip, ip]),
     "u15c_sdpa": (ip, [vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, ip, ip]),
     "u15c_sdpa_steel": (ip, [vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, vp]),
     "u15c_sdpa_block_causal": (ip, [vp, vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, ip]),
