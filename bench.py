@@ -337,18 +337,30 @@ def run_ours(args, rank, world, local):
             kern[name] = {"ms": t, "tflops": 2.0 * M_TOK * K * N / t / 1e9}
             del w, y, xin
         q = torch.randn(NH, M_TOK, HD, device="cuda").bfloat16()
+        npg = (TK + 63) // 64
+        kp = torch.randn(npg, KV, 64, HD, device="cuda").bfloat16()
+        vp = torch.randn(npg, KV, HD, 64, device="cuda").bfloat16()
+        table = torch.arange(npg, dtype=torch.int32, device="cuda")
+        o = torch.empty(M_TOK, NH * HD, device="cuda").bfloat16()
+        fn = lambda: ops.attention_paged(q, kp, vp, o, NH, KV, M_TOK, TK,  # noqa: E731
+                                         page_table=table)
+        fn()
+        t = ev_time(fn, max(5, args.steps))
+        kern["attention"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9,
+                             "kernel": "attn_tc_kernel (tcgen05, paged KV)"}
+        ws = ops.sage_workspace(NH, KV, M_TOK, TK)
+        fn = lambda: ops.attention_paged(q, kp, vp, o, NH, KV, M_TOK, TK,  # noqa: E731
+                                         page_table=table, sage_ws=ws)
+        fn()
+        t = ev_time(fn, max(5, args.steps))
+        kern["attention_sage"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9,
+                                  "kernel": "Sage prologue + attn_tc_kernel<int8 QK>"}
         kc = torch.randn(KV, TK, HD, device="cuda").bfloat16()
         vc = torch.randn(KV, TK, HD, device="cuda").bfloat16()
-        o = torch.empty(M_TOK, NH * HD, device="cuda").bfloat16()
         fn = lambda: ops.attention(q, kc, vc, o, NH, KV, M_TOK, TK, cap=TK)  # noqa: E731
         fn()
         t = ev_time(fn, max(5, args.steps))
-        kern["attention"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
-        ws = ops.sage_workspace(NH, KV, M_TOK, TK)
-        fn = lambda: ops.attention(q, kc, vc, o, NH, KV, M_TOK, TK, cap=TK, sage_ws=ws)  # noqa
-        fn()
-        t = ev_time(fn, max(5, args.steps))
-        kern["attention_sage"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
+        kern["attention_mma_sync_reference_layout"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
         torch.cuda.empty_cache()
 
     clk.__exit__(None, None, None)

@@ -203,6 +203,18 @@ int u15c_attention(u15c_stream stream, const void* q, const void* k, const void*
                    int tk, int head_dim, int mode, int q_offset, const int32_t* t_index,
                    void* sage_ws);
 
+/* The same over the model's paged cache layout: K pages
+ * [n_pages][hkv][64][128], V pages TRANSPOSED [n_pages][hkv][128][64] (dims as
+ * rows of 64 tokens, the operand layout of the tensor-core P.V), page table
+ * device int32 (NULL = identity). mode U15C_ATTN_BIDIRECTIONAL runs the
+ * tcgen05/TMEM flash kernel (Sage int8-QK when sage_ws is non-NULL); the
+ * causal rules run the masked kernel. Replaces MetalOps::sdpa_steel for the
+ * denoise pass (src/u15-metal-ops.cc:835-882). */
+int u15c_attention_paged(u15c_stream stream, const void* q, const void* k_pages,
+                         const void* vt_pages, const int32_t* page_table, int n_pages, void* out,
+                         int hq, int hkv, int tq, int tk, int head_dim, int mode, int q_offset,
+                         const int32_t* t_index, void* sage_ws);
+
 /* The reference's three attention entry points with their own argument
  * order, over the contiguous cache (kv stride = cap tokens):
  * MetalOps::sdpa (src/u15-metal-ops.h:214-232): full or causal. */
@@ -304,13 +316,19 @@ size_t u15c_model_scratch_bytes(const u15c_model* m, int n);
 size_t u15c_model_kv_bytes(const u15c_model* m, int capacity);
 
 /* U15Backbone::make_cache (src/u15-backbone.cc:63-90): a paged bf16 cache of
- * `capacity` tokens for every layer. */
+ * `capacity` tokens for every layer: per layer K pages [pages][kv_heads][64][128]
+ * and V pages stored transposed [pages][kv_heads][128][64], zero-initialised. */
 int u15c_kv_create(u15c_model* m, int capacity, u15c_kv** out);
 void u15c_kv_destroy(u15c_kv* kv);
 int u15c_kv_capacity(const u15c_kv* kv);
 /* Replace the logical->physical page map (host int32[n], a permutation of
  * the cache's pages); the paged layout is then exercised non-contiguously. */
 int u15c_kv_set_page_table(u15c_kv* kv, const int32_t* pages_host, int n);
+/* The device pools of one layer (K pages, transposed V pages), the page
+ * table and the number of pages, for u15c_attention_paged. Any out
+ * pointer may be NULL. */
+int u15c_kv_pages(u15c_kv* kv, int layer, void** k_pages, void** vt_pages,
+                  const int32_t** page_table, int* n_pages);
 /* Read one layer's K or V for tokens [0, n) into a contiguous
  * [kv_heads][n][128] buffer (tests, diagnostics). */
 int u15c_kv_read(u15c_kv* kv, u15c_stream stream, int layer, int which_v, void* out, int n);

@@ -134,3 +134,82 @@ def test_sage_refuses_masked(ops):
     q, k, v = qkv(4, 1, 16, 64, 14)
     with pytest.raises(u15b200.U15Error):
         run(ops, q, k, v, 64, mode=1, sage=True)
+
+
+# ---------------------------------------------------------------------------
+# the tcgen05 kernel over the model's paged layout (V pages transposed)
+# ---------------------------------------------------------------------------
+def to_model_pages(k, v, table):
+    """[hkv][cap][128] K and V -> K pool [P][hkv][64][128] and transposed V pool
+    [P][hkv][128][64] under a logical->physical page table."""
+    hkv, cap, _ = k.shape
+    n = len(table)
+    kp = np.zeros((n, hkv, 64, 128), np.float32)
+    vp = np.zeros((n, hkv, 128, 64), np.float32)
+    for lp in range(n):
+        ks = k[:, lp * 64:(lp + 1) * 64]
+        vs = v[:, lp * 64:(lp + 1) * 64]
+        kp[table[lp], :, :ks.shape[1]] = ks
+        vp[table[lp], :, :, :vs.shape[1]] = vs.transpose(0, 2, 1)
+    return kp, vp
+
+
+def run_paged(ops, q, k, v, tk, table=None, mode=0, q_offset=0, t_index=None, sage=False):
+    hq, tq, _ = q.shape
+    hkv, cap, _ = k.shape
+    n = (cap + 63) // 64
+    table = np.arange(n, dtype=np.int32) if table is None else np.asarray(table, np.int32)
+    kp, vp = to_model_pages(k, v, table)
+    out = torch.empty(tq, hq * 128, dtype=torch.bfloat16, device="cuda")
+    ws = ops.sage_workspace(hq, hkv, tq, tk) if sage else None
+    ops.attention_paged(dev_bf16(q), dev_bf16(kp), dev_bf16(vp), out, hq, hkv, tq, tk,
+                        page_table=dev_i32(table), mode=mode, q_offset=q_offset,
+                        t_index=dev_i32(t_index) if t_index is not None else None, sage_ws=ws)
+    ops.sync()
+    return host(out)
+
+
+@pytest.mark.parametrize("hq,hkv,tq,cap,tk", [(8, 2, 48, 88, 67), (4, 1, 300, 320, 320),
+                                              (32, 8, 257, 200, 130), (8, 8, 512, 640, 577)])
+def test_tc_bidirectional(ops, hq, hkv, tq, cap, tk):
+    q, k, v = qkv(hq, hkv, tq, cap, 21)
+    got = run_paged(ops, q, k, v, tk)
+    assert rel_l2(got, O.attention(q, k, v, tk=tk)) < BAR
+
+
+def test_tc_permuted_pages_and_gqa_control(ops):
+    q, k, v = qkv(32, 8, 260, 320, 22)
+    got = run_paged(ops, q, k, v, 300, table=[4, 2, 0, 3, 1])
+    ref = O.attention(q, k, v, tk=300)
+    assert rel_l2(got, ref) < BAR
+    wrong = O.attention(q, np.repeat(k, 4, axis=0)[np.arange(32) % 8 * 4],
+                        np.repeat(v, 4, axis=0)[np.arange(32) % 8 * 4], tk=300)
+    assert rel_l2(got, wrong) > 1e-2
+
+
+def test_tc_baseline_shape_sampled(ops):
+    tq, tk = 4096, 4416
+    q, k, v = qkv(32, 8, tq, tk, 23)
+    got = run_paged(ops, q, k, v, tk)
+    rows = np.sort(np.random.default_rng(24).choice(tq, 40, replace=False))
+    for h in (0, 9, 31):
+        hk = h // 4
+        ref = O.attention(q[h:h + 1, rows], k[hk:hk + 1], v[hk:hk + 1])
+        assert rel_l2(got[rows, h * 128:(h + 1) * 128], ref) < BAR
+
+
+def test_tc_sage(ops):
+    q, k, v = qkv(8, 2, 300, 256, 25, k_mean=0.7)
+    got = run_paged(ops, q, k, v, 230, sage=True)
+    assert rel_l2(got, O.sage_attention(q, k, v, tk=230, bq=64, bk=64)) < 1e-2
+    assert rel_l2(got, O.attention(q, k, v, tk=230)) < 3e-2
+
+
+def test_paged_masked_rules_transposed_v(ops):
+    q, k, v = qkv(8, 2, 40, 128, 26)
+    got = run_paged(ops, q, k, v, 100, table=[1, 0], mode=1, q_offset=60)
+    assert rel_l2(got, O.attention(q, k, v, tk=100, mode=O.CAUSAL, q_offset=60)) < BAR
+    t = np.array([0, 1] + [2] * 50 + [3, 4], np.int32)
+    q2, k2, v2 = qkv(8, 2, t.size, 64, 27)
+    got = run_paged(ops, q2, k2, v2, t.size, mode=2, t_index=t)
+    assert rel_l2(got, O.attention(q2, k2, v2, tk=t.size, mode=O.BLOCK_CAUSAL, t_index=t)) < BAR

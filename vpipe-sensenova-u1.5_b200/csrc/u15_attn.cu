@@ -105,7 +105,7 @@ __device__ __forceinline__ const __nv_bfloat16* kv_row(const KvView& kv, const v
          (long)h * kv.head_stride + (long)(j & 63) * 128;
 }
 
-template <bool SAGE>
+template <bool SAGE, bool VT>
 __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant__ AttnP p)
 {
   extern __shared__ __align__(128) uint8_t sm[];
@@ -167,12 +167,24 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         cp_async16(aK + buf * kKBytes + swz256(r, c), src, ok);
       }
     }
-    for (int i = tid; i < kKeys * 16; i += kThreads) {
-      const int r = i >> 4, c = i & 15;
-      const int j = j0 + r;
-      const bool ok = j < p.tk;
-      const __nv_bfloat16* src = kv_row(p.kv, p.kv.v, hk, ok ? j : 0) + c * 8;
-      cp_async16(aV + buf * kVBytes + swz256(r, c), src, ok);
+    if constexpr (VT) {
+      // transposed page: 128 dim rows of 64 keys (8 chunks), one page per tile
+      const long page = p.kv.page_table ? (long)p.kv.page_table[j0 >> 6] : (long)(j0 >> 6);
+      const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(p.kv.v) +
+                                page * p.kv.page_stride + (long)hk * p.kv.head_stride;
+      for (int i = tid; i < 128 * 8; i += kThreads) {
+        const int r = i >> 3, c = i & 7;
+        cp_async16(aV + buf * kVBytes + swz128(r, c), vb + (long)r * 64 + c * 8,
+                   j0 + c * 8 < p.tk);
+      }
+    } else {
+      for (int i = tid; i < kKeys * 16; i += kThreads) {
+        const int r = i >> 4, c = i & 15;
+        const int j = j0 + r;
+        const bool ok = j < p.tk;
+        const __nv_bfloat16* src = kv_row(p.kv, p.kv.v, hk, ok ? j : 0) + c * 8;
+        cp_async16(aV + buf * kVBytes + swz256(r, c), src, ok);
+      }
     }
   };
 
@@ -319,8 +331,13 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
 #pragma unroll
       for (int dp = 0; dp < 8; ++dp) {
         uint32_t b0, b1, b2, b3;
-        const int vr = kk * 16 + (l & 7) + ((l >> 3) & 1) * 8;
-        ldsm_x4_t(aV + buf * kVBytes + swz256(vr, 2 * dp + (l >> 4)), b0, b1, b2, b3);
+        if constexpr (VT) {
+          const int vr = dp * 16 + (l & 7) + (l >> 4) * 8;
+          ldsm_x4(aV + buf * kVBytes + swz128(vr, 2 * kk + ((l >> 3) & 1)), b0, b1, b2, b3);
+        } else {
+          const int vr = kk * 16 + (l & 7) + ((l >> 3) & 1) * 8;
+          ldsm_x4_t(aV + buf * kVBytes + swz256(vr, 2 * dp + (l >> 4)), b0, b1, b2, b3);
+        }
         mma_bf16_16816(o[2 * dp], a, b0, b1);
         mma_bf16_16816(o[2 * dp + 1], a, b2, b3);
       }
@@ -465,20 +482,18 @@ int attention(const AttnArgs& a, cudaStream_t st, std::string* err)
   const dim3 grid((a.tq + p.R - 1) / p.R, a.hkv);
   const int smem = sage ? (kRows * 128 + 2 * kKeys * 128 + 2 * kKeys * 256)
                         : (kRows * 256 + 2 * kKeys * 256 + 2 * kKeys * 256);
-  static bool set0 = false, set1 = false;
-  if (sage) {
-    if (!set1) {
-      cudaFuncSetAttribute(attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      set1 = true;
+  static bool attr_done[4] = {false, false, false, false};
+  auto launch = [&](auto kern, int which) {
+    if (!attr_done[which]) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      attr_done[which] = true;
     }
-    attn_kernel<true><<<grid, kThreads, smem, st>>>(p);
-  } else {
-    if (!set0) {
-      cudaFuncSetAttribute(attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      set0 = true;
-    }
-    attn_kernel<false><<<grid, kThreads, smem, st>>>(p);
-  }
+    kern<<<grid, kThreads, smem, st>>>(p);
+  };
+  if (sage)
+    a.kv.v_t ? launch(attn_kernel<true, true>, 3) : launch(attn_kernel<true, false>, 2);
+  else
+    a.kv.v_t ? launch(attn_kernel<false, true>, 1) : launch(attn_kernel<false, false>, 0);
   if (cudaGetLastError() != cudaSuccess) {
     *err = "attention: kernel launch failed";
     return 2;

@@ -1,0 +1,420 @@
+// Bidirectional flash attention on sm_100a tensor cores (tcgen05 + TMEM +
+// TMA), the denoise pass's attention (src/u15-metal-ops.cc:835-882 in the
+// reference: q head-major, every key of [prefix || block]).
+//
+// One CTA = 256 query rows of one head as two 128-row tiles that share
+// every K/V tile it loads. Warp roles:
+//   warp 0      TMA producer: Q once, then per 64-key tile one K page
+//               (2 boxes of [64 keys][64 dims]) and one transposed V page
+//               ([128 dims][64 keys]) into a 3-stage ring
+//   warp 1      MMA issuer (one thread):
+//                 S_t(j) = Q_t K_j^T     M=128 N=64  K=128  -> TMEM (2 buffers per tile)
+//                 O_t   += P_t(j) V_j    M=128 N=128 K=64   -> TMEM (one per tile)
+//               with S(j+1) issued before O(j) so the tensor core works on
+//               the next tile while the softmax warps are busy
+//   warps 2-9   softmax, four warps per tile, one query row per thread:
+//               tcgen05.ld the row of S, base-2 online softmax with lazy
+//               rescaling (O in TMEM is rescaled only when a row max grows
+//               by more than 2^8), P as bf16 into 128-byte-swizzled shared
+//               memory (the A operand of the P.V MMA), final O / l to global
+//               token-major [tq][hq*128]
+// TMEM: 512 columns = per tile S0 | S1 (64 each) | O (128).
+//
+// The Sage variant (int8 QK, SageAttention) feeds S from int8 Q and smoothed
+// int8 K (kind::i8, s32 accumulators) and scales the scores by the per-64-row
+// Q block and per-64-key K block scales; P.V stays bf16.
+//
+// K/V come from the paged cache: K page [64 tokens][128] and V page
+// transposed [128 dims][64 tokens], per kv head, page index from the page
+// table. Every wait is bounded (u15_common.cuh).
+#include "u15_common.cuh"
+#include "u15_kernels.h"
+
+#include <algorithm>
+#include <cmath>
+
+namespace u15 {
+
+namespace {
+
+constexpr int kTile = 128;      // query rows per MMA tile
+constexpr int kKeys = 64;       // keys per KV tile = one page
+constexpr int kStages = 3;
+constexpr int kThreads = 320;   // 10 warps
+constexpr int kQBytes = 2 * kTile * 256;       // bf16: 2 tiles x [128][128]; int8 uses half
+constexpr int kKBytes = kKeys * 256;           // bf16 [64][128] (2 boxes); int8 uses half
+constexpr int kVBytes = 128 * kKeys * 2;       // [128 dims][64 keys] bf16
+constexpr int kPBytes = kTile * kKeys * 2;     // [128 rows][64 keys] bf16
+constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 2 * kPBytes + 1024 + 512;
+
+struct TcAttnP {
+  int hq, hkv, tq, tk, G, n_tiles;
+  float scale_log2;
+  const int32_t* page_table;
+  __nv_bfloat16* out;
+  const float* sq;   // Sage: [hq][nqb]
+  const float* sk;   // Sage: [hkv][nkb]
+  int nqb, nkb;
+  long k8_stride;    // Sage: rows per kv head in the int8 K copy
+  unsigned* err;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
+{
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <bool SAGE>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
+{
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;                                   // tile t at t * (kQBytes/2)
+  uint8_t* sK = sQ + kQBytes;                           // stage s at s * kKBytes
+  uint8_t* sV = sK + kStages * kKBytes;                 // stage s at s * kVBytes
+  uint8_t* sP = sV + kStages * kVBytes;                 // tile t at t * kPBytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  // barrier slots
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0;
+  const uint32_t k_full = b0 + 8;                       // [kStages]
+  const uint32_t v_full = k_full + 8 * kStages;
+  const uint32_t k_empty = v_full + 8 * kStages;
+  const uint32_t v_empty = k_empty + 8 * kStages;
+  const uint32_t s_full = v_empty + 8 * kStages;        // [2 tiles][2 buffers]
+  const uint32_t p_full = s_full + 8 * 4;               // [2 tiles]
+  const uint32_t o_done = p_full + 8 * 2;               // [2 tiles]
+  const uint32_t drain = o_done + 8 * 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 4 + 2 + 2 + 1);
+
+  const int w = (int)warp_id();
+  const int h = blockIdx.y;
+  const int hk = h / p.G;
+  const int q0 = blockIdx.x * 2 * kTile;
+  const int n = p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(k_full + 8 * s, 1);
+      mbar_init(v_full + 8 * s, 1);
+      mbar_init(k_empty + 8 * s, 1);
+      mbar_init(v_empty + 8 * s, 1);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(s_full + 8 * i, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(p_full + 8 * t, 128);
+      mbar_init(o_done + 8 * t, 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (w == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (w == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane_id() == 0) {
+      const int qrow = h * p.tq + q0;
+      if constexpr (SAGE) {
+        mbar_arrive_expect_tx(q_full, 2 * kTile * 128);
+        for (int t = 0; t < 2; ++t)
+          tma_load_2d(smem_u32(sQ + t * kTile * 128), &tmQ, 0, qrow + t * kTile, q_full);
+      } else {
+        mbar_arrive_expect_tx(q_full, 2 * kTile * 256);
+        for (int t = 0; t < 2; ++t)
+          for (int d = 0; d < 2; ++d)
+            tma_load_2d(smem_u32(sQ + t * kTile * 256 + d * kTile * 128), &tmQ, d * 64,
+                        qrow + t * kTile, q_full);
+      }
+      int last_k[kStages], last_v[kStages];
+      for (int s = 0; s < kStages; ++s) last_k[s] = last_v[s] = -1;
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const int page = p.page_table ? p.page_table[j] : j;
+        if (!mbar_wait(k_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+        if constexpr (SAGE) {
+          mbar_arrive_expect_tx(k_full + 8 * s, kKeys * 128);
+          tma_load_2d(smem_u32(sK + s * kKBytes), &tmK, 0, (int)(hk * p.k8_stride) + j * kKeys,
+                      k_full + 8 * s);
+        } else {
+          mbar_arrive_expect_tx(k_full + 8 * s, kKeys * 256);
+          const int krow = (page * p.hkv + hk) * kKeys;
+          tma_load_2d(smem_u32(sK + s * kKBytes), &tmK, 0, krow, k_full + 8 * s);
+          tma_load_2d(smem_u32(sK + s * kKBytes + kKeys * 128), &tmK, 64, krow, k_full + 8 * s);
+        }
+        last_k[s] = j;
+        if (!mbar_wait(v_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+        mbar_arrive_expect_tx(v_full + 8 * s, kVBytes);
+        tma_load_2d(smem_u32(sV + s * kVBytes), &tmV, 0, (page * p.hkv + hk) * 128, v_full + 8 * s);
+        last_v[s] = j;
+      }
+      // unwinding: every copy issued must land before the CTA may exit
+      mbar_wait(q_full, 0, p.err, kDevWaitDrain);
+      for (int s = 0; s < kStages; ++s) {
+        if (last_k[s] >= 0) mbar_wait(k_full + 8 * s, (last_k[s] / kStages) & 1, p.err, kDevWaitDrain);
+        if (last_v[s] >= 0) mbar_wait(v_full + 8 * s, (last_v[s] / kStages) & 1, p.err, kDevWaitDrain);
+      }
+    }
+  } else if (w == 1) {
+    // ------------------------------------------------------------ MMA
+    if (lane_id() == 0) {
+      const uint32_t id_s = SAGE ? idesc_s8(kTile, kKeys) : idesc_bf16(kTile, kKeys);
+      const uint32_t id_o = idesc_bf16(kTile, 128);
+      bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
+      auto issue_s = [&](int j) -> bool {
+        const uint32_t s = j % kStages;
+        if (!mbar_wait(k_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) return false;
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t d = tmem + t * 256 + (j & 1) * 64;
+          if constexpr (SAGE) {
+            const uint32_t a0 = smem_u32(sQ + t * kTile * 128), b0 = smem_u32(sK + s * kKBytes);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), id_s, k != 0);
+          } else {
+            const uint32_t a0 = smem_u32(sQ + t * kTile * 256), b0 = smem_u32(sK + s * kKBytes);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
+                       smem_desc_sw128(b0 + (k >> 2) * kKeys * 128 + (k & 3) * 32), id_s, k != 0);
+          }
+          mma_commit(s_full + 8 * (t * 2 + (j & 1)));
+        }
+        mma_commit(k_empty + 8 * s);
+        return true;
+      };
+      if (ok && n > 0) ok = issue_s(0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n && !issue_s(j + 1)) break;
+        const uint32_t s = j % kStages;
+        if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!mbar_wait(p_full + 8 * t, j & 1, p.err, kDevWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + t * 256 + 128;
+          const uint32_t a0 = smem_u32(sP + t * kPBytes), b0 = smem_u32(sV + s * kVBytes);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_bf16(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), id_o,
+                     (j | k) != 0);
+          mma_commit(o_done + 8 * t);
+        }
+        mma_commit(v_empty + 8 * s);
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.err, kDevWaitDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = (w - 2) >> 2;              // tile
+    const int wq = w & 3;                    // TMEM lane quadrant
+    const int row = wq * 32 + (int)lane_id();
+    const int qi = q0 + t * kTile + row;     // query index within the head
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + t * 256 + lane_off, tO = tS + 128;
+    uint8_t* prow = sP + t * kPBytes + row * 128;
+    float sqv = 1.0f;
+    if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
+    float m_ref = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!mbar_wait(s_full + 8 * (t * 2 + (j & 1)), (j >> 1) & 1, p.err, kDevWaitAccFull)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tS + (j & 1) * 64, r0);
+      tmem_ld32(tS + (j & 1) * 64 + 32, r1);
+      tmem_ld_wait();
+      float s[64];
+      float f = p.scale_log2;
+      if constexpr (SAGE) f *= sqv * p.sk[(long)hk * p.nkb + j];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if constexpr (SAGE) {
+          s[i] = (float)(int32_t)r0[i] * f;
+          s[32 + i] = (float)(int32_t)r1[i] * f;
+        } else {
+          s[i] = __uint_as_float(r0[i]) * f;
+          s[32 + i] = __uint_as_float(r1[i]) * f;
+        }
+      }
+      const int kmax = p.tk - j * kKeys;   // valid keys in this tile
+      if (kmax < kKeys) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i >= kmax) s[i] = -INFINITY;
+      }
+      float mt = s[0];
+#pragma unroll
+      for (int i = 1; i < 64; ++i) mt = fmaxf(mt, s[i]);
+      const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
+      const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
+      bool waited = false;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // rescale this row's O (after the previous P.V has landed)
+        if (!mbar_wait(o_done + 8 * t, (j - 1) & 1, p.err, kDevWaitAccFull)) { ok = false; break; }
+        waited = true;
+        tc_fence_after();
+        const float fac = need ? exp2f(m_ref - m_new) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
+          tmem_st32(tO + c * 32, o);
+        }
+        tmem_st_wait();
+        l *= fac;
+      }
+      m_ref = m_new;
+      uint32_t pk[32];
+      float rs = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = exp2f(s[2 * i] - m_ref), b = exp2f(s[2 * i + 1] - m_ref);
+        rs += a + b;
+        pk[i] = pack_bf2(a, b);
+      }
+      l += rs;
+      if (j > 0 && !waited) {
+        if (!mbar_wait(o_done + 8 * t, (j - 1) & 1, p.err, kDevWaitAccFull)) { ok = false; break; }
+      }
+      // P row: 64 keys = 8 chunks of 16 B, 128-byte swizzle
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = v;
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full + 8 * t);
+    }
+    if (ok && n > 0 && mbar_wait(o_done + 8 * t, (n - 1) & 1, p.err, kDevWaitAccFull)) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_ld_wait();
+        if (qi < p.tq) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            uint4 v;
+            v.x = pack_bf2(__uint_as_float(o[qd * 8 + 0]) * inv, __uint_as_float(o[qd * 8 + 1]) * inv);
+            v.y = pack_bf2(__uint_as_float(o[qd * 8 + 2]) * inv, __uint_as_float(o[qd * 8 + 3]) * inv);
+            v.z = pack_bf2(__uint_as_float(o[qd * 8 + 4]) * inv, __uint_as_float(o[qd * 8 + 5]) * inv);
+            v.w = pack_bf2(__uint_as_float(o[qd * 8 + 6]) * inv, __uint_as_float(o[qd * 8 + 7]) * inv);
+            d4[qd] = v;
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (w == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
+{
+  if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv) {
+    *err = "attention: hq must be a positive multiple of hkv";
+    return 1;
+  }
+  if (a.tq <= 0 || a.tk <= 0) return 0;
+  const bool sage = a.q8 != nullptr;
+  TcAttnP p{};
+  p.hq = a.hq;
+  p.hkv = a.hkv;
+  p.tq = a.tq;
+  p.tk = a.tk;
+  p.G = a.hq / a.hkv;
+  p.n_tiles = (a.tk + kKeys - 1) / kKeys;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  p.page_table = a.page_table;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.sq = a.sq;
+  p.sk = a.sk;
+  p.nqb = (a.tq + 63) / 64;
+  p.nkb = (a.tk + 63) / 64;
+  p.k8_stride = (long)p.nkb * 64;
+  p.err = a.dev_err;
+  if (a.n_pages < p.n_tiles && a.page_table == nullptr) {
+    *err = "attention: the page pool holds fewer pages than the key length needs";
+    return 1;
+  }
+  CUtensorMap mq, mk, mv;
+  if (sage) {
+    if (make_tma_2d(&mq, a.q8, (uint64_t)a.hq * a.tq, 128, kTile, 1, err)) return 2;
+    if (make_tma_2d(&mk, a.k8, (uint64_t)a.hkv * p.k8_stride, 128, kKeys, 1, err)) return 2;
+  } else {
+    if (make_tma_2d(&mq, a.q, (uint64_t)a.hq * a.tq, 128, kTile, 2, err)) return 2;
+    if (make_tma_2d(&mk, a.k_pages, (uint64_t)a.n_pages * a.hkv * kKeys, 128, kKeys, 2, err))
+      return 2;
+  }
+  if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, kKeys, 128, 2, err))
+    return 2;
+  static bool set0 = false, set1 = false;
+  const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
+  if (sage) {
+    if (!set1) {
+      cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+      set1 = true;
+    }
+    attn_tc_kernel<true><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
+  } else {
+    if (!set0) {
+      cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+      set0 = true;
+    }
+    attn_tc_kernel<false><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
+  }
+  if (cudaGetLastError() != cudaSuccess) {
+    *err = "attention (tcgen05): kernel launch failed";
+    return 2;
+  }
+  return 0;
+}
+
+}  // namespace u15

@@ -176,6 +176,45 @@ int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, i
   return U15C_OK;
 }
 
+int run_attention_tc(cudaStream_t st, const void* q, const KvView& kv, int n_pages, void* out,
+                     int hq, int hkv, int tq, int tk, void* sage_ws)
+{
+  DevState* d = dev();
+  if (d == nullptr) return U15C_ECUDA;
+  if (q == nullptr || kv.k == nullptr || kv.v == nullptr || out == nullptr)
+    return fail(U15C_EINVAL, "attention: null buffer");
+  if (!kv.v_t || kv.page_stride != (long)hkv * kPageTokens * kHeadDim ||
+      kv.head_stride != (long)kPageTokens * kHeadDim)
+    return fail(U15C_EINVAL, "attention: the tcgen05 path needs the paged layout with transposed V");
+  if ((tk + kPageTokens - 1) / kPageTokens > n_pages)
+    return fail(U15C_EINVAL, "attention: key length exceeds the page pool");
+  TcAttnArgs a;
+  a.q = q;
+  a.k_pages = kv.k;
+  a.vt_pages = kv.v;
+  a.page_table = kv.page_table;
+  a.n_pages = n_pages;
+  a.out = out;
+  a.hq = hq;
+  a.hkv = hkv;
+  a.tq = tq;
+  a.tk = tk;
+  a.dev_err = d->err;
+  std::string err;
+  if (sage_ws != nullptr) {
+    SageWs s = sage_split(sage_ws, hq, hkv, tq, tk);
+    if (sage_prepare(q, kv, hq, hkv, tq, tk, s.q8, s.k8, s.sq, s.sk, s.kmean, st, &err))
+      return fail(U15C_ECUDA, err);
+    a.q8 = s.q8;
+    a.k8 = s.k8;
+    a.sq = s.sq;
+    a.sk = s.sk;
+  }
+  const int rc = attention_tc(a, st, &err);
+  if (rc) return fail(rc == 1 ? U15C_EINVAL : U15C_ECUDA, err);
+  return U15C_OK;
+}
+
 int run_gemm(GemmArgs& a, cudaStream_t st)
 {
   DevState* d = dev();
@@ -496,6 +535,27 @@ int u15c_attention(u15c_stream stream, const void* q, const void* k, const void*
   return run_attention(ST(stream), q, kv_view(const_cast<void*>(k), const_cast<void*>(v),
                                               page_table, cap, hkv),
                        out, hq, hkv, tq, tk, mode, q_offset, t_index, sage_ws);
+}
+
+int u15c_attention_paged(u15c_stream stream, const void* q, const void* k_pages,
+                         const void* vt_pages, const int32_t* page_table, int n_pages, void* out,
+                         int hq, int hkv, int tq, int tk, int head_dim, int mode, int q_offset,
+                         const int32_t* t_index, void* sage_ws)
+{
+  if (head_dim != 128) return fail(U15C_EINVAL, "attention: head_dim must be 128");
+  if (n_pages <= 0) return fail(U15C_EINVAL, "attention: n_pages must be positive");
+  KvView kv;
+  kv.k = const_cast<void*>(k_pages);
+  kv.v = const_cast<void*>(vt_pages);
+  kv.page_table = page_table;
+  kv.page_stride = (long)hkv * kPageTokens * kHeadDim;
+  kv.head_stride = (long)kPageTokens * kHeadDim;
+  kv.v_t = true;
+  if (mode == U15C_ATTN_BIDIRECTIONAL)
+    return run_attention_tc(ST(stream), q, kv, n_pages, out, hq, hkv, tq, tk, sage_ws);
+  if (sage_ws != nullptr)
+    return fail(U15C_EINVAL, "attention: Sage serves the bidirectional pass only");
+  return run_attention(ST(stream), q, kv, out, hq, hkv, tq, tk, mode, q_offset, t_index, nullptr);
 }
 
 int u15c_sdpa(u15c_stream stream, const void* q, const void* k, const void* v, void* out, int hq,

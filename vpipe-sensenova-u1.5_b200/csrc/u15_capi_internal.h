@@ -40,5 +40,9 @@ SageWs sage_split(void* ws, int hq, int hkv, int tq, int tk);
 int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, int hq, int hkv,
                   int tq, int tk, int mode, int q_offset, const int32_t* t_index, void* sage_ws);
 int run_gemm(GemmArgs& a, cudaStream_t st);
+// Bidirectional attention on the tcgen05 kernel over a paged cache with
+// transposed V pages (the model's layout); Sage when sage_ws is non-null.
+int run_attention_tc(cudaStream_t st, const void* q, const KvView& kv, int n_pages, void* out,
+                     int hq, int hkv, int tq, int tk, void* sage_ws);
 
 }  // namespace u15

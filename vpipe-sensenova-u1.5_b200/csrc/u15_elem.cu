@@ -249,8 +249,15 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv,
   } else {
     const int j = kv_off + t;
     const long page = kv.page_table ? kv.page_table[j >> 6] : (j >> 6);
-    dst = reinterpret_cast<__nv_bfloat16*>(kv.v) + page * kv.page_stride +
-          (long)(h - nh - nkv) * kv.head_stride + (long)(j & 63) * 128;
+    __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(kv.v) + page * kv.page_stride +
+                          (long)(h - nh - nkv) * kv.head_stride;
+    if (kv.v_t) {
+      // transposed page: dims are rows of 64 tokens
+#pragma unroll
+      for (int i = 0; i < 4; ++i) base[(long)(l * 4 + i) * 64 + (j & 63)] = f2bf(v[i]);
+      return;
+    }
+    dst = base + (long)(j & 63) * 128;
   }
   uint2 o;
   o.x = pack_bf2(v[0], v[1]);
@@ -305,6 +312,33 @@ __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ in, void* cac
   const uint4 v = *reinterpret_cast<const uint4*>(in + ((long)t * H + h) * 128 + c * 8);
   *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(cache) + page * page_stride +
                             h * head_stride + (long)(j & 63) * 128 + c * 8) = v;
+}
+
+// Contiguous [hkv][n][128] <-> cache view, one thread per 8 elements.
+__global__ void kv_copy_kernel(__nv_bfloat16* contig, KvView kv, bool is_v, bool to_cache, int n,
+                               int hkv)
+{
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)hkv * n * 16) return;
+  const int c = (int)(idx % 16);
+  const long ht = idx / 16;
+  const int t = (int)(ht % n), h = (int)(ht / n);
+  const long page = kv.page_table ? kv.page_table[t >> 6] : (t >> 6);
+  __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(is_v ? kv.v : kv.k) +
+                        page * kv.page_stride + (long)h * kv.head_stride;
+  __nv_bfloat16* lin = contig + ((long)h * n + t) * 128 + c * 8;
+  if (is_v && kv.v_t) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      __nv_bfloat16* e = base + (long)(c * 8 + i) * 64 + (t & 63);
+      if (to_cache) *e = lin[i];
+      else lin[i] = *e;
+    }
+  } else {
+    uint4* e = reinterpret_cast<uint4*>(base + (long)(t & 63) * 128 + c * 8);
+    if (to_cache) *e = *reinterpret_cast<const uint4*>(lin);
+    else *reinterpret_cast<uint4*>(lin) = *e;
+  }
 }
 
 // ---------------------------------------------------------------------
@@ -482,6 +516,16 @@ int launch_kv_append(const void* in, void* cache, const int32_t* page_table, lon
   kv_append_kernel<<<blocks_for(n, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(in),
                                                         cache, page_table, page_stride,
                                                         head_stride, T, H, off);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_kv_copy(void* contig, const KvView& kv, bool is_v, bool to_cache, int n, int hkv,
+                   cudaStream_t st)
+{
+  const long m = (long)hkv * n * 16;
+  if (m <= 0) return 0;
+  kv_copy_kernel<<<blocks_for(m, 256), 256, 0, st>>>(static_cast<__nv_bfloat16*>(contig), kv,
+                                                      is_v, to_cache, n, hkv);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 

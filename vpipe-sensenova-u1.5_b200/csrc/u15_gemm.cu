@@ -361,10 +361,12 @@ struct MapKeyHash {
   }
 };
 
+}  // namespace
+
 // A 2-D [rows][cols] row-major tensor (elsize 2 = bf16, 1 = int8), box of
 // 128 bytes x box_rows, 128-byte swizzle, zero fill out of bounds. Cached:
 // encoding costs microseconds and a layer calls the same maps every pass.
-int make_map(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+int make_tma_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
              int elsize, std::string* err)
 {
   static std::mutex mu;
@@ -401,6 +403,8 @@ int make_map(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, ui
   cache.emplace(key, *out);
   return 0;
 }
+
+namespace {
 
 template <bool I8, int EPI>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid,
@@ -498,8 +502,8 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   p.n_kblk = (a.K + bk - 1) / bk;
 
   CUtensorMap ma, mb;
-  if (make_map(&ma, a.x, (uint64_t)a.M, (uint64_t)a.K, kBM, es, err)) return 2;
-  if (make_map(&mb, a.w, (uint64_t)a.N * a.n_experts, (uint64_t)a.K, kBN, es, err)) return 2;
+  if (make_tma_2d(&ma, a.x, (uint64_t)a.M, (uint64_t)a.K, kBM, es, err)) return 2;
+  if (make_tma_2d(&mb, a.w, (uint64_t)a.N * a.n_experts, (uint64_t)a.K, kBN, es, err)) return 2;
 
   const int tiles = p.n_units * p.n_nblk;
   const int grid = std::min(tiles, a.num_sms > 0 ? a.num_sms : 148);

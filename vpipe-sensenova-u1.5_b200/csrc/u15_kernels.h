@@ -2,6 +2,7 @@
 // kernel files. Not installed; the public surface is include/u15c.h.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -56,6 +57,11 @@ struct KvView {
   const int32_t* page_table = nullptr;   // device; null = identity
   long page_stride = 0;                  // elements
   long head_stride = 0;                  // elements
+  // V pages stored transposed, [128 dims][64 tokens] per (page, head): token j,
+  // dim d of head h at v + page * page_stride + h * head_stride + d * 64 + (j & 63).
+  // The model's cache uses this form (the P.V operand of the tcgen05
+  // attention); the op-level reference layouts do not.
+  bool v_t = false;
 };
 constexpr int kPageTokens = 64;
 constexpr int kHeadDim = 128;
@@ -77,6 +83,30 @@ struct AttnArgs {
 };
 
 int attention(const AttnArgs& a, cudaStream_t st, std::string* err);
+
+// The tcgen05 bidirectional attention (u15_attn_tc.cu) over the paged cache:
+// K pages [n_pages][hkv][64][128], V pages transposed [n_pages][hkv][128][64].
+struct TcAttnArgs {
+  const void* q = nullptr;          // [hq][tq][128] bf16
+  const void* k_pages = nullptr;
+  const void* vt_pages = nullptr;
+  const int32_t* page_table = nullptr;   // device, null = identity
+  int n_pages = 0;                  // pages in the pool (tensor-map extent)
+  void* out = nullptr;              // [tq][hq*128] bf16
+  int hq = 0, hkv = 0, tq = 0, tk = 0;
+  // Sage int8 QK (from sage_prepare): q8 [hq][tq][128], k8 [hkv][nkb*64][128]
+  const int8_t* q8 = nullptr;
+  const int8_t* k8 = nullptr;
+  const float* sq = nullptr;
+  const float* sk = nullptr;
+  unsigned* dev_err = nullptr;
+};
+int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err);
+
+// A cached 2-D TMA map over a row-major [rows][cols] tensor (elsize 2 = bf16,
+// 1 = int8): box of 128 bytes x box_rows, 128-byte swizzle, zero fill.
+int make_tma_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols,
+                uint32_t box_rows, int elsize, std::string* err);
 
 // Sage prologue: K smoothing (mean over tk keys per kv head and channel),
 // per-64-row block int8 quantisation of Q and of the smoothed K.
@@ -106,5 +136,9 @@ int launch_add(void* d, const void* s, long n, cudaStream_t st);
 int launch_add_row(void* d, const void* r, long rows, int dim, cudaStream_t st);
 int launch_silu(void* x, long n, cudaStream_t st);
 int launch_quant_rows(const void* x, int8_t* q, float* s, int rows, int cols, cudaStream_t st);
+// Copy tokens [0, n) of one K or V cache view to/from a contiguous
+// [hkv][n][128] buffer (prefix seeding and diagnostics).
+int launch_kv_copy(void* contig, const KvView& kv, bool is_v, bool to_cache, int n, int hkv,
+                   cudaStream_t st);
 
 }  // namespace u15

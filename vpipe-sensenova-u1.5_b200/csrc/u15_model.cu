@@ -199,6 +199,7 @@ struct u15c_kv {
     kv.page_table = table;
     kv.page_stride = (long)m->cfg.kv_heads * u15::kPageTokens * 128;
     kv.head_stride = (long)u15::kPageTokens * 128;
+    kv.v_t = true;
     return kv;
   }
   ~u15c_kv()
@@ -274,9 +275,13 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
   if (u15::launch_qkv_post(m->qkv, L.norms, m->rcos, m->rsin, m->qh, view, n, c.heads,
                            c.kv_heads, kv_off, (float)c.eps, seg, st))
     return fail(U15C_ECUDA, "qkv_post launch failed");
-  if ((rc = u15::run_attention(st, m->qh, view, m->attn, c.heads, c.kv_heads, n, kv_len, attn,
-                               kv_off, t_index, sage ? m->sage_ws : nullptr)))
-    return rc;
+  if (attn == U15C_ATTN_BIDIRECTIONAL)
+    rc = u15::run_attention_tc(st, m->qh, view, kv->pages, m->attn, c.heads, c.kv_heads, n,
+                               kv_len, sage ? m->sage_ws : nullptr);
+  else
+    rc = u15::run_attention(st, m->qh, view, m->attn, c.heads, c.kv_heads, n, kv_len, attn,
+                            kv_off, t_index, nullptr);
+  if (rc) return rc;
   if ((rc = gemm(m->attn, m->qd(), L.o, L.o8, L.o_s, H, u15::kEpiResid, x))) return rc;
 
   // ---- MLP half (src/u15-backbone.cc:246-256) ----
@@ -526,22 +531,9 @@ int u15c_kv_read(u15c_kv* kv, u15c_stream stream, int layer, int which_v, void* 
   if (kv == nullptr || out == nullptr || n <= 0 || n > kv->capacity || layer < 0 ||
       layer >= kv->m->cfg.n_layers)
     return fail(U15C_EINVAL, "kv_read: bad argument");
-  std::vector<int32_t> table(kv->pages);
-  cudaError_t e = cudaMemcpy(table.data(), kv->table, table.size() * 4, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "kv_read");
-  const u15::KvView v = kv->view(layer);
-  const bf16* base = static_cast<const bf16*>(which_v ? v.v : v.k);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  for (int h = 0; h < kv->m->cfg.kv_heads; ++h) {
-    for (int p0 = 0; p0 < n; p0 += u15::kPageTokens) {
-      const int cnt = std::min(u15::kPageTokens, n - p0);
-      const bf16* src = base + (long)table[p0 / u15::kPageTokens] * v.page_stride +
-                        (long)h * v.head_stride;
-      e = cudaMemcpyAsync(static_cast<bf16*>(out) + ((long)h * n + p0) * 128, src,
-                          (size_t)cnt * 256, cudaMemcpyDeviceToDevice, st);
-      if (e != cudaSuccess) return cuda_fail(e, "kv_read copy");
-    }
-  }
+  if (u15::launch_kv_copy(out, kv->view(layer), which_v != 0, false, n, kv->m->cfg.kv_heads,
+                          static_cast<cudaStream_t>(stream)))
+    return fail(U15C_ECUDA, "kv_read: launch failed");
   return U15C_OK;
 }
 
@@ -550,22 +542,22 @@ int u15c_kv_write(u15c_kv* kv, u15c_stream stream, int layer, int which_v, const
   if (kv == nullptr || in == nullptr || n <= 0 || n > kv->capacity || layer < 0 ||
       layer >= kv->m->cfg.n_layers)
     return fail(U15C_EINVAL, "kv_write: bad argument");
-  std::vector<int32_t> table(kv->pages);
-  cudaError_t e = cudaMemcpy(table.data(), kv->table, table.size() * 4, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "kv_write");
+  if (u15::launch_kv_copy(const_cast<void*>(in), kv->view(layer), which_v != 0, true, n,
+                          kv->m->cfg.kv_heads, static_cast<cudaStream_t>(stream)))
+    return fail(U15C_ECUDA, "kv_write: launch failed");
+  return U15C_OK;
+}
+
+int u15c_kv_pages(u15c_kv* kv, int layer, void** k_pages, void** vt_pages,
+                  const int32_t** page_table, int* n_pages)
+{
+  if (kv == nullptr || layer < 0 || layer >= kv->m->cfg.n_layers)
+    return fail(U15C_EINVAL, "kv_pages: bad argument");
   const u15::KvView v = kv->view(layer);
-  bf16* base = static_cast<bf16*>(which_v ? v.v : v.k);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  for (int h = 0; h < kv->m->cfg.kv_heads; ++h) {
-    for (int p0 = 0; p0 < n; p0 += u15::kPageTokens) {
-      const int cnt = std::min(u15::kPageTokens, n - p0);
-      bf16* dst = base + (long)table[p0 / u15::kPageTokens] * v.page_stride +
-                  (long)h * v.head_stride;
-      e = cudaMemcpyAsync(dst, static_cast<const bf16*>(in) + ((long)h * n + p0) * 128,
-                          (size_t)cnt * 256, cudaMemcpyDeviceToDevice, st);
-      if (e != cudaSuccess) return cuda_fail(e, "kv_write copy");
-    }
-  }
+  if (k_pages) *k_pages = v.k;
+  if (vt_pages) *vt_pages = v.v;
+  if (page_table) *page_table = kv->table;
+  if (n_pages) *n_pages = kv->pages;
   return U15C_OK;
 }
 

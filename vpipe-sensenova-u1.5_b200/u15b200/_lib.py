@@ -73,6 +73,8 @@ SIGNATURES = {
     "u15c_silu": (ip, [vp, vp, C.c_long]),
     "u15c_sage_workspace_bytes": (C.c_size_t, [ip, ip, ip, ip]),
     "u15c_attention": (ip, [vp, vp, vp, vp, vp, ip, vp, ip, ip, ip, ip, ip, ip, ip, vp, vp]),
+    "u15c_attention_paged": (ip, [vp, vp, vp, vp, vp, ip, vp, ip, ip, ip, ip, ip, ip, ip, vp,
+                                  vp]),
     "u15c_attention_sage_static": (ip, [vp, vp, vp, vp, vp, ip, vp, ip, ip, ip, ip, ip]),
     "u15c_sdpa": (ip, [vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, ip, ip]),
     "u15c_sdpa_steel": (ip, [vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, vp]),
@@ -89,6 +91,8 @@ SIGNATURES = {
     "u15c_kv_destroy": (None, [vp]),
     "u15c_kv_capacity": (ip, [vp]),
     "u15c_kv_set_page_table": (ip, [vp, i32p, ip]),
+    "u15c_kv_pages": (ip, [vp, ip, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
+                           C.POINTER(C.c_int)]),
     "u15c_kv_read": (ip, [vp, vp, ip, ip, vp, ip]),
     "u15c_kv_write": (ip, [vp, vp, ip, ip, vp, ip]),
     "u15c_layer_forward": (ip, [vp, vp, ip, vp, ip, i32p, i32p, ip, vp, ip, ip, vp, vp, vp, ip,

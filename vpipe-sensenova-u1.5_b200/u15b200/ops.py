@@ -146,6 +146,16 @@ class CudaOps:
                                    hq, hkv, tq, tk, 128, mode, q_offset, _p(t_index),
                                    _p(sage_ws)))
 
+    def attention_paged(self, q, k_pages, vt_pages, out, hq, hkv, tq, tk, page_table=None,
+                        n_pages=None, mode=L.ATTN_BIDIRECTIONAL, q_offset=0, t_index=None,
+                        sage_ws=None):
+        """The model's cache layout: K pages [P][hkv][64][128], V pages transposed
+        [P][hkv][128][64]; bidirectional runs the tcgen05 kernel."""
+        n_pages = k_pages.shape[0] if n_pages is None else n_pages
+        check(lib().u15c_attention_paged(_stream(), _p(q), _p(k_pages), _p(vt_pages),
+                                         _p(page_table), n_pages, _p(out), hq, hkv, tq, tk, 128,
+                                         mode, q_offset, _p(t_index), _p(sage_ws)))
+
     def sdpa(self, q, k, v, out, hq, hkv, tq, tk, d, cap, causal, q_offset=0):
         check(lib().u15c_sdpa(_stream(), _p(q), _p(k), _p(v), _p(out), hq, hkv, tq, tk, d, cap,
                               int(causal), q_offset))
