@@ -93,6 +93,12 @@ def lib():
         L.orc_dequant_i8.argtypes = [_i32p, _f32p, _f32p, C.c_long, C.c_long, _f32p]
         L.orc_sage_attention.argtypes = [_f32p, _f32p, _f32p] + [C.c_long] * 8 + [_f32p]
         L.orc_time_schedule.argtypes = [C.c_int, C.c_double, _f32p]
+        L.orc_velocity.argtypes = [_f32p, _f32p, C.c_long, C.c_double, _f32p]
+        L.orc_optimized_scale.argtypes = [_f32p, _f32p, C.c_long]
+        L.orc_optimized_scale.restype = C.c_double
+        L.orc_cfg.argtypes = [_f32p, _f32p, _f32p, C.c_long, C.c_long, C.c_int, C.c_int,
+                              C.c_double, C.c_double, C.c_int, _f32p]
+        L.orc_euler.argtypes = [_f32p, _f32p, C.c_long, C.c_double]
         _lib = L
     return _lib
 
@@ -243,6 +249,39 @@ def time_schedule(n, shift):
     out = np.empty(n + 1, np.float32)
     lib().orc_time_schedule(n, shift, _fp(out))
     return out
+
+
+CFG_NONE, CFG_IMG, CFG_UNC, CFG_BOTH = 0, 1, 2, 3
+NORM_NONE, NORM_GLOBAL, NORM_CHANNEL, NORM_ZERO_STAR = 0, 1, 2, 3
+
+
+def velocity(x_pred, img, denom):
+    x_pred = _f32(x_pred); img = _f32(img)
+    v = np.empty_like(img)
+    lib().orc_velocity(_fp(x_pred), _fp(img), img.size, denom, _fp(v))
+    return v
+
+
+def optimized_scale(pos, neg):
+    pos = _f32(pos); neg = _f32(neg)
+    return lib().orc_optimized_scale(_fp(pos), _fp(neg), pos.size)
+
+
+def cfg(v_cond, v_unc, v_img, form, norm, cfg_scale, icfg, step):
+    """[H][W][3] velocities -> combined velocity (src/u15-generator.cc:596-693)."""
+    vc = _f32(v_cond)
+    H, W, _ = vc.shape
+    vu = _f32(v_unc) if v_unc is not None else vc
+    vi = _f32(v_img) if v_img is not None else vc
+    out = np.empty_like(vc)
+    lib().orc_cfg(_fp(vc), _fp(vu), _fp(vi), H, W, form, norm, cfg_scale, icfg, step, _fp(out))
+    return out
+
+
+def euler(img, v, dt):
+    img = _f32(img).copy()
+    lib().orc_euler(_fp(img), _fp(_f32(v)), img.size, dt)
+    return img
 
 
 # ---------------------------------------------------------------------------

@@ -551,3 +551,103 @@ void orc_time_schedule(int num_steps, double shift, float* out)
     out[i] = (float)(1.0 - sigma);
   }
 }
+
+/* ------------------------------------------------------------------ */
+/* the denoise step                                                    */
+/* ------------------------------------------------------------------ */
+
+/* src/u15-generator.cc:582-584 -- v = (x_pred - img) / denom in double. */
+void orc_velocity(const float* x_pred, const float* img, long n, double denom, float* v)
+{
+  for (long i = 0; i < n; ++i)
+    v[i] = (float)(((double)x_pred[i] - (double)img[i]) / denom);
+}
+
+/* src/u15-ref.cc:755-765 -- alpha = <pos, neg> / (||neg||^2 + 1e-8). */
+double orc_optimized_scale(const float* pos, const float* neg, long n)
+{
+  double dot = 0.0, nrm = 0.0;
+  for (long i = 0; i < n; ++i) {
+    dot += (double)pos[i] * (double)neg[i];
+    nrm += (double)neg[i] * (double)neg[i];
+  }
+  return dot / (nrm + 1e-8);
+}
+
+/* src/u15-generator.cc:596-693 -- the CFG combination and its renorms over an
+ * [H][W][3] image (32x32-pixel tokens for the per-token renorm).
+ *   ORC_CFG_IMG   v_img + cfg (v_cond - v_img)                 (img_cfg == 1)
+ *   ORC_CFG_UNC   v_unc + cfg (v_cond - v_unc), or with ORC_NORM_ZERO_STAR
+ *                 a = alpha v_unc; a + cfg (v_cond - a), exactly 0 at step 0
+ *   ORC_CFG_BOTH  v_unc + cfg (v_cond - v_img) + icfg (v_img - v_unc)
+ *   ORC_CFG_NONE  v_cond
+ * then ORC_NORM_GLOBAL scales by min(1, |v_cond| / (|out| + 1e-8)) over the
+ * image and ORC_NORM_CHANNEL does the same per token. */
+void orc_cfg(const float* vc, const float* vu, const float* vi, long H, long W, int form,
+             int norm, double cfg, double icfg, int step, float* out)
+{
+  const long n = H * W * 3;
+  if (form == ORC_CFG_IMG) {
+    for (long i = 0; i < n; ++i)
+      out[i] = (float)((double)vi[i] + cfg * ((double)vc[i] - (double)vi[i]));
+  } else if (form == ORC_CFG_UNC) {
+    if (norm == ORC_NORM_ZERO_STAR) {
+      const double alpha = orc_optimized_scale(vc, vu, n);
+      if (step <= 0) {
+        for (long i = 0; i < n; ++i) out[i] = 0.0f;
+      } else {
+        for (long i = 0; i < n; ++i) {
+          const double a = alpha * (double)vu[i];
+          out[i] = (float)(a + cfg * ((double)vc[i] - a));
+        }
+      }
+    } else {
+      for (long i = 0; i < n; ++i)
+        out[i] = (float)((double)vu[i] + cfg * ((double)vc[i] - (double)vu[i]));
+    }
+  } else if (form == ORC_CFG_BOTH) {
+    for (long i = 0; i < n; ++i)
+      out[i] = (float)((double)vu[i] + cfg * ((double)vc[i] - (double)vi[i]) +
+                       icfg * ((double)vi[i] - (double)vu[i]));
+  } else {
+    for (long i = 0; i < n; ++i) out[i] = vc[i];
+  }
+  if (norm == ORC_NORM_GLOBAL) {
+    double nc = 0.0, nv = 0.0;
+    for (long i = 0; i < n; ++i) {
+      nc += (double)vc[i] * vc[i];
+      nv += (double)out[i] * out[i];
+    }
+    double sc = sqrt(nc) / (sqrt(nv) + 1e-8);
+    if (sc > 1.0) sc = 1.0;
+    for (long i = 0; i < n; ++i) out[i] = (float)(out[i] * sc);
+  } else if (norm == ORC_NORM_CHANNEL) {
+    const long ps = 32, th = H / ps, tw = W / ps;
+    for (long ty = 0; ty < th; ++ty) {
+      for (long tx = 0; tx < tw; ++tx) {
+        double nc = 0.0, nv = 0.0;
+        for (long y = 0; y < ps; ++y)
+          for (long x = 0; x < ps; ++x)
+            for (long c = 0; c < 3; ++c) {
+              const long i = ((ty * ps + y) * W + (tx * ps + x)) * 3 + c;
+              nc += (double)vc[i] * vc[i];
+              nv += (double)out[i] * out[i];
+            }
+        double sc = sqrt(nc) / (sqrt(nv) + 1e-8);
+        if (sc > 1.0) sc = 1.0;
+        for (long y = 0; y < ps; ++y)
+          for (long x = 0; x < ps; ++x)
+            for (long c = 0; c < 3; ++c) {
+              const long i = ((ty * ps + y) * W + (tx * ps + x)) * 3 + c;
+              out[i] = (float)(out[i] * sc);
+            }
+      }
+    }
+  }
+}
+
+/* src/u15-generator.cc:701-705 -- img += dt v, in double. */
+void orc_euler(float* img, const float* v, long n, double dt)
+{
+  for (long i = 0; i < n; ++i) img[i] = (float)((double)img[i] + dt * (double)v[i]);
+}

@@ -95,6 +95,15 @@ void orc_sage_attention(const float* q, const float* k, const float* v,
 
 void orc_time_schedule(int num_steps, double shift, float* out);
 
+/* the denoise step (src/u15-generator.cc:582-705) */
+enum { ORC_CFG_NONE = 0, ORC_CFG_IMG = 1, ORC_CFG_UNC = 2, ORC_CFG_BOTH = 3 };
+enum { ORC_NORM_NONE = 0, ORC_NORM_GLOBAL = 1, ORC_NORM_CHANNEL = 2, ORC_NORM_ZERO_STAR = 3 };
+void orc_velocity(const float* x_pred, const float* img, long n, double denom, float* v);
+double orc_optimized_scale(const float* pos, const float* neg, long n);
+void orc_cfg(const float* v_cond, const float* v_unc, const float* v_img, long H, long W,
+             int form, int norm, double cfg, double icfg, int step, float* out);
+void orc_euler(float* img, const float* v, long n, double dt);
+
 #ifdef __cplusplus
 }
 #endif
