@@ -363,6 +363,12 @@ def run_ours(args, rank, world, local):
         kern["attention_mma_sync_reference_layout"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
         torch.cuda.empty_cache()
 
+    # ---- denoise steps/s (BASELINE config 5 geometry), one replica per rank ----
+    den = None
+    if args.denoise_steps > 0:
+        del m, kv
+        torch.cuda.empty_cache()
+        den = denoise_bench(args, rank, world, dist)
     clk.__exit__(None, None, None)
 
     # ---- CPU baseline (rank 0, N=1 only): bounded sample, ~10-30 s ----
@@ -407,10 +413,71 @@ def run_ours(args, rank, world, local):
                      "frac": (gu.get("tflops") or 0) / bf16_peak, "traffic": traffic,
                      "peak_kind": f"{peak_kind} burst bf16"},
         "kernels": kern,
+        "denoise": den,
         "clocks": clk.summary(),
         "cpu_baseline": cpu_line,
     }
     print(json.dumps(line), flush=True)
+
+
+def denoise_bench(args, rank, world, dist):
+    """Denoise steps/s at BASELINE config 5's geometry: 42 layers (random
+    N(0, 0.02) weights, both experts), 4096 generation tokens (64x64 token
+    grid, 2048x2048 px), three CFG forwards per step -- text-conditional
+    (320-token prefix), image-conditional (8 text + one 1024-token reference
+    image, block-causal prefill) and unconditional (13 tokens) -- shift 3.0,
+    cfg 4.0, img_cfg 1.5. The image path is the stand-in linear embedder and
+    head. Each rank runs its own seed (a replica): steps/s of the whole job =
+    ranks / max-over-ranks seconds per step."""
+    import torch
+    import u15b200
+    from u15b200 import _lib as L
+    from u15b200.generator import Branch, Generator
+
+    m = u15b200.Model(n_layers=42)
+    m.bind_random(seed=77 + rank, std=0.02, norm_mean=1.0, norm_std=0.2)
+    for e in range(2):
+        m.bind(0, e, "final_norm", torch.ones(H, device="cuda"))
+    g = torch.Generator(device="cuda").manual_seed(5 + rank)
+
+    def pre(n_text, n_img):
+        n = n_text + n_img
+        x = torch.randn(n, H, device="cuda", generator=g).bfloat16()
+        t = np.concatenate([np.arange(n_text), np.full(n_img, n_text)]).astype(np.int32)
+        h = np.concatenate([np.zeros(n_text), np.arange(n_img) // 32]).astype(np.int32)
+        w = np.concatenate([np.zeros(n_text), np.arange(n_img) % 32]).astype(np.int32)
+        return x, t, h, w
+
+    specs = [("cond", pre(320, 0), False), ("img_cond", pre(8, 1024), True),
+             ("uncond", pre(13, 0), False)]
+    branches = [Branch(nm, x, t, h, w, block_causal=bc) for nm, (x, t, h, w), bc in specs]
+    gen = Generator(m)
+    evs = []
+
+    def cb(step, img):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        evs.append(e)
+
+    n_steps = 1 + args.denoise_steps
+    if dist is not None:
+        dist.barrier()
+    gen.generate(branches, 2048, 2048, steps=n_steps, shift=3.0, cfg=4.0, icfg=1.5,
+                 form=L.CFG_BOTH, i_img=1, i_unc=2, seed=rank, step_callback=cb)
+    torch.cuda.synchronize()
+    s_per_step = evs[0].elapsed_time(evs[-1]) / 1e3 / args.denoise_steps
+    if dist is not None:
+        t = torch.tensor([s_per_step], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        s_per_step = float(t.item())
+    del gen, branches, m
+    torch.cuda.empty_cache()
+    return {"steps_per_s": world / s_per_step, "s_per_step_per_replica": s_per_step,
+            "timed_steps": args.denoise_steps, "warmup_steps": 1,
+            "config": "42 layers, 4096 gen tokens (BASELINE '1024^2' = 64x64 tokens = 2048^2 px),"
+                      " 3 CFG forwards/step (prefix 320 / 8+1024 img block-causal / 13),"
+                      " stand-in linear image path, replicas x%d" % world,
+            "layers_per_step": 3 * 42}
 
 
 def main():
@@ -421,6 +488,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--denoise-steps", type=int, default=3,
+                    help="timed denoise steps after one warm-up step (0: skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))

@@ -249,6 +249,37 @@ int u15c_attention_sage_static(u15c_stream stream, const void* q, const void* k,
                                int tq, int tk, int head_dim);
 
 /* ------------------------------------------------------------------ */
+/* the denoise step (Generator::generate, src/u15-generator.cc:468-706)  */
+/* ------------------------------------------------------------------ */
+
+#define U15C_CFG_NONE 0 /* v = v_cond */
+#define U15C_CFG_IMG 1  /* v_img + cfg (v_cond - v_img)               (img_cfg == 1) */
+#define U15C_CFG_UNC 2  /* v_unc + cfg (v_cond - v_unc)               (t2i, cfg == img_cfg) */
+#define U15C_CFG_BOTH 3 /* v_unc + cfg (v_cond - v_img) + icfg (v_img - v_unc) */
+#define U15C_NORM_NONE 0      /* CfgNorm::None */
+#define U15C_NORM_GLOBAL 1    /* CfgNorm::Global: min(1, |v_cond| / |v|) over the image */
+#define U15C_NORM_CHANNEL 2   /* CfgNorm::Channel: the same per 32x32 token */
+#define U15C_NORM_ZERO_STAR 3 /* CfgNorm::CfgZeroStar (U15C_CFG_UNC only) */
+
+/* v = (x_pred - img) / denom, fp64 arithmetic (src/u15-generator.cc:582-584);
+ * denom = max(1 - t, t_eps). f32 device arrays of n elements. */
+int u15c_velocity(u15c_stream stream, const float* x_pred, const float* img, float* v, long n,
+                  double denom);
+/* The CFG combination and renorm (src/u15-generator.cc:596-693) over [H][W][3]
+ * f32 velocities; unused inputs may be NULL. Reductions are fp64 and
+ * deterministic; workspace: u15c_cfg_workspace_bytes() bytes of device memory. */
+size_t u15c_cfg_workspace_bytes(void);
+int u15c_cfg_combine(u15c_stream stream, const float* v_cond, const float* v_unc,
+                     const float* v_img, float* out, int H, int W, int form, int norm, double cfg,
+                     double icfg, int step, void* workspace);
+/* img += dt * v in fp64 (src/u15-generator.cc:701-705). */
+int u15c_euler(u15c_stream stream, float* img, const float* v, long n, double dt);
+/* [H][W][3] f32 <-> [(H/32)*(W/32)][32*32*3] bf16 token rows, channel-last
+ * packing (the reference's patchify_channel_last, src/u15-ref.cc). */
+int u15c_patchify(u15c_stream stream, const float* img, void* rows, int H, int W);
+int u15c_unpatchify(u15c_stream stream, const void* rows, float* img, int H, int W);
+
+/* ------------------------------------------------------------------ */
 /* model: weights, KV cache, backbone                                   */
 /* ------------------------------------------------------------------ */
 

@@ -22,6 +22,8 @@ EXPERT_UND, EXPERT_GEN = 0, 1
 MODEL_INT8 = 1
 FWD_INT8, FWD_SAGE = 1, 2
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+CFG_NONE, CFG_IMG, CFG_UNC, CFG_BOTH = 0, 1, 2, 3
+NORM_NONE, NORM_GLOBAL, NORM_CHANNEL, NORM_ZERO_STAR = 0, 1, 2, 3
 TENSORS = ["input_layernorm", "post_attention_layernorm", "q_proj", "k_proj", "v_proj",
            "o_proj", "q_norm", "k_norm", "q_norm_hw", "k_norm_hw", "gate_proj", "up_proj",
            "down_proj", "final_norm"]
@@ -79,6 +81,13 @@ SIGNATURES = {
     "u15c_sdpa": (ip, [vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, ip, ip]),
     "u15c_sdpa_steel": (ip, [vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, vp]),
     "u15c_sdpa_block_causal": (ip, [vp, vp, vp, vp, vp, vp, ip, ip, ip, ip, ip, ip, ip]),
+    "u15c_velocity": (ip, [vp, vp, vp, vp, C.c_long, C.c_double]),
+    "u15c_cfg_workspace_bytes": (C.c_size_t, []),
+    "u15c_cfg_combine": (ip, [vp, vp, vp, vp, vp, ip, ip, ip, ip, C.c_double, C.c_double, ip,
+                              vp]),
+    "u15c_euler": (ip, [vp, vp, vp, C.c_long, C.c_double]),
+    "u15c_patchify": (ip, [vp, vp, vp, ip, ip]),
+    "u15c_unpatchify": (ip, [vp, vp, vp, ip, ip]),
     "u15c_model_create": (ip, [C.POINTER(Config), C.c_uint, C.POINTER(vp)]),
     "u15c_model_destroy": (None, [vp]),
     "u15c_model_bind": (ip, [vp, vp, ip, ip, ip, vp, ip, ip]),

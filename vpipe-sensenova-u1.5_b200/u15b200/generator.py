@@ -1,0 +1,269 @@
+"""The denoise loop: Generator::generate (src/u15-generator.cc:151-717 of the
+reference) over libu15c.
+
+Per generation: the CFG branches the reference would build
+(src/u15-generator.cc:174-276) -- conditional, image-conditional when
+editing with img_cfg != 1, unconditional when needed -- each with its own
+prefix prefilled into its own paged KV cache by the und expert (causal, or
+block-causal when the prefix holds a reference image), then seeded noise and
+the shifted flow-matching schedule. Per step: embed the current image, add
+the timestep row, run the 42-layer gen-expert pass of every branch against
+its frozen prefix (bidirectional), final norm + pixel head, then on the
+device v = (x_pred - z) / max(1 - t, t_eps), the CFG form and renorm, and
+the Euler update (u15c_velocity / u15c_cfg_combine / u15c_euler).
+
+The patch embedder and pixel head (the reference's ImagePath) are not part
+of this library yet; `LinearImagePath` stands in for them with one linear
+map each way per 32x32 token, computed by libu15c's GEMM, so the loop runs
+end to end and its cost is dominated, as in the reference, by the backbone.
+
+Across ranks (torch.distributed), branches are placed round-robin; after
+each step's forwards every rank all-gathers the velocities (the loop's one
+exchange) and applies CFG and Euler redundantly, so every rank holds the
+same image with no broadcast.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from ._lib import check, lib
+from .ops import CudaOps, _p, _stream
+
+PIX = 32   # pixels per LLM token side (src/u15-config.h:23-28)
+
+
+def time_schedule(num_steps: int, shift: float) -> list[float]:
+    """src/u15-ref.cc:722-733: sigma = 1 - i/n, shifted, t = 1 - sigma (f32)."""
+    out = []
+    for i in range(num_steps + 1):
+        sigma = 1.0 - i / num_steps
+        sigma = shift * sigma / (1.0 + (shift - 1.0) * sigma)
+        out.append(float(np.float32(1.0 - sigma)))
+    return out
+
+
+def image_positions(t: int, th: int, tw: int):
+    """src/u15-generator.cc:62-73: every image token at t, h = row, w = column."""
+    n = th * tw
+    return (np.full(n, t, np.int32), (np.arange(n) // tw).astype(np.int32),
+            (np.arange(n) % tw).astype(np.int32))
+
+
+def branch_plan(editing: bool, cfg: float, icfg: float):
+    """Which branches run (src/u15-generator.cc:174-186, 243-276): returns
+    (names, i_img, i_unc, form)."""
+    icfg = icfg if editing else 1.0
+    needs_cfg = not (cfg == 1.0 and icfg == 1.0)
+    needs_img = editing and needs_cfg and (icfg == 1.0 or cfg != icfg)
+    needs_unc = needs_cfg and (not editing or icfg != 1.0)
+    names = ["cond"] + (["img_cond"] if needs_img else []) + (["uncond"] if needs_unc else [])
+    i_img = 1 if needs_img else -1
+    i_unc = (2 if needs_img else 1) if needs_unc else -1
+    if i_img >= 0 and i_unc < 0:
+        form = L.CFG_IMG
+    elif i_img < 0 and i_unc >= 0:
+        form = L.CFG_UNC
+    elif i_img >= 0 and i_unc >= 0:
+        form = L.CFG_BOTH
+    else:
+        form = L.CFG_NONE
+    return names, i_img, i_unc, form
+
+
+def placement(n_branch: int, world: int) -> list[int]:
+    """Rank that runs each branch: round-robin."""
+    return [b % world for b in range(n_branch)]
+
+
+def exchange_velocities(local: dict, n_branch: int, numel: int, group=None, device=None):
+    """All-gather per-branch velocities so every rank holds all of them.
+
+    `local` maps branch index -> flat f32 tensor of `numel` elements for the
+    branches this rank ran. Each rank contributes ceil(n_branch / world)
+    slots (unused slots zero); returns a list of n_branch tensors."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    per = (n_branch + world - 1) // world
+    dev = device if device is not None else next(iter(local.values())).device
+    send = torch.zeros(per, numel, dtype=torch.float32, device=dev)
+    mine = [b for b in range(n_branch) if b % world == rank]
+    for i, b in enumerate(mine):
+        send[i].copy_(local[b].reshape(-1))
+    recv = torch.empty(world * per, numel, dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    out = [None] * n_branch
+    for r in range(world):
+        owned = [b for b in range(n_branch) if b % world == r]
+        for i, b in enumerate(owned):
+            out[b] = recv[r * per + i]
+    return out
+
+
+class LinearImagePath:
+    """Stand-in for the reference's ImagePath: token rows of 32x32x3 pixels
+    (channel-last) -> hidden by one linear map, hidden -> pixels by another,
+    plus a timestep row from the cos-first sinusoid through a fixed linear
+    map (src/u15-ref.cc:735-753 for the sinusoid). Seeded weights."""
+
+    def __init__(self, hidden: int, seed: int = 0, device="cuda"):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        d = PIX * PIX * 3
+        self.hidden = hidden
+        self.w_in = (torch.randn(hidden, d, generator=g) / d ** 0.5).to(device, torch.bfloat16)
+        self.w_out = (torch.randn(d, hidden, generator=g) / hidden ** 0.5).to(device,
+                                                                             torch.bfloat16)
+        self.w_t = (torch.randn(hidden, 256, generator=g) * 0.05).numpy()
+
+    @staticmethod
+    def sinusoid(t: float, dim: int = 256, max_period: float = 10000.0):
+        half = dim // 2
+        freqs = np.exp(-np.log(max_period) * np.arange(half) / half)
+        a = t * freqs
+        return np.concatenate([np.cos(a), np.sin(a)]).astype(np.float32)
+
+    def timestep_row(self, t: float) -> torch.Tensor:
+        row = self.w_t @ self.sinusoid(t * 1000.0)
+        return torch.from_numpy(row.astype(np.float32)).to("cuda", torch.bfloat16)
+
+    def embed(self, img: torch.Tensor, H: int, W: int, out: torch.Tensor, rows: torch.Tensor):
+        check(lib().u15c_patchify(_stream(), _p(img), _p(rows), H, W))
+        n = (H // PIX) * (W // PIX)
+        check(lib().u15c_linear_bf16(_stream(), _p(rows), _p(self.w_in), None, _p(out), n,
+                                     PIX * PIX * 3, self.hidden))
+
+    def decode(self, h: torch.Tensor, H: int, W: int, rows: torch.Tensor, x_pred: torch.Tensor):
+        n = (H // PIX) * (W // PIX)
+        check(lib().u15c_linear_bf16(_stream(), _p(h), _p(self.w_out), None, _p(rows), n,
+                                     self.hidden, PIX * PIX * 3))
+        check(lib().u15c_unpatchify(_stream(), _p(rows), _p(x_pred), H, W))
+
+
+@dataclass
+class Branch:
+    name: str
+    prefix: torch.Tensor                      # [n][hidden] bf16 prefix embeddings
+    t: np.ndarray                             # prefix positions
+    h: np.ndarray
+    w: np.ndarray
+    block_causal: bool = False
+    kv: object = None
+    pos: list = field(default_factory=list)   # device image positions (t, h, w)
+    v: torch.Tensor = None
+
+
+class Generator:
+    """Generator::generate over a u15b200.Model (both experts bound)."""
+
+    def __init__(self, model, image_path=None, device: int = 0, group=None):
+        self.m = model
+        self.ops = CudaOps(device)
+        self.hidden = model.cfg["hidden"]
+        self.image = image_path or LinearImagePath(self.hidden)
+        self.group = group
+
+    def prefill(self, b: Branch, ltok: int):
+        """Prefill one branch's prefix into its own cache with the und expert
+        (src/u15-generator.cc:308-392): causal, or block-causal when the
+        prefix holds a reference image."""
+        n = b.prefix.shape[0]
+        b.kv = self.m.make_cache(n + ltok)
+        x = b.prefix.clone()
+        pos = [torch.from_numpy(a).cuda() for a in (b.t, b.h, b.w)]
+        t_index = None
+        attn = L_CAUSAL
+        if b.block_causal:
+            ti = np.concatenate([b.t, np.zeros(ltok, np.int32)]).astype(np.int32)
+            t_index = torch.from_numpy(ti).cuda()
+            attn = L_BLOCK
+        self.m.forward(x, b.kv, 0, n, *pos, segments=[(0, n, L.EXPERT_UND)], attn=attn,
+                       t_index=t_index)
+        th_tw = self._geom
+        b.pos = [torch.from_numpy(a).cuda() for a in image_positions(int(b.t.max()) + 1, *th_tw)]
+
+    def generate(self, branches: list, H: int, W: int, steps: int = 20, shift: float = 3.0,
+                 cfg: float = 4.0, icfg: float = 1.0, cfg_norm: int = L.NORM_NONE,
+                 t_eps: float = 0.05, seed: int = 0, noise_scale: float = 1.0,
+                 form: int = None, i_img: int = -1, i_unc: int = -1,
+                 cfg_interval=(0.0, 1.0), int8: bool = False, sage: bool = False,
+                 init_noise: torch.Tensor = None, step_callback=None):
+        """Run the loop; returns the final [H][W][3] f32 image (device).
+        `branches` are already ordered cond, [img_cond], [uncond]."""
+        th, tw = H // PIX, W // PIX
+        Ltok = th * tw
+        self._geom = (th, tw)
+        dist = None
+        world, rank = 1, 0
+        if self.group is not None:
+            import torch.distributed as dist
+            world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
+        owner = placement(len(branches), world)
+        for bi, b in enumerate(branches):
+            if owner[bi] == rank:
+                self.prefill(b, Ltok)
+        if form is None:
+            form = {(-1, -1): L.CFG_NONE}.get((i_img, i_unc), L.CFG_NONE)
+        n = H * W * 3
+        if init_noise is not None:
+            img = init_noise.clone().reshape(H, W, 3).float().cuda()
+        else:
+            gen = torch.Generator(device="cuda").manual_seed(seed)
+            img = torch.randn(H, W, 3, device="cuda", generator=gen) * noise_scale
+        ts = time_schedule(steps, shift)
+        emb = torch.empty(Ltok, self.hidden, device="cuda", dtype=torch.bfloat16)
+        rows = torch.empty(Ltok, PIX * PIX * 3, device="cuda", dtype=torch.bfloat16)
+        hstate = torch.empty_like(emb)
+        x_pred = torch.empty(H, W, 3, device="cuda", dtype=torch.float32)
+        combined = torch.empty_like(x_pred)
+        ws = torch.empty(lib().u15c_cfg_workspace_bytes(), dtype=torch.uint8, device="cuda")
+        for b in branches:
+            b.v = torch.zeros(H, W, 3, device="cuda", dtype=torch.float32)
+        for step in range(steps):
+            t, t_next = ts[step], ts[step + 1]
+            self.image.embed(img, H, W, emb, rows)
+            self.ops.add_row(emb, self.image.timestep_row(t), Ltok, self.hidden)
+            denom = max(1.0 - t, t_eps)
+            lo, hi = cfg_interval
+            use_cfg = (lo < t < hi) or lo == 0.0
+            guided = form != L.CFG_NONE and use_cfg
+            n_branch = len(branches) if guided else 1
+            local = {}
+            for bi in range(n_branch):
+                if owner[bi] != rank:
+                    continue
+                b = branches[bi]
+                npre = b.prefix.shape[0]
+                hstate.copy_(emb)
+                self.m.forward(hstate, b.kv, npre, npre + Ltok, *b.pos,
+                               segments=[(0, Ltok, L.EXPERT_GEN)], int8=int8, sage=sage)
+                self.m.final_norm(hstate, L.EXPERT_GEN)
+                self.image.decode(hstate, H, W, rows, x_pred)
+                check(lib().u15c_velocity(_stream(), _p(x_pred), _p(img), _p(b.v), n, denom))
+                local[bi] = b.v
+            if world > 1:
+                vs = exchange_velocities(local, n_branch, n, self.group, device=img.device)
+                vs = [v.reshape(H, W, 3) for v in vs]
+            else:
+                vs = [branches[bi].v for bi in range(n_branch)]
+            if guided:
+                vu = vs[i_unc] if i_unc >= 0 else None
+                vi = vs[i_img] if i_img >= 0 else None
+                check(lib().u15c_cfg_combine(_stream(), _p(vs[0]), _p(vu), _p(vi),
+                                             _p(combined), H, W, form, cfg_norm, cfg, icfg, step,
+                                             _p(ws)))
+                v = combined
+            else:
+                v = vs[0]
+            check(lib().u15c_euler(_stream(), _p(img), _p(v), n, t_next - t))
+            if step_callback is not None:
+                step_callback(step, img)
+        return img
+
+
+L_CAUSAL = L.ATTN_CAUSAL
+L_BLOCK = L.ATTN_BLOCK_CAUSAL
