@@ -34,10 +34,12 @@ def test_velocity_and_euler_exact(lib):
     xp, img, v = (randn((H, W, 3), s) for s in (1, 2, 3))
     n = H * W * 3
     out = torch.empty(H, W, 3, device="cuda")
-    assert lib.u15c_velocity(_st(), _p(dev_f32(xp)), _p(dev_f32(img)), _p(out), n, 0.37) == 0
+    # keep every device input referenced while the library uses its pointer
+    xp_d, img_d, v_d = dev_f32(xp), dev_f32(img), dev_f32(v)
+    assert lib.u15c_velocity(_st(), _p(xp_d), _p(img_d), _p(out), n, 0.37) == 0
     assert np.array_equal(host(out), O.velocity(xp, img, 0.37))
     d = dev_f32(img)
-    assert lib.u15c_euler(_st(), _p(d), _p(dev_f32(v)), n, -0.061) == 0
+    assert lib.u15c_euler(_st(), _p(d), _p(v_d), n, -0.061) == 0
     assert np.array_equal(host(d), O.euler(img, v, -0.061))
 
 
@@ -53,7 +55,8 @@ def test_cfg_forms(lib, form, norm, step):
     vc, vu, vi = randn((H, W, 3), 4), randn((H, W, 3), 5), randn((H, W, 3), 6)
     ws = torch.empty(lib.u15c_cfg_workspace_bytes(), dtype=torch.uint8, device="cuda")
     out = torch.empty(H, W, 3, device="cuda")
-    rc = lib.u15c_cfg_combine(_st(), _p(dev_f32(vc)), _p(dev_f32(vu)), _p(dev_f32(vi)), _p(out),
+    vc_d, vu_d, vi_d = dev_f32(vc), dev_f32(vu), dev_f32(vi)
+    rc = lib.u15c_cfg_combine(_st(), _p(vc_d), _p(vu_d), _p(vi_d), _p(out),
                               H, W, form, norm, 4.0, 1.5, step, _p(ws))
     assert rc == 0
     ref = O.cfg(vc, vu, vi, form, norm, 4.0, 1.5, step)
@@ -69,7 +72,8 @@ def test_pixel_packing(lib):
     H, W = 64, 96
     img = bf16_round(randn((H, W, 3), 7))
     rows = torch.empty((H // 32) * (W // 32), 3072, dtype=torch.bfloat16, device="cuda")
-    assert lib.u15c_patchify(_st(), _p(dev_f32(img)), _p(rows), H, W) == 0
+    img_d = dev_f32(img)
+    assert lib.u15c_patchify(_st(), _p(img_d), _p(rows), H, W) == 0
     ref = img.reshape(H // 32, 32, W // 32, 32, 3).transpose(0, 2, 1, 3, 4).reshape(-1, 3072)
     assert np.array_equal(host(rows), ref)
     back = torch.empty(H, W, 3, device="cuda")

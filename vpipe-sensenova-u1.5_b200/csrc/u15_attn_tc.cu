@@ -45,7 +45,7 @@ constexpr int kQBytes = 2 * kTile * 256;       // bf16: 2 tiles x [128][128]; in
 constexpr int kKBytes = kKeys * 256;           // bf16 [64][128] (2 boxes); int8 uses half
 constexpr int kVBytes = 128 * kKeys * 2;       // [128 dims][64 keys] bf16
 constexpr int kPBytes = kTile * kKeys * 2;     // [128 rows][64 keys] bf16
-constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 2 * kPBytes + 1024 + 512;
+constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 4 * kPBytes + 1024 + 512;
 
 struct TcAttnP {
   int hq, hkv, tq, tk, G, n_tiles;
@@ -74,6 +74,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 2^x on the MUFU unit (PTX ex2.approx.ftz.f32; relative error ~2^-22,
+// far below the bf16 rounding P receives).
+__device__ __forceinline__ float ex2(float x)
+{
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <bool SAGE>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -86,8 +94,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem;                                   // tile t at t * (kQBytes/2)
   uint8_t* sK = sQ + kQBytes;                           // stage s at s * kKBytes
   uint8_t* sV = sK + kStages * kKBytes;                 // stage s at s * kVBytes
-  uint8_t* sP = sV + kStages * kVBytes;                 // tile t at t * kPBytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint8_t* sP = sV + kStages * kVBytes;                 // tile t, buffer b at (2t + b) * kPBytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * kPBytes);
   // barrier slots
   const uint32_t b0 = smem_u32(bars);
   const uint32_t q_full = b0;
@@ -96,10 +104,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t k_empty = v_full + 8 * kStages;
   const uint32_t v_empty = k_empty + 8 * kStages;
   const uint32_t s_full = v_empty + 8 * kStages;        // [2 tiles][2 buffers]
-  const uint32_t p_full = s_full + 8 * 4;               // [2 tiles]
-  const uint32_t o_done = p_full + 8 * 2;               // [2 tiles]
-  const uint32_t drain = o_done + 8 * 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 4 + 2 + 2 + 1);
+  // p_full[t][b] / o_done[t][b]: P(t, j) written / P.V(t, j) completed, for
+  // j & 1 == b. One barrier per P buffer keeps every waiter within one phase
+  // of its barrier (parity waits cannot tell phases two apart).
+  const uint32_t p_full = s_full + 8 * 4;               // [2 tiles][2 buffers]
+  const uint32_t o_done = p_full + 8 * 4;               // [2 tiles][2 buffers]
+  const uint32_t drain = o_done + 8 * 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 4 + 4 + 4 + 1);
 
   const int w = (int)warp_id();
   const int h = blockIdx.y;
@@ -116,10 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(v_empty + 8 * s, 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(s_full + 8 * i, 1);
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(p_full + 8 * t, 128);
-      mbar_init(o_done + 8 * t, 1);
-    }
+    for (int i = 0; i < 4; ++i) mbar_init(p_full + 8 * i, 128);
+    for (int i = 0; i < 4; ++i) mbar_init(o_done + 8 * i, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
   }
@@ -217,15 +226,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t s = j % kStages;
         if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
         for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait(p_full + 8 * t, j & 1, p.err, kDevWaitFull)) { ok = false; break; }
+          if (!mbar_wait(p_full + 8 * (2 * t + (j & 1)), (j >> 1) & 1, p.err, kDevWaitFull)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t d = tmem + t * 256 + 128;
-          const uint32_t a0 = smem_u32(sP + t * kPBytes), b0 = smem_u32(sV + s * kVBytes);
+          const uint32_t a0 = smem_u32(sP + (2 * t + (j & 1)) * kPBytes),
+                         b0 = smem_u32(sV + s * kVBytes);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             mma_bf16(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), id_o,
                      (j | k) != 0);
-          mma_commit(o_done + 8 * t);
+          mma_commit(o_done + 8 * (2 * t + (j & 1)));
         }
         mma_commit(v_empty + 8 * s);
       }
@@ -240,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qi = q0 + t * kTile + row;     // query index within the head
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + t * 256 + lane_off, tO = tS + 128;
-    uint8_t* prow = sP + t * kPBytes + row * 128;
+    uint8_t* prow0 = sP + (2 * t) * kPBytes + row * 128;
     float sqv = 1.0f;
     if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
     float m_ref = -INFINITY, l = 0.0f;
@@ -255,17 +268,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tS + (j & 1) * 64, r0);
       tmem_ld32(tS + (j & 1) * 64 + 32, r1);
       tmem_ld_wait();
+      // raw scores; the base-2 scale f > 0 is folded into the exponent's FFMA
       float s[64];
       float f = p.scale_log2;
       if constexpr (SAGE) f *= sqv * p.sk[(long)hk * p.nkb + j];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         if constexpr (SAGE) {
-          s[i] = (float)(int32_t)r0[i] * f;
-          s[32 + i] = (float)(int32_t)r1[i] * f;
+          s[i] = (float)(int32_t)r0[i];
+          s[32 + i] = (float)(int32_t)r1[i];
         } else {
-          s[i] = __uint_as_float(r0[i]) * f;
-          s[32 + i] = __uint_as_float(r1[i]) * f;
+          s[i] = __uint_as_float(r0[i]);
+          s[32 + i] = __uint_as_float(r1[i]);
         }
       }
       const int kmax = p.tk - j * kKeys;   // valid keys in this tile
@@ -274,18 +288,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 64; ++i)
           if (i >= kmax) s[i] = -INFINITY;
       }
-      float mt = s[0];
+      float mraw = s[0];
 #pragma unroll
-      for (int i = 1; i < 64; ++i) mt = fmaxf(mt, s[i]);
+      for (int i = 1; i < 64; ++i) mraw = fmaxf(mraw, s[i]);
+      const float mt = mraw * f;
       const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
       const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
-      bool waited = false;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // rescale this row's O (after the previous P.V has landed)
-        if (!mbar_wait(o_done + 8 * t, (j - 1) & 1, p.err, kDevWaitAccFull)) { ok = false; break; }
-        waited = true;
+        if (!mbar_wait(o_done + 8 * (2 * t + ((j - 1) & 1)), ((j - 1) >> 1) & 1, p.err,
+                       kDevWaitAccFull)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const float fac = need ? exp2f(m_ref - m_new) : 1.0f;
+        const float fac = need ? ex2(m_ref - m_new) : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -299,19 +316,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= fac;
       }
       m_ref = m_new;
+      const float nm = -m_ref;
       uint32_t pk[32];
       float rs = 0.0f;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float a = exp2f(s[2 * i] - m_ref), b = exp2f(s[2 * i + 1] - m_ref);
+        const float a = ex2(fmaf(s[2 * i], f, nm)), b = ex2(fmaf(s[2 * i + 1], f, nm));
         rs += a + b;
         pk[i] = pack_bf2(a, b);
       }
       l += rs;
-      if (j > 0 && !waited) {
-        if (!mbar_wait(o_done + 8 * t, (j - 1) & 1, p.err, kDevWaitAccFull)) { ok = false; break; }
+      // P buffer j&1 was last read by P.V(j-2)
+      if (j > 1) {
+        if (!mbar_wait(o_done + 8 * (2 * t + (j & 1)), ((j - 2) >> 1) & 1, p.err,
+                       kDevWaitAccFull)) {
+          ok = false;
+          break;
+        }
       }
       // P row: 64 keys = 8 chunks of 16 B, 128-byte swizzle
+      uint8_t* prow = prow0 + (j & 1) * kPBytes;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
@@ -319,9 +343,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full + 8 * t);
+      mbar_arrive(p_full + 8 * (2 * t + (j & 1)));
     }
-    if (ok && n > 0 && mbar_wait(o_done + 8 * t, (n - 1) & 1, p.err, kDevWaitAccFull)) {
+    if (ok && n > 0 &&
+        mbar_wait(o_done + 8 * (2 * t + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.err,
+                  kDevWaitAccFull)) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128;
