@@ -133,6 +133,14 @@ int u15c_mot_rms_norm(u15c_stream stream, const void* x, const void* w_stack, in
                       const int* seg_off, const int* seg_expert, int nseg, void* y, int rows,
                       int dim, float eps);
 
+/* RMSNorm fused with the W8A8 activation quantisation: the normed row, rounded
+ * to bf16 as u15c_mot_rms_norm stores it, quantised per token by the rule of
+ * u15c_quant_rows_i8 (codes bit-identical to the two calls in sequence).
+ * dim <= 4096, dim % 8 == 0. Feeds u15c_mot_linear_i8 directly. */
+int u15c_mot_rms_norm_quant_i8(u15c_stream stream, const void* x, const void* w_stack,
+                               int n_experts, const int* seg_off, const int* seg_expert, int nseg,
+                               int8_t* q, float* scale, int rows, int dim, float eps);
+
 /* MetalOps::split_qk_norm (src/u15-metal-ops.h:156-161,
  * src/u15-kernels.metal:50-87): in place on token-major [tokens][heads*128]. */
 int u15c_split_qk_norm(u15c_stream stream, void* x, const void* w_t, const void* w_hw,

@@ -53,6 +53,27 @@ def test_mot_rms_norm_routes_gains(ops):
     assert rel_l2(host(y), wrong) > 1e-2
 
 
+@pytest.mark.parametrize("rows,dim", [(5, 64), (300, 4096), (77, 2056)])
+def test_rms_norm_quant_fused_bit_exact(ops, rows, dim):
+    x = bf16_round(randn((rows, dim), 31))
+    w = bf16_round(randn((2, dim), 32, 0.2, 1.0))
+    segs = [(0, rows // 2, 1), (rows // 2, rows, 0)]
+    xd, wd = dev_bf16(x), dev_bf16(w)
+    y = torch.empty(rows, dim, dtype=torch.bfloat16, device="cuda")
+    ops.mot_rms_norm(xd, wd, segs, y, rows, dim, 1e-6)
+    q1 = torch.empty(rows, dim, dtype=torch.int8, device="cuda")
+    s1 = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ops.quant_rows_i8(y, q1, s1, rows, dim)
+    q2 = torch.empty_like(q1)
+    s2 = torch.empty_like(s1)
+    ops.mot_rms_norm_quant_i8(xd, wd, segs, q2, s2, rows, dim, 1e-6)
+    assert np.array_equal(host(q1), host(q2)) and np.array_equal(host(s1), host(s2))
+    # and against the restatement: quantise the oracle's bf16-rounded norm
+    ref = np.concatenate([bf16_round(O.rms_norm(x[a:b], w[e])) for a, b, e in segs])
+    rq, rs = O.quant_rows_i8(ref)
+    assert np.mean(host(q2) != rq) < 2e-3
+
+
 def test_rope_tables_fp64(ops):
     T = 257
     pt, ph, pw = positions(T, 5)

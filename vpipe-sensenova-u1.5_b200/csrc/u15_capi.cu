@@ -403,6 +403,21 @@ int u15c_mot_rms_norm(u15c_stream stream, const void* x, const void* w_stack, in
   LAUNCH(launch_rms_norm(x, w_stack, y, rows, dim, eps, seg, ST(stream)), "rms_norm");
 }
 
+int u15c_mot_rms_norm_quant_i8(u15c_stream stream, const void* x, const void* w_stack,
+                               int n_experts, const int* seg_off, const int* seg_expert, int nseg,
+                               int8_t* q, float* scale, int rows, int dim, float eps)
+{
+  if (x == nullptr || w_stack == nullptr || q == nullptr || scale == nullptr || dim <= 0 ||
+      dim % 8 || dim > 4096)
+    return fail(U15C_EINVAL, "rms_norm_quant: null buffer, or dim not a multiple of 8 up to 4096");
+  SegInfo seg;
+  std::string err;
+  if (!fill_seg(&seg, seg_off, seg_expert, nseg, rows, n_experts, &err))
+    return fail(U15C_EINVAL, "rms_norm_quant: " + err);
+  LAUNCH(launch_rms_norm_quant(x, w_stack, q, scale, rows, dim, eps, seg, ST(stream)),
+         "rms_norm_quant");
+}
+
 int u15c_split_qk_norm(u15c_stream stream, void* x, const void* w_t, const void* w_hw, int heads,
                        int tokens, int head_dim, float eps)
 {

@@ -93,6 +93,80 @@ __global__ void __launch_bounds__(kRmsThreads)
   }
 }
 
+// RMSNorm fused with the symmetric per-token int8 quantisation of its output
+// (the W8A8 path's activation half): the normed row is rounded to bf16 in
+// registers (the value the unfused path would store), its absmax reduced
+// over the CTA, and the codes written directly: q = rn_even(y / (amax/127)).
+// Codes are bit-identical to rms_norm followed by quant_rows. dim <= 4096.
+constexpr int kRmsQuantPer = 16;   // elements per thread: 256 x 16 = 4096
+__global__ void __launch_bounds__(kRmsThreads)
+    rms_norm_quant_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                          int8_t* __restrict__ q, float* __restrict__ scale, int rows, int dim,
+                          float eps, SegInfo seg)
+{
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + (long)row * dim;
+  const __nv_bfloat16* wr = w + (long)expert_of(row, seg) * dim;
+  __shared__ float red[kRmsThreads / 32];
+  float v[kRmsQuantPer];
+  float acc = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kRmsQuantPer / 8; ++k) {
+    const int c = (k * kRmsThreads + threadIdx.x) * 8;
+    float t[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c < dim) load8(xr + c, t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[k * 8 + i] = t[i];
+      acc += t[i] * t[i];
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane_id() == 0) red[warp_id()] = acc;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kRmsThreads / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / (float)dim + eps);
+  float m = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kRmsQuantPer / 8; ++k) {
+    const int c = (k * kRmsThreads + threadIdx.x) * 8;
+    float g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c < dim) load8(wr + c, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = bfround(v[k * 8 + i] * inv * g[i]);
+      v[k * 8 + i] = y;
+      m = fmaxf(m, fabsf(y));
+    }
+  }
+  m = warp_max(m);
+  __syncthreads();   // red[] reuse
+  if (lane_id() == 0) red[warp_id()] = m;
+  __syncthreads();
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kRmsThreads / 32; ++i) amax = fmaxf(amax, red[i]);
+  const float s = __fdiv_rn(amax, 127.0f);
+  if (threadIdx.x == 0) scale[row] = s;
+#pragma unroll
+  for (int k = 0; k < kRmsQuantPer / 8; ++k) {
+    const int c = (k * kRmsThreads + threadIdx.x) * 8;
+    if (c >= dim) continue;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int code = 0;
+      if (s > 0.0f) code = max(-127, min(127, __float2int_rn(__fdiv_rn(v[k * 8 + i], s))));
+      const uint32_t b = (uint32_t)(code & 0xff);
+      if (i < 4) lo |= b << (8 * i); else hi |= b << (8 * (i - 4));
+    }
+    *reinterpret_cast<uint2*>(q + (long)row * dim + c) = make_uint2(lo, hi);
+  }
+}
+
 // ---------------------------------------------------------------------
 // Split q/k RMSNorm (src/u15-kernels.metal:50-87): one warp per
 // (token, head) row of 128, lanes 0-15 own the t half [0,64) and lanes
@@ -448,6 +522,17 @@ int launch_rms_norm(const void* x, const void* w, void* y, int rows, int dim, fl
   rms_norm_kernel<<<rows, kRmsThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
                                                 static_cast<const __nv_bfloat16*>(w),
                                                 static_cast<__nv_bfloat16*>(y), rows, dim, eps, seg);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int launch_rms_norm_quant(const void* x, const void* w, int8_t* q, float* s, int rows, int dim,
+                          float eps, const SegInfo& seg, cudaStream_t st)
+{
+  if (rows <= 0) return 0;
+  if (dim > kRmsThreads * kRmsQuantPer || dim % 8) return 1;
+  rms_norm_quant_kernel<<<rows, kRmsThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                      static_cast<const __nv_bfloat16*>(w), q, s,
+                                                      rows, dim, eps, seg);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 

@@ -117,6 +117,9 @@ int sage_prepare(const void* q, const KvView& kv, int hq, int hkv, int tq, int t
 // bandwidth kernels (u15_elem.cu); all bf16 unless stated
 int launch_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,
                     const SegInfo& seg, cudaStream_t st);
+// RMSNorm + per-token int8 quantisation of the (bf16-rounded) output; dim <= 4096.
+int launch_rms_norm_quant(const void* x, const void* w, int8_t* q, float* s, int rows, int dim,
+                          float eps, const SegInfo& seg, cudaStream_t st);
 int launch_split_qk_norm(void* x, const void* w_t, const void* w_hw, int heads, int tokens,
                          float eps, cudaStream_t st);
 int launch_split_rope(void* x, const float* c, const float* s, int heads, int tokens,

@@ -238,8 +238,10 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
     return fail(U15C_EINVAL, "W8A8 requested but the model has no int8 twins "
                              "(create with U15C_MODEL_INT8 and call u15c_model_finalize)");
   int rc;
+  // prequant: the activation was already quantised into x8/s_tok (by the
+  // fused RMSNorm + quantisation), so the int8 path skips its own pass.
   auto gemm = [&](const void* in, int K, const bf16* w, const int8_t* w8, const float* ws, int N,
-                  int epi, void* y) -> int {
+                  int epi, void* y, bool prequant = false) -> int {
     u15::GemmArgs a;
     a.n_experts = E;
     a.M = n;
@@ -252,7 +254,7 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
     a.y = y;
     a.resid = epi == u15::kEpiResid ? x : nullptr;
     if (i8) {
-      if (u15::launch_quant_rows(in, m->x8, m->s_tok, n, K, st))
+      if (!prequant && u15::launch_quant_rows(in, m->x8, m->s_tok, n, K, st))
         return fail(U15C_ECUDA, "quant_rows launch failed");
       a.int8 = true;
       a.x = m->x8;
@@ -265,11 +267,19 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
     }
     return u15::run_gemm(a, st);
   };
+  // the layer norms: bf16 out, or (W8A8 with hidden <= 4096) fused with the
+  // activation quantisation
+  const bool fuse_q = i8 && H <= 4096;
+  auto norm = [&](const bf16* w) -> int {
+    const int r = fuse_q ? u15::launch_rms_norm_quant(x, w, m->x8, m->s_tok, n, H, (float)c.eps,
+                                                      seg, st)
+                         : u15::launch_rms_norm(x, w, m->xn, n, H, (float)c.eps, seg, st);
+    return r ? fail(U15C_ECUDA, "rms_norm launch failed") : U15C_OK;
+  };
 
   // ---- attention half (src/u15-backbone.cc:191-235) ----
-  if (u15::launch_rms_norm(x, L.ln_in, m->xn, n, H, (float)c.eps, seg, st))
-    return fail(U15C_ECUDA, "rms_norm launch failed");
-  if ((rc = gemm(m->xn, H, L.qkv, L.qkv8, L.qkv_s, m->qkv_n(), u15::kEpiStore, m->qkv)))
+  if ((rc = norm(L.ln_in))) return rc;
+  if ((rc = gemm(m->xn, H, L.qkv, L.qkv8, L.qkv_s, m->qkv_n(), u15::kEpiStore, m->qkv, fuse_q)))
     return rc;
   const u15::KvView view = kv->view(li);
   if (u15::launch_qkv_post(m->qkv, L.norms, m->rcos, m->rsin, m->qh, view, n, c.heads,
@@ -285,9 +295,8 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
   if ((rc = gemm(m->attn, m->qd(), L.o, L.o8, L.o_s, H, u15::kEpiResid, x))) return rc;
 
   // ---- MLP half (src/u15-backbone.cc:246-256) ----
-  if (u15::launch_rms_norm(x, L.ln_post, m->xn, n, H, (float)c.eps, seg, st))
-    return fail(U15C_ECUDA, "rms_norm launch failed");
-  if ((rc = gemm(m->xn, H, L.gu, L.gu8, L.gu_s, 2 * I, u15::kEpiSwiglu, m->h))) return rc;
+  if ((rc = norm(L.ln_post))) return rc;
+  if ((rc = gemm(m->xn, H, L.gu, L.gu8, L.gu_s, 2 * I, u15::kEpiSwiglu, m->h, fuse_q))) return rc;
   if ((rc = gemm(m->h, I, L.down, L.down8, L.down_s, H, u15::kEpiResid, x))) return rc;
   return U15C_OK;
 }

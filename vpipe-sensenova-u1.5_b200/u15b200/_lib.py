@@ -59,6 +59,8 @@ SIGNATURES = {
                                 ip, ip]),
     "u15c_rms_norm": (ip, [vp, vp, vp, vp, ip, ip, C.c_float]),
     "u15c_mot_rms_norm": (ip, [vp, vp, vp, ip, i32p, i32p, ip, vp, ip, ip, C.c_float]),
+    "u15c_mot_rms_norm_quant_i8": (ip, [vp, vp, vp, ip, i32p, i32p, ip, vp, vp, ip, ip,
+                                        C.c_float]),
     "u15c_split_qk_norm": (ip, [vp, vp, vp, vp, ip, ip, ip, C.c_float]),
     "u15c_split_rope": (ip, [vp, vp, vp, vp, ip, ip, ip, ip, ip]),
     "u15c_build_rope_tables": (ip, [vp, vp, vp, vp, ip, ip, ip, ip, C.c_double, C.c_double,

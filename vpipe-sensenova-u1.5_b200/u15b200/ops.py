@@ -83,6 +83,11 @@ class CudaOps:
         check(lib().u15c_mot_rms_norm(_stream(), _p(x), _p(w_stack), w_stack.shape[0], off, ex,
                                       n, _p(y), rows, dim, eps))
 
+    def mot_rms_norm_quant_i8(self, x, w_stack, segments, q, scale, rows, dim, eps):
+        off, ex, n = segments_arrays(segments, rows)
+        check(lib().u15c_mot_rms_norm_quant_i8(_stream(), _p(x), _p(w_stack), w_stack.shape[0],
+                                               off, ex, n, _p(q), _p(scale), rows, dim, eps))
+
     def split_qk_norm(self, x, w_t, w_hw, heads, tokens, head_dim, eps):
         check(lib().u15c_split_qk_norm(_stream(), _p(x), _p(w_t), _p(w_hw), heads, tokens,
                                        head_dim, eps))
