@@ -35,6 +35,7 @@
 #include "u15_kernels.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -318,6 +319,218 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------
+// The CTA-pair variant (tcgen05 cta_group::2): one 256x256 tile per pair of
+// SMs. CTA r of the pair loads A rows [m0 + 128r, +128) and B rows
+// [n0 + 128r, +128) -- half of each operand -- and the leader (r = 0)
+// issues M=256 N=256 MMAs that read both CTAs' halves; each CTA's TMEM
+// holds its own 128 rows x 256 columns of the accumulator. Per SM and
+// k-block that is 32 KB of operands for the same math the single-SM tile
+// needs 48 KB for, which is what the L2 -> SM path limits at int8 speed.
+// The leader's operand-full and accumulator-empty barriers count both
+// CTAs; its commits arrive on both CTAs' stage-empty and accumulator-full
+// barriers (multicast commit). No TMA multicast.
+// ---------------------------------------------------------------------
+constexpr int kStagesP = 6;
+constexpr int kAStageP = 128 * 128;   // per CTA: 128 rows x 128 B
+constexpr int kBStageP = 128 * 128;
+constexpr int kSmemP = kStagesP * (kAStageP + kBStageP) + 1024 + 256;
+
+template <bool I8, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const __grid_constant__ Params p)
+{
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStagesP * kAStageP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStagesP * kBStageP);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStagesP + 5);
+
+  const uint32_t full0 = smem_u32(bars);            // leader: count 2 (one per CTA) + tx
+  const uint32_t empty0 = full0 + 8 * kStagesP;     // each CTA: leader's multicast commit
+  const uint32_t accf0 = empty0 + 8 * kStagesP;     // each CTA: leader's multicast commit
+  const uint32_t acce0 = accf0 + 16;                // leader: 256 epilogue threads
+  const uint32_t drain = acce0 + 16;                // each CTA: leader's multicast commit
+
+  const uint32_t w = warp_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesP; ++s) {
+      mbar_init(full0 + 8 * s, 2);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf0 + 8 * a, 1);
+      mbar_init(acce0 + 8 * a, 256);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (w == 0) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  cluster_sync();   // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = p.n_units * p.n_nblk;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  constexpr int kBK = I8 ? 128 : 64;
+
+  if (w == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane_id() == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pair; t < n_tiles && ok; t += n_pairs) {
+        const Unit u = p.units[t % p.n_units];
+        const int nb = t / p.n_units;
+        const int arow = u.m0 + 128 * (int)rank;
+        const int brow = u.expert * p.N + nb * 256 + 128 * (int)rank;
+        for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
+          const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
+          if (!mbar_wait_cluster(empty0 + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = mapa_shared(full0 + 8 * s, 0);
+          mbar_arrive_expect_tx_cluster(fb, kAStageP + kBStageP);
+          tma_load_2d_pair(smem_u32(sA + s * kAStageP), &tmA, kb * kBK, arow, fb);
+          tma_load_2d_pair(smem_u32(sB + s * kBStageP), &tmB, kb * kBK, brow, fb);
+        }
+      }
+      // unwinding (leader): the last fill of every stage, both CTAs' halves,
+      // has landed once the leader's full barrier for it completes
+      if (leader) {
+        for (uint32_t s = 0; s < kStagesP; ++s) {
+          if (it > s) {
+            const uint32_t last = ((it - 1 - s) / kStagesP) * kStagesP + s;
+            mbar_wait_cluster(full0 + 8 * s, (last / kStagesP) & 1, p.err, kDevWaitDrain);
+          }
+        }
+      }
+    }
+  } else if (w == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (lane_id() == 0) {
+      if (leader) {
+        const uint32_t idesc = I8 ? idesc_s8(256, 256) : idesc_bf16(256, 256);
+        uint32_t it = 0;
+        int lt = 0;
+        bool ok = true;
+        for (int t = pair; t < n_tiles && ok; t += n_pairs, ++lt) {
+          const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+          if (!mbar_wait_cluster(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * 256;
+          for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
+            const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
+            if (!mbar_wait_cluster(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(sA + s * kAStageP);
+            const uint32_t b0 = smem_u32(sB + s * kBStageP);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = smem_desc_sw128(a0 + k * 32);
+              const uint64_t bd = smem_desc_sw128(b0 + k * 32);
+              if constexpr (I8)
+                mma_i8_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+              else
+                mma_bf16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            }
+            mma_commit_pair_mc(empty0 + 8 * s, 0x3);
+          }
+          if (!ok) break;
+          mma_commit_pair_mc(accf0 + 8 * acc, 0x3);
+        }
+        mma_commit_pair_mc(drain, 0x3);
+      }
+      // both CTAs: every MMA that writes this CTA's TMEM has completed
+      mbar_wait_cluster(drain, 0, p.err, kDevWaitDrain);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int wq = (int)(w & 3);
+    const int r_in = 128 * (int)rank + wq * 32 + (int)lane_id();
+    const uint32_t acce_leader0 = mapa_shared(acce0, 0);
+    int lt = 0;
+    for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
+      const Unit u = p.units[t % p.n_units];
+      const int nb = t / p.n_units;
+      const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
+      if (!mbar_wait_cluster(accf0 + 8 * acc, aph, p.err, kDevWaitAccFull)) break;
+      tc_fence_after();
+      const int row = u.m0 + r_in;
+      const bool row_ok = row >= u.row_lo && row < u.row_hi;
+      const uint32_t tb = tmem_base + acc * 256 + ((uint32_t)(wq * 32) << 16);
+      const int n0 = nb * 256;
+      if constexpr (EPI == kEpiSwiglu) {
+        const int nout = p.N / 2;
+        __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.y) + (long)row * p.ldy;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float g[32], v[32];
+          chunk_values<I8>(tb + c * 32, g, p, row, row_ok, n0 + c * 32, u.expert);
+          chunk_values<I8>(tb + 128 + c * 32, v, p, row, row_ok, n0 + 128 + c * 32, u.expert);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gg = bfround(g[i]), uu = bfround(v[i]);
+            g[i] = (gg / (1.0f + expf(-gg))) * uu;
+          }
+          const int oc = nb * 128 + c * 32;
+          if (row_ok) store_row32(yrow + oc, g, oc, nout);
+        }
+      } else {
+        __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.y) + (long)row * p.ldy;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float v[32];
+          const int col0 = n0 + c * 32;
+          chunk_values<I8>(tb + c * 32, v, p, row, row_ok, col0, u.expert);
+          if (!row_ok || col0 >= p.N) continue;
+          if (p.bias != nullptr) {
+            const __nv_bfloat16* b = p.bias + (long)u.expert * p.N + col0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.N) v[i] += bf2f(b[i]);
+          }
+          if constexpr (EPI == kEpiResid) {
+            float rr[32];
+            load_row32(p.resid + (long)row * p.ldr + col0, rr, col0, p.N);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = rr[i] + bfround(v[i]);
+          }
+          store_row32(yrow + col0, v, col0, p.N);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acce_leader0 + 8 * acc);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // the peer's smem and TMEM stay alive until the pair is done
+  if (w == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
 // ---------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------
@@ -422,6 +635,44 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, in
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
+template <bool I8, int EPI>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid,
+                cudaStream_t st)
+{
+  static bool attr_set = false;
+  auto k = gemm_tc_pair_kernel<I8, EPI>;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemP) !=
+        cudaSuccess)
+      return 2;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemP;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, ma, mb, p) == cudaSuccess ? 0 : 2;
+}
+
+// Which GEMM variant serves a call: the CTA pair by default, the single-SM
+// kernel when U15_GEMM_SINGLE is set (A/B measurement) or for tiny M.
+bool use_pair(int M)
+{
+  static const bool single = [] {
+    const char* e = std::getenv("U15_GEMM_SINGLE");
+    return e != nullptr && *e != '0';
+  }();
+  return !single && M > 128;
+}
+
 }  // namespace
 
 int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
@@ -475,9 +726,11 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
     *err = "gemm: segments must cover [0, M)";
     return 1;
   }
+  const bool pair = use_pair(a.M);
+  const int bm = pair ? 256 : kBM;
   int n_units = 0;
-  for (int m0 = 0; m0 < a.M; m0 += kBM) {
-    const int m1 = std::min(m0 + kBM, a.M);
+  for (int m0 = 0; m0 < a.M; m0 += bm) {
+    const int m1 = std::min(m0 + bm, a.M);
     for (int s = 0; s < nseg; ++s) {
       if (off[s + 1] < off[s]) {
         *err = "gemm: segment offsets must be non-decreasing";
@@ -503,11 +756,28 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
 
   CUtensorMap ma, mb;
   if (make_tma_2d(&ma, a.x, (uint64_t)a.M, (uint64_t)a.K, kBM, es, err)) return 2;
-  if (make_tma_2d(&mb, a.w, (uint64_t)a.N * a.n_experts, (uint64_t)a.K, kBN, es, err)) return 2;
+  if (make_tma_2d(&mb, a.w, (uint64_t)a.N * a.n_experts, (uint64_t)a.K, pair ? 128 : kBN, es,
+                  err))
+    return 2;
 
   const int tiles = p.n_units * p.n_nblk;
-  const int grid = std::min(tiles, a.num_sms > 0 ? a.num_sms : 148);
+  const int sms = a.num_sms > 0 ? a.num_sms : 148;
   int rc;
+  if (pair) {
+    const int grid = 2 * std::min(tiles, sms / 2);
+    if (a.int8) {
+      rc = a.epilogue == kEpiResid    ? launch_pair<true, kEpiResid>(ma, mb, p, grid, st)
+           : a.epilogue == kEpiSwiglu ? launch_pair<true, kEpiSwiglu>(ma, mb, p, grid, st)
+                                      : launch_pair<true, kEpiStore>(ma, mb, p, grid, st);
+    } else {
+      rc = a.epilogue == kEpiResid    ? launch_pair<false, kEpiResid>(ma, mb, p, grid, st)
+           : a.epilogue == kEpiSwiglu ? launch_pair<false, kEpiSwiglu>(ma, mb, p, grid, st)
+                                      : launch_pair<false, kEpiStore>(ma, mb, p, grid, st);
+    }
+    if (rc) *err = "gemm (CTA pair): kernel launch failed";
+    return rc;
+  }
+  const int grid = std::min(tiles, sms);
   if (a.int8) {
     rc = a.epilogue == kEpiResid    ? launch_one<true, kEpiResid>(ma, mb, p, grid, st)
          : a.epilogue == kEpiSwiglu ? launch_one<true, kEpiSwiglu>(ma, mb, p, grid, st)
