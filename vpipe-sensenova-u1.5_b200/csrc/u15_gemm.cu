@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int brow = u.expert * p.N + nb * 256 + 128 * (int)rank;
         for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
           const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
-          if (!mbar_wait_cluster(empty0 + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) {
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) {
             ok = false;
             break;
           }
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t s = 0; s < kStagesP; ++s) {
           if (it > s) {
             const uint32_t last = ((it - 1 - s) / kStagesP) * kStagesP + s;
-            mbar_wait_cluster(full0 + 8 * s, (last / kStagesP) & 1, p.err, kDevWaitDrain);
+            mbar_wait(full0 + 8 * s, (last / kStagesP) & 1, p.err, kDevWaitDrain);
           }
         }
       }
@@ -436,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t d_tmem = tmem_base + acc * 256;
           for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
             const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
-            if (!mbar_wait_cluster(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
+            if (!mbar_wait(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
               ok = false;
               break;
             }
@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit_pair_mc(drain, 0x3);
       }
       // both CTAs: every MMA that writes this CTA's TMEM has completed
-      mbar_wait_cluster(drain, 0, p.err, kDevWaitDrain);
+      mbar_wait(drain, 0, p.err, kDevWaitDrain);
     }
   } else {
     // ---------------- epilogue (warps 2..5, both CTAs) ----------------
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Unit u = p.units[t % p.n_units];
       const int nb = t / p.n_units;
       const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
-      if (!mbar_wait_cluster(accf0 + 8 * acc, aph, p.err, kDevWaitAccFull)) break;
+      if (!mbar_wait(accf0 + 8 * acc, aph, p.err, kDevWaitAccFull)) break;
       tc_fence_after();
       const int row = u.m0 + r_in;
       const bool row_ok = row >= u.row_lo && row < u.row_hi;
@@ -635,20 +635,18 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, in
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
+// Persistent grid for the CTA-pair kernel: as many pairs as can be resident
+// at once. Not every SM has a usable partner, so this can be fewer than
+// SMs / 2; launching more pairs than fit would run the excess pairs'
+// whole tile lists after the others and double the kernel's time.
 template <bool I8, int EPI>
-int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid,
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int tiles,
                 cudaStream_t st)
 {
   static bool attr_set = false;
+  static int max_pairs = 0;
   auto k = gemm_tc_pair_kernel<I8, EPI>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemP) !=
-        cudaSuccess)
-      return 2;
-    attr_set = true;
-  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemP;
   cfg.stream = st;
@@ -659,6 +657,18 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, i
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemP) !=
+        cudaSuccess)
+      return 2;
+    int n = 0;
+    cfg.gridDim = dim3(2);
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n <= 0) n = 64;
+    max_pairs = n;
+    attr_set = true;
+  }
+  const int grid = 2 * std::min(tiles, max_pairs);
+  cfg.gridDim = dim3(grid);
   return cudaLaunchKernelEx(&cfg, k, ma, mb, p) == cudaSuccess ? 0 : 2;
 }
 
@@ -764,15 +774,14 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   const int sms = a.num_sms > 0 ? a.num_sms : 148;
   int rc;
   if (pair) {
-    const int grid = 2 * std::min(tiles, sms / 2);
     if (a.int8) {
-      rc = a.epilogue == kEpiResid    ? launch_pair<true, kEpiResid>(ma, mb, p, grid, st)
-           : a.epilogue == kEpiSwiglu ? launch_pair<true, kEpiSwiglu>(ma, mb, p, grid, st)
-                                      : launch_pair<true, kEpiStore>(ma, mb, p, grid, st);
+      rc = a.epilogue == kEpiResid    ? launch_pair<true, kEpiResid>(ma, mb, p, tiles, st)
+           : a.epilogue == kEpiSwiglu ? launch_pair<true, kEpiSwiglu>(ma, mb, p, tiles, st)
+                                      : launch_pair<true, kEpiStore>(ma, mb, p, tiles, st);
     } else {
-      rc = a.epilogue == kEpiResid    ? launch_pair<false, kEpiResid>(ma, mb, p, grid, st)
-           : a.epilogue == kEpiSwiglu ? launch_pair<false, kEpiSwiglu>(ma, mb, p, grid, st)
-                                      : launch_pair<false, kEpiStore>(ma, mb, p, grid, st);
+      rc = a.epilogue == kEpiResid    ? launch_pair<false, kEpiResid>(ma, mb, p, tiles, st)
+           : a.epilogue == kEpiSwiglu ? launch_pair<false, kEpiSwiglu>(ma, mb, p, tiles, st)
+                                      : launch_pair<false, kEpiStore>(ma, mb, p, tiles, st);
     }
     if (rc) *err = "gemm (CTA pair): kernel launch failed";
     return rc;
