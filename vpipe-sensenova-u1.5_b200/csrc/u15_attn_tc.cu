@@ -39,13 +39,15 @@ namespace {
 
 constexpr int kTile = 128;      // query rows per MMA tile
 constexpr int kKeys = 64;       // keys per KV tile = one page
-constexpr int kStages = 3;
-constexpr int kThreads = 320;   // 10 warps
+constexpr int kStages = 2;
+constexpr int kSoftWarps = 8;                  // softmax warps per 128-row tile
+constexpr int kThreads = 64 + 2 * kSoftWarps * 32;   // producer, MMA, 2 x 8 softmax warps
 constexpr int kQBytes = 2 * kTile * 256;       // bf16: 2 tiles x [128][128]; int8 uses half
 constexpr int kKBytes = kKeys * 256;           // bf16 [64][128] (2 boxes); int8 uses half
 constexpr int kVBytes = 128 * kKeys * 2;       // [128 dims][64 keys] bf16
 constexpr int kPBytes = kTile * kKeys * 2;     // [128 rows][64 keys] bf16
-constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 4 * kPBytes + 1024 + 512;
+constexpr int kXBytes = 2 * 2 * 2 * kTile * 4;   // row-max exchange [tile][buf][half][row] f32
+constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 4 * kPBytes + kXBytes + 1024 + 768;
 
 struct TcAttnP {
   int hq, hkv, tq, tk, G, n_tiles;
@@ -95,7 +97,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sK = sQ + kQBytes;                           // stage s at s * kKBytes
   uint8_t* sV = sK + kStages * kKBytes;                 // stage s at s * kVBytes
   uint8_t* sP = sV + kStages * kVBytes;                 // tile t, buffer b at (2t + b) * kPBytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * kPBytes);
+  float* xchg = reinterpret_cast<float*>(sP + 4 * kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * kPBytes + kXBytes);
   // barrier slots
   const uint32_t b0 = smem_u32(bars);
   const uint32_t q_full = b0;
@@ -110,7 +113,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t p_full = s_full + 8 * 4;               // [2 tiles][2 buffers]
   const uint32_t o_done = p_full + 8 * 4;               // [2 tiles][2 buffers]
   const uint32_t drain = o_done + 8 * 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 4 + 4 + 4 + 1);
+  // xbar[t][q][b]: the two half-row warps of tile t, lane quadrant q have
+  // published their row maxima for iteration j (j & 1 == b); count 64.
+  const uint32_t xbar = drain + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 4 + 4 + 4 + 1 + 16);
 
   const int w = (int)warp_id();
   const int h = blockIdx.y;
@@ -127,7 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(v_empty + 8 * s, 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(s_full + 8 * i, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(p_full + 8 * i, 128);
+    for (int i = 0; i < 4; ++i) mbar_init(p_full + 8 * i, 2 * 128);
+    for (int i = 0; i < 16; ++i) mbar_init(xbar + 8 * i, 64);
     for (int i = 0; i < 4; ++i) mbar_init(o_done + 8 * i, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -247,55 +254,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int t = (w - 2) >> 2;              // tile
-    const int wq = w & 3;                    // TMEM lane quadrant
+    // 8 warps per tile: warp v of tile t serves TMEM lane quadrant w & 3 and
+    // column half v / 4 -- 32 of the tile's 64 S columns, 64 of the 128 O
+    // columns -- of 32 query rows. The two halves of a row exchange their row
+    // maxima each iteration through shared memory (bounded mbarrier waits);
+    // their row sums are combined once, at the end.
+    const int t = (w - 2) >> 3;
+    const int hh = ((w - 2) & 7) >> 2;
+    const int wq = w & 3;
     const int row = wq * 32 + (int)lane_id();
     const int qi = q0 + t * kTile + row;     // query index within the head
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const uint32_t tS = tmem + t * 256 + lane_off, tO = tS + 128;
+    const uint32_t tS = tmem + t * 256 + lane_off + hh * 32;
+    const uint32_t tO = tmem + t * 256 + lane_off + 128 + hh * 64;
     uint8_t* prow0 = sP + (2 * t) * kPBytes + row * 128;
+    float* xc = xchg + t * 2 * 2 * kTile;    // [buf][half][row]
+    const uint32_t xb = xbar + 8 * (t * 8 + wq * 2);
     float sqv = 1.0f;
     if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
     float m_ref = -INFINITY, l = 0.0f;
     bool ok = true;
+    // publish `v` for exchange round j and return the partner half's value
+    auto exchange = [&](int j, float v, float* other) -> bool {
+      xc[((j & 1) * 2 + hh) * kTile + row] = v;
+      mbar_arrive(xb + 8 * (j & 1));
+      if (!mbar_wait(xb + 8 * (j & 1), (j >> 1) & 1, p.err, kDevWaitAccFull)) return false;
+      *other = xc[((j & 1) * 2 + (hh ^ 1)) * kTile + row];
+      return true;
+    };
     for (int j = 0; j < n; ++j) {
       if (!mbar_wait(s_full + 8 * (t * 2 + (j & 1)), (j >> 1) & 1, p.err, kDevWaitAccFull)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t r0[32], r1[32];
+      uint32_t r0[32];
       tmem_ld32(tS + (j & 1) * 64, r0);
-      tmem_ld32(tS + (j & 1) * 64 + 32, r1);
       tmem_ld_wait();
       // raw scores; the base-2 scale f > 0 is folded into the exponent's FFMA
-      float s[64];
+      float s[32];
       float f = p.scale_log2;
       if constexpr (SAGE) f *= sqv * p.sk[(long)hk * p.nkb + j];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if constexpr (SAGE) {
-          s[i] = (float)(int32_t)r0[i];
-          s[32 + i] = (float)(int32_t)r1[i];
-        } else {
-          s[i] = __uint_as_float(r0[i]);
-          s[32 + i] = __uint_as_float(r1[i]);
-        }
+        if constexpr (SAGE) s[i] = (float)(int32_t)r0[i];
+        else s[i] = __uint_as_float(r0[i]);
       }
-      const int kmax = p.tk - j * kKeys;   // valid keys in this tile
-      if (kmax < kKeys) {
+      const int kmax = p.tk - j * kKeys - hh * 32;   // valid keys in this half
+      if (kmax < 32) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 32; ++i)
           if (i >= kmax) s[i] = -INFINITY;
       }
       float mraw = s[0];
 #pragma unroll
-      for (int i = 1; i < 64; ++i) mraw = fmaxf(mraw, s[i]);
+      for (int i = 1; i < 32; ++i) mraw = fmaxf(mraw, s[i]);
+      float mo;
+      if (!exchange(j, mraw, &mo)) { ok = false; break; }
+      mraw = fmaxf(mraw, mo);
       const float mt = mraw * f;
       const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
       const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // rescale this row's O (after the previous P.V has landed)
+        // rescale this half-row of O (after the previous P.V has landed)
         if (!mbar_wait(o_done + 8 * (2 * t + ((j - 1) & 1)), ((j - 1) >> 1) & 1, p.err,
                        kDevWaitAccFull)) {
           ok = false;
@@ -304,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float fac = need ? ex2(m_ref - m_new) : 1.0f;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_ld_wait();
@@ -317,10 +338,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       m_ref = m_new;
       const float nm = -m_ref;
-      uint32_t pk[32];
+      uint32_t pk[16];
       float rs = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float a = ex2(fmaf(s[2 * i], f, nm)), b = ex2(fmaf(s[2 * i + 1], f, nm));
         rs += a + b;
         pk[i] = pack_bf2(a, b);
@@ -334,25 +355,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
       }
-      // P row: 64 keys = 8 chunks of 16 B, 128-byte swizzle
+      // this half's 32 keys = chunks 4*hh .. 4*hh+3 of the 128-byte swizzled row
       uint8_t* prow = prow0 + (j & 1) * kPBytes;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         const uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(prow + (((hh * 4 + c) ^ (row & 7)) << 4)) = v;
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(p_full + 8 * (2 * t + (j & 1)));
     }
-    if (ok && n > 0 &&
+    float lo = 0.0f;
+    if (ok && n > 0 && exchange(n, l, &lo) &&
         mbar_wait(o_done + 8 * (2 * t + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.err,
                   kDevWaitAccFull)) {
       tc_fence_after();
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128;
+      const float lt = l + lo;
+      const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+      __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128 + hh * 64;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         tmem_ld32(tO + c * 32, o);
         tmem_ld_wait();
