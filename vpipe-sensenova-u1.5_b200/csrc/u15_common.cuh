@@ -266,14 +266,19 @@ __device__ __forceinline__ void cluster_sync()
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
                    "memory");
 }
+// Arrivals on a barrier of either CTA of the pair. Relaxed: a release here
+// would fence every earlier memory operation at cluster scope on each call
+// (a per-k-block stall for the producer), and neither caller needs one --
+// the operand bytes are tracked by the TMA transaction count, and the
+// epilogue's TMEM reads have completed (tcgen05.wait::ld) before it arrives.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
 {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes)
 {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
+  asm volatile("mbarrier.arrive.expect_tx.relaxed.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
                    cluster_addr),
                "r"(bytes)
                : "memory");
