@@ -336,6 +336,23 @@ def run_ours(args, rank, world, local):
             t = ev_time(fn, max(5, args.steps))
             kern[name] = {"ms": t, "tflops": 2.0 * M_TOK * K * N / t / 1e9}
             del w, y, xin
+        # the W8A8 projections (int8 x int8 -> int32, dequant epilogue)
+        xq = torch.randint(-127, 128, (M_TOK, I), device="cuda", dtype=torch.int8)
+        st_ = torch.rand(M_TOK, device="cuda") * 0.01
+        for name, (K, N) in GEMMS.items():
+            wq = torch.randint(-127, 128, (2, N, K), device="cuda", dtype=torch.int8)
+            sc = torch.rand(2, N, device="cuda") * 0.001
+            epi = {"gate_up": 2, "o": 1, "down": 1}.get(name, 0)
+            y = torch.zeros(M_TOK, N // 2 if epi == 2 else N, device="cuda").bfloat16()
+            xin = xq[:, :K].contiguous()
+            fn = lambda: ops.mot_linear_i8(xin, st_, wq, sc, segs, y, M_TOK, K, N,  # noqa
+                                           epilogue=epi, resid=y if epi == 1 else None)
+            for _ in range(3):
+                fn()
+            t = ev_time(fn, max(5, args.steps))
+            kern["i8_" + name] = {"ms": t, "tflops": 2.0 * M_TOK * K * N / t / 1e9,
+                                  "unit": "TOP/s"}
+            del wq, y, xin
         q = torch.randn(NH, M_TOK, HD, device="cuda").bfloat16()
         npg = (TK + 63) // 64
         kp = torch.randn(npg, KV, 64, HD, device="cuda").bfloat16()

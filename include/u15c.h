@@ -397,6 +397,28 @@ int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* s
                  const int32_t* pos_t, const int32_t* pos_h, const int32_t* pos_w, int attn,
                  const int32_t* t_index, unsigned flags, int (*stop)(void*), void* stop_ctx);
 
+/* One branch of a multi-branch pass (U15Backbone::PassSlot,
+ * src/u15-backbone.h:112-124). */
+typedef struct u15c_slot {
+  u15c_kv* kv;
+  int kv_off;              /* where this branch's K/V are written */
+  int kv_len;              /* keys attended */
+  const int32_t* pos_t;    /* device int32 [n] */
+  const int32_t* pos_h;
+  const int32_t* pos_w;
+  const int32_t* t_index;  /* block-causal only (device int32 [kv_len]) */
+} u15c_slot;
+
+/* U15Backbone::forward_many (src/u15-backbone.cc:279-432): every layer for
+ * every branch, layer-outermost. The branches' activations are one
+ * contiguous buffer x [nslots * n][hidden] (slot i at rows [i*n, (i+1)*n)),
+ * all routed to `expert`; the row-wise work of each layer (norms and the four
+ * projection GEMMs) runs once over all nslots * n rows, the attention and the
+ * K/V append per branch against its own cache. stop as u15c_forward. */
+int u15c_forward_many(u15c_model* m, u15c_stream stream, void* x, int n, const u15c_slot* slots,
+                      int nslots, int expert, int attn, unsigned flags, int (*stop)(void*),
+                      void* stop_ctx);
+
 /* U15Backbone::final_norm (src/u15-backbone.cc:140-148). */
 int u15c_final_norm(u15c_model* m, u15c_stream stream, void* x, int n, int expert);
 

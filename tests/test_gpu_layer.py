@@ -196,6 +196,42 @@ def test_stop_and_determinism(small):
     assert np.array_equal(outs[0], outs[1])
 
 
+def test_forward_many_equals_separate_passes(small):
+    """Branches through the stack together (one GEMM over all branches' rows)
+    give bit-identical results to one pass per branch."""
+    m, _ = small
+    T = 64
+    pos = [dev_i32(p) for p in grid_positions(0, 8, 8, 5)]
+    rng = np.random.default_rng(13)
+    pres = [bf16_round(rng.normal(0, 1, (1, npre, 128)).astype(np.float32)) for npre in
+            (9, 70, 3)]
+    xs = [bf16_round(randn((T, SMALL["hidden"]), 20 + i)) for i in range(3)]
+
+    def caches():
+        out = []
+        for kp in pres:
+            kv = m.make_cache(kp.shape[1] + T)
+            for layer in range(SMALL["n_layers"]):
+                kv.write(layer, False, dev_bf16(kp))
+                kv.write(layer, True, dev_bf16(kp * 0.5))
+            out.append(kv)
+        return out
+    sep = []
+    for x, kv, kp in zip(xs, caches(), pres):
+        xd = dev_bf16(x)
+        npre = kp.shape[1]
+        m.forward(xd, kv, npre, npre + T, *pos, segments=[(0, T, 1)])
+        sep.append(xd)
+    kvs = caches()
+    xb = dev_bf16(np.concatenate(xs))
+    slots = [{"kv": kv, "kv_off": kp.shape[1], "kv_len": kp.shape[1] + T, "pos": pos}
+             for kv, kp in zip(kvs, pres)]
+    m.forward_many(xb, T, slots)
+    torch.cuda.synchronize()
+    for i in range(3):
+        assert np.array_equal(host(xb[i * T:(i + 1) * T]), host(sep[i]))
+
+
 def test_layer_forward_host_matches_device(small):
     m, _ = small
     T = 64

@@ -224,16 +224,51 @@ int check_cfg(const u15c_config& c)
   return U15C_OK;
 }
 
-// Sequence the layer's steps on `st`. rcos/rsin already hold the tables.
-int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15::SegInfo& seg,
-               const int* seg_off, const int* seg_expert, int nseg, u15c_kv* kv, int kv_off,
-               int kv_len, int attn, const int32_t* t_index, unsigned flags)
+// One branch's share of a layer pass: its rows [row0, row0 + n) of the
+// activations, its cache and attention rule. (U15Backbone::PassSlot,
+// src/u15-backbone.h:112-124.)
+struct SlotRun {
+  int row0 = 0, n = 0;
+  u15c_kv* kv = nullptr;
+  int kv_off = 0, kv_len = 0, attn = 0;
+  const int32_t* t_index = nullptr;
+};
+
+// Restrict a row-segment map to rows [r0, r0 + n), renumbered from 0.
+u15::SegInfo slice_seg(const u15::SegInfo& g, int r0, int n)
+{
+  u15::SegInfo s;
+  s.nseg = 0;
+  for (int i = 0; i < g.nseg; ++i) {
+    const int lo = std::max(g.off[i], r0), hi = std::min(g.off[i + 1], r0 + n);
+    if (lo >= hi) continue;
+    s.off[s.nseg] = lo - r0;
+    s.expert[s.nseg] = g.expert[i];
+    ++s.nseg;
+    s.off[s.nseg] = hi - r0;
+  }
+  if (s.nseg == 0) {
+    s.nseg = 1;
+    s.off[0] = 0;
+    s.off[1] = n;
+    s.expert[0] = g.expert[0];
+  }
+  return s;
+}
+
+// One layer over every slot (U15Backbone::layer_step_, src/u15-backbone.cc:
+// 173-257). The row-wise steps -- both norms and all four projection GEMMs --
+// run once over all M rows of all slots; the QKV post-processing (into each
+// slot's own cache) and the attention (over each slot's own keys) run per
+// slot. rcos/rsin already hold the tables for all M rows.
+int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15::SegInfo& seg,
+               const int* seg_off, const int* seg_expert, int nseg,
+               const std::vector<SlotRun>& slots, unsigned flags)
 {
   const u15c_config& c = m->cfg;
   const LayerW& L = m->layers[li];
   const int E = c.n_experts, H = c.hidden, I = c.inter;
   const bool i8 = (flags & U15C_FWD_INT8) != 0;
-  const bool sage = (flags & U15C_FWD_SAGE) != 0 && attn == U15C_ATTN_BIDIRECTIONAL;
   if (i8 && L.qkv8 == nullptr)
     return fail(U15C_EINVAL, "W8A8 requested but the model has no int8 twins "
                              "(create with U15C_MODEL_INT8 and call u15c_model_finalize)");
@@ -244,7 +279,7 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
                   int epi, void* y, bool prequant = false) -> int {
     u15::GemmArgs a;
     a.n_experts = E;
-    a.M = n;
+    a.M = M;
     a.K = K;
     a.N = N;
     a.seg_off = seg_off;
@@ -254,7 +289,7 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
     a.y = y;
     a.resid = epi == u15::kEpiResid ? x : nullptr;
     if (i8) {
-      if (!prequant && u15::launch_quant_rows(in, m->x8, m->s_tok, n, K, st))
+      if (!prequant && u15::launch_quant_rows(in, m->x8, m->s_tok, M, K, st))
         return fail(U15C_ECUDA, "quant_rows launch failed");
       a.int8 = true;
       a.x = m->x8;
@@ -271,9 +306,9 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
   // activation quantisation
   const bool fuse_q = i8 && H <= 4096;
   auto norm = [&](const bf16* w) -> int {
-    const int r = fuse_q ? u15::launch_rms_norm_quant(x, w, m->x8, m->s_tok, n, H, (float)c.eps,
+    const int r = fuse_q ? u15::launch_rms_norm_quant(x, w, m->x8, m->s_tok, M, H, (float)c.eps,
                                                       seg, st)
-                         : u15::launch_rms_norm(x, w, m->xn, n, H, (float)c.eps, seg, st);
+                         : u15::launch_rms_norm(x, w, m->xn, M, H, (float)c.eps, seg, st);
     return r ? fail(U15C_ECUDA, "rms_norm launch failed") : U15C_OK;
   };
 
@@ -281,17 +316,24 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int n, const u15
   if ((rc = norm(L.ln_in))) return rc;
   if ((rc = gemm(m->xn, H, L.qkv, L.qkv8, L.qkv_s, m->qkv_n(), u15::kEpiStore, m->qkv, fuse_q)))
     return rc;
-  const u15::KvView view = kv->view(li);
-  if (u15::launch_qkv_post(m->qkv, L.norms, m->rcos, m->rsin, m->qh, view, n, c.heads,
-                           c.kv_heads, kv_off, (float)c.eps, seg, st))
-    return fail(U15C_ECUDA, "qkv_post launch failed");
-  if (attn == U15C_ATTN_BIDIRECTIONAL)
-    rc = u15::run_attention_tc(st, m->qh, view, kv->pages, m->attn, c.heads, c.kv_heads, n,
-                               kv_len, sage ? m->sage_ws : nullptr);
-  else
-    rc = u15::run_attention(st, m->qh, view, m->attn, c.heads, c.kv_heads, n, kv_len, attn,
-                            kv_off, t_index, nullptr);
-  if (rc) return rc;
+  for (const SlotRun& sl : slots) {
+    const u15::KvView view = sl.kv->view(li);
+    const u15::SegInfo sseg = slice_seg(seg, sl.row0, sl.n);
+    bf16* qh = m->qh + (long)sl.row0 * m->qd();
+    bf16* out = m->attn + (long)sl.row0 * m->qd();
+    if (u15::launch_qkv_post(m->qkv + (long)sl.row0 * m->qkv_n(), L.norms,
+                             m->rcos + (long)sl.row0 * 128, m->rsin + (long)sl.row0 * 128, qh,
+                             view, sl.n, c.heads, c.kv_heads, sl.kv_off, (float)c.eps, sseg, st))
+      return fail(U15C_ECUDA, "qkv_post launch failed");
+    const bool sage = (flags & U15C_FWD_SAGE) != 0 && sl.attn == U15C_ATTN_BIDIRECTIONAL;
+    if (sl.attn == U15C_ATTN_BIDIRECTIONAL)
+      rc = u15::run_attention_tc(st, qh, view, sl.kv->pages, out, c.heads, c.kv_heads, sl.n,
+                                 sl.kv_len, sage ? m->sage_ws : nullptr);
+    else
+      rc = u15::run_attention(st, qh, view, out, c.heads, c.kv_heads, sl.n, sl.kv_len, sl.attn,
+                              sl.kv_off, sl.t_index, nullptr);
+    if (rc) return rc;
+  }
   if ((rc = gemm(m->attn, m->qd(), L.o, L.o8, L.o_s, H, u15::kEpiResid, x))) return rc;
 
   // ---- MLP half (src/u15-backbone.cc:246-256) ----
@@ -588,8 +630,15 @@ int u15c_layer_forward(u15c_model* m, u15c_stream stream, int layer, void* x, in
   if (u15::launch_rope_tables(pos_t, pos_h, pos_w, n, 64, 32, m->cfg.theta_t, m->cfg.theta_hw,
                               m->rcos, m->rsin, st))
     return fail(U15C_ECUDA, "rope tables launch failed");
-  return layer_impl(m, st, layer, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, kv,
-                    kv_off, kv_len, attn, t_index, flags);
+  SlotRun sl;
+  sl.n = n;
+  sl.kv = kv;
+  sl.kv_off = kv_off;
+  sl.kv_len = kv_len;
+  sl.attn = attn;
+  sl.t_index = t_index;
+  return layer_impl(m, st, layer, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, {sl},
+                    flags);
 }
 
 int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* seg_off,
@@ -613,8 +662,63 @@ int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* s
     return fail(U15C_ECUDA, "rope tables launch failed");
   for (int li = 0; li < m->cfg.n_layers; ++li) {
     if (stop != nullptr && stop(stop_ctx) != 0) return fail(U15C_ESTOPPED, "stopped");
-    if ((rc = layer_impl(m, st, li, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, kv,
-                         kv_off, kv_len, attn, t_index, flags)))
+    SlotRun sl;
+    sl.n = n;
+    sl.kv = kv;
+    sl.kv_off = kv_off;
+    sl.kv_len = kv_len;
+    sl.attn = attn;
+    sl.t_index = t_index;
+    if ((rc = layer_impl(m, st, li, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, {sl},
+                         flags)))
+      return rc;
+  }
+  return U15C_OK;
+}
+
+int u15c_forward_many(u15c_model* m, u15c_stream stream, void* x, int n, const u15c_slot* slots,
+                      int nslots, int expert, int attn, unsigned flags, int (*stop)(void*),
+                      void* stop_ctx)
+{
+  if (m == nullptr || x == nullptr || slots == nullptr || nslots <= 0)
+    return fail(U15C_EINVAL, "forward_many: no branches to run");
+  if (expert < 0 || expert >= m->cfg.n_experts) return fail(U15C_EINVAL, "expert out of range");
+  int rc;
+  int max_kv = 0;
+  for (int i = 0; i < nslots; ++i) {
+    const u15c_slot& s = slots[i];
+    if ((rc = validate_pass(m, n, s.kv, s.kv_off, s.kv_len, attn, s.pos_t, s.pos_h, s.pos_w,
+                            s.t_index)))
+      return rc;
+    max_kv = std::max(max_kv, s.kv_len);
+  }
+  const int M = n * nslots;
+  if ((rc = m->ensure_scratch(M, max_kv))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<SlotRun> runs(nslots);
+  for (int i = 0; i < nslots; ++i) {
+    const u15c_slot& s = slots[i];
+    if (u15::launch_rope_tables(s.pos_t, s.pos_h, s.pos_w, n, 64, 32, m->cfg.theta_t,
+                                m->cfg.theta_hw, m->rcos + (long)i * n * 128,
+                                m->rsin + (long)i * n * 128, st))
+      return fail(U15C_ECUDA, "rope tables launch failed");
+    runs[i].row0 = i * n;
+    runs[i].n = n;
+    runs[i].kv = s.kv;
+    runs[i].kv_off = s.kv_off;
+    runs[i].kv_len = s.kv_len;
+    runs[i].attn = attn;
+    runs[i].t_index = s.t_index;
+  }
+  u15::SegInfo seg;
+  seg.nseg = 1;
+  seg.off[0] = 0;
+  seg.off[1] = M;
+  seg.expert[0] = expert;
+  const int off[2] = {0, M}, ex[1] = {expert};
+  for (int li = 0; li < m->cfg.n_layers; ++li) {
+    if (stop != nullptr && stop(stop_ctx) != 0) return fail(U15C_ESTOPPED, "stopped");
+    if ((rc = layer_impl(m, st, li, static_cast<bf16*>(x), M, seg, off, ex, 1, runs, flags)))
       return rc;
   }
   return U15C_OK;

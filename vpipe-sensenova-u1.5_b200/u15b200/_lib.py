@@ -43,6 +43,12 @@ class Config(C.Structure):
 
 
 vp, ip, i32p = C.c_void_p, C.c_int, C.POINTER(C.c_int)
+
+
+class Slot(C.Structure):
+    _fields_ = [("kv", C.c_void_p), ("kv_off", C.c_int), ("kv_len", C.c_int),
+                ("pos_t", C.c_void_p), ("pos_h", C.c_void_p), ("pos_w", C.c_void_p),
+                ("t_index", C.c_void_p)]
 STOP_FN = C.CFUNCTYPE(C.c_int, C.c_void_p)
 
 SIGNATURES = {
@@ -110,6 +116,8 @@ SIGNATURES = {
                                 vp, C.c_uint]),
     "u15c_forward": (ip, [vp, vp, vp, ip, i32p, i32p, ip, vp, ip, ip, vp, vp, vp, ip, vp,
                           C.c_uint, STOP_FN, vp]),
+    "u15c_forward_many": (ip, [vp, vp, vp, ip, C.POINTER(Slot), ip, ip, ip, C.c_uint, STOP_FN,
+                               vp]),
     "u15c_final_norm": (ip, [vp, vp, vp, ip, ip]),
     "u15c_layer_forward_host": (ip, [vp, vp, ip, vp, vp, ip, i32p, i32p, ip, vp, ip, ip, vp, vp,
                                      vp, ip, vp, C.c_uint]),

@@ -217,7 +217,11 @@ class Generator:
         ts = time_schedule(steps, shift)
         emb = torch.empty(Ltok, self.hidden, device="cuda", dtype=torch.bfloat16)
         rows = torch.empty(Ltok, PIX * PIX * 3, device="cuda", dtype=torch.bfloat16)
-        hstate = torch.empty_like(emb)
+        # one hidden state per branch this rank runs, contiguous, so the
+        # branches go through the stack together (u15c_forward_many)
+        mine = [bi for bi in range(len(branches)) if owner[bi] == rank]
+        hstate = torch.empty(max(len(mine), 1), Ltok, self.hidden, device="cuda",
+                             dtype=torch.bfloat16)
         x_pred = torch.empty(H, W, 3, device="cuda", dtype=torch.float32)
         combined = torch.empty_like(x_pred)
         ws = torch.empty(lib().u15c_cfg_workspace_bytes(), dtype=torch.uint8, device="cuda")
@@ -233,18 +237,25 @@ class Generator:
             guided = form != L.CFG_NONE and use_cfg
             n_branch = len(branches) if guided else 1
             local = {}
-            for bi in range(n_branch):
-                if owner[bi] != rank:
-                    continue
-                b = branches[bi]
-                npre = b.prefix.shape[0]
-                hstate.copy_(emb)
-                self.m.forward(hstate, b.kv, npre, npre + Ltok, *b.pos,
-                               segments=[(0, Ltok, L.EXPERT_GEN)], int8=int8, sage=sage)
-                self.m.final_norm(hstate, L.EXPERT_GEN)
-                self.image.decode(hstate, H, W, rows, x_pred)
-                check(lib().u15c_velocity(_stream(), _p(x_pred), _p(img), _p(b.v), n, denom))
-                local[bi] = b.v
+            run = [bi for bi in mine if bi < n_branch]
+            if run:
+                for i in range(len(run)):
+                    hstate[i].copy_(emb)
+                slots = []
+                for bi in run:
+                    b = branches[bi]
+                    npre = b.prefix.shape[0]
+                    slots.append({"kv": b.kv, "kv_off": npre, "kv_len": npre + Ltok,
+                                  "pos": b.pos})
+                self.m.forward_many(hstate[:len(run)], Ltok, slots, expert=L.EXPERT_GEN,
+                                    int8=int8, sage=sage)
+                for i, bi in enumerate(run):
+                    b = branches[bi]
+                    self.m.final_norm(hstate[i], L.EXPERT_GEN)
+                    self.image.decode(hstate[i], H, W, rows, x_pred)
+                    check(lib().u15c_velocity(_stream(), _p(x_pred), _p(img), _p(b.v), n,
+                                              denom))
+                    local[bi] = b.v
             if world > 1:
                 vs = exchange_velocities(local, n_branch, n, self.group, device=img.device)
                 vs = [v.reshape(H, W, 3) for v in vs]

@@ -101,6 +101,21 @@ class Model:
                                  _p(pos_t), _p(pos_h), _p(pos_w), attn, _p(t_index), flags, cb,
                                  None))
 
+    def forward_many(self, x, n, slots, expert=L.EXPERT_GEN, attn=L.ATTN_BIDIRECTIONAL,
+                     int8=False, sage=False, stop=None):
+        """x [len(slots) * n][hidden]; slots: list of dicts with kv, kv_off, kv_len,
+        pos (t, h, w device int32 tensors) and optional t_index."""
+        arr = (L.Slot * len(slots))()
+        for i, s in enumerate(slots):
+            pt, ph, pw = s["pos"]
+            arr[i] = L.Slot(s["kv"].h, s["kv_off"], s["kv_len"], pt.data_ptr(), ph.data_ptr(),
+                            pw.data_ptr(), s["t_index"].data_ptr() if s.get("t_index") is not None
+                            else None)
+        flags = (L.FWD_INT8 if int8 else 0) | (L.FWD_SAGE if sage else 0)
+        cb = L.STOP_FN(lambda _ctx: int(bool(stop()))) if stop is not None else L.STOP_FN()
+        check(lib().u15c_forward_many(self.h, _stream(), _p(x), n, arr, len(slots), expert, attn,
+                                      flags, cb, None))
+
     def final_norm(self, x, expert):
         check(lib().u15c_final_norm(self.h, _stream(), _p(x), x.shape[0], expert))
 
