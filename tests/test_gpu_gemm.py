@@ -182,3 +182,59 @@ def test_mot_linear_i8_routed_full_k(ops):
     rwq = rwq.reshape(2, N, K)
     ref = np.concatenate([O.gemm_i8(rxq[a:b], rwq[e]) for a, b, e in segs])
     assert np.array_equal(host(acc), ref)
+
+
+# ------------------------------------------------- split-tail schedule
+# Tile counts whose last round of the persistent schedule leaves at least
+# half of the B200's 74 SM pairs idle: those tiles run as half-width tiles
+# (each CTA stages 64 weight rows). Every row and column is checked.
+SPLIT_SEGS = [(0, 512, 0), (512, 2560, 1)]
+
+
+def test_split_tail_routed_bf16(ops):
+    M, K, N = 2560, 512, 2304   # 10 row blocks x 9 column blocks = 90 tiles
+    x = bf16_round(randn((M, K), 30))
+    w = bf16_round(randn((2, N, K), 31, 0.02))
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.mot_linear(dev_bf16(x), dev_bf16(w), SPLIT_SEGS, y, M, K, N)
+    ops.sync()
+    ref = np.concatenate([O.linear(x[a:b], w[e]) for a, b, e in SPLIT_SEGS])
+    assert rel_l2(host(y), ref) < BAR
+    # the tail's columns on their own (the last 34 tiles' column blocks)
+    assert rel_l2(host(y)[:, 1792:], ref[:, 1792:]) < BAR
+
+
+def test_split_tail_swiglu(ops):
+    M, K, I = 2560, 256, 1152   # gate+up 2304 rows: 90 tiles
+    x = bf16_round(randn((M, K), 32))
+    g = bf16_round(randn((I, K), 33, 0.05))
+    u = bf16_round(randn((I, K), 34, 0.05))
+    w = interleave_gate_up(g, u)[None]
+    y = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    ops.mot_linear(dev_bf16(x), dev_bf16(w), None, y, M, K, 2 * I, epilogue=EPI_SWIGLU)
+    ops.sync()
+    ref = O.swiglu(O.linear(x, g), O.linear(x, u))
+    assert rel_l2(host(y), ref) < BAR
+    assert rel_l2(host(y)[:, 896:], ref[:, 896:]) < BAR
+
+
+def test_split_tail_residual_i8_bit_exact(ops):
+    M, K, N = 2560, 256, 2304
+    x = bf16_round(randn((M, K), 35))
+    w = bf16_round(randn((2, N, K), 36, 0.02))
+    r = bf16_round(randn((M, N), 37))
+    xq, xs = quantised(ops, x)
+    wq, ws = quantised(ops, w.reshape(2 * N, K))
+    rd = dev_bf16(r)
+    acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+    ops.mot_linear_i8(xq, xs, wq.view(2, N, K), ws.view(2, N), SPLIT_SEGS, rd, M, K, N,
+                      epilogue=EPI_RESIDUAL, resid=rd, acc_dump=acc)
+    ops.sync()
+    rxq, rxs = O.quant_rows_i8(x)
+    rwq, rws = O.quant_rows_i8(w.reshape(2 * N, K))
+    rwq, rws = rwq.reshape(2, N, K), rws.reshape(2, N)
+    racc = np.concatenate([O.gemm_i8(rxq[a:b], rwq[e]) for a, b, e in SPLIT_SEGS])
+    assert np.array_equal(host(acc), racc)
+    deq = np.concatenate([O.dequant_i8(racc[a:b], rxs[a:b], rws[e]) for a, b, e in SPLIT_SEGS])
+    ref = bf16_round(r + bf16_round(deq))
+    assert rel_l2(host(rd), ref) < 2e-3

@@ -283,3 +283,33 @@ def test_full_width_c1_layer():
     ref, _, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos)
     check_layer(host(xd), x, ref, delta_bar=2e-2)
     m.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+def test_model_runs_on_its_own_device():
+    """A model created on GPU 1 keeps launching on GPU 1 after the caller's
+    current device moved to GPU 0 (u15c_init(0)), with results equal to the
+    same model built on GPU 0; both GEMM variants run (M > 128)."""
+    import u15b200
+    n_und, gh, gw = 64, 12, 16
+    T = n_und + gh * gw
+    segs = [(0, n_und, 0), (n_und, T, 1)]
+    pos = grid_positions(n_und, gh, gw, n_und)
+    x = bf16_round(randn((T, SMALL["hidden"]), 9))
+    outs = []
+    for d in (0, 1):
+        with torch.cuda.device(d):
+            m, _ = build(SMALL, 1)
+            kv = m.make_cache(T)
+            xd = dev_bf16(x)
+            pd = [dev_i32(p) for p in pos]
+            torch.cuda.synchronize(d)
+            u15b200.CudaOps(1 - d)   # the current device moves away from the model's
+            assert torch.cuda.current_device() == 1 - d
+            m.forward(xd, kv, 0, T, *pd, segments=segs)   # default stream
+            torch.cuda.synchronize(d)
+            outs.append(host(xd))
+            kv.close()
+            m.close()
+    assert np.array_equal(outs[0], outs[1])
+    assert rel_l2(outs[0], x) > 1e-3   # the layers ran

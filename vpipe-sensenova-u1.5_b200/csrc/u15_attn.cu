@@ -482,13 +482,9 @@ int attention(const AttnArgs& a, cudaStream_t st, std::string* err)
   const dim3 grid((a.tq + p.R - 1) / p.R, a.hkv);
   const int smem = sage ? (kRows * 128 + 2 * kKeys * 128 + 2 * kKeys * 256)
                         : (kRows * 256 + 2 * kKeys * 256 + 2 * kKeys * 256);
-  static bool attr_done[4] = {false, false, false, false};
+  static std::atomic<uint64_t> attr_done[4];
   auto launch = [&](auto kern, int which) {
-    if (!attr_done[which]) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      attr_done[which] = true;
-    }
-    kern<<<grid, kThreads, smem, st>>>(p);
+    if (smem_attr_once(kern, smem, attr_done[which])) kern<<<grid, kThreads, smem, st>>>(p);
   };
   if (sage)
     a.kv.v_t ? launch(attn_kernel<true, true>, 3) : launch(attn_kernel<true, false>, 2);

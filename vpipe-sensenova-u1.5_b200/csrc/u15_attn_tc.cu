@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 namespace u15 {
 
@@ -403,6 +404,408 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// =====================================================================
+// Version 2: 128-key blocks, one query row per softmax thread, P kept in
+// TMEM (written over its own S, read by the P.V MMA as the A operand), and
+// the two query tiles of a CTA in ping-pong: while the softmax warps of one
+// tile work, the tensor core runs the other tile's P.V and next S.
+//
+//   warp 0      TMA producer: Q once; per block j two K pages (four
+//               [64 keys][64 dims] boxes) and two transposed V pages
+//               ([128 dims][64 keys] each) into a 2-stage ring
+//   warp 1      MMA issuer, per block j and tile t (in this order):
+//                 wait P_t(j);  O_t += P_t(j) V_j   (A from TMEM)
+//                 S_t(j+1) = Q_t K_{j+1}^T          (overwrites P_t(j) in
+//                                                     issue order)
+//                 commit -> s_full[t]
+//               so s_full[t] completing means S_t(j+1) is ready AND every
+//               earlier P.V of the tile has finished: the softmax may
+//               rescale O_t and overwrite the S columns with P without
+//               another wait.
+//   warps 2-9   softmax, four warps per tile, one row per thread: the whole
+//               128-score row in registers, base-2 online softmax with lazy
+//               rescale (threshold 2^8), P as bf16 pairs into TMEM, final
+//               O / l to global token-major [tq][hq*128]
+// TMEM (512 columns): tile t at t*256: S_t / P_t [0,128) | O_t [128,256).
+//
+// Of each row's four 32-score chunks, kEmuMask selects the ones whose 2^x
+// is computed on the FMA pipe (ex2_fma) instead of the MUFU unit; the two
+// units then share the exponentials and neither bounds the softmax alone.
+// =====================================================================
+namespace v2 {
+
+constexpr int kTile = 128;
+constexpr int kBlk = 128;                       // keys per block: two pages
+constexpr int kStages = 2;
+constexpr int kThreads = 64 + 8 * 32;           // producer, MMA, 2 x 4 softmax warps
+constexpr int kQBytes = 2 * kTile * 256;        // bf16 Q, 2 tiles; int8 uses half
+constexpr int kKBytes = kBlk * 256;             // [2 dims blocks][128 keys][128 B]
+constexpr int kVBytes = 128 * kBlk * 2;         // [2 key blocks][128 dims][128 B]
+constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256;
+constexpr unsigned kEmuMask = 0x8;              // chunk 3 of 4: a quarter of the exponentials
+
+// 2^x for x <= 2^7 on the FMA pipe: x = n + f with n = rint(x) taken from
+// the low mantissa bits of x + 1.5 * 2^23, f in [-0.5, 0.5]; 2^f by a degree-3
+// polynomial fitted to minimise the relative error on that interval (max
+// relative error 7.5e-5, below the bf16 rounding P receives); 2^n added to
+// the exponent field. Inputs below -125 are clamped there (2^-125, a
+// normal float) so the exponent never underflows; masked scores (-inf) give
+// 2^-125 instead of 0, which no bf16 output can show.
+__device__ __forceinline__ float ex2_fma(float x)
+{
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const float f = x - (t - 12582912.0f);
+  float q = fmaf(0.05517132207751274f, f, 0.24261054396629333f);
+  q = fmaf(q, f, 0.6932609677314758f);
+  q = fmaf(q, f, 0.9999281167984009f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16])
+{
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A is M=128 lanes x K
+// bf16 packed two per 32-bit column.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate)
+{
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <bool SAGE>
+__global__ void __maxnreg__(200)
+    attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
+{
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kQBytes;
+  uint8_t* sV = sK + kStages * kKBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * kVBytes);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0;
+  const uint32_t k_full = b0 + 8;                 // [kStages]
+  const uint32_t v_full = k_full + 8 * kStages;
+  const uint32_t k_empty = v_full + 8 * kStages;
+  const uint32_t v_empty = k_empty + 8 * kStages;
+  const uint32_t s_full = v_empty + 8 * kStages;  // [2 tiles]
+  const uint32_t p_full = s_full + 16;            // [2 tiles], 128 arrivals
+  const uint32_t drain = p_full + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 2 + 2 + 1);
+
+  const int w = (int)warp_id();
+  const int h = blockIdx.y;
+  const int hk = h / p.G;
+  const int q0 = blockIdx.x * 2 * kTile;
+  const int n = (p.tk + kBlk - 1) / kBlk;
+  const int n_pg = (p.tk + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(k_full + 8 * s, 1);
+      mbar_init(v_full + 8 * s, 1);
+      mbar_init(k_empty + 8 * s, 1);
+      mbar_init(v_empty + 8 * s, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full + 8 * t, 1);
+      mbar_init(p_full + 8 * t, 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (w == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (w == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane_id() == 0) {
+      const int qrow = h * p.tq + q0;
+      if constexpr (SAGE) {
+        mbar_arrive_expect_tx(q_full, 2 * kTile * 128);
+        for (int t = 0; t < 2; ++t)
+          tma_load_2d(smem_u32(sQ + t * kTile * 128), &tmQ, 0, qrow + t * kTile, q_full);
+      } else {
+        mbar_arrive_expect_tx(q_full, 2 * kTile * 256);
+        for (int t = 0; t < 2; ++t)
+          for (int d = 0; d < 2; ++d)
+            tma_load_2d(smem_u32(sQ + t * kTile * 256 + d * kTile * 128), &tmQ, d * 64,
+                        qrow + t * kTile, q_full);
+      }
+      int nk = 0, nv = 0;   // blocks whose K / V loads were issued
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        // the block's two pages; past the last page the first one is loaded
+        // again (finite data under masked scores)
+        const int pg0 = 2 * j, pg1 = min(2 * j + 1, n_pg - 1);
+        const int page0 = p.page_table ? p.page_table[pg0] : pg0;
+        const int page1 = p.page_table ? p.page_table[pg1] : pg1;
+        if (!mbar_wait(k_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+        uint8_t* k_dst = sK + s * kKBytes;
+        if constexpr (SAGE) {
+          mbar_arrive_expect_tx(k_full + 8 * s, kBlk * 128);
+          const int krow = (int)(hk * p.k8_stride) + j * kBlk;
+          tma_load_2d(smem_u32(k_dst), &tmK, 0, krow, k_full + 8 * s);
+          tma_load_2d(smem_u32(k_dst + 64 * 128), &tmK, 0, krow + 64, k_full + 8 * s);
+        } else {
+          mbar_arrive_expect_tx(k_full + 8 * s, kKBytes);
+          for (int hf = 0; hf < 2; ++hf) {
+            const int krow = ((hf ? page1 : page0) * p.hkv + hk) * 64;
+            for (int d = 0; d < 2; ++d)
+              tma_load_2d(smem_u32(k_dst + d * kBlk * 128 + hf * 64 * 128), &tmK, d * 64, krow,
+                          k_full + 8 * s);
+          }
+        }
+        nk = j + 1;
+        if (!mbar_wait(v_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+        mbar_arrive_expect_tx(v_full + 8 * s, kVBytes);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_2d(smem_u32(sV + s * kVBytes + hf * 128 * 128), &tmV, 0,
+                      ((hf ? page1 : page0) * p.hkv + hk) * 128, v_full + 8 * s);
+        nv = j + 1;
+      }
+      // unwinding: every copy issued must land before the CTA may exit
+      mbar_wait(q_full, 0, p.err, kDevWaitDrain);
+      for (int s = 0; s < kStages; ++s) {
+        if (nk > s) {
+          const int last = ((nk - 1 - s) / kStages) * kStages + s;
+          mbar_wait(k_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
+        }
+        if (nv > s) {
+          const int last = ((nv - 1 - s) / kStages) * kStages + s;
+          mbar_wait(v_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
+        }
+      }
+    }
+  } else if (w == 1) {
+    // ------------------------------------------------------------ MMA
+    if (lane_id() == 0) {
+      const uint32_t id_s = SAGE ? idesc_s8(kTile, kBlk) : idesc_bf16(kTile, kBlk);
+      const uint32_t id_o = idesc_bf16(kTile, 128);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t d = tmem + t * 256;
+        const uint32_t kb = smem_u32(sK + (j % kStages) * kKBytes);
+        if constexpr (SAGE) {
+          const uint32_t a0 = smem_u32(sQ + t * kTile * 128);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(kb + k * 32), id_s, k != 0);
+        } else {
+          const uint32_t a0 = smem_u32(sQ + t * kTile * 256);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
+                     smem_desc_sw128(kb + (k >> 2) * kBlk * 128 + (k & 3) * 32), id_s, k != 0);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
+      if (ok && n > 0) {
+        ok = mbar_wait(k_full, 0, p.err, kDevWaitFull);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t) {
+            issue_s(t, 0);
+            mma_commit(s_full + 8 * t);
+          }
+          mma_commit(k_empty);
+        }
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const int s = j % kStages, s1 = (j + 1) % kStages;
+        if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
+        const uint32_t vb = smem_u32(sV + s * kVBytes);
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!mbar_wait(p_full + 8 * t, j & 1, p.err, kDevWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + t * 256 + 128, a = tmem + t * 256;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16_ts(d, a + k * 8, smem_desc_sw128(vb + (k >> 2) * 128 * 128 + (k & 3) * 32),
+                        id_o, (j | k) != 0);
+          if (j + 1 < n) {
+            if (t == 0 && !mbar_wait(k_full + 8 * s1, ((j + 1) / kStages) & 1, p.err,
+                                     kDevWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
+          mma_commit(s_full + 8 * t);
+        }
+        if (!ok) break;
+        mma_commit(v_empty + 8 * s);
+        if (j + 1 < n) mma_commit(k_empty + 8 * s1);
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.err, kDevWaitDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = (w - 2) >> 2;
+    const int wq = w & 3;
+    const int row = wq * 32 + (int)lane_id();
+    const int qi = q0 + t * kTile + row;
+    const uint32_t tS = tmem + t * 256 + ((uint32_t)(wq * 32) << 16);
+    const uint32_t tO = tS + 128;
+    float sqv = 1.0f;
+    if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
+    float m_ref = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      // warp-uniform: the TMEM loads and stores below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full + 8 * t, j & 1, p.err, kDevWaitAccFull))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[128];
+      tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tmem_ld_wait();
+      // base-2 scale of each 64-key half (Sage: per-block Q and K scales)
+      float f0 = p.scale_log2, f1 = p.scale_log2;
+      if constexpr (SAGE) {
+        const int kb0 = 2 * j, kb1 = min(2 * j + 1, p.nkb - 1);
+        f0 *= sqv * p.sk[(long)hk * p.nkb + kb0];
+        f1 *= sqv * p.sk[(long)hk * p.nkb + kb1];
+      }
+      float s[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        if constexpr (SAGE) s[i] = (float)(int32_t)r[i];
+        else s[i] = __uint_as_float(r[i]);
+      }
+      const int kmax = p.tk - j * kBlk;
+      if (kmax < kBlk) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= kmax) s[i] = -INFINITY;
+      }
+      float ma = s[0], mb = s[64];
+#pragma unroll
+      for (int i = 1; i < 64; ++i) {
+        ma = fmaxf(ma, s[i]);
+        mb = fmaxf(mb, s[64 + i]);
+      }
+      const float mt = fmaxf(ma * f0, mb * f1);
+      const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
+      const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O_t is final up to P.V(j-1): s_full[t] completed after it
+        const float fac = need ? ex2(m_ref - m_new) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
+          tmem_st32(tO + c * 32, o);
+        }
+        l *= fac;
+      }
+      m_ref = m_new;
+      const float nm = -m_ref;
+      float rs = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float fc = c < 2 ? f0 : f1;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
+          float a, b;
+          if ((kEmuMask >> c) & 1) {
+            a = ex2_fma(x0);
+            b = ex2_fma(x1);
+          } else {
+            a = ex2(x0);
+            b = ex2(x1);
+          }
+          rs += a + b;
+          pk[i] = pack_bf2(a, b);
+        }
+        // P chunk c -> columns [16c, 16c+16), whose scores were all read
+        tmem_st16(tS + 16 * c, pk);
+      }
+      tmem_st_wait();
+      l += rs;
+      tc_fence_before();
+      mbar_arrive(p_full + 8 * t);
+    }
+    // the commit after the last P.V of this tile
+    const bool fin = ok && n > 0 && mbar_wait(s_full + 8 * t, n & 1, p.err, kDevWaitAccFull);
+    if (__all_sync(0xffffffffu, fin)) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_ld_wait();
+        if (qi < p.tq) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            uint4 v;
+            v.x = pack_bf2(__uint_as_float(o[qd * 8 + 0]) * inv, __uint_as_float(o[qd * 8 + 1]) * inv);
+            v.y = pack_bf2(__uint_as_float(o[qd * 8 + 2]) * inv, __uint_as_float(o[qd * 8 + 3]) * inv);
+            v.z = pack_bf2(__uint_as_float(o[qd * 8 + 4]) * inv, __uint_as_float(o[qd * 8 + 5]) * inv);
+            v.w = pack_bf2(__uint_as_float(o[qd * 8 + 6]) * inv, __uint_as_float(o[qd * 8 + 7]) * inv);
+            d4[qd] = v;
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (w == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace v2
+
 }  // namespace
 
 int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
@@ -444,22 +847,29 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   }
   if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, kKeys, 128, 2, err))
     return 2;
-  static bool set0 = false, set1 = false;
+  static const bool use_v1 = [] {
+    const char* e = std::getenv("U15_ATTN_V2");
+    return !(e != nullptr && *e != '0');
+  }();
+  static std::atomic<uint64_t> set0, set1, set2, set3;
   const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
-  if (sage) {
-    if (!set1) {
-      cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-      set1 = true;
+  bool attr_ok;
+  if (!use_v1) {
+    if (sage) {
+      attr_ok = smem_attr_once(v2::attn_kernel<true>, v2::kSmem, set3);
+      if (attr_ok) v2::attn_kernel<true><<<grid, v2::kThreads, v2::kSmem, st>>>(mq, mk, mv, p);
+    } else {
+      attr_ok = smem_attr_once(v2::attn_kernel<false>, v2::kSmem, set2);
+      if (attr_ok) v2::attn_kernel<false><<<grid, v2::kThreads, v2::kSmem, st>>>(mq, mk, mv, p);
     }
-    attn_tc_kernel<true><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
+  } else if (sage) {
+    attr_ok = smem_attr_once(attn_tc_kernel<true>, kSmem, set1);
+    if (attr_ok) attn_tc_kernel<true><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
   } else {
-    if (!set0) {
-      cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-      set0 = true;
-    }
-    attn_tc_kernel<false><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
+    attr_ok = smem_attr_once(attn_tc_kernel<false>, kSmem, set0);
+    if (attr_ok) attn_tc_kernel<false><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
   }
-  if (cudaGetLastError() != cudaSuccess) {
+  if (!attr_ok || cudaGetLastError() != cudaSuccess) {
     *err = "attention (tcgen05): kernel launch failed";
     return 2;
   }

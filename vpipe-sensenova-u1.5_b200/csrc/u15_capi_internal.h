@@ -21,6 +21,26 @@ int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 
 int dev_init(int device);
+
+// Runs the enclosing C-ABI call on `device` (the one its model was created
+// on) and gives the caller back its own current device on return, so a
+// handle used from a thread or process whose current device differs still
+// launches where its memory lives.
+struct DeviceScope {
+  int prev = -1;
+  explicit DeviceScope(int device)
+  {
+    int cur = 0;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur != device && cudaSetDevice(device) == cudaSuccess)
+      prev = cur;
+  }
+  ~DeviceScope()
+  {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+};
 DevState* dev();   // state of the current device, initialised on first use
 
 bool fill_seg(SegInfo* s, const int* off, const int* ex, int nseg, int rows, int n_experts,

@@ -58,6 +58,7 @@ constexpr int kMaxUnits = 200;
 struct Params {
   int M, N, K;          // N: weight rows per expert (SWIGLU: 2x the output width)
   int n_units, n_nblk, n_kblk;
+  int n_full;           // tiles before the split tail (== n_units * n_nblk when none)
   void* y;
   long ldy;             // output row stride, elements
   const __nv_bfloat16* resid;
@@ -69,6 +70,32 @@ struct Params {
   unsigned* err;
   Unit units[kMaxUnits];
 };
+
+// Tile t of a launch. Tiles [0, n_full) are full width; each tile after
+// them (the last, partly filled round of the persistent schedule) runs as two
+// half-width tiles (half = 0, 1), so that round takes half as long.
+struct TileIdx {
+  int unit, nb, half;   // half: -1 full width
+};
+
+__device__ __forceinline__ TileIdx tile_at(const Params& p, int t)
+{
+  TileIdx r{0, 0, -1};
+  int tt = t;
+  if (t >= p.n_full) {
+    const int h = t - p.n_full;
+    tt = p.n_full + (h >> 1);
+    r.half = h & 1;
+  }
+  r.unit = tt % p.n_units;
+  r.nb = tt / p.n_units;
+  return r;
+}
+
+__host__ __device__ __forceinline__ int launch_tiles(const Params& p)
+{
+  return p.n_full + 2 * (p.n_units * p.n_nblk - p.n_full);
+}
 
 template <bool I8>
 __device__ __forceinline__ void chunk_values(uint32_t taddr, float (&v)[32], const Params& p,
@@ -340,7 +367,8 @@ constexpr int kSmemP = kStagesP * (kAStageP + kBStageP) + 1024 + 256;
 template <bool I8, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const __grid_constant__ Params p)
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ Params p)
 {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -378,13 +406,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 32) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmBh);
   }
   tc_fence_before();
   cluster_sync();   // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int n_tiles = p.n_units * p.n_nblk;
+  const int n_tiles = launch_tiles(p);
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
   constexpr int kBK = I8 ? 128 : 64;
 
@@ -394,10 +423,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int t = pair; t < n_tiles && ok; t += n_pairs) {
-        const Unit u = p.units[t % p.n_units];
-        const int nb = t / p.n_units;
+        const TileIdx ti = tile_at(p, t);
+        const Unit u = p.units[ti.unit];
+        const bool half = ti.half >= 0;
+        // B rows this CTA stages: its half of the tile's columns. A
+        // half-width SwiGLU tile keeps gate and up paired: CTA 0 takes 64
+        // gate rows, CTA 1 the 64 up rows that go with them.
+        const int boff = !half                 ? 128 * (int)rank
+                         : EPI == kEpiSwiglu   ? 128 * (int)rank + 64 * ti.half
+                                               : 128 * ti.half + 64 * (int)rank;
         const int arow = u.m0 + 128 * (int)rank;
-        const int brow = u.expert * p.N + nb * 256 + 128 * (int)rank;
+        const int brow = u.expert * p.N + ti.nb * 256 + boff;
+        const CUtensorMap* mb = half ? &tmBh : &tmB;
+        const uint32_t tx = kAStageP + (half ? kBStageP / 2 : kBStageP);
         for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
           const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) {
@@ -405,9 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t fb = mapa_shared(full0 + 8 * s, 0);
-          mbar_arrive_expect_tx_cluster(fb, kAStageP + kBStageP);
+          mbar_arrive_expect_tx_cluster(fb, tx);
           tma_load_2d_pair(smem_u32(sA + s * kAStageP), &tmA, kb * kBK, arow, fb);
-          tma_load_2d_pair(smem_u32(sB + s * kBStageP), &tmB, kb * kBK, brow, fb);
+          tma_load_2d_pair(smem_u32(sB + s * kBStageP), mb, kb * kBK, brow, fb);
         }
       }
       // unwinding (leader): the last fill of every stage, both CTAs' halves,
@@ -425,11 +463,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer (leader only) ----------------
     if (lane_id() == 0) {
       if (leader) {
-        const uint32_t idesc = I8 ? idesc_s8(256, 256) : idesc_bf16(256, 256);
+        const uint32_t idesc_full = I8 ? idesc_s8(256, 256) : idesc_bf16(256, 256);
+        const uint32_t idesc_half = I8 ? idesc_s8(256, 128) : idesc_bf16(256, 128);
         uint32_t it = 0;
         int lt = 0;
         bool ok = true;
         for (int t = pair; t < n_tiles && ok; t += n_pairs, ++lt) {
+          const uint32_t idesc = t < p.n_full ? idesc_full : idesc_half;
           const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
           if (!mbar_wait_cluster(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
           tc_fence_after();
@@ -469,35 +509,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t acce_leader0 = mapa_shared(acce0, 0);
     int lt = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
-      const Unit u = p.units[t % p.n_units];
-      const int nb = t / p.n_units;
+      const TileIdx ti = tile_at(p, t);
+      const Unit u = p.units[ti.unit];
+      const int nb = ti.nb;
+      const bool half = ti.half >= 0;
       const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
       if (!mbar_wait(accf0 + 8 * acc, aph, p.err, kDevWaitAccFull)) break;
       tc_fence_after();
       const int row = u.m0 + r_in;
       const bool row_ok = row >= u.row_lo && row < u.row_hi;
       const uint32_t tb = tmem_base + acc * 256 + ((uint32_t)(wq * 32) << 16);
-      const int n0 = nb * 256;
       if constexpr (EPI == kEpiSwiglu) {
+        // accumulator columns [0, gw) are gate rows, [gw, 2 gw) the matching up rows
         const int nout = p.N / 2;
+        const int gw = half ? 64 : 128;
+        const int gsub = half ? 64 * ti.half : 0;
         __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.y) + (long)row * p.ldy;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < gw / 32; ++c) {
           float g[32], v[32];
-          chunk_values<I8>(tb + c * 32, g, p, row, row_ok, n0 + c * 32, u.expert);
-          chunk_values<I8>(tb + 128 + c * 32, v, p, row, row_ok, n0 + 128 + c * 32, u.expert);
+          const int gc = nb * 256 + gsub + c * 32;
+          chunk_values<I8>(tb + c * 32, g, p, row, row_ok, gc, u.expert);
+          chunk_values<I8>(tb + gw + c * 32, v, p, row, row_ok, gc + 128, u.expert);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float gg = bfround(g[i]), uu = bfround(v[i]);
             g[i] = (gg / (1.0f + expf(-gg))) * uu;
           }
-          const int oc = nb * 128 + c * 32;
+          const int oc = nb * 128 + gsub + c * 32;
           if (row_ok) store_row32(yrow + oc, g, oc, nout);
         }
       } else {
+        const int n0 = nb * 256 + (half ? 128 * ti.half : 0);
+        const int nchunk = half ? 4 : 8;
         __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.y) + (long)row * p.ldy;
 #pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < nchunk; ++c) {
           float v[32];
           const int col0 = n0 + c * 32;
           chunk_values<I8>(tb + c * 32, v, p, row, row_ok, col0, u.expert);
@@ -623,16 +670,21 @@ template <bool I8, int EPI>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int grid,
                cudaStream_t st)
 {
-  static bool attr_set = false;   // per instantiation; benign race (idempotent)
+  static std::atomic<uint64_t> attr_set;
   auto k = gemm_tc_kernel<I8, EPI>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-        cudaSuccess)
-      return 2;
-    attr_set = true;
-  }
+  if (!smem_attr_once(k, kSmemBytes, attr_set)) return 2;
   k<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+// U15_GEMM_NO_SPLIT=1 keeps every tile full width (A/B measurement).
+bool no_split()
+{
+  static const bool v = [] {
+    const char* e = std::getenv("U15_GEMM_NO_SPLIT");
+    return e != nullptr && *e != '0';
+  }();
+  return v;
 }
 
 // Persistent grid for the CTA-pair kernel: as many pairs as can be resident
@@ -640,11 +692,11 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, in
 // SMs / 2; launching more pairs than fit would run the excess pairs'
 // whole tile lists after the others and double the kernel's time.
 template <bool I8, int EPI>
-int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int tiles,
-                cudaStream_t st)
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mbh, Params p,
+                int tiles, cudaStream_t st)
 {
-  static bool attr_set = false;
-  static int max_pairs = 0;
+  static std::atomic<uint64_t> attr_set;
+  static std::atomic<int> max_pairs_dev[64];   // resident pairs, per device (0: not yet known)
   auto k = gemm_tc_pair_kernel<I8, EPI>;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kThreads);
@@ -657,19 +709,24 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, i
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemP) !=
-        cudaSuccess)
-      return 2;
-    int n = 0;
+  if (!smem_attr_once(k, kSmemP, attr_set)) return 2;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 2;
+  int max_pairs = max_pairs_dev[dev & 63].load(std::memory_order_relaxed);
+  if (max_pairs <= 0) {
     cfg.gridDim = dim3(2);
-    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n <= 0) n = 64;
-    max_pairs = n;
-    attr_set = true;
+    if (cudaOccupancyMaxActiveClusters(&max_pairs, k, &cfg) != cudaSuccess || max_pairs <= 0)
+      max_pairs = 64;
+    max_pairs_dev[dev & 63].store(max_pairs, std::memory_order_relaxed);
   }
-  const int grid = 2 * std::min(tiles, max_pairs);
-  cfg.gridDim = dim3(grid);
-  return cudaLaunchKernelEx(&cfg, k, ma, mb, p) == cudaSuccess ? 0 : 2;
+  const int pairs = std::min(tiles, max_pairs);
+  // Split tail: when the last round of the persistent schedule would leave
+  // at least half the pairs idle, its tiles run as half-width tiles, which
+  // all fit in one round of half the length.
+  const int rest = tiles % pairs;
+  p.n_full = (rest > 0 && 2 * rest <= pairs && !no_split()) ? tiles - rest : tiles;
+  cfg.gridDim = dim3(2 * pairs);
+  return cudaLaunchKernelEx(&cfg, k, ma, mb, mbh, p) == cudaSuccess ? 0 : 2;
 }
 
 // Which GEMM variant serves a call: the CTA pair by default, the single-SM
@@ -761,13 +818,16 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   }
   p.n_units = n_units;
   p.n_nblk = (a.N + kBN - 1) / kBN;
+  p.n_full = n_units * p.n_nblk;
   const int bk = a.int8 ? 128 : 64;
   p.n_kblk = (a.K + bk - 1) / bk;
 
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mbh;
   if (make_tma_2d(&ma, a.x, (uint64_t)a.M, (uint64_t)a.K, kBM, es, err)) return 2;
   if (make_tma_2d(&mb, a.w, (uint64_t)a.N * a.n_experts, (uint64_t)a.K, pair ? 128 : kBN, es,
                   err))
+    return 2;
+  if (pair && make_tma_2d(&mbh, a.w, (uint64_t)a.N * a.n_experts, (uint64_t)a.K, 64, es, err))
     return 2;
 
   const int tiles = p.n_units * p.n_nblk;
@@ -775,13 +835,13 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   int rc;
   if (pair) {
     if (a.int8) {
-      rc = a.epilogue == kEpiResid    ? launch_pair<true, kEpiResid>(ma, mb, p, tiles, st)
-           : a.epilogue == kEpiSwiglu ? launch_pair<true, kEpiSwiglu>(ma, mb, p, tiles, st)
-                                      : launch_pair<true, kEpiStore>(ma, mb, p, tiles, st);
+      rc = a.epilogue == kEpiResid    ? launch_pair<true, kEpiResid>(ma, mb, mbh, p, tiles, st)
+           : a.epilogue == kEpiSwiglu ? launch_pair<true, kEpiSwiglu>(ma, mb, mbh, p, tiles, st)
+                                      : launch_pair<true, kEpiStore>(ma, mb, mbh, p, tiles, st);
     } else {
-      rc = a.epilogue == kEpiResid    ? launch_pair<false, kEpiResid>(ma, mb, p, tiles, st)
-           : a.epilogue == kEpiSwiglu ? launch_pair<false, kEpiSwiglu>(ma, mb, p, tiles, st)
-                                      : launch_pair<false, kEpiStore>(ma, mb, p, tiles, st);
+      rc = a.epilogue == kEpiResid    ? launch_pair<false, kEpiResid>(ma, mb, mbh, p, tiles, st)
+           : a.epilogue == kEpiSwiglu ? launch_pair<false, kEpiSwiglu>(ma, mb, mbh, p, tiles, st)
+                                      : launch_pair<false, kEpiStore>(ma, mb, mbh, p, tiles, st);
     }
     if (rc) *err = "gemm (CTA pair): kernel launch failed";
     return rc;

@@ -6,9 +6,28 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 namespace u15 {
+
+// Kernel attributes are per device: a process that drives several GPUs
+// (or that switches its current device between calls) must set a kernel's
+// dynamic shared-memory limit on each of them. `done` holds one bit per
+// device; the attribute is set the first time a launch meets a device.
+template <class Kernel>
+inline bool smem_attr_once(Kernel kern, int bytes, std::atomic<uint64_t>& done)
+{
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (d & 63);
+  if (done.load(std::memory_order_acquire) & bit) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return false;
+  done.fetch_or(bit, std::memory_order_release);
+  return true;
+}
 
 enum Epilogue { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2 };
 

@@ -25,6 +25,7 @@
 
 using u15::fail;
 using u15::cuda_fail;
+using u15::DeviceScope;
 
 namespace {
 
@@ -412,12 +413,18 @@ int u15c_model_create(const u15c_config* cfg, unsigned flags, u15c_model** out)
   return U15C_OK;
 }
 
-void u15c_model_destroy(u15c_model* m) { delete m; }
+void u15c_model_destroy(u15c_model* m)
+{
+  if (m == nullptr) return;
+  DeviceScope ds(m->device);
+  delete m;
+}
 
 int u15c_model_bind(u15c_model* m, u15c_stream stream, int layer, int expert, int tensor,
                     const void* src, int dtype, int src_on_host)
 {
   if (m == nullptr || src == nullptr) return fail(U15C_EINVAL, "null argument");
+  DeviceScope ds(m->device);
   const u15c_config& c = m->cfg;
   if (expert < 0 || expert >= c.n_experts) return fail(U15C_EINVAL, "expert out of range");
   if (tensor != U15C_T_FINAL_NORM && (layer < 0 || layer >= c.n_layers))
@@ -476,6 +483,7 @@ int u15c_model_bind_random(u15c_model* m, u15c_stream stream, uint64_t seed, flo
                            float norm_mean, float norm_std)
 {
   if (m == nullptr) return fail(U15C_EINVAL, "null model");
+  DeviceScope ds(m->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const u15c_config& c = m->cfg;
   const long E = c.n_experts, H = c.hidden, I = c.inter, QD = m->qd(), QKV = m->qkv_n();
@@ -501,6 +509,7 @@ int u15c_model_finalize(u15c_model* m, u15c_stream stream)
 {
   if (m == nullptr) return fail(U15C_EINVAL, "null model");
   if (!(m->flags & U15C_MODEL_INT8)) return U15C_OK;
+  DeviceScope ds(m->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const u15c_config& c = m->cfg;
   const int E = c.n_experts, H = c.hidden, I = c.inter, QD = m->qd(), QKV = m->qkv_n();
@@ -538,6 +547,7 @@ int u15c_kv_create(u15c_model* m, int capacity, u15c_kv** out)
   if (m == nullptr || out == nullptr) return fail(U15C_EINVAL, "null argument");
   *out = nullptr;
   if (capacity <= 0) return fail(U15C_EINVAL, "capacity must be positive");
+  DeviceScope ds(m->device);
   auto* kv = new u15c_kv();
   kv->m = m;
   kv->capacity = capacity;
@@ -559,7 +569,12 @@ int u15c_kv_create(u15c_model* m, int capacity, u15c_kv** out)
   return U15C_OK;
 }
 
-void u15c_kv_destroy(u15c_kv* kv) { delete kv; }
+void u15c_kv_destroy(u15c_kv* kv)
+{
+  if (kv == nullptr) return;
+  DeviceScope ds(kv->m->device);
+  delete kv;
+}
 
 int u15c_kv_capacity(const u15c_kv* kv) { return kv ? kv->capacity : 0; }
 
@@ -582,6 +597,7 @@ int u15c_kv_read(u15c_kv* kv, u15c_stream stream, int layer, int which_v, void* 
   if (kv == nullptr || out == nullptr || n <= 0 || n > kv->capacity || layer < 0 ||
       layer >= kv->m->cfg.n_layers)
     return fail(U15C_EINVAL, "kv_read: bad argument");
+  DeviceScope ds(kv->m->device);
   if (u15::launch_kv_copy(out, kv->view(layer), which_v != 0, false, n, kv->m->cfg.kv_heads,
                           static_cast<cudaStream_t>(stream)))
     return fail(U15C_ECUDA, "kv_read: launch failed");
@@ -593,6 +609,7 @@ int u15c_kv_write(u15c_kv* kv, u15c_stream stream, int layer, int which_v, const
   if (kv == nullptr || in == nullptr || n <= 0 || n > kv->capacity || layer < 0 ||
       layer >= kv->m->cfg.n_layers)
     return fail(U15C_EINVAL, "kv_write: bad argument");
+  DeviceScope ds(kv->m->device);
   if (u15::launch_kv_copy(const_cast<void*>(in), kv->view(layer), which_v != 0, true, n,
                           kv->m->cfg.kv_heads, static_cast<cudaStream_t>(stream)))
     return fail(U15C_ECUDA, "kv_write: launch failed");
@@ -621,6 +638,7 @@ int u15c_layer_forward(u15c_model* m, u15c_stream stream, int layer, void* x, in
   if (rc) return rc;
   if (layer < 0 || layer >= m->cfg.n_layers) return fail(U15C_EINVAL, "layer out of range");
   if (x == nullptr) return fail(U15C_EINVAL, "null activations");
+  DeviceScope ds(m->device);
   u15::SegInfo seg;
   std::string err;
   if (!u15::fill_seg(&seg, seg_off, seg_expert, nseg, n, m->cfg.n_experts, &err))
@@ -649,6 +667,7 @@ int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* s
   int rc = validate_pass(m, n, kv, kv_off, kv_len, attn, pos_t, pos_h, pos_w, t_index);
   if (rc) return rc;
   if (x == nullptr) return fail(U15C_EINVAL, "null activations");
+  DeviceScope ds(m->device);
   u15::SegInfo seg;
   std::string err;
   if (!u15::fill_seg(&seg, seg_off, seg_expert, nseg, n, m->cfg.n_experts, &err))
@@ -683,6 +702,7 @@ int u15c_forward_many(u15c_model* m, u15c_stream stream, void* x, int n, const u
   if (m == nullptr || x == nullptr || slots == nullptr || nslots <= 0)
     return fail(U15C_EINVAL, "forward_many: no branches to run");
   if (expert < 0 || expert >= m->cfg.n_experts) return fail(U15C_EINVAL, "expert out of range");
+  DeviceScope ds(m->device);
   int rc;
   int max_kv = 0;
   for (int i = 0; i < nslots; ++i) {
@@ -728,6 +748,7 @@ int u15c_final_norm(u15c_model* m, u15c_stream stream, void* x, int n, int exper
 {
   if (m == nullptr || x == nullptr || expert < 0 || expert >= m->cfg.n_experts)
     return fail(U15C_EINVAL, "final_norm: bad argument");
+  DeviceScope ds(m->device);
   u15::SegInfo seg;
   seg.nseg = 1;
   seg.off[0] = 0;
@@ -748,6 +769,7 @@ int u15c_layer_forward_host(u15c_model* m, u15c_stream stream, int layer, const 
 {
   if (m == nullptr || x_host == nullptr || out_host == nullptr)
     return fail(U15C_EINVAL, "layer_forward_host: null argument");
+  DeviceScope ds(m->device);
   int rc = m->ensure_scratch(n, kv_len);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

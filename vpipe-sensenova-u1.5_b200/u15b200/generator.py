@@ -160,9 +160,10 @@ class Branch:
 class Generator:
     """Generator::generate over a u15b200.Model (both experts bound)."""
 
-    def __init__(self, model, image_path=None, device: int = 0, group=None):
+    def __init__(self, model, image_path=None, device: int | None = None, group=None):
         self.m = model
-        self.ops = CudaOps(device)
+        # the model's device is the caller's current one (one process per GPU)
+        self.ops = CudaOps(torch.cuda.current_device() if device is None else device)
         self.hidden = model.cfg["hidden"]
         self.image = image_path or LinearImagePath(self.hidden)
         self.group = group
