@@ -48,6 +48,7 @@ typedef void* u15c_stream; /* a cudaStream_t (NULL: the legacy default stream) *
 #define U15C_EPI_STORE 0    /* y = acc (+ bias) */
 #define U15C_EPI_RESIDUAL 1 /* y = resid + acc (o_proj / down_proj + add) */
 #define U15C_EPI_SWIGLU 2   /* gate|up rows interleaved in 128-row blocks: y = silu(g)*u */
+#define U15C_EPI_STORE_F32 3 /* y f32 [M][N] = acc (+ bias): a row-parallel partial product */
 
 #define U15C_ATTN_BIDIRECTIONAL 0 /* Attn::Bidirectional, src/u15-backbone.h:48-57 */
 #define U15C_ATTN_CAUSAL 1        /* Attn::Causal */
@@ -334,6 +335,25 @@ typedef struct u15c_config {
  * cfg (all layers, all experts). */
 int u15c_model_create(const u15c_config* cfg, unsigned flags, u15c_model** out);
 void u15c_model_destroy(u15c_model* m);
+
+/* Tensor parallelism for one large render (no reference counterpart: the
+ * reference runs one device). Rank tp_rank of tp_size (1, 2, 4, 8) holds
+ * heads/tp q heads and kv_heads/tp kv heads (column-parallel q/k/v, KV cache
+ * sharded by kv head), inter/tp of the MLP (column-parallel gate/up), and
+ * the matching columns of o_proj and down_proj (row-parallel). cfg is the
+ * FULL model; u15c_model_bind takes full tensors and keeps this rank's
+ * share. Before a pass, install the all-reduce the row-parallel products
+ * need with u15c_model_set_allreduce. */
+int u15c_model_create_tp(const u15c_config* cfg, unsigned flags, int tp_rank, int tp_size,
+                         u15c_model** out);
+int u15c_model_tp(const u15c_model* m, int* tp_rank, int* tp_size);
+/* fn(ctx, count, stream): sum buf[0 : count) over the tensor-parallel ranks
+ * in place (f32), ordered after the work already on `stream` and before the
+ * work enqueued on it next (e.g. ncclAllReduce on that stream); 0 = ok.
+ * buf: device, at least tokens x hidden floats of the largest pass. */
+typedef int (*u15c_allreduce_fn)(void* ctx, long count, u15c_stream stream);
+int u15c_model_set_allreduce(u15c_model* m, u15c_allreduce_fn fn, void* ctx, float* buf,
+                             long buf_elems);
 
 /* U15Weights bind_bf16_/bind_matrix_ (src/u15-weights.cc:102-151,
  * 516-603): convert one tensor (f32/f16/bf16, host or device) to bf16 with

@@ -2,23 +2,40 @@
 // TMA), the denoise pass's attention (src/u15-metal-ops.cc:835-882 in the
 // reference: q head-major, every key of [prefix || block]).
 //
-// One CTA = 256 query rows of one head as two 128-row tiles that share
-// every K/V tile it loads. Warp roles:
-//   warp 0      TMA producer: Q once, then per 64-key tile one K page
-//               (2 boxes of [64 keys][64 dims]) and one transposed V page
-//               ([128 dims][64 keys]) into a 3-stage ring
-//   warp 1      MMA issuer (one thread):
-//                 S_t(j) = Q_t K_j^T     M=128 N=64  K=128  -> TMEM (2 buffers per tile)
-//                 O_t   += P_t(j) V_j    M=128 N=128 K=64   -> TMEM (one per tile)
-//               with S(j+1) issued before O(j) so the tensor core works on
-//               the next tile while the softmax warps are busy
-//   warps 2-9   softmax, four warps per tile, one query row per thread:
-//               tcgen05.ld the row of S, base-2 online softmax with lazy
-//               rescaling (O in TMEM is rescaled only when a row max grows
-//               by more than 2^8), P as bf16 into 128-byte-swizzled shared
-//               memory (the A operand of the P.V MMA), final O / l to global
+// One CTA = 256 query rows of one head as two 128-row tiles sharing every
+// K/V block it loads; keys in blocks of 128 (two 64-token pages of the
+// paged cache). One query row per softmax thread, P kept in TMEM (written
+// over its own S, read by the P.V MMA as the A operand), and the two tiles
+// in ping-pong: while the softmax warps of one tile work, the tensor core
+// runs the other tile's P.V and next S.
+//
+//   warp 0      TMA producer: Q once; per block j two K pages (four
+//               [64 keys][64 dims] boxes) and two transposed V pages
+//               ([128 dims][64 keys] each) into a 2-stage ring
+//   warp 1      MMA issuer, per block j and tile t (in this order):
+//                 wait P_t(j);  O_t += P_t(j) V_j   (A from TMEM)
+//                 S_t(j+1) = Q_t K_{j+1}^T          (overwrites P_t(j); the
+//                                                     MMAs run in issue order)
+//                 commit -> s_full[t]
+//               so s_full[t] completing means S_t(j+1) is ready AND every
+//               earlier P.V of the tile has finished: the softmax may
+//               rescale O_t and overwrite the S columns with P without
+//               another wait.
+//   warps 2-3   idle (they complete the first warpgroup)
+//   warps 4-11  softmax, four warps per tile, one row per thread: the whole
+//               128-score row in registers, base-2 online softmax with lazy
+//               rescale (O is rescaled only when a row max grows by more
+//               than 2^8), P as bf16 pairs into TMEM, final O / l to global
 //               token-major [tq][hq*128]
-// TMEM: 512 columns = per tile S0 | S1 (64 each) | O (128).
+// TMEM (512 columns): tile t at t*256: S_t / P_t [0,128) | O_t [128,256).
+//
+// Of each row's four 32-score chunks, the EMU template mask selects the
+// ones whose 2^x is computed on the FMA pipe (ex2_fma) instead of the MUFU
+// unit; the two units then share the exponentials and neither bounds the
+// softmax alone. The mask must be a compile-time constant: as a run-time
+// value every chunk became its own basic block with both code paths, which
+// kept the scheduler from interleaving MUFU and FMA work across chunks and
+// doubled the loop's code (instruction-cache misses).
 //
 // The Sage variant (int8 QK, SageAttention) feeds S from int8 Q and smoothed
 // int8 K (kind::i8, s32 accumulators) and scales the scores by the per-64-row
@@ -38,20 +55,26 @@ namespace u15 {
 
 namespace {
 
-constexpr int kTile = 128;      // query rows per MMA tile
-constexpr int kKeys = 64;       // keys per KV tile = one page
+constexpr int kTile = 128;
+constexpr int kBlk = 128;                       // keys per block: two pages
 constexpr int kStages = 2;
-constexpr int kSoftWarps = 8;                  // softmax warps per 128-row tile
-constexpr int kThreads = 64 + 2 * kSoftWarps * 32;   // producer, MMA, 2 x 8 softmax warps
-constexpr int kQBytes = 2 * kTile * 256;       // bf16: 2 tiles x [128][128]; int8 uses half
-constexpr int kKBytes = kKeys * 256;           // bf16 [64][128] (2 boxes); int8 uses half
-constexpr int kVBytes = 128 * kKeys * 2;       // [128 dims][64 keys] bf16
-constexpr int kPBytes = kTile * kKeys * 2;     // [128 rows][64 keys] bf16
-constexpr int kXBytes = 2 * 2 * 2 * kTile * 4;   // row-max exchange [tile][buf][half][row] f32
-constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 4 * kPBytes + kXBytes + 1024 + 768;
+// Three warpgroups: WG0 = producer, MMA issuer and two idle warps; WG1 and
+// WG2 = the softmax of tile 0 and tile 1. Launched at 168 registers a thread
+// (the most 12 warps fit: three warps share each quarter of the register
+// file), WG0 then gives registers back (setmaxnreg.dec to 72) and the
+// softmax warpgroups take them (setmaxnreg.inc to 216) so a whole 128-score
+// row stays in registers: 128 x 72 + 256 x 216 = 384 x 168, the launch's
+// total, which the increase may not exceed.
+constexpr int kThreads = 384;
+constexpr int kRegsLow = 72, kRegsHigh = 216;
+constexpr int kQBytes = 2 * kTile * 256;        // bf16 Q, 2 tiles; int8 uses half
+constexpr int kKBytes = kBlk * 256;             // [2 dims blocks][128 keys][128 B]
+constexpr int kVBytes = 128 * kBlk * 2;         // [2 key blocks][128 dims][128 B]
+constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256;
+constexpr unsigned kEmuMaskDefault = 0x8;       // chunk 3 of 4: a quarter of the exponentials
 
 struct TcAttnP {
-  int hq, hkv, tq, tk, G, n_tiles;
+  int hq, hkv, tq, tk, G;
   float scale_log2;
   const int32_t* page_table;
   __nv_bfloat16* out;
@@ -75,8 +98,9 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // 2^x on the MUFU unit (PTX ex2.approx.ftz.f32; relative error ~2^-22,
 // far below the bf16 rounding P receives).
 __device__ __forceinline__ float ex2(float x)
@@ -85,365 +109,6 @@ __device__ __forceinline__ float ex2(float x)
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-
-template <bool SAGE>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
-{
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;                                   // tile t at t * (kQBytes/2)
-  uint8_t* sK = sQ + kQBytes;                           // stage s at s * kKBytes
-  uint8_t* sV = sK + kStages * kKBytes;                 // stage s at s * kVBytes
-  uint8_t* sP = sV + kStages * kVBytes;                 // tile t, buffer b at (2t + b) * kPBytes
-  float* xchg = reinterpret_cast<float*>(sP + 4 * kPBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * kPBytes + kXBytes);
-  // barrier slots
-  const uint32_t b0 = smem_u32(bars);
-  const uint32_t q_full = b0;
-  const uint32_t k_full = b0 + 8;                       // [kStages]
-  const uint32_t v_full = k_full + 8 * kStages;
-  const uint32_t k_empty = v_full + 8 * kStages;
-  const uint32_t v_empty = k_empty + 8 * kStages;
-  const uint32_t s_full = v_empty + 8 * kStages;        // [2 tiles][2 buffers]
-  // p_full[t][b] / o_done[t][b]: P(t, j) written / P.V(t, j) completed, for
-  // j & 1 == b. One barrier per P buffer keeps every waiter within one phase
-  // of its barrier (parity waits cannot tell phases two apart).
-  const uint32_t p_full = s_full + 8 * 4;               // [2 tiles][2 buffers]
-  const uint32_t o_done = p_full + 8 * 4;               // [2 tiles][2 buffers]
-  const uint32_t drain = o_done + 8 * 4;
-  // xbar[t][q][b]: the two half-row warps of tile t, lane quadrant q have
-  // published their row maxima for iteration j (j & 1 == b); count 64.
-  const uint32_t xbar = drain + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 4 + 4 + 4 + 1 + 16);
-
-  const int w = (int)warp_id();
-  const int h = blockIdx.y;
-  const int hk = h / p.G;
-  const int q0 = blockIdx.x * 2 * kTile;
-  const int n = p.n_tiles;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(k_full + 8 * s, 1);
-      mbar_init(v_full + 8 * s, 1);
-      mbar_init(k_empty + 8 * s, 1);
-      mbar_init(v_empty + 8 * s, 1);
-    }
-    for (int i = 0; i < 4; ++i) mbar_init(s_full + 8 * i, 1);
-    for (int i = 0; i < 4; ++i) mbar_init(p_full + 8 * i, 2 * 128);
-    for (int i = 0; i < 16; ++i) mbar_init(xbar + 8 * i, 64);
-    for (int i = 0; i < 4; ++i) mbar_init(o_done + 8 * i, 1);
-    mbar_init(drain, 1);
-    fence_barrier_init();
-  }
-  if (w == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  if (threadIdx.x == 32) {
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (w == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane_id() == 0) {
-      const int qrow = h * p.tq + q0;
-      if constexpr (SAGE) {
-        mbar_arrive_expect_tx(q_full, 2 * kTile * 128);
-        for (int t = 0; t < 2; ++t)
-          tma_load_2d(smem_u32(sQ + t * kTile * 128), &tmQ, 0, qrow + t * kTile, q_full);
-      } else {
-        mbar_arrive_expect_tx(q_full, 2 * kTile * 256);
-        for (int t = 0; t < 2; ++t)
-          for (int d = 0; d < 2; ++d)
-            tma_load_2d(smem_u32(sQ + t * kTile * 256 + d * kTile * 128), &tmQ, d * 64,
-                        qrow + t * kTile, q_full);
-      }
-      int last_k[kStages], last_v[kStages];
-      for (int s = 0; s < kStages; ++s) last_k[s] = last_v[s] = -1;
-      for (int j = 0; j < n; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const int page = p.page_table ? p.page_table[j] : j;
-        if (!mbar_wait(k_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
-        if constexpr (SAGE) {
-          mbar_arrive_expect_tx(k_full + 8 * s, kKeys * 128);
-          tma_load_2d(smem_u32(sK + s * kKBytes), &tmK, 0, (int)(hk * p.k8_stride) + j * kKeys,
-                      k_full + 8 * s);
-        } else {
-          mbar_arrive_expect_tx(k_full + 8 * s, kKeys * 256);
-          const int krow = (page * p.hkv + hk) * kKeys;
-          tma_load_2d(smem_u32(sK + s * kKBytes), &tmK, 0, krow, k_full + 8 * s);
-          tma_load_2d(smem_u32(sK + s * kKBytes + kKeys * 128), &tmK, 64, krow, k_full + 8 * s);
-        }
-        last_k[s] = j;
-        if (!mbar_wait(v_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
-        mbar_arrive_expect_tx(v_full + 8 * s, kVBytes);
-        tma_load_2d(smem_u32(sV + s * kVBytes), &tmV, 0, (page * p.hkv + hk) * 128, v_full + 8 * s);
-        last_v[s] = j;
-      }
-      // unwinding: every copy issued must land before the CTA may exit
-      mbar_wait(q_full, 0, p.err, kDevWaitDrain);
-      for (int s = 0; s < kStages; ++s) {
-        if (last_k[s] >= 0) mbar_wait(k_full + 8 * s, (last_k[s] / kStages) & 1, p.err, kDevWaitDrain);
-        if (last_v[s] >= 0) mbar_wait(v_full + 8 * s, (last_v[s] / kStages) & 1, p.err, kDevWaitDrain);
-      }
-    }
-  } else if (w == 1) {
-    // ------------------------------------------------------------ MMA
-    if (lane_id() == 0) {
-      const uint32_t id_s = SAGE ? idesc_s8(kTile, kKeys) : idesc_bf16(kTile, kKeys);
-      const uint32_t id_o = idesc_bf16(kTile, 128);
-      bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
-      auto issue_s = [&](int j) -> bool {
-        const uint32_t s = j % kStages;
-        if (!mbar_wait(k_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) return false;
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t) {
-          const uint32_t d = tmem + t * 256 + (j & 1) * 64;
-          if constexpr (SAGE) {
-            const uint32_t a0 = smem_u32(sQ + t * kTile * 128), b0 = smem_u32(sK + s * kKBytes);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), id_s, k != 0);
-          } else {
-            const uint32_t a0 = smem_u32(sQ + t * kTile * 256), b0 = smem_u32(sK + s * kKBytes);
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
-                       smem_desc_sw128(b0 + (k >> 2) * kKeys * 128 + (k & 3) * 32), id_s, k != 0);
-          }
-          mma_commit(s_full + 8 * (t * 2 + (j & 1)));
-        }
-        mma_commit(k_empty + 8 * s);
-        return true;
-      };
-      if (ok && n > 0) ok = issue_s(0);
-      for (int j = 0; j < n && ok; ++j) {
-        if (j + 1 < n && !issue_s(j + 1)) break;
-        const uint32_t s = j % kStages;
-        if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait(p_full + 8 * (2 * t + (j & 1)), (j >> 1) & 1, p.err, kDevWaitFull)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + t * 256 + 128;
-          const uint32_t a0 = smem_u32(sP + (2 * t + (j & 1)) * kPBytes),
-                         b0 = smem_u32(sV + s * kVBytes);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_bf16(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), id_o,
-                     (j | k) != 0);
-          mma_commit(o_done + 8 * (2 * t + (j & 1)));
-        }
-        mma_commit(v_empty + 8 * s);
-      }
-      mma_commit(drain);
-      mbar_wait(drain, 0, p.err, kDevWaitDrain);
-    }
-  } else {
-    // ------------------------------------------------------------ softmax
-    // 8 warps per tile: warp v of tile t serves TMEM lane quadrant w & 3 and
-    // column half v / 4 -- 32 of the tile's 64 S columns, 64 of the 128 O
-    // columns -- of 32 query rows. The two halves of a row exchange their row
-    // maxima each iteration through shared memory (bounded mbarrier waits);
-    // their row sums are combined once, at the end.
-    const int t = (w - 2) >> 3;
-    const int hh = ((w - 2) & 7) >> 2;
-    const int wq = w & 3;
-    const int row = wq * 32 + (int)lane_id();
-    const int qi = q0 + t * kTile + row;     // query index within the head
-    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const uint32_t tS = tmem + t * 256 + lane_off + hh * 32;
-    const uint32_t tO = tmem + t * 256 + lane_off + 128 + hh * 64;
-    uint8_t* prow0 = sP + (2 * t) * kPBytes + row * 128;
-    float* xc = xchg + t * 2 * 2 * kTile;    // [buf][half][row]
-    const uint32_t xb = xbar + 8 * (t * 8 + wq * 2);
-    float sqv = 1.0f;
-    if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
-    float m_ref = -INFINITY, l = 0.0f;
-    bool ok = true;
-    // publish `v` for exchange round j and return the partner half's value
-    auto exchange = [&](int j, float v, float* other) -> bool {
-      xc[((j & 1) * 2 + hh) * kTile + row] = v;
-      mbar_arrive(xb + 8 * (j & 1));
-      if (!mbar_wait(xb + 8 * (j & 1), (j >> 1) & 1, p.err, kDevWaitAccFull)) return false;
-      *other = xc[((j & 1) * 2 + (hh ^ 1)) * kTile + row];
-      return true;
-    };
-    for (int j = 0; j < n; ++j) {
-      if (!mbar_wait(s_full + 8 * (t * 2 + (j & 1)), (j >> 1) & 1, p.err, kDevWaitAccFull)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t r0[32];
-      tmem_ld32(tS + (j & 1) * 64, r0);
-      tmem_ld_wait();
-      // raw scores; the base-2 scale f > 0 is folded into the exponent's FFMA
-      float s[32];
-      float f = p.scale_log2;
-      if constexpr (SAGE) f *= sqv * p.sk[(long)hk * p.nkb + j];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if constexpr (SAGE) s[i] = (float)(int32_t)r0[i];
-        else s[i] = __uint_as_float(r0[i]);
-      }
-      const int kmax = p.tk - j * kKeys - hh * 32;   // valid keys in this half
-      if (kmax < 32) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i >= kmax) s[i] = -INFINITY;
-      }
-      float mraw = s[0];
-#pragma unroll
-      for (int i = 1; i < 32; ++i) mraw = fmaxf(mraw, s[i]);
-      float mo;
-      if (!exchange(j, mraw, &mo)) { ok = false; break; }
-      mraw = fmaxf(mraw, mo);
-      const float mt = mraw * f;
-      const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
-      const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // rescale this half-row of O (after the previous P.V has landed)
-        if (!mbar_wait(o_done + 8 * (2 * t + ((j - 1) & 1)), ((j - 1) >> 1) & 1, p.err,
-                       kDevWaitAccFull)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float fac = need ? ex2(m_ref - m_new) : 1.0f;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
-          tmem_st32(tO + c * 32, o);
-        }
-        tmem_st_wait();
-        l *= fac;
-      }
-      m_ref = m_new;
-      const float nm = -m_ref;
-      uint32_t pk[16];
-      float rs = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float a = ex2(fmaf(s[2 * i], f, nm)), b = ex2(fmaf(s[2 * i + 1], f, nm));
-        rs += a + b;
-        pk[i] = pack_bf2(a, b);
-      }
-      l += rs;
-      // P buffer j&1 was last read by P.V(j-2)
-      if (j > 1) {
-        if (!mbar_wait(o_done + 8 * (2 * t + (j & 1)), ((j - 2) >> 1) & 1, p.err,
-                       kDevWaitAccFull)) {
-          ok = false;
-          break;
-        }
-      }
-      // this half's 32 keys = chunks 4*hh .. 4*hh+3 of the 128-byte swizzled row
-      uint8_t* prow = prow0 + (j & 1) * kPBytes;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        *reinterpret_cast<uint4*>(prow + (((hh * 4 + c) ^ (row & 7)) << 4)) = v;
-      }
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full + 8 * (2 * t + (j & 1)));
-    }
-    float lo = 0.0f;
-    if (ok && n > 0 && exchange(n, l, &lo) &&
-        mbar_wait(o_done + 8 * (2 * t + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.err,
-                  kDevWaitAccFull)) {
-      tc_fence_after();
-      const float lt = l + lo;
-      const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
-      __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128 + hh * 64;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_ld_wait();
-        if (qi < p.tq) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            uint4 v;
-            v.x = pack_bf2(__uint_as_float(o[qd * 8 + 0]) * inv, __uint_as_float(o[qd * 8 + 1]) * inv);
-            v.y = pack_bf2(__uint_as_float(o[qd * 8 + 2]) * inv, __uint_as_float(o[qd * 8 + 3]) * inv);
-            v.z = pack_bf2(__uint_as_float(o[qd * 8 + 4]) * inv, __uint_as_float(o[qd * 8 + 5]) * inv);
-            v.w = pack_bf2(__uint_as_float(o[qd * 8 + 6]) * inv, __uint_as_float(o[qd * 8 + 7]) * inv);
-            d4[qd] = v;
-          }
-        }
-      }
-    }
-    tc_fence_before();
-  }
-
-  __syncthreads();
-  if (w == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-
-// =====================================================================
-// Version 2: 128-key blocks, one query row per softmax thread, P kept in
-// TMEM (written over its own S, read by the P.V MMA as the A operand), and
-// the two query tiles of a CTA in ping-pong: while the softmax warps of one
-// tile work, the tensor core runs the other tile's P.V and next S.
-//
-//   warp 0      TMA producer: Q once; per block j two K pages (four
-//               [64 keys][64 dims] boxes) and two transposed V pages
-//               ([128 dims][64 keys] each) into a 2-stage ring
-//   warp 1      MMA issuer, per block j and tile t (in this order):
-//                 wait P_t(j);  O_t += P_t(j) V_j   (A from TMEM)
-//                 S_t(j+1) = Q_t K_{j+1}^T          (overwrites P_t(j) in
-//                                                     issue order)
-//                 commit -> s_full[t]
-//               so s_full[t] completing means S_t(j+1) is ready AND every
-//               earlier P.V of the tile has finished: the softmax may
-//               rescale O_t and overwrite the S columns with P without
-//               another wait.
-//   warps 2-9   softmax, four warps per tile, one row per thread: the whole
-//               128-score row in registers, base-2 online softmax with lazy
-//               rescale (threshold 2^8), P as bf16 pairs into TMEM, final
-//               O / l to global token-major [tq][hq*128]
-// TMEM (512 columns): tile t at t*256: S_t / P_t [0,128) | O_t [128,256).
-//
-// Of each row's four 32-score chunks, kEmuMask selects the ones whose 2^x
-// is computed on the FMA pipe (ex2_fma) instead of the MUFU unit; the two
-// units then share the exponentials and neither bounds the softmax alone.
-// =====================================================================
-namespace v2 {
-
-constexpr int kTile = 128;
-constexpr int kBlk = 128;                       // keys per block: two pages
-constexpr int kStages = 2;
-constexpr int kThreads = 64 + 8 * 32;           // producer, MMA, 2 x 4 softmax warps
-constexpr int kQBytes = 2 * kTile * 256;        // bf16 Q, 2 tiles; int8 uses half
-constexpr int kKBytes = kBlk * 256;             // [2 dims blocks][128 keys][128 B]
-constexpr int kVBytes = 128 * kBlk * 2;         // [2 key blocks][128 dims][128 B]
-constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256;
-constexpr unsigned kEmuMask = 0x8;              // chunk 3 of 4: a quarter of the exponentials
 
 // 2^x for x <= 2^7 on the FMA pipe: x = n + f with n = rint(x) taken from
 // the low mantissa bits of x + 1.5 * 2^23, f in [-0.5, 0.5]; 2^f by a degree-3
@@ -487,9 +152,9 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-template <bool SAGE>
-__global__ void __maxnreg__(200)
-    attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+template <bool SAGE, unsigned EMU>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
 {
   extern __shared__ uint8_t smem_raw[];
@@ -545,137 +210,140 @@ __global__ void __maxnreg__(200)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (w == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane_id() == 0) {
-      const int qrow = h * p.tq + q0;
-      if constexpr (SAGE) {
-        mbar_arrive_expect_tx(q_full, 2 * kTile * 128);
-        for (int t = 0; t < 2; ++t)
-          tma_load_2d(smem_u32(sQ + t * kTile * 128), &tmQ, 0, qrow + t * kTile, q_full);
-      } else {
-        mbar_arrive_expect_tx(q_full, 2 * kTile * 256);
-        for (int t = 0; t < 2; ++t)
-          for (int d = 0; d < 2; ++d)
-            tma_load_2d(smem_u32(sQ + t * kTile * 256 + d * kTile * 128), &tmQ, d * 64,
-                        qrow + t * kTile, q_full);
-      }
-      int nk = 0, nv = 0;   // blocks whose K / V loads were issued
-      for (int j = 0; j < n; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        // the block's two pages; past the last page the first one is loaded
-        // again (finite data under masked scores)
-        const int pg0 = 2 * j, pg1 = min(2 * j + 1, n_pg - 1);
-        const int page0 = p.page_table ? p.page_table[pg0] : pg0;
-        const int page1 = p.page_table ? p.page_table[pg1] : pg1;
-        if (!mbar_wait(k_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
-        uint8_t* k_dst = sK + s * kKBytes;
+  if (w < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    if (w == 0) {
+      // ------------------------------------------------------------ producer
+      if (lane_id() == 0) {
+        const int qrow = h * p.tq + q0;
         if constexpr (SAGE) {
-          mbar_arrive_expect_tx(k_full + 8 * s, kBlk * 128);
-          const int krow = (int)(hk * p.k8_stride) + j * kBlk;
-          tma_load_2d(smem_u32(k_dst), &tmK, 0, krow, k_full + 8 * s);
-          tma_load_2d(smem_u32(k_dst + 64 * 128), &tmK, 0, krow + 64, k_full + 8 * s);
+          mbar_arrive_expect_tx(q_full, 2 * kTile * 128);
+          for (int t = 0; t < 2; ++t)
+            tma_load_2d(smem_u32(sQ + t * kTile * 128), &tmQ, 0, qrow + t * kTile, q_full);
         } else {
-          mbar_arrive_expect_tx(k_full + 8 * s, kKBytes);
-          for (int hf = 0; hf < 2; ++hf) {
-            const int krow = ((hf ? page1 : page0) * p.hkv + hk) * 64;
+          mbar_arrive_expect_tx(q_full, 2 * kTile * 256);
+          for (int t = 0; t < 2; ++t)
             for (int d = 0; d < 2; ++d)
-              tma_load_2d(smem_u32(k_dst + d * kBlk * 128 + hf * 64 * 128), &tmK, d * 64, krow,
-                          k_full + 8 * s);
+              tma_load_2d(smem_u32(sQ + t * kTile * 256 + d * kTile * 128), &tmQ, d * 64,
+                          qrow + t * kTile, q_full);
+        }
+        int nk = 0, nv = 0;   // blocks whose K / V loads were issued
+        for (int j = 0; j < n; ++j) {
+          const int s = j % kStages;
+          const uint32_t ph = (j / kStages) & 1;
+          // the block's two pages; past the last page the first one is loaded
+          // again (finite data under masked scores)
+          const int pg0 = 2 * j, pg1 = min(2 * j + 1, n_pg - 1);
+          const int page0 = p.page_table ? p.page_table[pg0] : pg0;
+          const int page1 = p.page_table ? p.page_table[pg1] : pg1;
+          if (!mbar_wait(k_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+          uint8_t* k_dst = sK + s * kKBytes;
+          if constexpr (SAGE) {
+            mbar_arrive_expect_tx(k_full + 8 * s, kBlk * 128);
+            const int krow = (int)(hk * p.k8_stride) + j * kBlk;
+            tma_load_2d(smem_u32(k_dst), &tmK, 0, krow, k_full + 8 * s);
+            tma_load_2d(smem_u32(k_dst + 64 * 128), &tmK, 0, krow + 64, k_full + 8 * s);
+          } else {
+            mbar_arrive_expect_tx(k_full + 8 * s, kKBytes);
+            for (int hf = 0; hf < 2; ++hf) {
+              const int krow = ((hf ? page1 : page0) * p.hkv + hk) * 64;
+              for (int d = 0; d < 2; ++d)
+                tma_load_2d(smem_u32(k_dst + d * kBlk * 128 + hf * 64 * 128), &tmK, d * 64, krow,
+                            k_full + 8 * s);
+            }
+          }
+          nk = j + 1;
+          if (!mbar_wait(v_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+          mbar_arrive_expect_tx(v_full + 8 * s, kVBytes);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_2d(smem_u32(sV + s * kVBytes + hf * 128 * 128), &tmV, 0,
+                        ((hf ? page1 : page0) * p.hkv + hk) * 128, v_full + 8 * s);
+          nv = j + 1;
+        }
+        // unwinding: every copy issued must land before the CTA may exit
+        mbar_wait(q_full, 0, p.err, kDevWaitDrain);
+        for (int s = 0; s < kStages; ++s) {
+          if (nk > s) {
+            const int last = ((nk - 1 - s) / kStages) * kStages + s;
+            mbar_wait(k_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
+          }
+          if (nv > s) {
+            const int last = ((nv - 1 - s) / kStages) * kStages + s;
+            mbar_wait(v_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
           }
         }
-        nk = j + 1;
-        if (!mbar_wait(v_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
-        mbar_arrive_expect_tx(v_full + 8 * s, kVBytes);
-        for (int hf = 0; hf < 2; ++hf)
-          tma_load_2d(smem_u32(sV + s * kVBytes + hf * 128 * 128), &tmV, 0,
-                      ((hf ? page1 : page0) * p.hkv + hk) * 128, v_full + 8 * s);
-        nv = j + 1;
       }
-      // unwinding: every copy issued must land before the CTA may exit
-      mbar_wait(q_full, 0, p.err, kDevWaitDrain);
-      for (int s = 0; s < kStages; ++s) {
-        if (nk > s) {
-          const int last = ((nk - 1 - s) / kStages) * kStages + s;
-          mbar_wait(k_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
-        }
-        if (nv > s) {
-          const int last = ((nv - 1 - s) / kStages) * kStages + s;
-          mbar_wait(v_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
-        }
-      }
-    }
-  } else if (w == 1) {
-    // ------------------------------------------------------------ MMA
-    if (lane_id() == 0) {
-      const uint32_t id_s = SAGE ? idesc_s8(kTile, kBlk) : idesc_bf16(kTile, kBlk);
-      const uint32_t id_o = idesc_bf16(kTile, 128);
-      auto issue_s = [&](int t, int j) {
-        const uint32_t d = tmem + t * 256;
-        const uint32_t kb = smem_u32(sK + (j % kStages) * kKBytes);
-        if constexpr (SAGE) {
-          const uint32_t a0 = smem_u32(sQ + t * kTile * 128);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(kb + k * 32), id_s, k != 0);
-        } else {
-          const uint32_t a0 = smem_u32(sQ + t * kTile * 256);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
-                     smem_desc_sw128(kb + (k >> 2) * kBlk * 128 + (k & 3) * 32), id_s, k != 0);
-        }
-      };
-      bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
-      if (ok && n > 0) {
-        ok = mbar_wait(k_full, 0, p.err, kDevWaitFull);
-        if (ok) {
-          tc_fence_after();
-          for (int t = 0; t < 2; ++t) {
-            issue_s(t, 0);
-            mma_commit(s_full + 8 * t);
+    } else if (w == 1) {
+      // ------------------------------------------------------------ MMA
+      if (lane_id() == 0) {
+        const uint32_t id_s = SAGE ? idesc_s8(kTile, kBlk) : idesc_bf16(kTile, kBlk);
+        const uint32_t id_o = idesc_bf16(kTile, 128);
+        auto issue_s = [&](int t, int j) {
+          const uint32_t d = tmem + t * 256;
+          const uint32_t kb = smem_u32(sK + (j % kStages) * kKBytes);
+          if constexpr (SAGE) {
+            const uint32_t a0 = smem_u32(sQ + t * kTile * 128);
+  #pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(kb + k * 32), id_s, k != 0);
+          } else {
+            const uint32_t a0 = smem_u32(sQ + t * kTile * 256);
+  #pragma unroll
+            for (int k = 0; k < 8; ++k)
+              mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
+                       smem_desc_sw128(kb + (k >> 2) * kBlk * 128 + (k & 3) * 32), id_s, k != 0);
           }
-          mma_commit(k_empty);
-        }
-      }
-      for (int j = 0; j < n && ok; ++j) {
-        const int s = j % kStages, s1 = (j + 1) % kStages;
-        if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
-        const uint32_t vb = smem_u32(sV + s * kVBytes);
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait(p_full + 8 * t, j & 1, p.err, kDevWaitFull)) {
-            ok = false;
-            break;
+        };
+        bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
+        if (ok && n > 0) {
+          ok = mbar_wait(k_full, 0, p.err, kDevWaitFull);
+          if (ok) {
+            tc_fence_after();
+            for (int t = 0; t < 2; ++t) {
+              issue_s(t, 0);
+              mma_commit(s_full + 8 * t);
+            }
+            mma_commit(k_empty);
           }
-          tc_fence_after();
-          const uint32_t d = tmem + t * 256 + 128, a = tmem + t * 256;
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            mma_bf16_ts(d, a + k * 8, smem_desc_sw128(vb + (k >> 2) * 128 * 128 + (k & 3) * 32),
-                        id_o, (j | k) != 0);
-          if (j + 1 < n) {
-            if (t == 0 && !mbar_wait(k_full + 8 * s1, ((j + 1) / kStages) & 1, p.err,
-                                     kDevWaitFull)) {
+        }
+        for (int j = 0; j < n && ok; ++j) {
+          const int s = j % kStages, s1 = (j + 1) % kStages;
+          if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
+          const uint32_t vb = smem_u32(sV + s * kVBytes);
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!mbar_wait(p_full + 8 * t, j & 1, p.err, kDevWaitFull)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_s(t, j + 1);
+            const uint32_t d = tmem + t * 256 + 128, a = tmem + t * 256;
+  #pragma unroll
+            for (int k = 0; k < 8; ++k)
+              mma_bf16_ts(d, a + k * 8, smem_desc_sw128(vb + (k >> 2) * 128 * 128 + (k & 3) * 32),
+                          id_o, (j | k) != 0);
+            if (j + 1 < n) {
+              if (t == 0 && !mbar_wait(k_full + 8 * s1, ((j + 1) / kStages) & 1, p.err,
+                                       kDevWaitFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(t, j + 1);
+            }
+            mma_commit(s_full + 8 * t);
           }
-          mma_commit(s_full + 8 * t);
+          if (!ok) break;
+          mma_commit(v_empty + 8 * s);
+          if (j + 1 < n) mma_commit(k_empty + 8 * s1);
         }
-        if (!ok) break;
-        mma_commit(v_empty + 8 * s);
-        if (j + 1 < n) mma_commit(k_empty + 8 * s1);
+        mma_commit(drain);
+        mbar_wait(drain, 0, p.err, kDevWaitDrain);
       }
-      mma_commit(drain);
-      mbar_wait(drain, 0, p.err, kDevWaitDrain);
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------------------------------------ softmax
-    const int t = (w - 2) >> 2;
+    const int t = (w - 4) >> 2;
     const int wq = w & 3;
     const int row = wq * 32 + (int)lane_id();
     const int qi = q0 + t * kTile + row;
@@ -751,7 +419,7 @@ __global__ void __maxnreg__(200)
         for (int i = 0; i < 16; ++i) {
           const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
           float a, b;
-          if ((kEmuMask >> c) & 1) {
+          if ((EMU >> c) & 1) {   // folded: c is a constant after unrolling
             a = ex2_fma(x0);
             b = ex2_fma(x1);
           } else {
@@ -804,8 +472,6 @@ __global__ void __maxnreg__(200)
   }
 }
 
-}  // namespace v2
-
 }  // namespace
 
 int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
@@ -816,13 +482,23 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   }
   if (a.tq <= 0 || a.tk <= 0) return 0;
   const bool sage = a.q8 != nullptr;
+  const int n_pages_needed = (a.tk + 63) / 64;
+  if (a.n_pages < n_pages_needed && a.page_table == nullptr) {
+    *err = "attention: the page pool holds fewer pages than the key length needs";
+    return 1;
+  }
+  // U15_ATTN_EMU (0, 8 or 12): which 32-score chunks use the FMA-pipe 2^x
+  static const unsigned emu = [] {
+    const char* e = std::getenv("U15_ATTN_EMU");
+    const unsigned v = e != nullptr ? (unsigned)std::strtoul(e, nullptr, 0) : kEmuMaskDefault;
+    return (v == 0 || v == 8 || v == 12) ? v : kEmuMaskDefault;
+  }();
   TcAttnP p{};
   p.hq = a.hq;
   p.hkv = a.hkv;
   p.tq = a.tq;
   p.tk = a.tk;
   p.G = a.hq / a.hkv;
-  p.n_tiles = (a.tk + kKeys - 1) / kKeys;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
   p.page_table = a.page_table;
   p.out = static_cast<__nv_bfloat16*>(a.out);
@@ -832,45 +508,38 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   p.nkb = (a.tk + 63) / 64;
   p.k8_stride = (long)p.nkb * 64;
   p.err = a.dev_err;
-  if (a.n_pages < p.n_tiles && a.page_table == nullptr) {
-    *err = "attention: the page pool holds fewer pages than the key length needs";
-    return 1;
-  }
   CUtensorMap mq, mk, mv;
   if (sage) {
     if (make_tma_2d(&mq, a.q8, (uint64_t)a.hq * a.tq, 128, kTile, 1, err)) return 2;
-    if (make_tma_2d(&mk, a.k8, (uint64_t)a.hkv * p.k8_stride, 128, kKeys, 1, err)) return 2;
+    if (make_tma_2d(&mk, a.k8, (uint64_t)a.hkv * p.k8_stride, 128, 64, 1, err)) return 2;
   } else {
     if (make_tma_2d(&mq, a.q, (uint64_t)a.hq * a.tq, 128, kTile, 2, err)) return 2;
-    if (make_tma_2d(&mk, a.k_pages, (uint64_t)a.n_pages * a.hkv * kKeys, 128, kKeys, 2, err))
-      return 2;
+    if (make_tma_2d(&mk, a.k_pages, (uint64_t)a.n_pages * a.hkv * 64, 128, 64, 2, err)) return 2;
   }
-  if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, kKeys, 128, 2, err))
-    return 2;
-  static const bool use_v1 = [] {
-    const char* e = std::getenv("U15_ATTN_V2");
-    return !(e != nullptr && *e != '0');
-  }();
-  static std::atomic<uint64_t> set0, set1, set2, set3;
+  if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, 64, 128, 2, err)) return 2;
+  static std::atomic<uint64_t> set_attr[6];
   const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
-  bool attr_ok;
-  if (!use_v1) {
-    if (sage) {
-      attr_ok = smem_attr_once(v2::attn_kernel<true>, v2::kSmem, set3);
-      if (attr_ok) v2::attn_kernel<true><<<grid, v2::kThreads, v2::kSmem, st>>>(mq, mk, mv, p);
-    } else {
-      attr_ok = smem_attr_once(v2::attn_kernel<false>, v2::kSmem, set2);
-      if (attr_ok) v2::attn_kernel<false><<<grid, v2::kThreads, v2::kSmem, st>>>(mq, mk, mv, p);
-    }
-  } else if (sage) {
-    attr_ok = smem_attr_once(attn_tc_kernel<true>, kSmem, set1);
-    if (attr_ok) attn_tc_kernel<true><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcAttnP);
+  const int ei = emu == 0 ? 0 : emu == 8 ? 1 : 2;
+  static const Kern kerns[6] = {attn_tc_kernel<false, 0>, attn_tc_kernel<false, 8>,
+                                attn_tc_kernel<false, 12>, attn_tc_kernel<true, 0>,
+                                attn_tc_kernel<true, 8>, attn_tc_kernel<true, 12>};
+  const int ki = (sage ? 3 : 0) + ei;
+  Kern k = kerns[ki];
+  cudaError_t e = cudaSuccess;
+  if (smem_attr_once(k, kSmem, set_attr[ki])) {
+    k<<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
+    e = cudaGetLastError();
   } else {
-    attr_ok = smem_attr_once(attn_tc_kernel<false>, kSmem, set0);
-    if (attr_ok) attn_tc_kernel<false><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaErrorInvalidValue;
   }
-  if (!attr_ok || cudaGetLastError() != cudaSuccess) {
-    *err = "attention (tcgen05): kernel launch failed";
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, k);
+    *err = std::string("attention (tcgen05): kernel launch failed: ") + cudaGetErrorString(e) +
+           " (registers " + std::to_string(fa.numRegs) + ", max threads " +
+           std::to_string(fa.maxThreadsPerBlock) + ", dynamic smem " + std::to_string(kSmem) + ")";
     return 2;
   }
   return 0;

@@ -59,6 +59,7 @@ struct Params {
   int M, N, K;          // N: weight rows per expert (SWIGLU: 2x the output width)
   int n_units, n_nblk, n_kblk;
   int n_full;           // tiles before the split tail (== n_units * n_nblk when none)
+  int group;            // tile order: units (row blocks) per group, >= 1
   void* y;
   long ldy;             // output row stride, elements
   const __nv_bfloat16* resid;
@@ -87,8 +88,14 @@ __device__ __forceinline__ TileIdx tile_at(const Params& p, int t)
     tt = p.n_full + (h >> 1);
     r.half = h & 1;
   }
-  r.unit = tt % p.n_units;
-  r.nb = tt / p.n_units;
+  // grouped order: the units of one group sweep all column blocks before
+  // the next group starts, so a round of the schedule touches `group` row
+  // blocks of A and a proportionate share of B
+  const int g0 = (tt / (p.group * p.n_nblk)) * p.group;
+  const int gs = min(p.group, p.n_units - g0);
+  const int rr = tt - g0 * p.n_nblk;
+  r.unit = g0 + rr % gs;
+  r.nb = rr / gs;
   return r;
 }
 
@@ -144,6 +151,21 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)
 #pragma unroll
     for (int i = 0; i < 32; ++i)
       if (col0 + i < ncols) dst[i] = f2bf(v[i]);
+  }
+}
+
+// Store 32 f32 values of one row (columns >= ncols dropped).
+__device__ __forceinline__ void store_row32_f32(float* dst, const float (&v)[32], int col0,
+                                                int ncols)
+{
+  if (col0 + 32 <= ncols && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < ncols) dst[i] = v[i];
   }
 }
 
@@ -219,8 +241,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-        const Unit u = p.units[t % p.n_units];
-        const int nb = t / p.n_units;
+        const TileIdx ti = tile_at(p, t);
+        const Unit u = p.units[ti.unit];
+        const int nb = ti.nb;
         const int brow = u.expert * p.N + nb * kBN;
         for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
           const uint32_t s = it % kStages, ph = (it / kStages) & 1;
@@ -286,8 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r_in = wq * 32 + (int)lane_id();
     int lt = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
-      const Unit u = p.units[t % p.n_units];
-      const int nb = t / p.n_units;
+      const TileIdx ti = tile_at(p, t);
+      const Unit u = p.units[ti.unit];
+      const int nb = ti.nb;
       const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
       if (!mbar_wait(accf0 + 8 * acc, aph, p.err, kDevWaitAccFull)) break;
       tc_fence_after();
@@ -331,7 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = rr[i] + bfround(v[i]);
           }
-          store_row32(yrow + col0, v, col0, p.N);
+          if constexpr (EPI == kEpiStoreF32)
+            store_row32_f32(reinterpret_cast<float*>(p.y) + (long)row * p.ldy + col0, v, col0, p.N);
+          else
+            store_row32(yrow + col0, v, col0, p.N);
         }
       }
       tc_fence_before();
@@ -561,7 +588,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = rr[i] + bfround(v[i]);
           }
-          store_row32(yrow + col0, v, col0, p.N);
+          if constexpr (EPI == kEpiStoreF32)
+            store_row32_f32(reinterpret_cast<float*>(p.y) + (long)row * p.ldy + col0, v, col0, p.N);
+          else
+            store_row32(yrow + col0, v, col0, p.N);
         }
       }
       tc_fence_before();
@@ -819,6 +849,14 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   p.n_units = n_units;
   p.n_nblk = (a.N + kBN - 1) / kBN;
   p.n_full = n_units * p.n_nblk;
+  p.group = n_units;
+  {
+    static const int grp = [] {
+      const char* e = std::getenv("U15_GEMM_GROUP");
+      return e != nullptr ? std::atoi(e) : 0;
+    }();
+    if (grp > 0 && grp < n_units) p.group = grp;
+  }
   const int bk = a.int8 ? 128 : 64;
   p.n_kblk = (a.K + bk - 1) / bk;
 
@@ -837,10 +875,12 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
     if (a.int8) {
       rc = a.epilogue == kEpiResid    ? launch_pair<true, kEpiResid>(ma, mb, mbh, p, tiles, st)
            : a.epilogue == kEpiSwiglu ? launch_pair<true, kEpiSwiglu>(ma, mb, mbh, p, tiles, st)
+           : a.epilogue == kEpiStoreF32 ? launch_pair<true, kEpiStoreF32>(ma, mb, mbh, p, tiles, st)
                                       : launch_pair<true, kEpiStore>(ma, mb, mbh, p, tiles, st);
     } else {
       rc = a.epilogue == kEpiResid    ? launch_pair<false, kEpiResid>(ma, mb, mbh, p, tiles, st)
            : a.epilogue == kEpiSwiglu ? launch_pair<false, kEpiSwiglu>(ma, mb, mbh, p, tiles, st)
+           : a.epilogue == kEpiStoreF32 ? launch_pair<false, kEpiStoreF32>(ma, mb, mbh, p, tiles, st)
                                       : launch_pair<false, kEpiStore>(ma, mb, mbh, p, tiles, st);
     }
     if (rc) *err = "gemm (CTA pair): kernel launch failed";
@@ -850,10 +890,12 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   if (a.int8) {
     rc = a.epilogue == kEpiResid    ? launch_one<true, kEpiResid>(ma, mb, p, grid, st)
          : a.epilogue == kEpiSwiglu ? launch_one<true, kEpiSwiglu>(ma, mb, p, grid, st)
+         : a.epilogue == kEpiStoreF32 ? launch_one<true, kEpiStoreF32>(ma, mb, p, grid, st)
                                     : launch_one<true, kEpiStore>(ma, mb, p, grid, st);
   } else {
     rc = a.epilogue == kEpiResid    ? launch_one<false, kEpiResid>(ma, mb, p, grid, st)
          : a.epilogue == kEpiSwiglu ? launch_one<false, kEpiSwiglu>(ma, mb, p, grid, st)
+         : a.epilogue == kEpiStoreF32 ? launch_one<false, kEpiStoreF32>(ma, mb, p, grid, st)
                                     : launch_one<false, kEpiStore>(ma, mb, p, grid, st);
   }
   if (rc) *err = "gemm: kernel launch failed";

@@ -29,7 +29,7 @@ inline bool smem_attr_once(Kernel kern, int bytes, std::atomic<uint64_t>& done)
   return true;
 }
 
-enum Epilogue { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2 };
+enum Epilogue { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2, kEpiStoreF32 = 3 };
 
 // Token segments routed to experts: rows [off[i], off[i+1]) use expert[i].
 constexpr int kMaxSeg = 8;

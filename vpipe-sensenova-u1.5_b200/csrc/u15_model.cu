@@ -59,17 +59,31 @@ __device__ __forceinline__ float src_value(const void* src, int dtype, long i)
   return __bfloat162float(static_cast<const bf16*>(src)[i]);
 }
 
-// dst row for source row r: base + r, or (interleave >= 0) the gate/up
-// block layout base + (r/128)*256 + interleave*128 + r%128.
-__global__ void bind_kernel(const void* src, int dtype, long rows, long cols, bf16* dst,
-                            int interleave)
+// Element (r, c) of the [rows][cols] destination comes from source element
+// (src_r0 + r, src_c0 + c) of a row-major source with src_ld columns: the
+// whole tensor, or (tensor parallelism) this rank's rows or columns of it.
+// dst row for r: r, or (interleave >= 0) the gate/up block layout
+// (r/128)*256 + interleave*128 + r%128.
+__global__ void bind_kernel(const void* src, int dtype, long rows, long cols, long src_ld,
+                            long src_r0, long src_c0, bf16* dst, int interleave)
 {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * cols) return;
   const long r = i / cols, c = i % cols;
   long dr = r;
   if (interleave >= 0) dr = (r / 128) * 256 + interleave * 128 + r % 128;
-  dst[dr * cols + c] = __float2bfloat16_rn(src_value(src, dtype, i));
+  dst[dr * cols + c] =
+      __float2bfloat16_rn(src_value(src, dtype, (src_r0 + r) * src_ld + src_c0 + c));
+}
+
+// x = bf16(x + bf16(sum)): the residual epilogue's rounding points, applied
+// after the ranks' f32 partial products were summed.
+__global__ void resid_add_f32_kernel(bf16* x, const float* sum, long n)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float proj = __bfloat162float(__float2bfloat16_rn(sum[i]));
+  x[i] = __float2bfloat16_rn(__bfloat162float(x[i]) + proj);
 }
 
 __device__ __forceinline__ uint64_t splitmix(uint64_t x)
@@ -98,7 +112,17 @@ inline unsigned nblk(long n, int t) { return (unsigned)((n + t - 1) / t); }
 }  // namespace
 
 struct u15c_model {
+  // cfg: this rank's share (heads, kv_heads and inter divided by tp_size);
+  // full: the model as the caller described it (bind reads full tensors)
   u15c_config cfg{};
+  u15c_config full{};
+  int tp_rank = 0, tp_size = 1;
+  // tensor parallelism: the caller's all-reduce of part[0 : count) (f32 sum
+  // over the ranks, in place, ordered on the stream)
+  u15c_allreduce_fn ar_fn = nullptr;
+  void* ar_ctx = nullptr;
+  float* part = nullptr;
+  long part_elems = 0;
   unsigned flags = 0;
   int device = 0;
   std::vector<LayerW> layers;
@@ -303,6 +327,26 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
     }
     return u15::run_gemm(a, st);
   };
+  // o_proj / down_proj + residual. One device: the GEMM's residual
+  // epilogue. Tensor parallelism (row-parallel split, this rank holds K/tp of
+  // the inner dimension): f32 partial products, the caller's all-reduce sums
+  // them across the ranks, then x = bf16(x + bf16(sum)).
+  auto row_parallel = [&](const void* in, int K, const bf16* w, const int8_t* w8,
+                          const float* ws) -> int {
+    if (m->tp_size == 1) return gemm(in, K, w, w8, ws, H, u15::kEpiResid, x);
+    const long n = (long)M * H;
+    if (m->ar_fn == nullptr || m->part == nullptr || m->part_elems < n)
+      return fail(U15C_EINVAL, "tensor-parallel model: no all-reduce installed, or its "
+                               "buffer holds fewer than tokens x hidden floats "
+                               "(u15c_model_set_allreduce)");
+    int r = gemm(in, K, w, w8, ws, H, u15::kEpiStoreF32, m->part);
+    if (r) return r;
+    if (m->ar_fn(m->ar_ctx, n, static_cast<u15c_stream>(st)) != 0)
+      return fail(U15C_ECUDA, "tensor-parallel all-reduce failed");
+    resid_add_f32_kernel<<<nblk(n, 256), 256, 0, st>>>(x, m->part, n);
+    return cudaGetLastError() == cudaSuccess ? U15C_OK
+                                             : fail(U15C_ECUDA, "residual add launch failed");
+  };
   // the layer norms: bf16 out, or (W8A8 with hidden <= 4096) fused with the
   // activation quantisation
   const bool fuse_q = i8 && H <= 4096;
@@ -335,12 +379,12 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
                               sl.kv_off, sl.t_index, nullptr);
     if (rc) return rc;
   }
-  if ((rc = gemm(m->attn, m->qd(), L.o, L.o8, L.o_s, H, u15::kEpiResid, x))) return rc;
+  if ((rc = row_parallel(m->attn, m->qd(), L.o, L.o8, L.o_s))) return rc;
 
   // ---- MLP half (src/u15-backbone.cc:246-256) ----
   if ((rc = norm(L.ln_post))) return rc;
   if ((rc = gemm(m->xn, H, L.gu, L.gu8, L.gu_s, 2 * I, u15::kEpiSwiglu, m->h, fuse_q))) return rc;
-  if ((rc = gemm(m->h, I, L.down, L.down8, L.down_s, H, u15::kEpiResid, x))) return rc;
+  if ((rc = row_parallel(m->h, I, L.down, L.down8, L.down_s))) return rc;
   return U15C_OK;
 }
 
@@ -370,14 +414,34 @@ extern "C" {
 
 int u15c_model_create(const u15c_config* cfg, unsigned flags, u15c_model** out)
 {
-  if (cfg == nullptr || out == nullptr) return fail(U15C_EINVAL, "null argument");
+  return u15c_model_create_tp(cfg, flags, 0, 1, out);
+}
+
+int u15c_model_create_tp(const u15c_config* full, unsigned flags, int tp_rank, int tp_size,
+                         u15c_model** out)
+{
+  if (full == nullptr || out == nullptr) return fail(U15C_EINVAL, "null argument");
   *out = nullptr;
-  int rc = check_cfg(*cfg);
+  int rc = check_cfg(*full);
   if (rc) return rc;
+  if (tp_size < 1 || tp_size > 8 || (tp_size & (tp_size - 1)) || tp_rank < 0 ||
+      tp_rank >= tp_size)
+    return fail(U15C_EINVAL, "tensor parallelism: tp_size must be 1, 2, 4 or 8 and "
+                             "0 <= tp_rank < tp_size");
+  if (full->heads % tp_size || full->kv_heads % tp_size || full->inter % (128 * tp_size))
+    return fail(U15C_EINVAL, "tensor parallelism: heads and kv_heads must divide by tp_size "
+                             "and inter by 128 * tp_size");
   if (u15::dev() == nullptr) return U15C_ECUDA;
   auto* m = new u15c_model();
-  m->cfg = *cfg;
+  m->full = *full;
+  m->cfg = *full;
+  m->cfg.heads /= tp_size;
+  m->cfg.kv_heads /= tp_size;
+  m->cfg.inter /= tp_size;
+  m->tp_rank = tp_rank;
+  m->tp_size = tp_size;
   m->flags = flags;
+  const u15c_config* cfg = &m->cfg;
   cudaGetDevice(&m->device);
   const size_t E = cfg->n_experts, H = cfg->hidden, I = cfg->inter;
   const size_t QKV = (size_t)m->qkv_n(), QD = (size_t)m->qd();
@@ -413,6 +477,27 @@ int u15c_model_create(const u15c_config* cfg, unsigned flags, u15c_model** out)
   return U15C_OK;
 }
 
+int u15c_model_set_allreduce(u15c_model* m, u15c_allreduce_fn fn, void* ctx, float* buf,
+                             long buf_elems)
+{
+  if (m == nullptr) return fail(U15C_EINVAL, "null model");
+  if (fn != nullptr && (buf == nullptr || buf_elems <= 0))
+    return fail(U15C_EINVAL, "set_allreduce: the partial-sum buffer is required");
+  m->ar_fn = fn;
+  m->ar_ctx = ctx;
+  m->part = fn ? buf : nullptr;
+  m->part_elems = fn ? buf_elems : 0;
+  return U15C_OK;
+}
+
+int u15c_model_tp(const u15c_model* m, int* tp_rank, int* tp_size)
+{
+  if (m == nullptr) return fail(U15C_EINVAL, "null model");
+  if (tp_rank) *tp_rank = m->tp_rank;
+  if (tp_size) *tp_size = m->tp_size;
+  return U15C_OK;
+}
+
 void u15c_model_destroy(u15c_model* m)
 {
   if (m == nullptr) return;
@@ -431,32 +516,51 @@ int u15c_model_bind(u15c_model* m, u15c_stream stream, int layer, int expert, in
     return fail(U15C_EINVAL, "layer out of range");
   if (dtype < 0 || dtype > 2) return fail(U15C_EINVAL, "unknown source dtype");
   const long H = c.hidden, I = c.inter, QD = m->qd(), KD = (long)c.kv_heads * c.head_dim;
-  const long E = c.n_experts;
+  // the source is always the full tensor; with tensor parallelism this rank
+  // binds its q/k/v heads and gate/up rows (column-parallel) and its columns
+  // of o and down (row-parallel)
+  const long r = m->tp_rank;
+  const long QDf = (long)m->full.heads * c.head_dim, If = m->full.inter;
   LayerW* L = tensor == U15C_T_FINAL_NORM ? nullptr : &m->layers[layer];
   bf16* dst = nullptr;
-  long rows = 0, cols = 0;
+  long rows = 0, cols = 0, src_rows = 0, src_ld = 0, r0 = 0, c0 = 0;
   int inter = -1;
+  auto whole = [&](long n) { rows = 1; cols = n; src_rows = 1; src_ld = n; };
   switch (tensor) {
-    case U15C_T_INPUT_LN: dst = L->ln_in + expert * H; rows = 1; cols = H; break;
-    case U15C_T_POST_LN: dst = L->ln_post + expert * H; rows = 1; cols = H; break;
-    case U15C_T_Q: dst = L->qkv + (long)expert * m->qkv_n() * H; rows = QD; cols = H; break;
-    case U15C_T_K: dst = L->qkv + ((long)expert * m->qkv_n() + QD) * H; rows = KD; cols = H; break;
+    case U15C_T_INPUT_LN: dst = L->ln_in + expert * H; whole(H); break;
+    case U15C_T_POST_LN: dst = L->ln_post + expert * H; whole(H); break;
+    case U15C_T_Q:
+      dst = L->qkv + (long)expert * m->qkv_n() * H;
+      rows = QD; cols = H; src_rows = QDf; src_ld = H; r0 = r * QD;
+      break;
+    case U15C_T_K:
     case U15C_T_V:
-      dst = L->qkv + ((long)expert * m->qkv_n() + QD + KD) * H; rows = KD; cols = H; break;
-    case U15C_T_O: dst = L->o + (long)expert * H * QD; rows = H; cols = QD; break;
-    case U15C_T_Q_NORM: dst = L->norms + expert * 256 + 0; rows = 1; cols = 64; break;
-    case U15C_T_Q_NORM_HW: dst = L->norms + expert * 256 + 64; rows = 1; cols = 64; break;
-    case U15C_T_K_NORM: dst = L->norms + expert * 256 + 128; rows = 1; cols = 64; break;
-    case U15C_T_K_NORM_HW: dst = L->norms + expert * 256 + 192; rows = 1; cols = 64; break;
-    case U15C_T_GATE: dst = L->gu + (long)expert * 2 * I * H; rows = I; cols = H; inter = 0; break;
-    case U15C_T_UP: dst = L->gu + (long)expert * 2 * I * H; rows = I; cols = H; inter = 1; break;
-    case U15C_T_DOWN: dst = L->down + (long)expert * H * I; rows = H; cols = I; break;
-    case U15C_T_FINAL_NORM: dst = m->final_norm + expert * H; rows = 1; cols = H; break;
+      dst = L->qkv + ((long)expert * m->qkv_n() + QD + (tensor == U15C_T_V ? KD : 0)) * H;
+      rows = KD; cols = H; src_rows = KD * m->tp_size; src_ld = H; r0 = r * KD;
+      break;
+    case U15C_T_O:
+      dst = L->o + (long)expert * H * QD;
+      rows = H; cols = QD; src_rows = H; src_ld = QDf; c0 = r * QD;
+      break;
+    case U15C_T_Q_NORM: dst = L->norms + expert * 256 + 0; whole(64); break;
+    case U15C_T_Q_NORM_HW: dst = L->norms + expert * 256 + 64; whole(64); break;
+    case U15C_T_K_NORM: dst = L->norms + expert * 256 + 128; whole(64); break;
+    case U15C_T_K_NORM_HW: dst = L->norms + expert * 256 + 192; whole(64); break;
+    case U15C_T_GATE:
+    case U15C_T_UP:
+      dst = L->gu + (long)expert * 2 * I * H;
+      rows = I; cols = H; src_rows = If; src_ld = H; r0 = r * I;
+      inter = tensor == U15C_T_GATE ? 0 : 1;
+      break;
+    case U15C_T_DOWN:
+      dst = L->down + (long)expert * H * I;
+      rows = H; cols = I; src_rows = H; src_ld = If; c0 = r * I;
+      break;
+    case U15C_T_FINAL_NORM: dst = m->final_norm + expert * H; whole(H); break;
     default: return fail(U15C_EINVAL, "unknown tensor id");
   }
-  (void)E;
   const size_t es = dtype == U15C_DT_F32 ? 4 : 2;
-  const size_t bytes = (size_t)rows * cols * es;
+  const size_t bytes = (size_t)src_rows * src_ld * es;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const void* dsrc = src;
   void* staging = nullptr;
@@ -470,7 +574,8 @@ int u15c_model_bind(u15c_model* m, u15c_stream stream, int layer, int expert, in
     }
     dsrc = staging;
   }
-  bind_kernel<<<nblk(rows * cols, 256), 256, 0, st>>>(dsrc, dtype, rows, cols, dst, inter);
+  bind_kernel<<<nblk(rows * cols, 256), 256, 0, st>>>(dsrc, dtype, rows, cols, src_ld, r0, c0,
+                                                       dst, inter);
   cudaError_t e = cudaGetLastError();
   if (staging != nullptr) {
     cudaStreamSynchronize(st);

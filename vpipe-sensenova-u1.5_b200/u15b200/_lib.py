@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(PKG, "lib", "libu15c.so")
 HEADER = os.path.join(ROOT, "include", "u15c.h")
 
 OK, EINVAL, ECUDA, ENOMEM, EDEVICE, ESTOPPED = 0, 1, 2, 3, 4, 5
-EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32 = 0, 1, 2, 3
 ATTN_BIDIRECTIONAL, ATTN_CAUSAL, ATTN_BLOCK_CAUSAL = 0, 1, 2
 EXPERT_UND, EXPERT_GEN = 0, 1
 MODEL_INT8 = 1
@@ -50,6 +50,7 @@ class Slot(C.Structure):
                 ("pos_t", C.c_void_p), ("pos_h", C.c_void_p), ("pos_w", C.c_void_p),
                 ("t_index", C.c_void_p)]
 STOP_FN = C.CFUNCTYPE(C.c_int, C.c_void_p)
+ALLREDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_long, C.c_void_p)
 
 SIGNATURES = {
     "u15c_last_error": (C.c_char_p, []),
@@ -98,6 +99,9 @@ SIGNATURES = {
     "u15c_unpatchify": (ip, [vp, vp, vp, ip, ip]),
     "u15c_model_create": (ip, [C.POINTER(Config), C.c_uint, C.POINTER(vp)]),
     "u15c_model_destroy": (None, [vp]),
+    "u15c_model_create_tp": (ip, [C.POINTER(Config), C.c_uint, ip, ip, C.POINTER(vp)]),
+    "u15c_model_tp": (ip, [vp, i32p, i32p]),
+    "u15c_model_set_allreduce": (ip, [vp, ALLREDUCE_FN, vp, vp, C.c_long]),
     "u15c_model_bind": (ip, [vp, vp, ip, ip, ip, vp, ip, ip]),
     "u15c_model_bind_random": (ip, [vp, vp, C.c_uint64, C.c_float, C.c_float, C.c_float]),
     "u15c_model_finalize": (ip, [vp, vp]),

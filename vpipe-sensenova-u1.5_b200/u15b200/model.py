@@ -17,18 +17,41 @@ FULL = dict(n_layers=42, hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=
 
 
 class Model:
-    """U15Weights + U15Backbone for one device."""
+    """U15Weights + U15Backbone for one device, or this rank's share of a
+    tensor-parallel model (tp_size > 1: bind full tensors, then install the
+    all-reduce with set_allreduce before the first pass)."""
 
-    def __init__(self, int8: bool = False, **cfg):
+    def __init__(self, int8: bool = False, tp_rank: int = 0, tp_size: int = 1, **cfg):
         c = dict(FULL)
         c.update(cfg)
         self.cfg = c
         self._cfg = L.Config(**c)
         h = C.c_void_p()
-        check(lib().u15c_model_create(C.byref(self._cfg), L.MODEL_INT8 if int8 else 0,
-                                      C.byref(h)))
+        check(lib().u15c_model_create_tp(C.byref(self._cfg), L.MODEL_INT8 if int8 else 0,
+                                         tp_rank, tp_size, C.byref(h)))
         self.h = h
         self.int8 = int8
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        self._ar_cb = None
+        self._part = None
+
+    def set_allreduce(self, group, max_tokens: int) -> None:
+        """Sum the row-parallel partial products over `group` with
+        torch.distributed.all_reduce (NCCL on GPUs), on the stream of the pass."""
+        import torch.distributed as dist
+        self._part = torch.empty(max_tokens * self.cfg["hidden"], dtype=torch.float32,
+                                 device="cuda")
+        part = self._part
+
+        def _ar(_ctx, count, _stream):
+            try:
+                dist.all_reduce(part[:count], group=group)
+                return 0
+            except Exception:   # reported to the caller as the pass's error
+                return 1
+
+        self._ar_cb = L.ALLREDUCE_FN(_ar)
+        check(lib().u15c_model_set_allreduce(self.h, self._ar_cb, None, _p(part), part.numel()))
 
     def close(self):
         if self.h:
@@ -157,7 +180,7 @@ class KvCache:
         check(lib().u15c_kv_set_page_table(self.h, arr, len(pages)))
 
     def read(self, layer: int, v: bool, n: int) -> torch.Tensor:
-        hkv = self.model.cfg["kv_heads"]
+        hkv = self.model.cfg["kv_heads"] // self.model.tp_size   # this rank's kv heads
         out = torch.empty(hkv, n, 128, dtype=torch.bfloat16, device="cuda")
         check(lib().u15c_kv_read(self.h, _stream(), layer, int(v), _p(out), n))
         return out
