@@ -380,10 +380,19 @@ def run_ours(args, rank, world, local):
         kern["attention_mma_sync_reference_layout"] = {"ms": t, "tflops": ATTN_FLOP / t / 1e9}
         torch.cuda.empty_cache()
 
+    # ---- one render over all ranks: tensor parallelism (N > 1) ----
+    tp = None
+    if world > 1:
+        del m, kv
+        torch.cuda.empty_cache()
+        tp = tp_bench(args, rank, world, dist, timed, pos, segs, x0)
+        tp["speedup_vs_one_gpu"] = ms_step / tp["ms_per_layer_fused"]
+
     # ---- denoise steps/s (BASELINE config 5 geometry), one replica per rank ----
     den = None
     if args.denoise_steps > 0:
-        del m, kv
+        if world == 1:
+            del m, kv
         torch.cuda.empty_cache()
         den = denoise_bench(args, rank, world, dist)
     clk.__exit__(None, None, None)
@@ -430,11 +439,61 @@ def run_ours(args, rank, world, local):
                      "frac": (gu.get("tflops") or 0) / bf16_peak, "traffic": traffic,
                      "peak_kind": f"{peak_kind} burst bf16"},
         "kernels": kern,
+        "tensor_parallel": tp,
         "denoise": den,
         "clocks": clk.summary(),
         "cpu_baseline": cpu_line,
     }
     print(json.dumps(line), flush=True)
+
+
+def tp_bench(args, rank, world, dist, timed, pos, segs, x0):
+    """The same layer workload as ONE render split over all ranks (tensor
+    parallelism: q/k/v heads, KV cache and gate/up by rank; o_proj and
+    down_proj row-parallel). Two forms of the row-parallel reduction: the
+    fused GEMM + reduction over NVLink peer memory (the product) and the
+    GEMM followed by NCCL all_reduce (the baseline). ms per layer is the
+    max over ranks of CUDA-event time."""
+    import torch
+    import u15b200
+    out = {"ranks": world, "workload": "the layer above, one copy split over all ranks"}
+    for form in ("nccl", "fused"):
+        m = u15b200.Model(int8=True, n_layers=args.layers, tp_rank=rank, tp_size=world)
+        m.bind_random(seed=4321, std=0.02, norm_mean=1.0, norm_std=0.2)
+        m.finalize()
+        if form == "fused":
+            m.tp_connect(None, M_TOK)
+        else:
+            m.set_allreduce(None, M_TOK)
+        kv = m.make_cache(TK)
+        g = torch.Generator(device="cuda").manual_seed(7 + rank)
+        for li in range(args.layers):
+            for v in (False, True):
+                kv.write(li, v, torch.randn(KV // world, N_PRE, HD, device="cuda",
+                                            generator=g).bfloat16())
+        x = x0.clone()
+        state = {"i": 0}
+
+        def step(int8=False):
+            li = state["i"] % args.layers
+            state["i"] += 1
+            m.layer_forward(li, x, kv, N_PRE, TK, *pos, segments=segs, int8=int8)
+
+        for int8 in (False, True):
+            for _ in range(args.warmup):
+                step(int8)
+            torch.cuda.synchronize()
+            x.copy_(x0)
+            ms = timed(lambda: step(int8), args.steps) / args.steps
+            out[f"ms_per_layer_{form}" + ("_i8" if int8 else "")] = ms
+        torch.cuda.synchronize()
+        if form == "fused":
+            m.tp_disconnect(None)
+        del kv
+        m.close()
+        del m
+        torch.cuda.empty_cache()
+    return out
 
 
 def denoise_bench(args, rank, world, dist):

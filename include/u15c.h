@@ -354,6 +354,22 @@ int u15c_model_tp(const u15c_model* m, int* tp_rank, int* tp_size);
 typedef int (*u15c_allreduce_fn)(void* ctx, long count, u15c_stream stream);
 int u15c_model_set_allreduce(u15c_model* m, u15c_allreduce_fn fn, void* ctx, float* buf,
                              long buf_elems);
+/* The fused form: o_proj / down_proj and their all-reduce in ONE kernel over
+ * NVLink peer memory (each rank's f32 partial tile goes to the tile's owner,
+ * the owner adds the ranks' partials and the residual and stores the bf16
+ * result into every rank's activations). Each rank exports a region sized
+ * for passes of up to max_tokens tokens and gets a U15C_TP_BLOB_BYTES blob
+ * (a CUDA IPC handle and the GPU's UUID); the caller gathers the blobs of
+ * all ranks in rank order (e.g. an all-gather) and imports them. Then every
+ * pass uses the fused kernel; the ranks must run the same passes in the same
+ * order, each on its own GPU (refused otherwise). */
+#define U15C_TP_BLOB_BYTES 128
+int u15c_model_tp_export(u15c_model* m, int max_tokens, void* blob);
+int u15c_model_tp_import(u15c_model* m, const void* blobs);
+/* Unmap the peers' regions (waits for this device's work first). Every rank
+ * calls it and the ranks meet (a barrier) before any of them destroys its
+ * model: a region may not be freed while a peer still maps it. */
+int u15c_model_tp_disconnect(u15c_model* m);
 
 /* U15Weights bind_bf16_/bind_matrix_ (src/u15-weights.cc:102-151,
  * 516-603): convert one tensor (f32/f16/bf16, host or device) to bf16 with

@@ -3,7 +3,9 @@ and gate/up split column-wise, o_proj and down_proj row-wise with an
 all-reduce of the f32 partial products (NCCL through torch.distributed).
 Two spawned ranks bind the same full weights; their outputs must be equal,
 match the CPU restatement of the layer (same bars as the one-GPU layer
-tests) and match a one-GPU model on the same weights."""
+tests) and match a one-GPU model on the same weights. Both forms of the
+row-parallel reduction are checked: the all-reduce hook (NCCL) and the
+fused GEMM + reduction over peer memory."""
 import os
 import socket
 from datetime import timedelta
@@ -50,19 +52,23 @@ def _bind(m, cfg, seed):
     return W
 
 
-def _tp_worker(rank, world, port, q):
+def _tp_worker(rank, world, port, q, fused=False):
     import torch.distributed as dist
     import u15b200
     torch.cuda.set_device(rank)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     try:
         T, segs, pos, x = _inputs()
         m = u15b200.Model(tp_rank=rank, tp_size=world, **TPCFG)
         _bind(m, TPCFG, 1)
-        m.set_allreduce(None, T)
+        if fused:
+            m.tp_connect(None, T)
+        else:
+            m.set_allreduce(None, T)
         pd = [dev_i32(p) for p in pos]
         kv = m.make_cache(T)
         xd = dev_bf16(x)
@@ -74,28 +80,36 @@ def _tp_worker(rank, world, port, q):
         m.forward(xd2, kv2, 0, T, *pd, segments=segs)
         torch.cuda.synchronize()
         q.put((rank, layer_out, k0, host(xd2)))
+        if fused:
+            m.tp_disconnect(None)
         dist.barrier()
+        m.close()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
-def test_tp2_layer_and_stack():
+def _run_ranks(fused):
     import multiprocessing as mp
-    import u15b200
-    from oracle import oracle as O
-    from test_gpu_layer import check_layer, dims_of
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q, fused)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    (_, l0, k0, f0), (_, l1, k1, f1) = res
+    return res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+@pytest.mark.parametrize("fused", [False, True], ids=["nccl_hook", "fused_peer"])
+def test_tp2_layer_and_stack(fused):
+    import u15b200
+    from oracle import oracle as O
+    from test_gpu_layer import check_layer, dims_of
+    (_, l0, k0, f0), (_, l1, k1, f1) = _run_ranks(fused)
     # the all-reduce hands every rank the same sums: replicas stay identical
     assert np.array_equal(l0, l1) and np.array_equal(f0, f1)
     T, segs, pos, x = _inputs()

@@ -29,13 +29,11 @@
 //               token-major [tq][hq*128]
 // TMEM (512 columns): tile t at t*256: S_t / P_t [0,128) | O_t [128,256).
 //
-// Of each row's four 32-score chunks, the EMU template mask selects the
-// ones whose 2^x is computed on the FMA pipe (ex2_fma) instead of the MUFU
-// unit; the two units then share the exponentials and neither bounds the
-// softmax alone. The mask must be a compile-time constant: as a run-time
-// value every chunk became its own basic block with both code paths, which
-// kept the scheduler from interleaving MUFU and FMA work across chunks and
-// doubled the loop's code (instruction-cache misses).
+// The exponentials stay on the MUFU unit: moving a quarter or half of them
+// to the FMA pipe (a fitted polynomial on the fraction plus an exponent-field
+// add) measured 4 % and 12 % slower on B200 -- the softmax is bound by its
+// dependency latency, not by the MUFU's throughput -- so the row max and
+// row sum are split into independent chains instead.
 //
 // The Sage variant (int8 QK, SageAttention) feeds S from int8 Q and smoothed
 // int8 K (kind::i8, s32 accumulators) and scales the scores by the per-64-row
@@ -71,7 +69,6 @@ constexpr int kQBytes = 2 * kTile * 256;        // bf16 Q, 2 tiles; int8 uses ha
 constexpr int kKBytes = kBlk * 256;             // [2 dims blocks][128 keys][128 B]
 constexpr int kVBytes = 128 * kBlk * 2;         // [2 key blocks][128 dims][128 B]
 constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256;
-constexpr unsigned kEmuMaskDefault = 0x8;       // chunk 3 of 4: a quarter of the exponentials
 
 struct TcAttnP {
   int hq, hkv, tq, tk, G;
@@ -110,24 +107,6 @@ __device__ __forceinline__ float ex2(float x)
   return y;
 }
 
-// 2^x for x <= 2^7 on the FMA pipe: x = n + f with n = rint(x) taken from
-// the low mantissa bits of x + 1.5 * 2^23, f in [-0.5, 0.5]; 2^f by a degree-3
-// polynomial fitted to minimise the relative error on that interval (max
-// relative error 7.5e-5, below the bf16 rounding P receives); 2^n added to
-// the exponent field. Inputs below -125 are clamped there (2^-125, a
-// normal float) so the exponent never underflows; masked scores (-inf) give
-// 2^-125 instead of 0, which no bf16 output can show.
-__device__ __forceinline__ float ex2_fma(float x)
-{
-  x = fmaxf(x, -125.0f);
-  const float t = x + 12582912.0f;
-  const float f = x - (t - 12582912.0f);
-  float q = fmaf(0.05517132207751274f, f, 0.24261054396629333f);
-  q = fmaf(q, f, 0.6932609677314758f);
-  q = fmaf(q, f, 0.9999281167984009f);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
-}
-
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16])
 {
   asm volatile(
@@ -152,7 +131,7 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-template <bool SAGE, unsigned EMU>
+template <bool SAGE>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
@@ -385,13 +364,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= kmax) s[i] = -INFINITY;
       }
-      float ma = s[0], mb = s[64];
+      // row maxima of the two 64-key halves, four independent chains each
+      // (one serial chain of 64 would put its latency on the critical path)
+      float ma[4], mb[4];
 #pragma unroll
-      for (int i = 1; i < 64; ++i) {
-        ma = fmaxf(ma, s[i]);
-        mb = fmaxf(mb, s[64 + i]);
+      for (int k = 0; k < 4; ++k) {
+        ma[k] = s[k];
+        mb[k] = s[64 + k];
       }
-      const float mt = fmaxf(ma * f0, mb * f1);
+#pragma unroll
+      for (int i = 4; i < 64; i += 4) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          ma[k] = fmaxf(ma[k], s[i + k]);
+          mb[k] = fmaxf(mb[k], s[64 + i + k]);
+        }
+      }
+      const float mt = fmaxf(fmaxf(fmaxf(ma[0], ma[1]), fmaxf(ma[2], ma[3])) * f0,
+                             fmaxf(fmaxf(mb[0], mb[1]), fmaxf(mb[2], mb[3])) * f1);
       const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
       const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
@@ -410,30 +400,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       m_ref = m_new;
       const float nm = -m_ref;
-      float rs = 0.0f;
+      float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // four independent partial sums
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const float fc = c < 2 ? f0 : f1;
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
-          float a, b;
-          if ((EMU >> c) & 1) {   // folded: c is a constant after unrolling
-            a = ex2_fma(x0);
-            b = ex2_fma(x1);
-          } else {
-            a = ex2(x0);
-            b = ex2(x1);
-          }
-          rs += a + b;
+          const float a = ex2(fmaf(s[32 * c + 2 * i], fc, nm));
+          const float b = ex2(fmaf(s[32 * c + 2 * i + 1], fc, nm));
+          rs[i & 3] += a + b;
           pk[i] = pack_bf2(a, b);
         }
         // P chunk c -> columns [16c, 16c+16), whose scores were all read
         tmem_st16(tS + 16 * c, pk);
       }
       tmem_st_wait();
-      l += rs;
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tc_fence_before();
       mbar_arrive(p_full + 8 * t);
     }
@@ -487,12 +470,6 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
     *err = "attention: the page pool holds fewer pages than the key length needs";
     return 1;
   }
-  // U15_ATTN_EMU (0, 8 or 12): which 32-score chunks use the FMA-pipe 2^x
-  static const unsigned emu = [] {
-    const char* e = std::getenv("U15_ATTN_EMU");
-    const unsigned v = e != nullptr ? (unsigned)std::strtoul(e, nullptr, 0) : kEmuMaskDefault;
-    return (v == 0 || v == 8 || v == 12) ? v : kEmuMaskDefault;
-  }();
   TcAttnP p{};
   p.hq = a.hq;
   p.hkv = a.hkv;
@@ -517,17 +494,11 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
     if (make_tma_2d(&mk, a.k_pages, (uint64_t)a.n_pages * a.hkv * 64, 128, 64, 2, err)) return 2;
   }
   if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, 64, 128, 2, err)) return 2;
-  static std::atomic<uint64_t> set_attr[6];
+  static std::atomic<uint64_t> set_attr[2];
   const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
-  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcAttnP);
-  const int ei = emu == 0 ? 0 : emu == 8 ? 1 : 2;
-  static const Kern kerns[6] = {attn_tc_kernel<false, 0>, attn_tc_kernel<false, 8>,
-                                attn_tc_kernel<false, 12>, attn_tc_kernel<true, 0>,
-                                attn_tc_kernel<true, 8>, attn_tc_kernel<true, 12>};
-  const int ki = (sage ? 3 : 0) + ei;
-  Kern k = kerns[ki];
+  auto k = sage ? attn_tc_kernel<true> : attn_tc_kernel<false>;
   cudaError_t e = cudaSuccess;
-  if (smem_attr_once(k, kSmem, set_attr[ki])) {
+  if (smem_attr_once(k, kSmem, set_attr[sage ? 1 : 0])) {
     k<<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
     e = cudaGetLastError();
   } else {

@@ -219,7 +219,7 @@ int run_gemm(GemmArgs& a, cudaStream_t st)
 {
   DevState* d = dev();
   if (d == nullptr) return U15C_ECUDA;
-  if (a.x == nullptr || a.w == nullptr || a.y == nullptr)
+  if (a.x == nullptr || a.w == nullptr || (a.y == nullptr && a.epilogue != kEpiTpReduce))
     return fail(U15C_EINVAL, "gemm: null buffer");
   a.dev_err = d->err;
   a.num_sms = d->sms;

@@ -28,6 +28,7 @@ enum DevErr : unsigned {
   kDevWaitAccFull = 0x103,   // epilogue waited too long for an accumulator
   kDevWaitAccEmpty = 0x104,  // MMA waited too long for the epilogue
   kDevWaitDrain = 0x105,     // unwinding waited too long for in-flight work
+  kDevWaitPeer = 0x106,      // a tensor-parallel rank's partial or result did not arrive
   kDevBadArg = 0x201,        // a kernel saw an argument it cannot serve
 };
 
@@ -64,6 +65,32 @@ __device__ __forceinline__ uint64_t globaltimer()
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// ---------------------------------------------------------------------
+// cross-GPU signalling (tensor parallelism over peer memory): 64-bit
+// counters in a rank's memory, incremented by its peers with release
+// semantics at system scope, read with acquire semantics.
+// ---------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p)
+{
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned long long* p, unsigned long long v)
+{
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Bounded wait until *p >= target (U15_WAIT_LIMIT_NS): false, with `code` in
+// the status word, when it runs out.
+__device__ __forceinline__ bool wait_counter_sys(const unsigned long long* p,
+                                                 unsigned long long target, unsigned* err,
+                                                 unsigned code);
+// named barrier over `threads` threads (a multiple of 32) of the CTA
+__device__ __forceinline__ void named_bar_sync(int id, int threads)
+{
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
 {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -115,6 +142,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > U15_WAIT_LIMIT_NS) {
+      dev_fail(err, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool wait_counter_sys(const unsigned long long* p,
+                                                 unsigned long long target, unsigned* err,
+                                                 unsigned code)
+{
+  if (ld_acquire_sys(p) >= target) return true;
+  const uint64_t t0 = globaltimer();
+#pragma unroll 1
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(p) >= target) return true;
     if (globaltimer() - t0 > U15_WAIT_LIMIT_NS) {
       dev_fail(err, code);
       return false;

@@ -69,6 +69,7 @@ struct Params {
   const float* s_ch;           // int8: [E][N]
   int32_t* acc_dump;           // int8 debug: [M][N] raw accumulators, or null
   unsigned* err;
+  TpPeers tp;           // kEpiTpReduce
   Unit units[kMaxUnits];
 };
 
@@ -566,6 +567,90 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int oc = nb * 128 + gsub + c * 32;
           if (row_ok) store_row32(yrow + oc, g, oc, nout);
         }
+      } else if constexpr (EPI == kEpiTpReduce) {
+        // Row-parallel product over tensor-parallel ranks. 1) this rank's f32
+        // partial -> the owner's inbox plane [rank]; the accumulator is free
+        // once read, so the MMA may start the next tile while the ranks meet.
+        const TpPeers& tp = p.tp;
+        const int owner = nb % tp.size, lb = nb / tp.size;
+        const long cols = (long)p.N / tp.size;
+        const long plane = tp.rows * cols;
+        float* mine = tp.inbox[owner] + (long)tp.rank * plane + (long)row * cols + lb * 256;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float v[32];
+          chunk_values<I8>(tb + c * 32, v, p, row, row_ok, nb * 256 + c * 32, u.expert);
+          if (row_ok) store_row32_f32(mine + c * 32, v, 0, 32);
+        }
+        tc_fence_before();
+        mbar_arrive_cluster(acce_leader0 + 8 * acc);
+        named_bar_sync(1, 128);   // this CTA's 128 rows are stored
+        unsigned long long* arrive = tp.arrive[owner] + 2 * (long)t + rank;
+        if (owner != tp.rank) {
+          if (threadIdx.x == 64) {
+            __threadfence_system();
+            red_release_sys_add(arrive, 1ull);
+          }
+          continue;
+        }
+        // 2) owner: the other ranks' partials of these rows, then
+        //    x = bf16(x + bf16(sum of the planes)) into every rank's x
+        if (threadIdx.x == 64) {
+          wait_counter_sys(arrive, (unsigned long long)(tp.size - 1), p.err, kDevWaitPeer);
+          *arrive = 0ull;   // ready for the next pass: no rank adds to it before done below
+        }
+        named_bar_sync(1, 128);
+        if (row_ok) {
+          const float* src = tp.inbox[tp.rank] + (long)row * cols + lb * 256;
+          const long xo = (long)row * p.N + nb * 256;
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            float acc32[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc32[i] = 0.0f;
+#pragma unroll 1
+            for (int q = 0; q < tp.size; ++q) {
+              const float4* s4 = reinterpret_cast<const float4*>(src + q * plane + c * 32);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const float4 f = __ldcg(s4 + k);
+                acc32[4 * k] += f.x;
+                acc32[4 * k + 1] += f.y;
+                acc32[4 * k + 2] += f.z;
+                acc32[4 * k + 3] += f.w;
+              }
+            }
+            const uint4* r4 = reinterpret_cast<const uint4*>(
+                static_cast<const __nv_bfloat16*>(tp.x[tp.rank]) + xo + c * 32);
+            uint4 o4[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 rr = __ldcg(r4 + k);
+              const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
+              uint32_t ow[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 xr = unpack_bf2(rw[e]);
+                ow[e] = pack_bf2(xr.x + bfround(acc32[8 * k + 2 * e]),
+                                 xr.y + bfround(acc32[8 * k + 2 * e + 1]));
+              }
+              o4[k] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            }
+#pragma unroll 1
+            for (int q = 0; q < tp.size; ++q) {
+              uint4* d4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(tp.x[q]) + xo +
+                                                   c * 32);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) d4[k] = o4[k];
+            }
+          }
+        }
+        named_bar_sync(1, 128);   // every rank's copy of these rows is stored
+        if (threadIdx.x == 64) {
+          __threadfence_system();
+          for (int q = 0; q < tp.size; ++q) red_release_sys_add(tp.done[q], 1ull);
+        }
+        continue;
       } else {
         const int n0 = nb * 256 + (half ? 128 * ti.half : 0);
         const int nchunk = half ? 4 : 8;
@@ -723,7 +808,7 @@ bool no_split()
 // whole tile lists after the others and double the kernel's time.
 template <bool I8, int EPI>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mbh, Params p,
-                int tiles, cudaStream_t st)
+                int tiles, cudaStream_t st, bool allow_split = true)
 {
   static std::atomic<uint64_t> attr_set;
   static std::atomic<int> max_pairs_dev[64];   // resident pairs, per device (0: not yet known)
@@ -754,7 +839,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   // at least half the pairs idle, its tiles run as half-width tiles, which
   // all fit in one round of half the length.
   const int rest = tiles % pairs;
-  p.n_full = (rest > 0 && 2 * rest <= pairs && !no_split()) ? tiles - rest : tiles;
+  p.n_full = (allow_split && rest > 0 && 2 * rest <= pairs && !no_split()) ? tiles - rest : tiles;
   cfg.gridDim = dim3(2 * pairs);
   return cudaLaunchKernelEx(&cfg, k, ma, mb, mbh, p) == cudaSuccess ? 0 : 2;
 }
@@ -795,6 +880,13 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
     *err = "gemm: the residual epilogue needs a residual input";
     return 1;
   }
+  const bool tp = a.epilogue == kEpiTpReduce;
+  if (tp && (a.tp == nullptr || a.tp->size < 2 || a.tp->size > kMaxTp || a.N % (256 * a.tp->size) ||
+             a.M > a.tp->rows)) {
+    *err = "gemm: the tensor-parallel epilogue needs its peers, N a multiple of 256 x ranks "
+           "and M within the peers' buffers";
+    return 1;
+  }
   Params p{};
   p.M = a.M;
   p.N = a.N;
@@ -808,6 +900,7 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   p.s_ch = a.s_ch;
   p.acc_dump = a.acc_dump;
   p.err = a.dev_err;
+  if (tp) p.tp = *a.tp;
 
   // Units: 128-row blocks intersected with the routing segments.
   int nseg = a.nseg;
@@ -823,7 +916,7 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
     *err = "gemm: segments must cover [0, M)";
     return 1;
   }
-  const bool pair = use_pair(a.M);
+  const bool pair = tp || use_pair(a.M);   // the fused TP epilogue exists in the pair kernel
   const int bm = pair ? 256 : kBM;
   int n_units = 0;
   for (int m0 = 0; m0 < a.M; m0 += bm) {
@@ -871,6 +964,15 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   const int tiles = p.n_units * p.n_nblk;
   const int sms = a.num_sms > 0 ? a.num_sms : 148;
   int rc;
+  if (a.out_tiles != nullptr) *a.out_tiles = tiles;
+  if (tp) {
+    // every rank enumerates the same full-width tiles (no split tail): the
+    // arrival counters are indexed by tile
+    rc = a.int8 ? launch_pair<true, kEpiTpReduce>(ma, mb, mbh, p, tiles, st, false)
+                : launch_pair<false, kEpiTpReduce>(ma, mb, mbh, p, tiles, st, false);
+    if (rc) *err = "gemm (tensor-parallel): kernel launch failed";
+    return rc;
+  }
   if (pair) {
     if (a.int8) {
       rc = a.epilogue == kEpiResid    ? launch_pair<true, kEpiResid>(ma, mb, mbh, p, tiles, st)
@@ -900,6 +1002,21 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   }
   if (rc) *err = "gemm: kernel launch failed";
   return rc;
+}
+
+namespace {
+__global__ void tp_wait_kernel(const unsigned long long* done, unsigned long long target,
+                               unsigned* err)
+{
+  if (threadIdx.x == 0) wait_counter_sys(done, target, err, kDevWaitPeer);
+}
+}  // namespace
+
+int launch_tp_wait(const unsigned long long* done, unsigned long long target, unsigned* err,
+                   cudaStream_t st)
+{
+  tp_wait_kernel<<<1, 32, 0, st>>>(done, target, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
 }  // namespace u15

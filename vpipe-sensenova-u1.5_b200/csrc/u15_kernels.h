@@ -29,7 +29,30 @@ inline bool smem_attr_once(Kernel kern, int bytes, std::atomic<uint64_t>& done)
   return true;
 }
 
-enum Epilogue { kEpiStore = 0, kEpiResid = 1, kEpiSwiglu = 2, kEpiStoreF32 = 3 };
+enum Epilogue {
+  kEpiStore = 0,
+  kEpiResid = 1,
+  kEpiSwiglu = 2,
+  kEpiStoreF32 = 3,
+  kEpiTpReduce = 4,   // row-parallel product summed over tensor-parallel ranks (TpPeers)
+};
+
+// Tensor-parallel peers for the fused row-parallel GEMM (kEpiTpReduce).
+// Column block nb (256 columns) of the [M][N] product is owned by rank
+// nb % size. Every rank stores its f32 partial of a tile into the owner's
+// inbox plane [rank] and counts it on the owner's arrive[tile][cta]; the
+// owner adds the planes and the residual x, rounds as the residual epilogue
+// does, stores the bf16 result into every rank's x and counts it on every
+// rank's done.
+constexpr int kMaxTp = 8;
+struct TpPeers {
+  int rank = 0, size = 1;
+  long rows = 0;                              // rows of an inbox plane / of x
+  float* inbox[kMaxTp] = {};                  // owner q: [size][rows][N / size] f32
+  void* x[kMaxTp] = {};                       // rank q: residual stream [rows][N] bf16
+  unsigned long long* arrive[kMaxTp] = {};    // owner q: [tiles][2] (reset by the owner)
+  unsigned long long* done[kMaxTp] = {};      // rank q: cumulative count of finished tile halves
+};
 
 // Token segments routed to experts: rows [off[i], off[i+1]) use expert[i].
 constexpr int kMaxSeg = 8;
@@ -59,9 +82,15 @@ struct GemmArgs {
   int32_t* acc_dump = nullptr;   // int8 debug [M][N]
   unsigned* dev_err = nullptr;
   int num_sms = 148;
+  const TpPeers* tp = nullptr;   // kEpiTpReduce
+  int* out_tiles = nullptr;      // kEpiTpReduce: tiles of the launch (done counts 2 per tile)
 };
 
 int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err);
+// One thread waits (bounded) until *done >= target with acquire semantics at
+// system scope, so the stream's later kernels see the peers' stores.
+int launch_tp_wait(const unsigned long long* done, unsigned long long target, unsigned* err,
+                   cudaStream_t st);
 
 // Paged or contiguous K/V addressing shared by the attention and KV kernels.
 // Token j of kv head h lives at

@@ -123,6 +123,15 @@ struct u15c_model {
   void* ar_ctx = nullptr;
   float* part = nullptr;
   long part_elems = 0;
+  // tensor parallelism fused over peer memory (u15c_model_tp_export/import):
+  // this rank's region [inbox | x | arrive | done], the peers' mappings of
+  // theirs, and the done count every rank reaches after each fused product
+  void* tp_mem = nullptr;
+  int tp_rows = 0;
+  void* tp_peer[u15::kMaxTp] = {};
+  u15::TpPeers tpp;
+  bool tp_fused = false;
+  unsigned long long tp_done_target = 0;
   unsigned flags = 0;
   int device = 0;
   std::vector<LayerW> layers;
@@ -203,6 +212,9 @@ struct u15c_model {
   ~u15c_model()
   {
     free_scratch();
+    for (int q = 0; q < u15::kMaxTp; ++q)
+      if (tp_peer[q] != nullptr && tp_peer[q] != tp_mem) cudaIpcCloseMemHandle(tp_peer[q]);
+    if (tp_mem != nullptr) cudaFree(tp_mem);
     for (void* p : allocs) cudaFree(p);
   }
 };
@@ -301,7 +313,7 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
   // prequant: the activation was already quantised into x8/s_tok (by the
   // fused RMSNorm + quantisation), so the int8 path skips its own pass.
   auto gemm = [&](const void* in, int K, const bf16* w, const int8_t* w8, const float* ws, int N,
-                  int epi, void* y, bool prequant = false) -> int {
+                  int epi, void* y, bool prequant = false, int* out_tiles = nullptr) -> int {
     u15::GemmArgs a;
     a.n_experts = E;
     a.M = M;
@@ -313,6 +325,10 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
     a.epilogue = epi;
     a.y = y;
     a.resid = epi == u15::kEpiResid ? x : nullptr;
+    if (epi == u15::kEpiTpReduce) {
+      a.tp = &m->tpp;
+      a.out_tiles = out_tiles;
+    }
     if (i8) {
       if (!prequant && u15::launch_quant_rows(in, m->x8, m->s_tok, M, K, st))
         return fail(U15C_ECUDA, "quant_rows launch failed");
@@ -334,6 +350,19 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
   auto row_parallel = [&](const void* in, int K, const bf16* w, const int8_t* w8,
                           const float* ws) -> int {
     if (m->tp_size == 1) return gemm(in, K, w, w8, ws, H, u15::kEpiResid, x);
+    if (m->tp_fused) {
+      // one kernel: partial products to their owners over NVLink, the
+      // owners' sums + residual into every rank's x, then wait for all of x
+      int tiles = 0;
+      int r = gemm(in, K, w, w8, ws, H, u15::kEpiTpReduce, nullptr, false, &tiles);
+      if (r) return r;
+      m->tp_done_target += 2ull * (unsigned long long)tiles;
+      u15::DevState* d = u15::dev();
+      if (u15::launch_tp_wait(m->tpp.done[m->tp_rank], m->tp_done_target, d ? d->err : nullptr,
+                              st))
+        return fail(U15C_ECUDA, "tensor-parallel wait launch failed");
+      return U15C_OK;
+    }
     const long n = (long)M * H;
     if (m->ar_fn == nullptr || m->part == nullptr || m->part_elems < n)
       return fail(U15C_EINVAL, "tensor-parallel model: no all-reduce installed, or its "
@@ -387,6 +416,36 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
   if ((rc = row_parallel(m->h, I, L.down, L.down8, L.down_s))) return rc;
   return U15C_OK;
 }
+
+// Fused tensor parallelism runs a pass on this rank's residual stream in
+// the peer region (the owners of the row-parallel products store their
+// results there on every rank): copy the caller's activations in before the
+// layers and out after them.
+struct TpStream {
+  u15c_model* m;
+  void* user;
+  long bytes;
+  cudaStream_t st;
+  bf16* x = nullptr;
+  int enter(int M)
+  {
+    x = static_cast<bf16*>(user);
+    if (!m->tp_fused) return U15C_OK;
+    if (M > m->tp_rows)
+      return fail(U15C_EINVAL, "tensor-parallel pass of " + std::to_string(M) +
+                                   " tokens exceeds the peer buffers (" +
+                                   std::to_string(m->tp_rows) + ")");
+    x = static_cast<bf16*>(m->tpp.x[m->tp_rank]);
+    const cudaError_t e = cudaMemcpyAsync(x, user, bytes, cudaMemcpyDeviceToDevice, st);
+    return e == cudaSuccess ? U15C_OK : cuda_fail(e, "tensor-parallel pass: copy in");
+  }
+  int leave(int rc)
+  {
+    if (rc != U15C_OK || !m->tp_fused) return rc;
+    const cudaError_t e = cudaMemcpyAsync(user, x, bytes, cudaMemcpyDeviceToDevice, st);
+    return e == cudaSuccess ? U15C_OK : cuda_fail(e, "tensor-parallel pass: copy out");
+  }
+};
 
 int validate_pass(u15c_model* m, int n, u15c_kv* kv, int kv_off, int kv_len, int attn,
                   const int32_t* pos_t, const int32_t* pos_h, const int32_t* pos_w,
@@ -496,6 +555,133 @@ int u15c_model_tp(const u15c_model* m, int* tp_rank, int* tp_size)
   if (tp_rank) *tp_rank = m->tp_rank;
   if (tp_size) *tp_size = m->tp_size;
   return U15C_OK;
+}
+
+namespace {
+// the peer region of one rank: [inbox f32 rows x H | x bf16 rows x H |
+// arrive u64 [tiles][2] | done u64], sections 256-byte aligned
+struct TpLayout {
+  size_t inbox, x, arrive, done, total;
+  TpLayout(long rows, long H)
+  {
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const long tiles = ((rows + 255) / 256 + u15::kMaxSeg) * (H / 256);
+    inbox = 0;
+    x = up(inbox + (size_t)rows * H * 4);
+    arrive = up(x + (size_t)rows * H * 2);
+    done = up(arrive + (size_t)tiles * 2 * 8);
+    total = up(done + 8);
+  }
+};
+struct TpBlob {   // U15C_TP_BLOB_BYTES: what one rank hands its peers
+  cudaIpcMemHandle_t handle;   // 64 bytes
+  unsigned char uuid[16];
+  int rows, rank, size, hidden;
+  unsigned char pad[128 - 64 - 16 - 16];
+};
+static_assert(sizeof(TpBlob) == U15C_TP_BLOB_BYTES, "tp blob size");
+}  // namespace
+
+int u15c_model_tp_export(u15c_model* m, int max_tokens, void* blob)
+{
+  if (m == nullptr || blob == nullptr || max_tokens <= 0)
+    return fail(U15C_EINVAL, "tp_export: bad argument");
+  if (m->tp_size < 2) return fail(U15C_EINVAL, "tp_export: the model is not tensor-parallel");
+  if (m->cfg.hidden % (256 * m->tp_size))
+    return fail(U15C_EINVAL, "tp_export: hidden must be a multiple of 256 x tp_size");
+  if (m->tp_mem != nullptr) return fail(U15C_EINVAL, "tp_export: already exported");
+  DeviceScope ds(m->device);
+  const TpLayout lay(max_tokens, m->cfg.hidden);
+  cudaError_t e = cudaMalloc(&m->tp_mem, lay.total);
+  if (e != cudaSuccess) {
+    m->tp_mem = nullptr;
+    return fail(U15C_ENOMEM, "tp_export: peer region allocation failed");
+  }
+  e = cudaMemset(m->tp_mem, 0, lay.total);
+  TpBlob b{};
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&b.handle, m->tp_mem);
+  cudaDeviceProp prop{};
+  if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, m->device);
+  if (e != cudaSuccess) {
+    cudaFree(m->tp_mem);
+    m->tp_mem = nullptr;
+    return cuda_fail(e, "tp_export");
+  }
+  std::memcpy(b.uuid, prop.uuid.bytes, 16);
+  b.rows = max_tokens;
+  b.rank = m->tp_rank;
+  b.size = m->tp_size;
+  b.hidden = m->cfg.hidden;
+  std::memcpy(blob, &b, sizeof b);
+  m->tp_rows = max_tokens;
+  return U15C_OK;
+}
+
+int u15c_model_tp_import(u15c_model* m, const void* blobs)
+{
+  if (m == nullptr || blobs == nullptr) return fail(U15C_EINVAL, "tp_import: bad argument");
+  if (m->tp_mem == nullptr) return fail(U15C_EINVAL, "tp_import: call u15c_model_tp_export first");
+  if (m->tp_fused) return fail(U15C_EINVAL, "tp_import: already connected");
+  const int P = m->tp_size;
+  std::vector<TpBlob> b(P);
+  std::memcpy(b.data(), blobs, sizeof(TpBlob) * P);
+  for (int q = 0; q < P; ++q) {
+    if (b[q].rank != q || b[q].size != P || b[q].rows != m->tp_rows || b[q].hidden != m->cfg.hidden)
+      return fail(U15C_EINVAL, "tp_import: the ranks' blobs disagree (order by rank; same "
+                               "max_tokens and model on every rank)");
+    for (int r = 0; r < q; ++r)
+      if (std::memcmp(b[q].uuid, b[r].uuid, 16) == 0)
+        return fail(U15C_EINVAL, "tp_import: two ranks share one GPU; the fused ranks wait on "
+                                 "each other inside their kernels and need a GPU each");
+  }
+  DeviceScope ds(m->device);
+  for (int q = 0; q < P; ++q) {
+    if (q == m->tp_rank) {
+      m->tp_peer[q] = m->tp_mem;
+      continue;
+    }
+    void* ptr = nullptr;
+    const cudaError_t e =
+        cudaIpcOpenMemHandle(&ptr, b[q].handle, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int r = 0; r < q; ++r)
+        if (r != m->tp_rank && m->tp_peer[r]) cudaIpcCloseMemHandle(m->tp_peer[r]);
+      for (int r = 0; r < P; ++r) m->tp_peer[r] = nullptr;
+      return cuda_fail(e, "tp_import: opening a peer's region");
+    }
+    m->tp_peer[q] = ptr;
+  }
+  const TpLayout lay(m->tp_rows, m->cfg.hidden);
+  m->tpp.rank = m->tp_rank;
+  m->tpp.size = P;
+  m->tpp.rows = m->tp_rows;
+  for (int q = 0; q < P; ++q) {
+    char* base = static_cast<char*>(m->tp_peer[q]);
+    m->tpp.inbox[q] = reinterpret_cast<float*>(base + lay.inbox);
+    m->tpp.x[q] = base + lay.x;
+    m->tpp.arrive[q] = reinterpret_cast<unsigned long long*>(base + lay.arrive);
+    m->tpp.done[q] = reinterpret_cast<unsigned long long*>(base + lay.done);
+  }
+  m->tp_done_target = 0;
+  m->tp_fused = true;
+  return U15C_OK;
+}
+
+int u15c_model_tp_disconnect(u15c_model* m)
+{
+  if (m == nullptr) return fail(U15C_EINVAL, "null model");
+  DeviceScope ds(m->device);
+  cudaError_t e = cudaDeviceSynchronize();   // no kernel of ours still touches a peer
+  for (int q = 0; q < u15::kMaxTp; ++q) {
+    if (m->tp_peer[q] != nullptr && m->tp_peer[q] != m->tp_mem) {
+      const cudaError_t c = cudaIpcCloseMemHandle(m->tp_peer[q]);
+      if (e == cudaSuccess) e = c;
+    }
+    m->tp_peer[q] = nullptr;
+  }
+  m->tpp = u15::TpPeers{};
+  m->tp_fused = false;
+  return e == cudaSuccess ? U15C_OK : cuda_fail(e, "tp_disconnect");
 }
 
 void u15c_model_destroy(u15c_model* m)
@@ -760,8 +946,10 @@ int u15c_layer_forward(u15c_model* m, u15c_stream stream, int layer, void* x, in
   sl.kv_len = kv_len;
   sl.attn = attn;
   sl.t_index = t_index;
-  return layer_impl(m, st, layer, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, {sl},
-                    flags);
+  TpStream tx{m, x, (long)n * m->cfg.hidden * 2, st};
+  if ((rc = tx.enter(n))) return rc;
+  return tx.leave(
+      layer_impl(m, st, layer, tx.x, n, seg, seg_off, seg_expert, nseg, {sl}, flags));
 }
 
 int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* seg_off,
@@ -784,7 +972,11 @@ int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* s
   if (u15::launch_rope_tables(pos_t, pos_h, pos_w, n, 64, 32, m->cfg.theta_t, m->cfg.theta_hw,
                               m->rcos, m->rsin, st))
     return fail(U15C_ECUDA, "rope tables launch failed");
+  TpStream tx{m, x, (long)n * m->cfg.hidden * 2, st};
+  if ((rc = tx.enter(n))) return rc;
   for (int li = 0; li < m->cfg.n_layers; ++li) {
+    // with tensor parallelism the stop callback must answer alike on every
+    // rank (the ranks meet in every layer)
     if (stop != nullptr && stop(stop_ctx) != 0) return fail(U15C_ESTOPPED, "stopped");
     SlotRun sl;
     sl.n = n;
@@ -793,11 +985,10 @@ int u15c_forward(u15c_model* m, u15c_stream stream, void* x, int n, const int* s
     sl.kv_len = kv_len;
     sl.attn = attn;
     sl.t_index = t_index;
-    if ((rc = layer_impl(m, st, li, static_cast<bf16*>(x), n, seg, seg_off, seg_expert, nseg, {sl},
-                         flags)))
+    if ((rc = layer_impl(m, st, li, tx.x, n, seg, seg_off, seg_expert, nseg, {sl}, flags)))
       return rc;
   }
-  return U15C_OK;
+  return tx.leave(U15C_OK);
 }
 
 int u15c_forward_many(u15c_model* m, u15c_stream stream, void* x, int n, const u15c_slot* slots,
@@ -841,12 +1032,13 @@ int u15c_forward_many(u15c_model* m, u15c_stream stream, void* x, int n, const u
   seg.off[1] = M;
   seg.expert[0] = expert;
   const int off[2] = {0, M}, ex[1] = {expert};
+  TpStream tx{m, x, (long)M * m->cfg.hidden * 2, st};
+  if ((rc = tx.enter(M))) return rc;
   for (int li = 0; li < m->cfg.n_layers; ++li) {
     if (stop != nullptr && stop(stop_ctx) != 0) return fail(U15C_ESTOPPED, "stopped");
-    if ((rc = layer_impl(m, st, li, static_cast<bf16*>(x), M, seg, off, ex, 1, runs, flags)))
-      return rc;
+    if ((rc = layer_impl(m, st, li, tx.x, M, seg, off, ex, 1, runs, flags))) return rc;
   }
-  return U15C_OK;
+  return tx.leave(U15C_OK);
 }
 
 int u15c_final_norm(u15c_model* m, u15c_stream stream, void* x, int n, int expert)

@@ -17,6 +17,7 @@ HEADER = os.path.join(ROOT, "include", "u15c.h")
 
 OK, EINVAL, ECUDA, ENOMEM, EDEVICE, ESTOPPED = 0, 1, 2, 3, 4, 5
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32 = 0, 1, 2, 3
+TP_BLOB_BYTES = 128
 ATTN_BIDIRECTIONAL, ATTN_CAUSAL, ATTN_BLOCK_CAUSAL = 0, 1, 2
 EXPERT_UND, EXPERT_GEN = 0, 1
 MODEL_INT8 = 1
@@ -102,6 +103,9 @@ SIGNATURES = {
     "u15c_model_create_tp": (ip, [C.POINTER(Config), C.c_uint, ip, ip, C.POINTER(vp)]),
     "u15c_model_tp": (ip, [vp, i32p, i32p]),
     "u15c_model_set_allreduce": (ip, [vp, ALLREDUCE_FN, vp, vp, C.c_long]),
+    "u15c_model_tp_export": (ip, [vp, ip, vp]),
+    "u15c_model_tp_import": (ip, [vp, vp]),
+    "u15c_model_tp_disconnect": (ip, [vp]),
     "u15c_model_bind": (ip, [vp, vp, ip, ip, ip, vp, ip, ip]),
     "u15c_model_bind_random": (ip, [vp, vp, C.c_uint64, C.c_float, C.c_float, C.c_float]),
     "u15c_model_finalize": (ip, [vp, vp]),

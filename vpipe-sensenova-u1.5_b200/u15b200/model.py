@@ -53,6 +53,25 @@ class Model:
         self._ar_cb = L.ALLREDUCE_FN(_ar)
         check(lib().u15c_model_set_allreduce(self.h, self._ar_cb, None, _p(part), part.numel()))
 
+    def tp_connect(self, group, max_tokens: int) -> None:
+        """The fused form: o_proj / down_proj and their all-reduce in one kernel
+        over NVLink peer memory. Exchanges the ranks' peer-region handles over
+        `group` (an all-gather of small host blobs)."""
+        import torch.distributed as dist
+        blob = (C.c_char * L.TP_BLOB_BYTES)()
+        check(lib().u15c_model_tp_export(self.h, max_tokens, blob))
+        blobs = [None] * self.tp_size
+        dist.all_gather_object(blobs, bytes(blob), group=group)
+        arr = (C.c_char * (L.TP_BLOB_BYTES * self.tp_size)).from_buffer_copy(b"".join(blobs))
+        check(lib().u15c_model_tp_import(self.h, arr))
+
+    def tp_disconnect(self, group) -> None:
+        """Unmap the peers' regions, then meet the other ranks: after this
+        every rank may destroy its model."""
+        import torch.distributed as dist
+        check(lib().u15c_model_tp_disconnect(self.h))
+        dist.barrier(group=group)
+
     def close(self):
         if self.h:
             lib().u15c_model_destroy(self.h)
