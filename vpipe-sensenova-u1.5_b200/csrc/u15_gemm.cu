@@ -391,6 +391,7 @@ constexpr int kStagesP = 6;
 constexpr int kAStageP = 128 * 128;   // per CTA: 128 rows x 128 B
 constexpr int kBStageP = 128 * 128;
 constexpr int kSmemP = kStagesP * (kAStageP + kBStageP) + 1024 + 256;
+constexpr int kSmemPTp = kSmemP + 4 * 32 * 32 * 4;   // + the TP epilogue's staging
 
 template <bool I8, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -405,6 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB = smem + kStagesP * kAStageP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStagesP * kBStageP);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStagesP + 5);
+  // kEpiTpReduce only (launched with kSmemPTp): 4 warps x [32][32] f32 staging
+  float* tp_stage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  (void)tp_stage;
 
   const uint32_t full0 = smem_u32(bars);            // leader: count 2 (one per CTA) + tx
   const uint32_t empty0 = full0 + 8 * kStagesP;     // each CTA: leader's multicast commit
@@ -568,19 +572,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row_ok) store_row32(yrow + oc, g, oc, nout);
         }
       } else if constexpr (EPI == kEpiTpReduce) {
-        // Row-parallel product over tensor-parallel ranks. 1) this rank's f32
-        // partial -> the owner's inbox plane [rank]; the accumulator is free
-        // once read, so the MMA may start the next tile while the ranks meet.
+        // Row-parallel product over tensor-parallel ranks.
+        // 1) this rank's f32 partial -> the owner's inbox plane [rank]. A
+        //    warp's 32 rows x 32 columns of a chunk go through its 4 KB of
+        //    shared memory (XOR-swizzled rows) so that every global store
+        //    instruction writes 512 contiguous bytes over NVLink.
         const TpPeers& tp = p.tp;
-        const int owner = nb % tp.size, lb = nb / tp.size;
-        const long cols = (long)p.N / tp.size;
-        const long plane = tp.rows * cols;
-        float* mine = tp.inbox[owner] + (long)tp.rank * plane + (long)row * cols + lb * 256;
+        const int owner = nb % tp.size;
+        const int nbo = p.n_nblk / tp.size;
+        const long slot = (long)ti.unit * nbo + nb / tp.size;
+        const int lane = (int)lane_id();
+        float* wsm = tp_stage + wq * 1024;   // [32 rows][32 floats]
+        // chunk c of this warp's rows: plane + ((slot*2 + cta)*8 + c)*4096 + (32 wq)*32
+        const long tile_off = (slot * 2 + rank) * 8 * 4096 + wq * 32 * 32;
+        float* mine = tp.inbox[owner] + (long)tp.rank * tp.plane + tile_off;
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
           float v[32];
           chunk_values<I8>(tb + c * 32, v, p, row, row_ok, nb * 256 + c * 32, u.expert);
-          if (row_ok) store_row32_f32(mine + c * 32, v, 0, 32);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<float4*>(wsm + lane * 32 + ((k ^ (lane & 7)) << 2)) =
+                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int r = 4 * k + (lane >> 3), q4 = lane & 7;
+            *reinterpret_cast<float4*>(mine + c * 4096 + r * 32 + q4 * 4) =
+                *reinterpret_cast<const float4*>(wsm + r * 32 + ((q4 ^ (r & 7)) << 2));
+          }
+          __syncwarp();
         }
         tc_fence_before();
         mbar_arrive_cluster(acce_leader0 + 8 * acc);
@@ -593,55 +614,68 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           continue;
         }
-        // 2) owner: the other ranks' partials of these rows, then
-        //    x = bf16(x + bf16(sum of the planes)) into every rank's x
+        // 2) owner: wait for the other ranks' partials of these rows, then
+        //    x = bf16(x + bf16(sum of the planes)) into every rank's x. Lanes
+        //    run along the columns: each plane read is 512 contiguous bytes,
+        //    each x store 64 bytes of a row.
         if (threadIdx.x == 64) {
           wait_counter_sys(arrive, (unsigned long long)(tp.size - 1), p.err, kDevWaitPeer);
           *arrive = 0ull;   // ready for the next pass: no rank adds to it before done below
         }
         named_bar_sync(1, 128);
-        if (row_ok) {
-          const float* src = tp.inbox[tp.rank] + (long)row * cols + lb * 256;
-          const long xo = (long)row * p.N + nb * 256;
+        const float* own = tp.inbox[tp.rank] + tile_off;
+        const int wrow0 = u.m0 + 128 * (int)rank + wq * 32;   // this warp's first row
+        const int q4 = lane & 7;
+        // two chunks per pass: 16 independent loads per plane in flight
+        // (a serial load -> add -> store chain per element made this epilogue
+        // latency-bound)
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            float acc32[32];
+        for (int c = 0; c < 8; c += 2) {
+          float4 acc4[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc32[i] = 0.0f;
+          for (int i = 0; i < 16; ++i) acc4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 1
-            for (int q = 0; q < tp.size; ++q) {
-              const float4* s4 = reinterpret_cast<const float4*>(src + q * plane + c * 32);
+          for (int q = 0; q < tp.size; ++q) {
+            const float* base = own + q * tp.plane + c * 4096;
+            float4 f[16];
 #pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                const float4 f = __ldcg(s4 + k);
-                acc32[4 * k] += f.x;
-                acc32[4 * k + 1] += f.y;
-                acc32[4 * k + 2] += f.z;
-                acc32[4 * k + 3] += f.w;
-              }
+            for (int i = 0; i < 16; ++i) {
+              const int r = 4 * (i & 7) + (lane >> 3);
+              f[i] = __ldcg(reinterpret_cast<const float4*>(base + (i >> 3) * 4096 + r * 32 + q4 * 4));
             }
-            const uint4* r4 = reinterpret_cast<const uint4*>(
-                static_cast<const __nv_bfloat16*>(tp.x[tp.rank]) + xo + c * 32);
-            uint4 o4[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint4 rr = __ldcg(r4 + k);
-              const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
-              uint32_t ow[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 xr = unpack_bf2(rw[e]);
-                ow[e] = pack_bf2(xr.x + bfround(acc32[8 * k + 2 * e]),
-                                 xr.y + bfround(acc32[8 * k + 2 * e + 1]));
-              }
-              o4[k] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            for (int i = 0; i < 16; ++i) {
+              acc4[i].x += f[i].x;
+              acc4[i].y += f[i].y;
+              acc4[i].z += f[i].z;
+              acc4[i].w += f[i].w;
             }
-#pragma unroll 1
-            for (int q = 0; q < tp.size; ++q) {
-              uint4* d4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(tp.x[q]) + xo +
-                                                   c * 32);
+          }
+          const __nv_bfloat16* xme = static_cast<const __nv_bfloat16*>(tp.x[tp.rank]);
+          uint2 xr[16];
+          bool okr[16];
 #pragma unroll
-              for (int k = 0; k < 4; ++k) d4[k] = o4[k];
+          for (int i = 0; i < 16; ++i) {
+            const int grow = wrow0 + 4 * (i & 7) + (lane >> 3);
+            okr[i] = grow >= u.row_lo && grow < u.row_hi;
+            const long xo = (long)grow * p.N + nb * 256 + (c + (i >> 3)) * 32 + q4 * 4;
+            xr[i] = okr[i] ? __ldcg(reinterpret_cast<const uint2*>(xme + xo)) : make_uint2(0u, 0u);
+          }
+          uint2 o2[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 x01 = unpack_bf2(xr[i].x), x23 = unpack_bf2(xr[i].y);
+            o2[i] = make_uint2(pack_bf2(x01.x + bfround(acc4[i].x), x01.y + bfround(acc4[i].y)),
+                               pack_bf2(x23.x + bfround(acc4[i].z), x23.y + bfround(acc4[i].w)));
+          }
+#pragma unroll 1
+          for (int q = 0; q < tp.size; ++q) {
+            __nv_bfloat16* xq = static_cast<__nv_bfloat16*>(tp.x[q]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int grow = wrow0 + 4 * (i & 7) + (lane >> 3);
+              const long xo = (long)grow * p.N + nb * 256 + (c + (i >> 3)) * 32 + q4 * 4;
+              if (okr[i]) *reinterpret_cast<uint2*>(xq + xo) = o2[i];
             }
           }
         }
@@ -813,9 +847,10 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   static std::atomic<uint64_t> attr_set;
   static std::atomic<int> max_pairs_dev[64];   // resident pairs, per device (0: not yet known)
   auto k = gemm_tc_pair_kernel<I8, EPI>;
+  constexpr int smem = EPI == kEpiTpReduce ? kSmemPTp : kSmemP;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemP;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -824,7 +859,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!smem_attr_once(k, kSmemP, attr_set)) return 2;
+  if (!smem_attr_once(k, smem, attr_set)) return 2;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 2;
   int max_pairs = max_pairs_dev[dev & 63].load(std::memory_order_relaxed);
@@ -942,6 +977,10 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   p.n_units = n_units;
   p.n_nblk = (a.N + kBN - 1) / kBN;
   p.n_full = n_units * p.n_nblk;
+  if (tp && (long)n_units * (p.n_nblk / a.tp->size) * 2 * 8 * 4096 > a.tp->plane) {
+    *err = "gemm: the pass needs more tile slots than the tensor-parallel planes hold";
+    return 1;
+  }
   p.group = n_units;
   {
     static const int grp = [] {

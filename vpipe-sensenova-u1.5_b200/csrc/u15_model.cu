@@ -558,16 +558,22 @@ int u15c_model_tp(const u15c_model* m, int* tp_rank, int* tp_size)
 }
 
 namespace {
-// the peer region of one rank: [inbox f32 rows x H | x bf16 rows x H |
-// arrive u64 [tiles][2] | done u64], sections 256-byte aligned
+// the peer region of one rank: [inbox: P planes of f32 tile slots | x bf16
+// rows x H | arrive u64 [tiles][2] | done u64], sections 256-byte aligned.
+// A pass of `rows` tokens has at most rows/256 + 8 row units (one more per
+// segment boundary) and H/256 column blocks, P-th of them owned here; a
+// slot holds one 256 x 256 f32 tile (2 CTAs x 8 chunks x 128 x 32).
 struct TpLayout {
   size_t inbox, x, arrive, done, total;
-  TpLayout(long rows, long H)
+  long plane;   // floats
+  TpLayout(long rows, long H, int P)
   {
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
-    const long tiles = ((rows + 255) / 256 + u15::kMaxSeg) * (H / 256);
+    const long units = (rows + 255) / 256 + u15::kMaxSeg;
+    const long tiles = units * (H / 256);
+    plane = units * (H / 256 / P) * 2 * 8 * 4096;
     inbox = 0;
-    x = up(inbox + (size_t)rows * H * 4);
+    x = up(inbox + (size_t)plane * P * 4);
     arrive = up(x + (size_t)rows * H * 2);
     done = up(arrive + (size_t)tiles * 2 * 8);
     total = up(done + 8);
@@ -591,7 +597,7 @@ int u15c_model_tp_export(u15c_model* m, int max_tokens, void* blob)
     return fail(U15C_EINVAL, "tp_export: hidden must be a multiple of 256 x tp_size");
   if (m->tp_mem != nullptr) return fail(U15C_EINVAL, "tp_export: already exported");
   DeviceScope ds(m->device);
-  const TpLayout lay(max_tokens, m->cfg.hidden);
+  const TpLayout lay(max_tokens, m->cfg.hidden, m->tp_size);
   cudaError_t e = cudaMalloc(&m->tp_mem, lay.total);
   if (e != cudaSuccess) {
     m->tp_mem = nullptr;
@@ -651,7 +657,8 @@ int u15c_model_tp_import(u15c_model* m, const void* blobs)
     }
     m->tp_peer[q] = ptr;
   }
-  const TpLayout lay(m->tp_rows, m->cfg.hidden);
+  const TpLayout lay(m->tp_rows, m->cfg.hidden, P);
+  m->tpp.plane = lay.plane;
   m->tpp.rank = m->tp_rank;
   m->tpp.size = P;
   m->tpp.rows = m->tp_rows;
