@@ -502,8 +502,8 @@ def denoise_bench(args, rank, world, dist):
     grid, 2048x2048 px), three CFG forwards per step -- text-conditional
     (320-token prefix), image-conditional (8 text + one 1024-token reference
     image, block-causal prefill) and unconditional (13 tokens) -- shift 3.0,
-    cfg 4.0, img_cfg 1.5. The image path is the stand-in linear embedder and
-    head. Each rank runs its own seed (a replica): steps/s of the whole job =
+    cfg 4.0, img_cfg 1.5. The image path is the device ImagePath (patch
+    embedder, timestep + noise-scale row, pixel head) with seeded weights. Each rank runs its own seed (a replica): steps/s of the whole job =
     ranks / max-over-ranks seconds per step."""
     import torch
     import u15b200
@@ -552,7 +552,8 @@ def denoise_bench(args, rank, world, dist):
             "timed_steps": args.denoise_steps, "warmup_steps": 1,
             "config": "42 layers, 4096 gen tokens (BASELINE '1024^2' = 64x64 tokens = 2048^2 px),"
                       " 3 CFG forwards/step (prefix 320 / 8+1024 img block-causal / 13),"
-                      " stand-in linear image path, replicas x%d" % world,
+                      " device image path (patch embedder, timestep + noise-scale row,"
+                      " pixel head; seeded weights), replicas x%d" % world,
             "layers_per_step": 3 * 42}
 
 

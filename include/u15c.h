@@ -289,6 +289,97 @@ int u15c_patchify(u15c_stream stream, const float* img, void* rows, int H, int W
 int u15c_unpatchify(u15c_stream stream, const void* rows, float* img, int H, int W);
 
 /* ------------------------------------------------------------------ */
+/* the prefill's inputs from token ids (src/u15-generator.cc:308-392)   */
+/* ------------------------------------------------------------------ */
+
+/* out[i][:] = table[ids[i]][:] (bf16 [vocab][hidden] -> [n][hidden]),
+ * the embed_tokens lookup; ids are device int32. An id outside [0, vocab)
+ * gives a zero row and U15C_EDEVICE at the next u15c_sync. */
+int u15c_embed_tokens(u15c_stream stream, const void* table, int vocab, int hidden,
+                      const int32_t* ids, int n, void* out);
+/* Prompt::thw_indexes (src/u15-prompt.cc:349-386), host arrays: t grows by
+ * one per token that is not <IMG_CONTEXT> and by one more right after an
+ * <img>, so an image's context tokens share one t; h / w count the context
+ * tokens of each image row-major on its merged grid (grid_w / 2 per row),
+ * restarting per image. grid_hw: [n_imgs][2] patch grids (h, w). The
+ * generated image's tokens then sit at t = max(t) + 1. */
+int u15c_thw_indexes(const int32_t* ids, int n, int img_id, int img_ctx_id, const int* grid_hw,
+                     int n_imgs, int32_t* t, int32_t* h, int32_t* w);
+/* copy image k's patch embeddings [image_tokens[k]][hidden] (device) over
+ * the k-th run of <IMG_CONTEXT> rows of x [n][hidden] (ids on the host) */
+int u15c_splice_image_rows(u15c_stream stream, void* x, int hidden, const int32_t* ids_host,
+                           int n, int img_ctx_id, const void* const* image_embeds,
+                           const int* image_tokens, int n_imgs);
+
+/* ------------------------------------------------------------------ */
+/* the image path (ImagePath, src/u15-image.h:24-100; CPU forms          */
+/* src/u15-ref.cc vision_embed / conv_decoder): patch embedder in,      */
+/* pixel head out, timestep + noise-scale embedding. Channel-last.      */
+/* ------------------------------------------------------------------ */
+
+typedef struct u15c_image u15c_image;
+typedef struct u15c_image_config {
+  int vision_hidden;         /* 1024: patch embedding width */
+  int llm_hidden;            /* 4096: backbone hidden size */
+  int patch;                 /* 16 */
+  int merge;                 /* 2: tiles merged by the dense embedding */
+  int head_hidden;           /* 1024: the pixel head's conv1 width */
+  int freq_dim;              /* 256: the timestep sinusoid's width */
+  int noise_scale_embedding; /* 1: add the noise-scale embedder's row */
+  double vision_theta;       /* 1e4: the patch embedder's 2-D RoPE */
+} u15c_image_config;
+
+/* tensor ids for u15c_image_bind, the checkpoint's shapes; patch/dense
+ * take expert 0 (vision_model, understanding) or 1 (vision_model_mot_gen) */
+#define U15C_I_PATCH_W 0   /* [vision_hidden][3][p][p] */
+#define U15C_I_PATCH_B 1
+#define U15C_I_DENSE_W 2   /* [llm_hidden][vision_hidden][m][m] */
+#define U15C_I_DENSE_B 3
+#define U15C_I_CONV1_W 4   /* [head_hidden][llm_hidden/4][3][3] */
+#define U15C_I_CONV1_B 5
+#define U15C_I_CONV2_W 6   /* [192][head_hidden/4][3][3] */
+#define U15C_I_CONV2_B 7
+#define U15C_I_TSTEP_W0 8  /* [llm_hidden][freq_dim] */
+#define U15C_I_TSTEP_B0 9
+#define U15C_I_TSTEP_W2 10 /* [llm_hidden][llm_hidden] */
+#define U15C_I_TSTEP_B2 11
+#define U15C_I_NSCALE_W0 12
+#define U15C_I_NSCALE_B0 13
+#define U15C_I_NSCALE_W2 14
+#define U15C_I_NSCALE_B2 15
+
+/* ImagePath::create */
+int u15c_image_create(const u15c_image_config* cfg, u15c_image** out);
+void u15c_image_destroy(u15c_image* im);
+/* bind one tensor (f32/f16/bf16, host or device) into the device layout;
+ * the conv kernels are repacked to [cout][ky][kx][cin] for the im2col GEMM
+ * (ImagePath::build_conv_weights_, src/u15-image.cc:56-131) */
+int u15c_image_bind(u15c_image* im, u15c_stream stream, int tensor, int expert, const void* src,
+                    int dtype, int src_on_host);
+int u15c_image_bind_random(u15c_image* im, u15c_stream stream, uint64_t seed, float std);
+/* ImagePath::patchify_for_embed: img [H][W][3] f32 -> px [(H/p)(W/p)][3p^2]
+ * bf16, each patch channel-FIRST */
+int u15c_image_patchify(u15c_stream stream, const float* img, void* px, int H, int W, int patch);
+/* ImagePath::embed (src/u15-image.cc:145-197): px [gh*gw][3p^2] ->
+ * out [(gh/m)(gw/m)][llm_hidden] bf16 */
+int u15c_image_embed(u15c_image* im, u15c_stream stream, const void* px, int grid_h, int grid_w,
+                     int expert, void* out);
+/* ImagePath::timestep_row (src/u15-image.cc:199-251), on the device:
+ * out [llm_hidden] f32 */
+int u15c_image_timestep_row(u15c_image* im, u15c_stream stream, double t, double noise_ratio,
+                            float* out);
+/* the row rounded to bf16 and added to every row of x [rows][llm_hidden]
+ * (the generator's add_row, src/u15-generator.cc:489-499) */
+int u15c_image_add_timestep(u15c_image* im, u15c_stream stream, void* x, int rows, double t,
+                            double noise_ratio);
+/* ImagePath::decode (src/u15-image.cc:253-303): hidden [th*tw][llm_hidden]
+ * bf16 -> out_px [32 th][32 tw][3] f32 (bf16-exact values), model space */
+int u15c_image_decode(u15c_image* im, u15c_stream stream, const void* hidden, int th, int tw,
+                      float* out_px);
+/* ImagePath::to_u8_planar: [H][W][3] model space -> [3][H][W] u8 */
+int u15c_image_to_u8_planar(u15c_stream stream, const float* px, uint8_t* out, int H, int W);
+
+/* ------------------------------------------------------------------ */
 /* model: weights, KV cache, backbone                                   */
 /* ------------------------------------------------------------------ */
 

@@ -99,6 +99,11 @@ def lib():
         L.orc_cfg.argtypes = [_f32p, _f32p, _f32p, C.c_long, C.c_long, C.c_int, C.c_int,
                               C.c_double, C.c_double, C.c_int, _f32p]
         L.orc_euler.argtypes = [_f32p, _f32p, C.c_long, C.c_double]
+        L.orc_patchify_cf.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+        L.orc_gelu_erf.argtypes = [_f32p, C.c_long]
+        L.orc_vision_embed.argtypes = [_f32p] * 5 + [C.c_int] * 6 + [C.c_double, _f32p]
+        L.orc_conv_decoder_hwc.argtypes = [_f32p] * 5 + [C.c_int] * 4 + [_f32p]
+        L.orc_timestep_row.argtypes = [C.c_double, C.c_double, C.c_int, C.c_int] + [_f32p] * 9
         _lib = L
     return _lib
 
@@ -286,6 +291,79 @@ def euler(img, v, dt):
 
 # ---------------------------------------------------------------------------
 # the reference's own CPU code (fixture generation and pinning only)
+# ---- the image path ---------------------------------------------------------
+# Weight dicts use the checkpoint's names and layouts: patch_w [C][3p^2],
+# patch_b [C], dense_w [LLM][C m^2], dense_b [LLM]; conv1_w [hid][in/4][3][3],
+# conv1_b, conv2_w [192][hid/4][3][3], conv2_b; tstep_w0 [H][dim], tstep_b0,
+# tstep_w2 [H][H], tstep_b2 (and nscale_* the same, optional).
+
+def patchify_cf(img_hwc, p=16):
+    H, W, c = img_hwc.shape
+    img = _f32(img_hwc)
+    out = np.empty(((H // p) * (W // p), c * p * p), np.float32)
+    lib().orc_patchify_cf(_fp(img), c, H, W, p, _fp(out))
+    return out
+
+
+def gelu_erf(x):
+    y = _f32(x).copy()
+    lib().orc_gelu_erf(_fp(y), y.size)
+    return y
+
+
+def vision_embed(px, w, gh, gw, p=16, merge=2, theta=1e4):
+    pw, pb, dw, db = (_f32(w[k]) for k in ("patch_w", "patch_b", "dense_w", "dense_b"))
+    C_, LLM = pw.shape[0], dw.shape[0]
+    out = np.empty(((gh // merge) * (gw // merge), LLM), np.float32)
+    lib().orc_vision_embed(_fp(_f32(px)), _fp(pw), _fp(pb), _fp(dw), _fp(db), gh, gw, p, C_,
+                           LLM, merge, theta, _fp(out))
+    return out
+
+
+def conv_decoder_hwc(x, w, th, tw):
+    """x [th*tw][in_ch] (a [th][tw][in_ch] map) -> [32 th][32 tw][3]."""
+    c1w, c1b, c2w, c2b = (_f32(w[k]) for k in ("conv1_w", "conv1_b", "conv2_w", "conv2_b"))
+    in_ch, hid = x.shape[-1], c1w.shape[0]
+    out = np.empty((32 * th, 32 * tw, 3), np.float32)
+    lib().orc_conv_decoder_hwc(_fp(_f32(x)), _fp(c1w), _fp(c1b), _fp(c2w), _fp(c2b), in_ch, th,
+                               tw, hid, _fp(out))
+    return out
+
+
+def timestep_row(t, ratio, w):
+    w0, b0, w2, b2 = (_f32(w[k]) for k in ("tstep_w0", "tstep_b0", "tstep_w2", "tstep_b2"))
+    H, dim = w0.shape
+    ns = [w.get(k) for k in ("nscale_w0", "nscale_b0", "nscale_w2", "nscale_b2")]
+    ns = [_f32(a) if a is not None else None for a in ns]
+    out = np.empty(H, np.float32)
+    lib().orc_timestep_row(t, ratio, dim, H, _fp(w0), _fp(b0), _fp(w2), _fp(b2),
+                           *(_fp(a) for a in ns), _fp(out))
+    return out
+
+
+def thw_indexes(ids, img_id, img_ctx_id, grids):
+    """Prompt::thw_indexes (src/u15-prompt.cc:349-386), restated loop by loop."""
+    n = len(ids)
+    t, h, w = np.zeros(n, np.int32), np.zeros(n, np.int32), np.zeros(n, np.int32)
+    cum = 0
+    for i in range(n):
+        shift = 1 if (i > 0 and ids[i - 1] == img_id) else 0
+        cum += shift + (0 if ids[i] == img_ctx_id else 1)
+        t[i] = cum - 1
+    img, seen = 0, 0
+    for i in range(n):
+        if ids[i] != img_ctx_id:
+            continue
+        while img < len(grids) and seen >= (grids[img][0] // 2) * (grids[img][1] // 2):
+            img, seen = img + 1, 0
+        if img >= len(grids):
+            break
+        tw = grids[img][1] // 2
+        h[i], w[i] = seen // tw, seen % tw
+        seen += 1
+    return t, h, w
+
+
 # ---------------------------------------------------------------------------
 
 _ref = None
@@ -314,5 +392,10 @@ def ref():
         L.refx_time_schedule.argtypes = [C.c_int, C.c_double, _f32p]
         L.refx_optimized_scale.argtypes = [_f32p, _f32p, C.c_long]
         L.refx_optimized_scale.restype = C.c_double
+        L.refx_vision_embed.argtypes = [_f32p] * 5 + [C.c_int] * 6 + [C.c_double, _f32p]
+        L.refx_conv_decoder.argtypes = [_f32p] * 5 + [C.c_int] * 4 + [_f32p]
+        L.refx_patchify_channel_first_hwc.argtypes = [_f32p] + [C.c_int] * 4 + [_f32p]
+        L.refx_timestep_sinusoid.argtypes = [C.c_double, C.c_int, C.c_double, _f32p]
+        L.refx_gelu_erf.argtypes = [_f32p, C.c_long]
         _ref = L
     return _ref

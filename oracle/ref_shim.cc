@@ -116,4 +116,47 @@ double refx_optimized_scale(const float* pos, const float* neg, long n)
   return optimized_scale(pos, neg, (std::size_t)n);
 }
 
+
+// ---- the image path (src/u15-ref.cc: vision_embed, conv_decoder,
+// patchify_channel_first_hwc, timestep_sinusoid, gelu_erf) ----
+
+void refx_vision_embed(const float* px, const float* patch_w, const float* patch_b,
+                       const float* dense_w, const float* dense_b, int grid_h, int grid_w,
+                       int patch_px, int hidden, int llm_hidden, int merge, double theta,
+                       float* out)
+{
+  VisionWeights w;
+  w.patch_w = patch_w;
+  w.patch_b = patch_b;
+  w.dense_w = dense_w;
+  w.dense_b = dense_b;
+  vision_embed(px, w, grid_h, grid_w, patch_px, hidden, llm_hidden, merge, theta, out);
+}
+
+void refx_conv_decoder(const float* x_chw, const float* conv1_w, const float* conv1_b,
+                       const float* conv2_w, const float* conv2_b, int in_ch, int th, int tw,
+                       int hidden_ch, float* out_chw)
+{
+  HeadWeights w;
+  w.conv1_w = conv1_w;
+  w.conv1_b = conv1_b;
+  w.conv2_w = conv2_w;
+  w.conv2_b = conv2_b;
+  conv_decoder(x_chw, w, in_ch, th, tw, hidden_ch, out_chw);
+}
+
+void refx_patchify_channel_first_hwc(const float* img_hwc, int c, int h, int w, int p,
+                                     float* out)
+{
+  patchify_channel_first_hwc(img_hwc, c, h, w, p, out);
+}
+
+void refx_timestep_sinusoid(double t, int dim, double max_period, float* out)
+{
+  const std::vector<float> e = timestep_sinusoid(t, dim, max_period);
+  std::memcpy(out, e.data(), e.size() * sizeof(float));
+}
+
+void refx_gelu_erf(float* x, long n) { gelu_erf(x, (std::size_t)n); }
+
 }  // extern "C"

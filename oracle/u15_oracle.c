@@ -651,3 +651,187 @@ void orc_euler(float* img, const float* v, long n, double dt)
 {
   for (long i = 0; i < n; ++i) img[i] = (float)((double)img[i] + dt * (double)v[i]);
 }
+
+/* ------------------------------------------------------------------ */
+/* the image path (src/u15-ref.cc: patchify_channel_first_hwc,         */
+/* gelu_erf, rope_interleaved_inplace, vision_embed, pixel_shuffle,    */
+/* conv3x3, conv_decoder, timestep_sinusoid; the timestep MLP of       */
+/* src/u15-image.cc ImagePath::timestep_row)                           */
+/* ------------------------------------------------------------------ */
+
+/* img [H][W][c] -> [gh*gw][c*p*p], each patch packed channel-FIRST
+ * (ci, pi, qi): the patch embedder's input (src/u15-ref.cc
+ * patchify_channel_first_hwc). */
+void orc_patchify_cf(const float* img, int c, int H, int W, int p, float* out)
+{
+  const int gh = H / p, gw = W / p;
+  const long stride = (long)c * p * p;
+  for (int hi = 0; hi < gh; ++hi)
+    for (int wi = 0; wi < gw; ++wi) {
+      float* o = out + ((long)hi * gw + wi) * stride;
+      for (int ci = 0; ci < c; ++ci)
+        for (int pi = 0; pi < p; ++pi)
+          for (int qi = 0; qi < p; ++qi)
+            o[((long)ci * p + pi) * p + qi] =
+                img[((long)(hi * p + pi) * W + (wi * p + qi)) * c + ci];
+    }
+}
+
+/* the exact erf GELU, in double */
+void orc_gelu_erf(float* x, long n)
+{
+  for (long i = 0; i < n; ++i) {
+    const double v = x[i];
+    x[i] = (float)(0.5 * v * (1.0 + erf(v / sqrt(2.0))));
+  }
+}
+
+/* rotate (2i, 2i+1) pairs of x[0:dim) by position * inv[i] (double) */
+static void rope_pairs(float* x, const float* inv, int dim, double pos)
+{
+  for (int i = 0; i < dim / 2; ++i) {
+    const double a = pos * (double)inv[i], c = cos(a), s = sin(a);
+    const double u = x[2 * i], v = x[2 * i + 1];
+    x[2 * i] = (float)(u * c - v * s);
+    x[2 * i + 1] = (float)(u * s + v * c);
+  }
+}
+
+/* The patch embedder (src/u15-ref.cc vision_embed): per-patch linear
+ * (C x 3p^2) + bias, GELU, interleaved 2-D RoPE (first half of each
+ * embedding by the patch column, second half by its row; inverse
+ * frequencies of C/2 dims, as float), m x m tiles gathered channel-slowest,
+ * dense linear (LLM x C m^2) + bias. px [gh*gw][3p^2] -> out [(gh/m)(gw/m)][LLM]. */
+void orc_vision_embed(const float* px, const float* patch_w, const float* patch_b,
+                      const float* dense_w, const float* dense_b, int gh, int gw, int p,
+                      int C, int LLM, int m, double theta, float* out)
+{
+  const long n = (long)gh * gw, pin = 3L * p * p;
+  float* emb = (float*)malloc(sizeof(float) * n * C);
+  orc_linear(px, patch_w, patch_b, n, pin, C, emb);
+  orc_gelu_erf(emb, n * C);
+  const int half = C / 2;
+  float* inv = (float*)malloc(sizeof(float) * (half / 2));
+  for (int i = 0; i < half / 2; ++i)
+    inv[i] = (float)(1.0 / pow(theta, (double)(2 * i) / (double)half));
+  for (int r = 0; r < gh; ++r)
+    for (int c = 0; c < gw; ++c) {
+      float* e = emb + ((long)r * gw + c) * C;
+      rope_pairs(e, inv, half, (double)c);
+      rope_pairs(e + half, inv, half, (double)r);
+    }
+  const int oh = gh / m, ow = gw / m;
+  const long tile = (long)C * m * m;
+  float* g = (float*)malloc(sizeof(float) * oh * ow * tile);
+  for (int r = 0; r < oh; ++r)
+    for (int c = 0; c < ow; ++c)
+      for (int ch = 0; ch < C; ++ch)
+        for (int i = 0; i < m; ++i)
+          for (int j = 0; j < m; ++j)
+            g[((long)r * ow + c) * tile + ((long)ch * m + i) * m + j] =
+                emb[((long)(r * m + i) * gw + (c * m + j)) * C + ch];
+  orc_linear(g, dense_w, dense_b, (long)oh * ow, tile, LLM, out);
+  free(g);
+  free(inv);
+  free(emb);
+}
+
+/* PixelShuffle(r) on a channel-last map: input channel c*r*r + i*r + j of
+ * pixel (y, x) -> output channel c of pixel (y*r + i, x*r + j). */
+static void ps_hwc(const float* in, int H, int W, int Cin, int r, float* out)
+{
+  const int Co = Cin / (r * r);
+  for (int y = 0; y < H; ++y)
+    for (int x = 0; x < W; ++x)
+      for (int ci = 0; ci < Cin; ++ci) {
+        const int c = ci / (r * r), i = (ci % (r * r)) / r, j = ci % r;
+        out[((long)(y * r + i) * (W * r) + (x * r + j)) * Co + c] =
+            in[((long)y * W + x) * Cin + ci];
+      }
+}
+
+/* 3x3 convolution, padding 1, channel-last; weight [cout][cin][3][3]
+ * (the checkpoint's order), double accumulation. */
+static void conv3x3_hwc(const float* x, const float* w, const float* b, int cin, int cout,
+                        int H, int W, float* out)
+{
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int y = 0; y < H; ++y)
+    for (int xx = 0; xx < W; ++xx)
+      for (int oc = 0; oc < cout; ++oc) {
+        double acc = b ? (double)b[oc] : 0.0;
+        for (int ky = 0; ky < 3; ++ky) {
+          const int sy = y + ky - 1;
+          if (sy < 0 || sy >= H) continue;
+          for (int kx = 0; kx < 3; ++kx) {
+            const int sx = xx + kx - 1;
+            if (sx < 0 || sx >= W) continue;
+            const float* src = x + ((long)sy * W + sx) * cin;
+            const float* wk = w + (long)oc * cin * 9 + ky * 3 + kx;
+            for (int ic = 0; ic < cin; ++ic) acc += (double)wk[(long)ic * 9] * (double)src[ic];
+          }
+        }
+        out[((long)y * W + xx) * cout + oc] = (float)acc;
+      }
+}
+
+/* The pixel head (src/u15-ref.cc conv_decoder) in the channel-last layout
+ * the device runs: x [th][tw][in_ch] -> PS(2) -> conv1 3x3 (in_ch/4 ->
+ * hidden_ch) + bias -> GELU -> PS(2) -> conv2 3x3 (hidden_ch/4 -> 192) +
+ * bias -> PS(8) -> out [32 th][32 tw][3]. */
+void orc_conv_decoder_hwc(const float* x, const float* conv1_w, const float* conv1_b,
+                          const float* conv2_w, const float* conv2_b, int in_ch, int th, int tw,
+                          int hidden_ch, float* out)
+{
+  const int c1 = in_ch / 4, c2 = hidden_ch / 4;
+  float* a = (float*)malloc(sizeof(float) * (long)c1 * 4 * th * tw);
+  float* b = (float*)malloc(sizeof(float) * (long)hidden_ch * 4 * th * tw);
+  float* c = (float*)malloc(sizeof(float) * (long)c2 * 16 * th * tw);
+  float* e = (float*)malloc(sizeof(float) * 192L * 16 * th * tw);
+  ps_hwc(x, th, tw, in_ch, 2, a);
+  conv3x3_hwc(a, conv1_w, conv1_b, c1, hidden_ch, 2 * th, 2 * tw, b);
+  orc_gelu_erf(b, (long)hidden_ch * 4 * th * tw);
+  ps_hwc(b, 2 * th, 2 * tw, hidden_ch, 2, c);
+  conv3x3_hwc(c, conv2_w, conv2_b, c2, 192, 4 * th, 4 * tw, e);
+  ps_hwc(e, 4 * th, 4 * tw, 192, 8, out);
+  free(e);
+  free(c);
+  free(b);
+  free(a);
+}
+
+/* sinusoid of `dim` (cos first, then sin; max period 1e4) -> Linear(dim
+ * -> H) -> SiLU -> Linear(H -> H), f32 values with double accumulation
+ * (src/u15-image.cc ImagePath::timestep_row); the noise-scale embedder,
+ * when its weights are given, is evaluated the same way at `ratio` and
+ * added. */
+static void scalar_mlp(double v, int dim, int H, const float* w0, const float* b0,
+                       const float* w2, const float* b2, float* out)
+{
+  float* s = (float*)malloc(sizeof(float) * dim);
+  float* h = (float*)malloc(sizeof(float) * H);
+  const int half = dim / 2;
+  for (int i = 0; i < half; ++i) {
+    const double f = exp(-log(10000.0) * (double)i / (double)half);
+    s[i] = (float)cos(v * f);
+    s[i + half] = (float)sin(v * f);
+  }
+  orc_linear(s, w0, b0, 1, dim, H, h);
+  orc_silu(h, H);
+  orc_linear(h, w2, b2, 1, H, H, out);
+  free(h);
+  free(s);
+}
+
+void orc_timestep_row(double t, double ratio, int dim, int H, const float* w0, const float* b0,
+                      const float* w2, const float* b2, const float* nw0, const float* nb0,
+                      const float* nw2, const float* nb2, float* out)
+{
+  scalar_mlp(t, dim, H, w0, b0, w2, b2, out);
+  if (nw0 != NULL) {
+    float* ns = (float*)malloc(sizeof(float) * H);
+    scalar_mlp(ratio, dim, H, nw0, nb0, nw2, nb2, ns);
+    for (int i = 0; i < H; ++i) out[i] += ns[i];
+    free(ns);
+  }
+}

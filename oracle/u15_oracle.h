@@ -104,6 +104,19 @@ void orc_cfg(const float* v_cond, const float* v_unc, const float* v_img, long H
              int form, int norm, double cfg, double icfg, int step, float* out);
 void orc_euler(float* img, const float* v, long n, double dt);
 
+/* the image path (src/u15-ref.cc vision_embed / conv_decoder; src/u15-image.cc) */
+void orc_patchify_cf(const float* img, int c, int H, int W, int p, float* out);
+void orc_gelu_erf(float* x, long n);
+void orc_vision_embed(const float* px, const float* patch_w, const float* patch_b,
+                      const float* dense_w, const float* dense_b, int gh, int gw, int p,
+                      int C, int LLM, int m, double theta, float* out);
+void orc_conv_decoder_hwc(const float* x, const float* conv1_w, const float* conv1_b,
+                          const float* conv2_w, const float* conv2_b, int in_ch, int th, int tw,
+                          int hidden_ch, float* out);
+void orc_timestep_row(double t, double ratio, int dim, int H, const float* w0, const float* b0,
+                      const float* w2, const float* b2, const float* nw0, const float* nb0,
+                      const float* nw2, const float* nb2, float* out);
+
 #ifdef __cplusplus
 }
 #endif

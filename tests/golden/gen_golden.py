@@ -177,6 +177,41 @@ def main():
                "dl.joint.out_und": ref_decoder_layer(xj, wu, dims, *pj, None),
                "dl.joint.out_gen": ref_decoder_layer(xj, wg, dims, *pj, None)})
 
+    # ---- the image path (src/u15-ref.cc vision_embed, conv_decoder) ------
+    img = rng.uniform(-1, 1, (32, 48, 3)).astype(np.float32)     # [H][W][3]
+    pc = np.empty((6, 3 * 16 * 16), np.float32)
+    R.refx_patchify_channel_first_hwc(fp(img), 3, 32, 48, 16, fp(pc))
+    fx.update({"img.hwc": img, "img.patch_cf": pc})
+    g = np.linspace(-6, 6, 97).astype(np.float32)
+    gy = g.copy()
+    R.refx_gelu_erf(fp(gy), gy.size)
+    fx.update({"gelu.x": g, "gelu.y": gy})
+    gh, gw, Cv, LLM = 4, 6, 32, 48
+    ve = {"px": rng.normal(0, 1, (gh * gw, 768)).astype(np.float32),
+          "patch_w": rng.normal(0, 0.03, (Cv, 768)).astype(np.float32),
+          "patch_b": rng.normal(0, 0.1, Cv).astype(np.float32),
+          "dense_w": rng.normal(0, 0.05, (LLM, Cv * 4)).astype(np.float32),
+          "dense_b": rng.normal(0, 0.1, LLM).astype(np.float32)}
+    vo = np.empty(((gh // 2) * (gw // 2), LLM), np.float32)
+    R.refx_vision_embed(fp(ve["px"]), fp(ve["patch_w"]), fp(ve["patch_b"]), fp(ve["dense_w"]),
+                        fp(ve["dense_b"]), gh, gw, 16, Cv, LLM, 2, 1e4, fp(vo))
+    fx.update({f"ve.{k}": v for k, v in ve.items()})
+    fx["ve.out"] = vo
+    in_ch, th, tw, hid = 64, 2, 3, 32
+    cd = {"x_chw": rng.normal(0, 1, (in_ch, th, tw)).astype(np.float32),
+          "conv1_w": rng.normal(0, 0.05, (hid, in_ch // 4, 3, 3)).astype(np.float32),
+          "conv1_b": rng.normal(0, 0.1, hid).astype(np.float32),
+          "conv2_w": rng.normal(0, 0.05, (192, hid // 4, 3, 3)).astype(np.float32),
+          "conv2_b": rng.normal(0, 0.1, 192).astype(np.float32)}
+    co = np.empty((3, 32 * th, 32 * tw), np.float32)
+    R.refx_conv_decoder(fp(cd["x_chw"]), fp(cd["conv1_w"]), fp(cd["conv1_b"]),
+                        fp(cd["conv2_w"]), fp(cd["conv2_b"]), in_ch, th, tw, hid, fp(co))
+    fx.update({f"cd.{k}": v for k, v in cd.items()})
+    fx["cd.out_chw"] = co
+    sn = np.empty(256, np.float32)
+    R.refx_timestep_sinusoid(0.37, 256, 10000.0, fp(sn))
+    fx["tsin.t037.d256"] = sn
+
     # ---- sampling ---------------------------------------------------------
     ts = np.empty(21, np.float32)
     R.refx_time_schedule(20, 3.0, fp(ts))

@@ -166,3 +166,69 @@ def test_short_denoise_three_branches():
     assert rel_l2(got - noise, z - noise) < 5e-2
     assert np.isfinite(got).all()
     assert isinstance(m, u15b200.Model)
+
+
+def test_denoise_with_device_image_path():
+    """Two steps of the loop with the device image path (patch embedder,
+    timestep + noise-scale row, pixel head) against the same steps restated on
+    the CPU from the pinned restatements (vision_embed, conv_decoder,
+    timestep_row)."""
+    import u15b200
+    from u15b200 import _lib as L
+    from u15b200.generator import Branch, DeviceImagePath, Generator, time_schedule
+    from test_gpu_image import make
+    from test_gpu_layer import SMALL, build, dims_of
+
+    cfg = dict(SMALL)
+    m, Wts = build(cfg, 400)
+    hidden = cfg["hidden"]
+    icfg = dict(vision_hidden=64, llm_hidden=hidden, patch=16, merge=2, head_hidden=64,
+                freq_dim=256, noise_scale_embedding=1, vision_theta=1e4)
+    im, Wv, Hw = make(icfg, 12)
+    H = W = 128
+    th, tw = H // 32, W // 32
+    Ltok = th * tw
+    rng = np.random.default_rng(13)
+    n_text = 10
+    px0 = bf16_round(rng.normal(0, 1, (n_text, hidden)).astype(np.float32))
+    t_pre = np.arange(n_text).astype(np.int32)
+    z0 = np.zeros(n_text, np.int32)
+    branches = [Branch("cond", dev_bf16(px0), t_pre, z0, z0)]
+    gen = Generator(m, DeviceImagePath(im))
+    noise = randn((H, W, 3), 14)
+    steps, shift, t_eps, nscale = 2, 3.0, 0.05, 4.0
+    img = gen.generate(branches, H, W, steps=steps, shift=shift, form=L.CFG_NONE, t_eps=t_eps,
+                       init_noise=torch.from_numpy(noise), noise_scale=nscale)
+    torch.cuda.synchronize()
+
+    # ---- the same loop on the CPU ----
+    D = dims_of(cfg)
+    ks, vs = [], []
+    cur = px0
+    for li in range(cfg["n_layers"]):
+        cur, kn, vn = O.mot_layer(cur, [(0, n_text, 0)], Wts[li], D, t_pre, z0, z0,
+                                  mode=O.CAUSAL)
+        ks.append(kn)
+        vs.append(vn)
+    ts = time_schedule(steps, shift)
+    z = noise.copy()
+    ratio = nscale / 16.0
+    for step in range(steps):
+        t, tn = ts[step], ts[step + 1]
+        px = bf16_round(O.patchify_cf(z, 16))
+        emb = bf16_round(O.vision_embed(px, Wv[1], H // 16, W // 16))
+        emb = bf16_round(emb + bf16_round(O.timestep_row(t, ratio, Hw))[None])
+        pt = np.full(Ltok, n_text, np.int32)
+        ph = (np.arange(Ltok) // tw).astype(np.int32)
+        pw = (np.arange(Ltok) % tw).astype(np.int32)
+        hcur = emb
+        for li in range(cfg["n_layers"]):
+            hcur, _, _ = O.mot_layer(hcur, [(0, Ltok, 1)], Wts[li], D, pt, ph, pw,
+                                     k_prefix=ks[li], v_prefix=vs[li])
+        hn = bf16_round(O.rms_norm(hcur, np.ones(hidden, np.float32)))
+        xp = O.conv_decoder_hwc(hn, Hw, th, tw)
+        z = O.euler(z, O.velocity(xp, z, max(1 - t, t_eps)), tn - t)
+    got = host(img)
+    assert np.isfinite(got).all()
+    assert rel_l2(got - noise, z - noise) < 5e-2
+    assert isinstance(im, u15b200.ImagePath)

@@ -238,3 +238,22 @@ def test_split_tail_residual_i8_bit_exact(ops):
     deq = np.concatenate([O.dequant_i8(racc[a:b], rxs[a:b], rws[e]) for a, b, e in SPLIT_SEGS])
     ref = bf16_round(r + bf16_round(deq))
     assert rel_l2(host(rd), ref) < 2e-3
+
+
+def test_single_segment_unbounded_rows(ops):
+    """One routing segment has implicit row units: M far beyond the routed
+    table's 200 units (the pixel head's conv2 at 2048^2 px: M = 65536,
+    N = 192 as one partial column tile, bias)."""
+    M, K, N = 65536, 144, 192
+    torch.manual_seed(40)
+    xd = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    wd = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    bd = (torch.randn(N, device="cuda") * 0.1).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.linear(xd, wd, bd, y, M, K, N)
+    ops.sync()
+    rows = np.union1d(sample_rows(M, 40, 41), [0, 255, 256, 51199, 51200, M - 1])
+    idx = torch.from_numpy(rows).cuda()
+    got = host(y[idx])
+    ref = O.linear(host(xd[idx]), host(wd), host(bd))
+    assert rel_l2(got, ref) < BAR

@@ -171,3 +171,52 @@ def test_sage_close_to_exact():
     sage = O.sage_attention(q, k, v, tk=83, bq=64, bk=64)
     err = rel_l2(sage, exact)
     assert 1e-5 < err < 3e-2
+
+
+# ---- the image path: patch embedder, pixel head, timestep embedding ----
+
+def test_patchify_channel_first(golden):
+    assert np.array_equal(O.patchify_cf(golden["img.hwc"], 16), golden["img.patch_cf"])
+
+
+def test_gelu_erf(golden):
+    assert np.abs(O.gelu_erf(golden["gelu.x"]) - golden["gelu.y"]).max() < 1e-6
+
+
+def test_vision_embed(golden):
+    w = {k: golden[f"ve.{k}"] for k in ("patch_w", "patch_b", "dense_w", "dense_b")}
+    out = O.vision_embed(golden["ve.px"], w, 4, 6)
+    assert rel_l2(out, golden["ve.out"]) < 5e-6
+    # negative control: the row/column halves of the 2-D RoPE swapped
+    # (a transposed patch grid) must be caught
+    px_t = golden["ve.px"].reshape(4, 6, -1).transpose(1, 0, 2).reshape(24, -1)
+    assert rel_l2(O.vision_embed(px_t, w, 6, 4)[:6], golden["ve.out"]) > 1e-2
+
+
+def test_conv_decoder_channel_last(golden):
+    w = {k: golden[f"cd.{k}"] for k in ("conv1_w", "conv1_b", "conv2_w", "conv2_b")}
+    x_hwc = golden["cd.x_chw"].transpose(1, 2, 0).reshape(6, 64)
+    out = O.conv_decoder_hwc(x_hwc, w, 2, 3)
+    ref_hwc = golden["cd.out_chw"].transpose(1, 2, 0)
+    assert rel_l2(out, ref_hwc) < 5e-6
+    # negative control: a channel-FASTEST pixel shuffle reading of the input
+    x_bad = golden["cd.x_chw"].reshape(16, 4, 2, 3).transpose(2, 3, 1, 0).reshape(6, 64)
+    assert rel_l2(O.conv_decoder_hwc(x_bad, w, 2, 3), ref_hwc) > 1e-1
+
+
+def test_timestep_row_composition(golden):
+    rng = np.random.default_rng(5)
+    H = 48
+    w = {"tstep_w0": rng.normal(0, 0.05, (H, 256)).astype(np.float32),
+         "tstep_b0": rng.normal(0, 0.1, H).astype(np.float32),
+         "tstep_w2": rng.normal(0, 0.05, (H, H)).astype(np.float32),
+         "tstep_b2": rng.normal(0, 0.1, H).astype(np.float32)}
+    # the reference's own sinusoid (cos first) through Linear -> SiLU -> Linear
+    h = O.linear(golden["tsin.t037.d256"][None], w["tstep_w0"], w["tstep_b0"])
+    h = h / (1.0 + np.exp(-h.astype(np.float64)))
+    want = O.linear(h.astype(np.float32), w["tstep_w2"], w["tstep_b2"])[0]
+    assert rel_l2(O.timestep_row(0.37, 0.0, w), want) < 1e-6
+    # with the noise-scale embedder: the sum of the two rows
+    w2 = dict(w, nscale_w0=w["tstep_w0"], nscale_b0=w["tstep_b0"], nscale_w2=w["tstep_w2"],
+              nscale_b2=w["tstep_b2"])
+    assert rel_l2(O.timestep_row(0.37, 0.37, w2), 2 * want) < 1e-6

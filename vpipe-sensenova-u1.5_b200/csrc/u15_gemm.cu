@@ -60,6 +60,8 @@ struct Params {
   int n_units, n_nblk, n_kblk;
   int n_full;           // tiles before the split tail (== n_units * n_nblk when none)
   int group;            // tile order: units (row blocks) per group, >= 1
+  int implicit_bm;      // > 0: units are implicit row blocks of this size (one segment)
+  int implicit_expert;
   void* y;
   long ldy;             // output row stride, elements
   const __nv_bfloat16* resid;
@@ -98,6 +100,18 @@ __device__ __forceinline__ TileIdx tile_at(const Params& p, int t)
   r.unit = g0 + rr % gs;
   r.nb = rr / gs;
   return r;
+}
+
+// Row unit i: from the table, or (one routing segment) the implicit
+// block [i * bm, (i + 1) * bm) of that segment's expert, so a single-expert
+// GEMM has no limit on M.
+__device__ __forceinline__ Unit unit_at(const Params& p, int i)
+{
+  if (p.implicit_bm > 0) {
+    const int m0 = i * p.implicit_bm;
+    return Unit{m0, m0, min(m0 + p.implicit_bm, p.M), p.implicit_expert};
+  }
+  return p.units[i];
 }
 
 __host__ __device__ __forceinline__ int launch_tiles(const Params& p)
@@ -243,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
         const TileIdx ti = tile_at(p, t);
-        const Unit u = p.units[ti.unit];
+        const Unit u = unit_at(p, ti.unit);
         const int nb = ti.nb;
         const int brow = u.expert * p.N + nb * kBN;
         for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
@@ -311,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int lt = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
       const TileIdx ti = tile_at(p, t);
-      const Unit u = p.units[ti.unit];
+      const Unit u = unit_at(p, ti.unit);
       const int nb = ti.nb;
       const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
       if (!mbar_wait(accf0 + 8 * acc, aph, p.err, kDevWaitAccFull)) break;
@@ -456,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = pair; t < n_tiles && ok; t += n_pairs) {
         const TileIdx ti = tile_at(p, t);
-        const Unit u = p.units[ti.unit];
+        const Unit u = unit_at(p, ti.unit);
         const bool half = ti.half >= 0;
         // B rows this CTA stages: its half of the tile's columns. A
         // half-width SwiGLU tile keeps gate and up paired: CTA 0 takes 64
@@ -542,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int lt = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const TileIdx ti = tile_at(p, t);
-      const Unit u = p.units[ti.unit];
+      const Unit u = unit_at(p, ti.unit);
       const int nb = ti.nb;
       const bool half = ti.half >= 0;
       const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
@@ -954,7 +968,16 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   const bool pair = tp || use_pair(a.M);   // the fused TP epilogue exists in the pair kernel
   const int bm = pair ? 256 : kBM;
   int n_units = 0;
-  for (int m0 = 0; m0 < a.M; m0 += bm) {
+  if (nseg == 1) {
+    if (ex[0] < 0 || ex[0] >= a.n_experts) {
+      *err = "gemm: segment expert out of range";
+      return 1;
+    }
+    p.implicit_bm = bm;
+    p.implicit_expert = ex[0];
+    n_units = (a.M + bm - 1) / bm;
+  }
+  for (int m0 = 0; nseg > 1 && m0 < a.M; m0 += bm) {
     const int m1 = std::min(m0 + bm, a.M);
     for (int s = 0; s < nseg; ++s) {
       if (off[s + 1] < off[s]) {

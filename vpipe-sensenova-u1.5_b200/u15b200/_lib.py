@@ -46,6 +46,17 @@ class Config(C.Structure):
 vp, ip, i32p = C.c_void_p, C.c_int, C.POINTER(C.c_int)
 
 
+class ImageConfig(C.Structure):
+    _fields_ = [("vision_hidden", C.c_int), ("llm_hidden", C.c_int), ("patch", C.c_int),
+                ("merge", C.c_int), ("head_hidden", C.c_int), ("freq_dim", C.c_int),
+                ("noise_scale_embedding", C.c_int), ("vision_theta", C.c_double)]
+
+
+IMAGE_TENSORS = ["patch_w", "patch_b", "dense_w", "dense_b", "conv1_w", "conv1_b", "conv2_w",
+                 "conv2_b", "tstep_w0", "tstep_b0", "tstep_w2", "tstep_b2", "nscale_w0",
+                 "nscale_b0", "nscale_w2", "nscale_b2"]
+
+
 class Slot(C.Structure):
     _fields_ = [("kv", C.c_void_p), ("kv_off", C.c_int), ("kv_len", C.c_int),
                 ("pos_t", C.c_void_p), ("pos_h", C.c_void_p), ("pos_w", C.c_void_p),
@@ -97,6 +108,19 @@ SIGNATURES = {
                               vp]),
     "u15c_euler": (ip, [vp, vp, vp, C.c_long, C.c_double]),
     "u15c_patchify": (ip, [vp, vp, vp, ip, ip]),
+    "u15c_embed_tokens": (ip, [vp, vp, ip, ip, vp, ip, vp]),
+    "u15c_thw_indexes": (ip, [vp, ip, ip, ip, vp, ip, vp, vp, vp]),
+    "u15c_splice_image_rows": (ip, [vp, vp, ip, vp, ip, ip, C.POINTER(vp), i32p, ip]),
+    "u15c_image_create": (ip, [C.POINTER(ImageConfig), C.POINTER(vp)]),
+    "u15c_image_destroy": (None, [vp]),
+    "u15c_image_bind": (ip, [vp, vp, ip, ip, vp, ip, ip]),
+    "u15c_image_bind_random": (ip, [vp, vp, C.c_uint64, C.c_float]),
+    "u15c_image_patchify": (ip, [vp, vp, vp, ip, ip, ip]),
+    "u15c_image_embed": (ip, [vp, vp, vp, ip, ip, ip, vp]),
+    "u15c_image_timestep_row": (ip, [vp, vp, C.c_double, C.c_double, vp]),
+    "u15c_image_add_timestep": (ip, [vp, vp, vp, ip, C.c_double, C.c_double]),
+    "u15c_image_decode": (ip, [vp, vp, vp, ip, ip, vp]),
+    "u15c_image_to_u8_planar": (ip, [vp, vp, vp, ip, ip]),
     "u15c_unpatchify": (ip, [vp, vp, vp, ip, ip]),
     "u15c_model_create": (ip, [C.POINTER(Config), C.c_uint, C.POINTER(vp)]),
     "u15c_model_destroy": (None, [vp]),

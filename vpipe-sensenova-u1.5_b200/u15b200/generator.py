@@ -12,10 +12,11 @@ its frozen prefix (bidirectional), final norm + pixel head, then on the
 device v = (x_pred - z) / max(1 - t, t_eps), the CFG form and renorm, and
 the Euler update (u15c_velocity / u15c_cfg_combine / u15c_euler).
 
-The patch embedder and pixel head (the reference's ImagePath) are not part
-of this library yet; `LinearImagePath` stands in for them with one linear
-map each way per 32x32 token, computed by libu15c's GEMM, so the loop runs
-end to end and its cost is dominated, as in the reference, by the backbone.
+The image half of each step is the reference's ImagePath on the device
+(`DeviceImagePath` over u15b200.ImagePath: patch embedder, pixel head,
+timestep + noise-scale row); `LinearImagePath` is a lighter stand-in (one
+linear map each way per 32x32 token) that tests use when they restate the
+whole loop on the CPU.
 
 Across ranks (torch.distributed), branches are placed round-robin; after
 each step's forwards every rank all-gathers the velocities (the loop's one
@@ -137,11 +138,44 @@ class LinearImagePath:
         check(lib().u15c_linear_bf16(_stream(), _p(rows), _p(self.w_in), None, _p(out), n,
                                      PIX * PIX * 3, self.hidden))
 
-    def decode(self, h: torch.Tensor, H: int, W: int, rows: torch.Tensor, x_pred: torch.Tensor):
+    def decode(self, h: torch.Tensor, H: int, W: int, x_pred: torch.Tensor):
         n = (H // PIX) * (W // PIX)
+        rows = self._rows(n)
         check(lib().u15c_linear_bf16(_stream(), _p(h), _p(self.w_out), None, _p(rows), n,
                                      self.hidden, PIX * PIX * 3))
         check(lib().u15c_unpatchify(_stream(), _p(rows), _p(x_pred), H, W))
+
+    def _rows(self, n):
+        if getattr(self, "_rowbuf", None) is None or self._rowbuf.shape[0] < n:
+            self._rowbuf = torch.empty(n, PIX * PIX * 3, device="cuda", dtype=torch.bfloat16)
+        return self._rowbuf[:n]
+
+    def embed_step(self, img, H: int, W: int, emb, t: float, noise_ratio: float):
+        """embed the current image and add the timestep row (the stand-in
+        ignores the noise-scale ratio)"""
+        n = (H // PIX) * (W // PIX)
+        self.embed(img, H, W, emb, self._rows(n))
+        check(lib().u15c_add_row(_stream(), _p(emb), _p(self.timestep_row(t)), n, self.hidden))
+
+
+class DeviceImagePath:
+    """The reference's ImagePath on the device (u15b200.ImagePath): per step
+    patchify (channel-first, patch 16), the generation twin of the patch
+    embedder, the timestep + noise-scale row added to every token
+    (src/u15-generator.cc:477-499), and the pixel head after the final norm
+    (src/u15-generator.cc:554-568)."""
+
+    def __init__(self, image):
+        self.im = image
+
+    def embed_step(self, img, H: int, W: int, emb, t: float, noise_ratio: float):
+        p = self.im.cfg["patch"]
+        px = self.im.patchify(img)
+        self.im.embed(px, H // p, W // p, gen=True, out=emb)
+        self.im.add_timestep(emb, t, noise_ratio)
+
+    def decode(self, h, H: int, W: int, x_pred):
+        self.im.decode(h, H // PIX, W // PIX, out=x_pred)
 
 
 @dataclass
@@ -157,15 +191,64 @@ class Branch:
     v: torch.Tensor = None
 
 
+def branch_from_ids(name: str, ids, embed_table: torch.Tensor, *, img_id: int = 151665,
+                    img_ctx_id: int = 151667, images=(), image_path=None):
+    """A prefix from token ids (src/u15-generator.cc:308-392): the
+    embed_tokens rows of the ids, each reference image's patch embedding --
+    the UNDERSTANDING twin, src/u15-generator.cc:231-238 -- spliced over its
+    <IMG_CONTEXT> run, and the (t, h, w) triple of Prompt::thw_indexes.
+    `images`: [H][W][3] f32 device tensors in model space; block-causal
+    prefill when there are any."""
+    ids = np.ascontiguousarray(np.asarray(ids, np.int32))
+    n = len(ids)
+    vocab, hidden = embed_table.shape
+    x = torch.empty(n, hidden, dtype=torch.bfloat16, device="cuda")
+    ids_dev = torch.from_numpy(ids).cuda()
+    check(lib().u15c_embed_tokens(_stream(), _p(embed_table), vocab, hidden, _p(ids_dev), n,
+                                  _p(x)))
+    grids = []
+    if images:
+        if image_path is None:
+            raise ValueError("reference images need the image path (its understanding twin)")
+        im = image_path.im if hasattr(image_path, "im") else image_path
+        p = im.cfg["patch"]
+        embeds, tokens = [], []
+        for img in images:
+            gh, gw = img.shape[0] // p, img.shape[1] // p
+            grids.append((gh, gw))
+            e = im.embed(im.patchify(img), gh, gw, gen=False)
+            embeds.append(e)
+            tokens.append(e.shape[0])
+        ptrs = (C.c_void_p * len(embeds))(*[e.data_ptr() for e in embeds])
+        toks = (C.c_int * len(tokens))(*tokens)
+        check(lib().u15c_splice_image_rows(_stream(), _p(x), hidden,
+                                           C.c_void_p(ids.ctypes.data), n, img_ctx_id, ptrs,
+                                           toks, len(embeds)))
+        torch.cuda.current_stream().synchronize()   # the embeddings may go out of scope
+    t, h, w = (np.zeros(n, np.int32) for _ in range(3))
+    g = np.ascontiguousarray(np.array(grids, np.int32).reshape(-1))
+    vp = lambda a: C.c_void_p(a.ctypes.data)  # noqa: E731
+    check(lib().u15c_thw_indexes(vp(ids), n, img_id, img_ctx_id, vp(g) if grids else None,
+                                 len(grids), vp(t), vp(h), vp(w)))
+    return Branch(name, x, t, h, w, block_causal=bool(images))
+
+
 class Generator:
     """Generator::generate over a u15b200.Model (both experts bound)."""
 
-    def __init__(self, model, image_path=None, device: int | None = None, group=None):
+    def __init__(self, model, image_path=None, device: int | None = None, group=None,
+                 image_seed: int = 0):
         self.m = model
         # the model's device is the caller's current one (one process per GPU)
         self.ops = CudaOps(torch.cuda.current_device() if device is None else device)
         self.hidden = model.cfg["hidden"]
-        self.image = image_path or LinearImagePath(self.hidden)
+        if image_path is None:
+            # no checkpoint here: the device image path with seeded weights
+            from .image import ImagePath
+            im = ImagePath(llm_hidden=self.hidden)
+            im.bind_random(image_seed, 0.02)
+            image_path = DeviceImagePath(im)
+        self.image = image_path
         self.group = group
 
     def prefill(self, b: Branch, ltok: int):
@@ -192,7 +275,8 @@ class Generator:
                  t_eps: float = 0.05, seed: int = 0, noise_scale: float = 1.0,
                  form: int = None, i_img: int = -1, i_unc: int = -1,
                  cfg_interval=(0.0, 1.0), int8: bool = False, sage: bool = False,
-                 init_noise: torch.Tensor = None, step_callback=None):
+                 init_noise: torch.Tensor = None, step_callback=None,
+                 noise_scale_max: float = 16.0):
         """Run the loop; returns the final [H][W][3] f32 image (device).
         `branches` are already ordered cond, [img_cond], [uncond]."""
         th, tw = H // PIX, W // PIX
@@ -217,7 +301,9 @@ class Generator:
             img = torch.randn(H, W, 3, device="cuda", generator=gen) * noise_scale
         ts = time_schedule(steps, shift)
         emb = torch.empty(Ltok, self.hidden, device="cuda", dtype=torch.bfloat16)
-        rows = torch.empty(Ltok, PIX * PIX * 3, device="cuda", dtype=torch.bfloat16)
+        # the noise-scale embedder sees the scale as a ratio of its maximum
+        # (src/u15-generator.cc:465-466)
+        ns_ratio = noise_scale / max(1e-9, noise_scale_max)
         # one hidden state per branch this rank runs, contiguous, so the
         # branches go through the stack together (u15c_forward_many)
         mine = [bi for bi in range(len(branches)) if owner[bi] == rank]
@@ -230,8 +316,7 @@ class Generator:
             b.v = torch.zeros(H, W, 3, device="cuda", dtype=torch.float32)
         for step in range(steps):
             t, t_next = ts[step], ts[step + 1]
-            self.image.embed(img, H, W, emb, rows)
-            self.ops.add_row(emb, self.image.timestep_row(t), Ltok, self.hidden)
+            self.image.embed_step(img, H, W, emb, t, ns_ratio)
             denom = max(1.0 - t, t_eps)
             lo, hi = cfg_interval
             use_cfg = (lo < t < hi) or lo == 0.0
@@ -253,7 +338,7 @@ class Generator:
                 for i, bi in enumerate(run):
                     b = branches[bi]
                     self.m.final_norm(hstate[i], L.EXPERT_GEN)
-                    self.image.decode(hstate[i], H, W, rows, x_pred)
+                    self.image.decode(hstate[i], H, W, x_pred)
                     check(lib().u15c_velocity(_stream(), _p(x_pred), _p(img), _p(b.v), n,
                                               denom))
                     local[bi] = b.v
