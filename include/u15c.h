@@ -468,6 +468,15 @@ int u15c_model_tp_disconnect(u15c_model* m);
  * gate|up interleaved, experts stacked). */
 int u15c_model_bind(u15c_model* m, u15c_stream stream, int layer, int expert, int tensor,
                     const void* src, int dtype, int src_on_host);
+/* The checkpoint's affine-quantized matrices (bind_matrix_,
+ * src/u15-weights.cc:248-325): codes u32 [N][K*bits/32] (code k of a row at
+ * bits (k % (32/bits)) * bits of word k / (32/bits)), scales and biases
+ * [N][K/group] (F16 / BF16 / F32, rounded to bf16 as the reference binds
+ * them); out bf16 [N][K] = scale * code + bias. bits 4 or 8, group 32 or 64.
+ * Dequantized once at bind time; pass `out` to u15c_model_bind (BF16). */
+int u15c_dequant_affine(u15c_stream stream, const uint32_t* codes, const void* scales,
+                        const void* biases, int scale_dtype, int N, int K, int bits, int group,
+                        void* out);
 /* Seeded synthetic weights (no checkpoint): projections N(0, std), norm
  * gains N(norm_mean, norm_std). */
 int u15c_model_bind_random(u15c_model* m, u15c_stream stream, uint64_t seed, float std,

@@ -109,6 +109,7 @@ SIGNATURES = {
     "u15c_euler": (ip, [vp, vp, vp, C.c_long, C.c_double]),
     "u15c_patchify": (ip, [vp, vp, vp, ip, ip]),
     "u15c_embed_tokens": (ip, [vp, vp, ip, ip, vp, ip, vp]),
+    "u15c_dequant_affine": (ip, [vp, vp, vp, vp, ip, ip, ip, ip, ip, vp]),
     "u15c_thw_indexes": (ip, [vp, ip, ip, ip, vp, ip, vp, vp, vp]),
     "u15c_splice_image_rows": (ip, [vp, vp, ip, vp, ip, ip, C.POINTER(vp), i32p, ip]),
     "u15c_image_create": (ip, [C.POINTER(ImageConfig), C.POINTER(vp)]),
