@@ -503,58 +503,89 @@ def denoise_bench(args, rank, world, dist):
     (320-token prefix), image-conditional (8 text + one 1024-token reference
     image, block-causal prefill) and unconditional (13 tokens) -- shift 3.0,
     cfg 4.0, img_cfg 1.5. The image path is the device ImagePath (patch
-    embedder, timestep + noise-scale row, pixel head) with seeded weights. Each rank runs its own seed (a replica): steps/s of the whole job =
-    ranks / max-over-ranks seconds per step."""
+    embedder, timestep + noise-scale row, pixel head) with seeded weights.
+
+    Three placements (N > 1; at N = 1 only the first):
+      replicas    every rank runs its own seed: job steps/s = N / max-over-ranks s/step
+      branches    ONE image, its three CFG branches placed round-robin over the
+                  ranks, one velocity all-gather per step (NCCL)
+      tensor_par  ONE image, every branch on all ranks, the model split by
+                  tensor parallelism (fused row-parallel reduction over NVLink)
+    """
     import torch
     import u15b200
     from u15b200 import _lib as L
     from u15b200.generator import Branch, Generator
 
+    def specs_on(seed):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+
+        def pre(n_text, n_img):
+            n = n_text + n_img
+            x = torch.randn(n, H, device="cuda", generator=g).bfloat16()
+            t = np.concatenate([np.arange(n_text), np.full(n_img, n_text)]).astype(np.int32)
+            h = np.concatenate([np.zeros(n_text), np.arange(n_img) // 32]).astype(np.int32)
+            w = np.concatenate([np.zeros(n_text), np.arange(n_img) % 32]).astype(np.int32)
+            return x, t, h, w
+        specs = [("cond", pre(320, 0), False), ("img_cond", pre(8, 1024), True),
+                 ("uncond", pre(13, 0), False)]
+        return [Branch(nm, x, t, h, w, block_causal=bc) for nm, (x, t, h, w), bc in specs]
+
+    def run(gen, branches, seed):
+        evs = []
+
+        def cb(step, img):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append(e)
+        if dist is not None:
+            dist.barrier()
+        gen.generate(branches, 2048, 2048, steps=1 + args.denoise_steps, shift=3.0, cfg=4.0,
+                     icfg=1.5, form=L.CFG_BOTH, i_img=1, i_unc=2, seed=seed, step_callback=cb)
+        torch.cuda.synchronize()
+        sps = evs[0].elapsed_time(evs[-1]) / 1e3 / args.denoise_steps
+        if dist is not None:
+            t = torch.tensor([sps], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sps = float(t.item())
+        return sps
+
     m = u15b200.Model(n_layers=42)
-    m.bind_random(seed=77 + rank, std=0.02, norm_mean=1.0, norm_std=0.2)
+    m.bind_random(seed=77, std=0.02, norm_mean=1.0, norm_std=0.2)
     for e in range(2):
         m.bind(0, e, "final_norm", torch.ones(H, device="cuda"))
-    g = torch.Generator(device="cuda").manual_seed(5 + rank)
-
-    def pre(n_text, n_img):
-        n = n_text + n_img
-        x = torch.randn(n, H, device="cuda", generator=g).bfloat16()
-        t = np.concatenate([np.arange(n_text), np.full(n_img, n_text)]).astype(np.int32)
-        h = np.concatenate([np.zeros(n_text), np.arange(n_img) // 32]).astype(np.int32)
-        w = np.concatenate([np.zeros(n_text), np.arange(n_img) % 32]).astype(np.int32)
-        return x, t, h, w
-
-    specs = [("cond", pre(320, 0), False), ("img_cond", pre(8, 1024), True),
-             ("uncond", pre(13, 0), False)]
-    branches = [Branch(nm, x, t, h, w, block_causal=bc) for nm, (x, t, h, w), bc in specs]
-    gen = Generator(m)
-    evs = []
-
-    def cb(step, img):
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        evs.append(e)
-
-    n_steps = 1 + args.denoise_steps
-    if dist is not None:
-        dist.barrier()
-    gen.generate(branches, 2048, 2048, steps=n_steps, shift=3.0, cfg=4.0, icfg=1.5,
-                 form=L.CFG_BOTH, i_img=1, i_unc=2, seed=rank, step_callback=cb)
-    torch.cuda.synchronize()
-    s_per_step = evs[0].elapsed_time(evs[-1]) / 1e3 / args.denoise_steps
-    if dist is not None:
-        t = torch.tensor([s_per_step], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        s_per_step = float(t.item())
-    del gen, branches, m
+    s_rep = run(Generator(m), specs_on(5 + rank), rank)
+    out = {"steps_per_s": world / s_rep, "s_per_step_per_replica": s_rep,
+           "timed_steps": args.denoise_steps, "warmup_steps": 1,
+           "config": "42 layers, 4096 gen tokens (BASELINE '1024^2' = 64x64 tokens = 2048^2 px),"
+                     " 3 CFG forwards/step (prefix 320 / 8+1024 img block-causal / 13),"
+                     " device image path (patch embedder, timestep + noise-scale row,"
+                     " pixel head; seeded weights), replicas x%d" % world,
+           "layers_per_step": 3 * 42}
+    if world > 1:
+        # one image, branches over the ranks (same weights and inputs everywhere)
+        s_br = run(Generator(m, group=dist.group.WORLD), specs_on(5), 0)
+        out["one_image_branch_placement"] = {"steps_per_s": 1.0 / s_br, "s_per_step": s_br,
+                                             "branches_per_rank": -(-3 // world)}
+        del m
+        torch.cuda.empty_cache()
+        # one image, tensor parallelism over all ranks
+        mt = u15b200.Model(n_layers=42, tp_rank=rank, tp_size=world)
+        mt.bind_random(seed=77, std=0.02, norm_mean=1.0, norm_std=0.2)
+        for e in range(2):
+            mt.bind(0, e, "final_norm", torch.ones(H, device="cuda"))
+        mt.tp_connect(None, 3 * M_TOK)
+        s_tp = run(Generator(mt), specs_on(5), 0)
+        out["one_image_tensor_parallel"] = {"steps_per_s": 1.0 / s_tp, "s_per_step": s_tp,
+                                            "tp": world, "reduction": "fused, peer memory"}
+        torch.cuda.synchronize()
+        mt.tp_disconnect(None)
+        mt.close()
+        del mt
+    else:
+        del m
     torch.cuda.empty_cache()
-    return {"steps_per_s": world / s_per_step, "s_per_step_per_replica": s_per_step,
-            "timed_steps": args.denoise_steps, "warmup_steps": 1,
-            "config": "42 layers, 4096 gen tokens (BASELINE '1024^2' = 64x64 tokens = 2048^2 px),"
-                      " 3 CFG forwards/step (prefix 320 / 8+1024 img block-causal / 13),"
-                      " device image path (patch embedder, timestep + noise-scale row,"
-                      " pixel head; seeded weights), replicas x%d" % world,
-            "layers_per_step": 3 * 42}
+    return out
 
 
 def main():

@@ -247,6 +247,27 @@ def test_layer_forward_host_matches_device(small):
     assert np.array_equal(oh.float().numpy(), host(xd))
 
 
+@pytest.mark.parametrize("int8", [False, True], ids=["bf16", "w8a8"])
+def test_layer_forward_host_pipelined(int8):
+    """Passes of >= 1024 rows overlap their host copies with the layer (row
+    chunks on a copy stream); every row's arithmetic is the device pass's, so
+    the result is identical. Routed, the segment boundary inside a chunk."""
+    m, _ = build(SMALL, 77, int8=int8)
+    n_und, gh, gw = 700, 20, 40
+    T = n_und + gh * gw
+    segs = [(0, n_und, 0), (n_und, T, 1)]
+    pos = [dev_i32(p) for p in grid_positions(n_und, gh, gw, n_und)]
+    x = bf16_round(randn((T, SMALL["hidden"]), 12))
+    kv = m.make_cache(T)
+    xd = dev_bf16(x)
+    m.layer_forward(1, xd, kv, 0, T, *pos, segments=segs, int8=int8)
+    torch.cuda.synchronize()
+    xh = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    m.layer_forward_host(1, xh, oh, kv, 0, T, *pos, segments=segs, int8=int8)
+    assert np.array_equal(oh.float().numpy(), host(xd))
+
+
 def test_42_layer_drift():
     cfg = dict(SMALL, n_layers=42)
     m, W = build(cfg, 50)

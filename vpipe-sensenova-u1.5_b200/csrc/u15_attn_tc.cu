@@ -131,7 +131,25 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-template <bool SAGE>
+// 2^x for x <= 2^7 on the FMA pipe: x = n + f with n = rint(x) taken from
+// the low mantissa bits of x + 1.5 * 2^23, f in [-0.5, 0.5]; 2^f by a degree-3
+// polynomial fitted to minimise the relative error on that interval (max
+// relative error 7.5e-5, below the bf16 rounding P receives); 2^n added to
+// the exponent field. Inputs below -125 are clamped there (2^-125, a
+// normal float) so the exponent never underflows; masked scores (-inf) give
+// 2^-125 instead of 0, which no bf16 output can show.
+__device__ __forceinline__ float ex2_fma(float x)
+{
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const float f = x - (t - 12582912.0f);
+  float q = fmaf(0.05517132207751274f, f, 0.24261054396629333f);
+  q = fmaf(q, f, 0.6932609677314758f);
+  q = fmaf(q, f, 0.9999281167984009f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
+
+template <bool SAGE, bool EMU>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
@@ -407,8 +425,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float a = ex2(fmaf(s[32 * c + 2 * i], fc, nm));
-          const float b = ex2(fmaf(s[32 * c + 2 * i + 1], fc, nm));
+          const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
+          // EMU: every fourth pair on the FMA pipe, interleaved with the MUFU
+          // ones (i is a constant after unrolling); the Sage instantiation
+          const bool fma_pipe = EMU && (i & 3) == 3;
+          const float a = fma_pipe ? ex2_fma(x0) : ex2(x0);
+          const float b = fma_pipe ? ex2_fma(x1) : ex2(x1);
           rs[i & 3] += a + b;
           pk[i] = pack_bf2(a, b);
         }
@@ -456,330 +478,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
-// =====================================================================
-// 64-key blocks with S double-buffered per tile. The per-tile chain of the
-// 128-key kernel above is softmax(j) -> P.V(j) + S(j+1) on the tensor core
-// -> softmax(j+1): the MMA sits inside every tile's critical path. Here S of
-// the next block is already in the other TMEM buffer when the softmax
-// finishes a block: the MMA issuer queues S(j+2) right behind P.V(j) (same
-// buffer: P(j) was written over S(j)), so the softmax runs block after
-// block and the tensor core works in the background.
-//   TMEM per tile t (256 columns at 256 t): S / P buffer 0 [0,64), buffer 1
-//   [64,128), O [128,256). P (bf16 pairs, 32 columns) over its own S.
-//   warps: 0 TMA (4-stage ring of one K page + one transposed V page),
-//   1 MMA issuer, 2-5 softmax tile 0, 6-9 softmax tile 1 (one row each).
-// o_done[t] completes after each P.V of tile t: a lazy O rescale at block j
-// waits for P.V(j-1) (S(j) completing already implies P.V(j-2), so the
-// barrier is never two phases behind); o_final[t] after the last one.
-// =====================================================================
-namespace b64 {
-
-constexpr int kKeys = 64;
-constexpr int kStages = 4;
-constexpr int kThreads = 64 + 8 * 32;
-constexpr int kQBytes = 2 * kTile * 256;
-constexpr int kKBytes = kKeys * 256;        // [2 dims blocks][64 keys][128 B]
-constexpr int kVBytes = 128 * kKeys * 2;    // [128 dims][64 keys]
-constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 512;
-
-template <bool SAGE>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
-{
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kQBytes;
-  uint8_t* sV = sK + kStages * kKBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * kVBytes);
-  const uint32_t b0 = smem_u32(bars);
-  const uint32_t q_full = b0;
-  const uint32_t k_full = b0 + 8;                   // [kStages]
-  const uint32_t v_full = k_full + 8 * kStages;
-  const uint32_t k_empty = v_full + 8 * kStages;
-  const uint32_t v_empty = k_empty + 8 * kStages;
-  const uint32_t s_full = v_empty + 8 * kStages;    // [2 tiles][2 buffers]
-  const uint32_t p_full = s_full + 32;              // [2 tiles][2 buffers], 128 arrivals
-  const uint32_t o_done = p_full + 32;              // [2 tiles]
-  const uint32_t o_final = o_done + 16;             // [2 tiles]
-  const uint32_t drain = o_final + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 4 + 4 + 2 + 2 + 1);
-
-  const int w = (int)warp_id();
-  const int h = blockIdx.y;
-  const int hk = h / p.G;
-  const int q0 = blockIdx.x * 2 * kTile;
-  const int n = (p.tk + kKeys - 1) / kKeys;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(k_full + 8 * s, 1);
-      mbar_init(v_full + 8 * s, 1);
-      mbar_init(k_empty + 8 * s, 1);
-      mbar_init(v_empty + 8 * s, 1);
-    }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(s_full + 8 * i, 1);
-      mbar_init(p_full + 8 * i, 128);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(o_done + 8 * t, 1);
-      mbar_init(o_final + 8 * t, 1);
-    }
-    mbar_init(drain, 1);
-    fence_barrier_init();
-  }
-  if (w == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  if (threadIdx.x == 32) {
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (w == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane_id() == 0) {
-      const int qrow = h * p.tq + q0;
-      if constexpr (SAGE) {
-        mbar_arrive_expect_tx(q_full, 2 * kTile * 128);
-        for (int t = 0; t < 2; ++t)
-          tma_load_2d(smem_u32(sQ + t * kTile * 128), &tmQ, 0, qrow + t * kTile, q_full);
-      } else {
-        mbar_arrive_expect_tx(q_full, 2 * kTile * 256);
-        for (int t = 0; t < 2; ++t)
-          for (int d = 0; d < 2; ++d)
-            tma_load_2d(smem_u32(sQ + t * kTile * 256 + d * kTile * 128), &tmQ, d * 64,
-                        qrow + t * kTile, q_full);
-      }
-      int nk = 0, nv = 0;
-      for (int j = 0; j < n; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const int page = p.page_table ? p.page_table[j] : j;
-        if (!mbar_wait(k_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
-        uint8_t* kd = sK + s * kKBytes;
-        if constexpr (SAGE) {
-          mbar_arrive_expect_tx(k_full + 8 * s, kKeys * 128);
-          tma_load_2d(smem_u32(kd), &tmK, 0, (int)(hk * p.k8_stride) + j * kKeys, k_full + 8 * s);
-        } else {
-          mbar_arrive_expect_tx(k_full + 8 * s, kKBytes);
-          const int krow = (page * p.hkv + hk) * kKeys;
-          tma_load_2d(smem_u32(kd), &tmK, 0, krow, k_full + 8 * s);
-          tma_load_2d(smem_u32(kd + kKeys * 128), &tmK, 64, krow, k_full + 8 * s);
-        }
-        nk = j + 1;
-        if (!mbar_wait(v_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
-        mbar_arrive_expect_tx(v_full + 8 * s, kVBytes);
-        tma_load_2d(smem_u32(sV + s * kVBytes), &tmV, 0, (page * p.hkv + hk) * 128, v_full + 8 * s);
-        nv = j + 1;
-      }
-      mbar_wait(q_full, 0, p.err, kDevWaitDrain);
-      for (int s = 0; s < kStages; ++s) {
-        if (nk > s) {
-          const int last = ((nk - 1 - s) / kStages) * kStages + s;
-          mbar_wait(k_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
-        }
-        if (nv > s) {
-          const int last = ((nv - 1 - s) / kStages) * kStages + s;
-          mbar_wait(v_full + 8 * s, (last / kStages) & 1, p.err, kDevWaitDrain);
-        }
-      }
-    }
-  } else if (w == 1) {
-    // ------------------------------------------------------------ MMA
-    if (lane_id() == 0) {
-      const uint32_t id_s = SAGE ? idesc_s8(kTile, kKeys) : idesc_bf16(kTile, kKeys);
-      const uint32_t id_o = idesc_bf16(kTile, 128);
-      auto issue_s = [&](int t, int j) {
-        const uint32_t d = tmem + t * 256 + (j & 1) * 64;
-        const uint32_t kb = smem_u32(sK + (j % kStages) * kKBytes);
-        if constexpr (SAGE) {
-          const uint32_t a0 = smem_u32(sQ + t * kTile * 128);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(kb + k * 32), id_s, k != 0);
-        } else {
-          const uint32_t a0 = smem_u32(sQ + t * kTile * 256);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
-                     smem_desc_sw128(kb + (k >> 2) * kKeys * 128 + (k & 3) * 32), id_s, k != 0);
-        }
-        mma_commit(s_full + 8 * (2 * t + (j & 1)));
-      };
-      bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
-      // S of the first two blocks into the two buffers
-      for (int j = 0; j < 2 && j < n && ok; ++j) {
-        ok = mbar_wait(k_full + 8 * (j % kStages), (j / kStages) & 1, p.err, kDevWaitFull);
-        if (!ok) break;
-        tc_fence_after();
-        issue_s(0, j);
-        issue_s(1, j);
-        mma_commit(k_empty + 8 * (j % kStages));
-      }
-      for (int j = 0; j < n && ok; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
-        const uint32_t vb = smem_u32(sV + s * kVBytes);
-        const int j2 = j + 2, s2 = j2 % kStages;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait(p_full + 8 * (2 * t + (j & 1)), (j >> 1) & 1, p.err, kDevWaitFull)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + t * 256 + 128, a = tmem + t * 256 + (j & 1) * 64;
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_bf16_ts(d, a + k * 8, smem_desc_sw128(vb + k * 32), id_o, (j | k) != 0);
-          mma_commit(o_done + 8 * t);
-          if (j + 1 == n) mma_commit(o_final + 8 * t);
-          if (j2 < n) {
-            // S(j+2) into the buffer P(j) just left (the MMAs run in issue order)
-            if (t == 0 && !mbar_wait(k_full + 8 * s2, (j2 / kStages) & 1, p.err, kDevWaitFull)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(t, j2);
-          }
-        }
-        if (!ok) break;
-        mma_commit(v_empty + 8 * s);
-        if (j2 < n) mma_commit(k_empty + 8 * s2);
-      }
-      mma_commit(drain);
-      mbar_wait(drain, 0, p.err, kDevWaitDrain);
-    }
-  } else {
-    // ------------------------------------------------------------ softmax
-    const int t = (w - 2) >> 2;
-    const int wq = w & 3;
-    const int row = wq * 32 + (int)lane_id();
-    const int qi = q0 + t * kTile + row;
-    const uint32_t tS = tmem + t * 256 + ((uint32_t)(wq * 32) << 16);
-    const uint32_t tO = tS + 128;
-    float sqv = 1.0f;
-    if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
-    float m_ref = -INFINITY, l = 0.0f;
-    bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      const int b = j & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full + 8 * (2 * t + b), (j >> 1) & 1, p.err,
-                                             kDevWaitAccFull))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t r[64];
-      tmem_ld32(tS + b * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld32(tS + b * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_ld_wait();
-      float f = p.scale_log2;
-      if constexpr (SAGE) f *= sqv * p.sk[(long)hk * p.nkb + j];
-      float sv[64];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        if constexpr (SAGE) sv[i] = (float)(int32_t)r[i];
-        else sv[i] = __uint_as_float(r[i]);
-      }
-      const int kmax = p.tk - j * kKeys;
-      if (kmax < kKeys) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i >= kmax) sv[i] = -INFINITY;
-      }
-      float mx[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-      for (int i = 4; i < 64; i += 4) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) mx[q] = fmaxf(mx[q], sv[i + q]);
-      }
-      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * f;
-      const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
-      const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O must hold P.V(j - 1) before it is rescaled
-        if (!__all_sync(0xffffffffu, mbar_wait(o_done + 8 * t, (j - 1) & 1, p.err,
-                                               kDevWaitAccFull))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float fac = need ? ex2(m_ref - m_new) : 1.0f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
-          tmem_st32(tO + c * 32, o);
-        }
-        l *= fac;
-      }
-      m_ref = m_new;
-      const float nm = -m_ref;
-      float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      uint32_t pk[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = ex2(fmaf(sv[2 * i], f, nm)), c = ex2(fmaf(sv[2 * i + 1], f, nm));
-        rs[i & 3] += a + c;
-        pk[i] = pack_bf2(a, c);
-      }
-      tmem_st32(tS + b * 64, pk);   // P(j): 32 packed columns over S(j)
-      tmem_st_wait();
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
-      tc_fence_before();
-      mbar_arrive(p_full + 8 * (2 * t + b));
-    }
-    const bool fin = ok && n > 0 && mbar_wait(o_final + 8 * t, 0, p.err, kDevWaitAccFull);
-    if (__all_sync(0xffffffffu, fin)) {
-      tc_fence_after();
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_ld_wait();
-        if (qi < p.tq) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            uint4 v;
-            v.x = pack_bf2(__uint_as_float(o[qd * 8 + 0]) * inv, __uint_as_float(o[qd * 8 + 1]) * inv);
-            v.y = pack_bf2(__uint_as_float(o[qd * 8 + 2]) * inv, __uint_as_float(o[qd * 8 + 3]) * inv);
-            v.z = pack_bf2(__uint_as_float(o[qd * 8 + 4]) * inv, __uint_as_float(o[qd * 8 + 5]) * inv);
-            v.w = pack_bf2(__uint_as_float(o[qd * 8 + 6]) * inv, __uint_as_float(o[qd * 8 + 7]) * inv);
-            d4[qd] = v;
-          }
-        }
-      }
-    }
-    tc_fence_before();
-  }
-
-  __syncthreads();
-  if (w == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-}  // namespace b64
-
 }  // namespace
 
 int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
@@ -819,20 +517,15 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
     if (make_tma_2d(&mk, a.k_pages, (uint64_t)a.n_pages * a.hkv * 64, 128, 64, 2, err)) return 2;
   }
   if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, 64, 128, 2, err)) return 2;
-  // U15_ATTN_64=1: the 64-key double-buffered kernel (A/B measurement)
-  static const bool blk64 = [] {
-    const char* e = std::getenv("U15_ATTN_64");
-    return e != nullptr && *e != '0';
-  }();
-  static std::atomic<uint64_t> set_attr[4];
+  // The Sage kernel computes a quarter of its exponentials on the FMA pipe:
+  // its int8 S MMA is twice as fast, which leaves the MUFU the busier unit
+  // (measured 7-10 % faster); the bf16 kernel measured 5-10 % slower with it.
+  static std::atomic<uint64_t> set_attr[2];
   const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
-  auto k = blk64 ? (sage ? b64::attn_kernel<true> : b64::attn_kernel<false>)
-                 : (sage ? attn_tc_kernel<true> : attn_tc_kernel<false>);
-  const int threads = blk64 ? b64::kThreads : kThreads;
-  const int smem = blk64 ? b64::kSmem : kSmem;
+  auto k = sage ? attn_tc_kernel<true, true> : attn_tc_kernel<false, false>;
   cudaError_t e = cudaSuccess;
-  if (smem_attr_once(k, smem, set_attr[(sage ? 1 : 0) + (blk64 ? 2 : 0)])) {
-    k<<<grid, threads, smem, st>>>(mq, mk, mv, p);
+  if (smem_attr_once(k, kSmem, set_attr[sage ? 1 : 0])) {
+    k<<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
     e = cudaGetLastError();
   } else {
     e = cudaGetLastError();

@@ -154,6 +154,9 @@ struct u15c_model {
   void* sage_ws = nullptr;
   size_t sage_ws_bytes = 0;
   bf16* io = nullptr;   // layer_forward_host staging
+  // layer_forward_host's copy stream and its chunk events (made on first use)
+  cudaStream_t copy_st = nullptr;
+  cudaEvent_t copy_ev[2 * 4 + 1] = {};
   std::vector<void*> scratch_allocs;
 
   int qkv_n() const { return (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim; }
@@ -211,6 +214,9 @@ struct u15c_model {
 
   ~u15c_model()
   {
+    for (cudaEvent_t e : copy_ev)
+      if (e) cudaEventDestroy(e);
+    if (copy_st) cudaStreamDestroy(copy_st);
     free_scratch();
     for (int q = 0; q < u15::kMaxTp; ++q)
       if (tp_peer[q] != nullptr && tp_peer[q] != tp_mem) cudaIpcCloseMemHandle(tp_peer[q]);
@@ -298,9 +304,15 @@ u15::SegInfo slice_seg(const u15::SegInfo& g, int r0, int n)
 // run once over all M rows of all slots; the QKV post-processing (into each
 // slot's own cache) and the attention (over each slot's own keys) run per
 // slot. rcos/rsin already hold the tables for all M rows.
-int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15::SegInfo& seg,
-               const int* seg_off, const int* seg_expert, int nseg,
-               const std::vector<SlotRun>& slots, unsigned flags)
+// The parts of a layer pass. The row-wise parts (the norm + QKV before the
+// attention, o_proj through down_proj after it) can run on a range of rows,
+// which is how u15c_layer_forward_host overlaps its host copies with them.
+enum LayerPart { kPartPre = 1, kPartAttn = 2, kPartPost = 4, kPartAll = 7 };
+
+int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x_all, int M,
+               const u15::SegInfo& seg_all, const int* seg_off_all, const int* seg_expert_all,
+               int nseg_all, const std::vector<SlotRun>& slots, unsigned flags,
+               int parts = kPartAll, int r0 = 0, int rn = -1)
 {
   const u15c_config& c = m->cfg;
   const LayerW& L = m->layers[li];
@@ -310,13 +322,24 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
     return fail(U15C_EINVAL, "W8A8 requested but the model has no int8 twins "
                              "(create with U15C_MODEL_INT8 and call u15c_model_finalize)");
   int rc;
+  // the row range of the row-wise parts, its segments renumbered from 0
+  const bool whole = r0 == 0 && (rn < 0 || rn == M);
+  const int Mr = whole ? M : rn;
+  const u15::SegInfo seg = whole ? seg_all : slice_seg(seg_all, r0, Mr);
+  int roff[u15::kMaxSeg + 1], rex[u15::kMaxSeg];
+  for (int i = 0; i <= seg.nseg; ++i) roff[i] = seg.off[i];
+  for (int i = 0; i < seg.nseg; ++i) rex[i] = seg.expert[i];
+  const int* seg_off = whole ? seg_off_all : roff;
+  const int* seg_expert = whole ? seg_expert_all : rex;
+  const int nseg = whole ? nseg_all : seg.nseg;
+  bf16* x = x_all + (long)r0 * H;
   // prequant: the activation was already quantised into x8/s_tok (by the
   // fused RMSNorm + quantisation), so the int8 path skips its own pass.
   auto gemm = [&](const void* in, int K, const bf16* w, const int8_t* w8, const float* ws, int N,
                   int epi, void* y, bool prequant = false, int* out_tiles = nullptr) -> int {
     u15::GemmArgs a;
     a.n_experts = E;
-    a.M = M;
+    a.M = Mr;
     a.K = K;
     a.N = N;
     a.seg_off = seg_off;
@@ -330,7 +353,7 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
       a.out_tiles = out_tiles;
     }
     if (i8) {
-      if (!prequant && u15::launch_quant_rows(in, m->x8, m->s_tok, M, K, st))
+      if (!prequant && u15::launch_quant_rows(in, m->x8, m->s_tok, Mr, K, st))
         return fail(U15C_ECUDA, "quant_rows launch failed");
       a.int8 = true;
       a.x = m->x8;
@@ -363,7 +386,7 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
         return fail(U15C_ECUDA, "tensor-parallel wait launch failed");
       return U15C_OK;
     }
-    const long n = (long)M * H;
+    const long n = (long)Mr * H;
     if (m->ar_fn == nullptr || m->part == nullptr || m->part_elems < n)
       return fail(U15C_EINVAL, "tensor-parallel model: no all-reduce installed, or its "
                                "buffer holds fewer than tokens x hidden floats "
@@ -380,17 +403,22 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
   // activation quantisation
   const bool fuse_q = i8 && H <= 4096;
   auto norm = [&](const bf16* w) -> int {
-    const int r = fuse_q ? u15::launch_rms_norm_quant(x, w, m->x8, m->s_tok, M, H, (float)c.eps,
+    const int r = fuse_q ? u15::launch_rms_norm_quant(x, w, m->x8, m->s_tok, Mr, H, (float)c.eps,
                                                       seg, st)
-                         : u15::launch_rms_norm(x, w, m->xn, M, H, (float)c.eps, seg, st);
+                         : u15::launch_rms_norm(x, w, m->xn, Mr, H, (float)c.eps, seg, st);
     return r ? fail(U15C_ECUDA, "rms_norm launch failed") : U15C_OK;
   };
 
   // ---- attention half (src/u15-backbone.cc:191-235) ----
-  if ((rc = norm(L.ln_in))) return rc;
-  if ((rc = gemm(m->xn, H, L.qkv, L.qkv8, L.qkv_s, m->qkv_n(), u15::kEpiStore, m->qkv, fuse_q)))
-    return rc;
+  if (parts & kPartPre) {
+    if ((rc = norm(L.ln_in))) return rc;
+    if ((rc = gemm(m->xn, H, L.qkv, L.qkv8, L.qkv_s, m->qkv_n(), u15::kEpiStore,
+                   m->qkv + (long)r0 * m->qkv_n(), fuse_q)))
+      return rc;
+  }
   for (const SlotRun& sl : slots) {
+    if (!(parts & kPartAttn)) break;
+    const u15::SegInfo& seg = seg_all;
     const u15::KvView view = sl.kv->view(li);
     const u15::SegInfo sseg = slice_seg(seg, sl.row0, sl.n);
     bf16* qh = m->qh + (long)sl.row0 * m->qd();
@@ -408,7 +436,8 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x, int M, const u15
                               sl.kv_off, sl.t_index, nullptr);
     if (rc) return rc;
   }
-  if ((rc = row_parallel(m->attn, m->qd(), L.o, L.o8, L.o_s))) return rc;
+  if (!(parts & kPartPost)) return U15C_OK;
+  if ((rc = row_parallel(m->attn + (long)r0 * m->qd(), m->qd(), L.o, L.o8, L.o_s))) return rc;
 
   // ---- MLP half (src/u15-backbone.cc:246-256) ----
   if ((rc = norm(L.ln_post))) return rc;
@@ -1077,7 +1106,81 @@ int u15c_layer_forward_host(u15c_model* m, u15c_stream stream, int layer, const 
   int rc = m->ensure_scratch(n, kv_len);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t bytes = (size_t)n * m->cfg.hidden * 2;
+  const int H = m->cfg.hidden;
+  const size_t bytes = (size_t)n * H * 2;
+  // Pipelined: the upload in 4 row chunks on a copy stream, each chunk's
+  // norm + QKV as soon as it lands; attention over all rows; o_proj through
+  // down_proj per chunk, each chunk's download while the next one runs. The
+  // host buffers should be pinned for the copies to overlap. Small passes
+  // and tensor-parallel models take the plain upload -> layer -> download.
+  constexpr int kChunks = 4;
+  if (n >= 1024 && m->tp_size == 1) {
+    if ((rc = validate_pass(m, n, kv, kv_off, kv_len, attn, pos_t, pos_h, pos_w, t_index)))
+      return rc;
+    if (layer < 0 || layer >= m->cfg.n_layers) return fail(U15C_EINVAL, "layer out of range");
+    u15::SegInfo seg;
+    std::string err;
+    if (!u15::fill_seg(&seg, seg_off, seg_expert, nseg, n, m->cfg.n_experts, &err))
+      return fail(U15C_EINVAL, err);
+    if (m->copy_st == nullptr) {
+      if (cudaStreamCreateWithFlags(&m->copy_st, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(U15C_ECUDA, "layer_forward_host: copy stream");
+      for (cudaEvent_t& e : m->copy_ev)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+          return fail(U15C_ECUDA, "layer_forward_host: copy events");
+    }
+    cudaStream_t cs = m->copy_st;
+    const int rows = ((n + kChunks - 1) / kChunks + 255) / 256 * 256;   // whole 256-row blocks
+    const char* hin = static_cast<const char*>(x_host);
+    char* hout = static_cast<char*>(out_host);
+    cudaEvent_t* in_ev = m->copy_ev;
+    cudaEvent_t* out_ev = m->copy_ev + kChunks;
+    // the copy stream starts after what the caller already queued on `st`
+    cudaEventRecord(m->copy_ev[2 * kChunks], st);
+    cudaStreamWaitEvent(cs, m->copy_ev[2 * kChunks], 0);
+    for (int k = 0, r0 = 0; r0 < n; ++k, r0 += rows) {
+      const size_t off = (size_t)r0 * H * 2, len = (size_t)std::min(rows, n - r0) * H * 2;
+      cudaError_t e = cudaMemcpyAsync(reinterpret_cast<char*>(m->io) + off, hin + off, len,
+                                      cudaMemcpyHostToDevice, cs);
+      if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host: upload");
+      cudaEventRecord(in_ev[k], cs);
+    }
+    if (u15::launch_rope_tables(pos_t, pos_h, pos_w, n, 64, 32, m->cfg.theta_t, m->cfg.theta_hw,
+                                m->rcos, m->rsin, st))
+      return fail(U15C_ECUDA, "rope tables launch failed");
+    SlotRun sl;
+    sl.n = n;
+    sl.kv = kv;
+    sl.kv_off = kv_off;
+    sl.kv_len = kv_len;
+    sl.attn = attn;
+    sl.t_index = t_index;
+    const std::vector<SlotRun> slots{sl};
+    for (int k = 0, r0 = 0; r0 < n; ++k, r0 += rows) {
+      cudaStreamWaitEvent(st, in_ev[k], 0);
+      if ((rc = layer_impl(m, st, layer, m->io, n, seg, seg_off, seg_expert, nseg, slots, flags,
+                           kPartPre, r0, std::min(rows, n - r0))))
+        return rc;
+    }
+    if ((rc = layer_impl(m, st, layer, m->io, n, seg, seg_off, seg_expert, nseg, slots, flags,
+                         kPartAttn)))
+      return rc;
+    for (int k = 0, r0 = 0; r0 < n; ++k, r0 += rows) {
+      const int rk = std::min(rows, n - r0);
+      if ((rc = layer_impl(m, st, layer, m->io, n, seg, seg_off, seg_expert, nseg, slots, flags,
+                           kPartPost, r0, rk)))
+        return rc;
+      cudaEventRecord(out_ev[k], st);
+      cudaStreamWaitEvent(cs, out_ev[k], 0);
+      const size_t off = (size_t)r0 * H * 2;
+      cudaError_t e = cudaMemcpyAsync(hout + off, reinterpret_cast<char*>(m->io) + off,
+                                      (size_t)rk * H * 2, cudaMemcpyDeviceToHost, cs);
+      if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host: download");
+    }
+    cudaEventRecord(m->copy_ev[2 * kChunks], cs);
+    cudaStreamWaitEvent(st, m->copy_ev[2 * kChunks], 0);
+    return u15c_sync(stream);
+  }
   cudaError_t e = cudaMemcpyAsync(m->io, x_host, bytes, cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host: upload");
   rc = u15c_layer_forward(m, stream, layer, m->io, n, seg_off, seg_expert, nseg, kv, kv_off,
