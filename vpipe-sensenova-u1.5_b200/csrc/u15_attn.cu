@@ -25,6 +25,7 @@
 #include "u15_common.cuh"
 #include "u15_kernels.h"
 
+#include <algorithm>
 #include <cmath>
 
 namespace u15 {
@@ -376,63 +377,129 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
 // ---------------------------------------------------------------------
 // Sage prologue
 // ---------------------------------------------------------------------
-// kmean[hk][c] = sum_j<tk K[hk][j][c] / tk; 1024 threads per kv head,
-// 8 key-strided partial sums per channel combined in a fixed order.
-__global__ void __launch_bounds__(1024) kmean_kernel(KvView kv, int tk, float* kmean)
+// Two launches. The first runs, side by side, the Q blocks (one 64-row
+// block of one head per CTA: absmax, s = amax / 127, int8 codes) and the
+// K-mean partials (one 64-key page of one kv head per CTA: the page's
+// channel sums). The second runs the K blocks: each CTA forms kmean[c] =
+// sum of the page partials / tk (fixed page order), smooths its 64 keys by
+// it and quantizes them like Q. Rows stay in registers between the absmax
+// and the codes: 32 elements a thread, 16-byte loads, 8-byte stores.
+constexpr int kSageThreads = 256;
+
+__device__ __forceinline__ void load8_bf(const __nv_bfloat16* p, float (&v)[8])
 {
-  const int hk = blockIdx.x, c = threadIdx.x & 127, part = threadIdx.x >> 7;
-  float acc = 0.0f;
-  for (int j = part; j < tk; j += 8) acc += bf2f(kv_row(kv, kv.k, hk, j)[c]);
-  __shared__ float red[8][128];
-  red[part][c] = acc;
-  __syncthreads();
-  if (part == 0) {
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += red[i][c];
-    kmean[hk * 128 + c] = s / (float)tk;
-  }
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
 }
 
-// One CTA per 64-row block: absmax over the block, s = amax/127, codes.
-// K blocks read the smoothed K (K - kmean) from the cache view.
-template <bool IS_K>
-__global__ void __launch_bounds__(256)
-    sage_quant_kernel(const __nv_bfloat16* q, KvView kv, const float* kmean, int rows_valid,
-                      int nblk, int8_t* out, float* scale, long out_stride)
+__device__ __forceinline__ float block_absmax(float m, float* red)
 {
-  const int b = blockIdx.x, h = blockIdx.y;
-  const int r0 = b * 64;
-  __shared__ float red[8];
-  float m = 0.0f;
-  for (int i = threadIdx.x; i < 64 * 128; i += 256) {
-    const int r = r0 + i / 128, c = i % 128;
-    if (r >= rows_valid) continue;
-    float v;
-    if (IS_K) v = bf2f(kv_row(kv, kv.k, h, r)[c]) - kmean[h * 128 + c];
-    else v = bf2f(q[((long)h * rows_valid + r) * 128 + c]);
-    m = fmaxf(m, fabsf(v));
-  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  if (lane_id() == 0) red[warp_id()] = m;
   __syncthreads();
   float amax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, red[i]);
-  const float s = __fdiv_rn(amax, 127.0f);
-  if (threadIdx.x == 0) scale[(long)h * nblk + b] = s;
-  for (int i = threadIdx.x; i < 64 * 128; i += 256) {
-    const int r = r0 + i / 128, c = i % 128;
-    int k = 0;
-    if (r < rows_valid && s > 0.0f) {
-      float v;
-      if (IS_K) v = bf2f(kv_row(kv, kv.k, h, r)[c]) - kmean[h * 128 + c];
-      else v = bf2f(q[((long)h * rows_valid + r) * 128 + c]);
-      k = max(-127, min(127, __float2int_rn(__fdiv_rn(v, s))));
+  for (int i = 0; i < kSageThreads / 32; ++i) amax = fmaxf(amax, red[i]);
+  return amax;
+}
+
+// codes of v[4][8] (rows r0 + 16 i, columns 8 c8 ..) with scale s
+__device__ __forceinline__ void store_codes(const float (&v)[4][8], float s, bool (&valid)[4],
+                                            int8_t* out, long row0, int c8)
+{
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (!valid[i]) continue;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int q = s > 0.0f ? max(-127, min(127, __float2int_rn(__fdiv_rn(v[i][k], s)))) : 0;
+      w[k >> 2] |= (uint32_t)(q & 0xff) << (8 * (k & 3));
     }
-    if (IS_K || r < rows_valid) out[((long)h * out_stride + r) * 128 + c] = (int8_t)k;
+    *reinterpret_cast<uint2*>(out + (row0 + 16 * i) * 128 + c8 * 8) = make_uint2(w[0], w[1]);
   }
+}
+
+__global__ void __launch_bounds__(kSageThreads)
+    sage_q_kernel(const __nv_bfloat16* q, KvView kv, int hq, int hkv, int tq, int tk, int nqb,
+                  int npg, int8_t* q8, float* sq, float* kpart)
+{
+  __shared__ float red[kSageThreads / 32];
+  const int tid = threadIdx.x;
+  if ((int)blockIdx.x >= nqb) {
+    // K-mean partial of one page: two threads per channel, 32 keys each
+    const int pg = (int)blockIdx.x - nqb, hk = blockIdx.y;
+    if (hk >= hkv) return;
+    const int c = tid & 127, half = tid >> 7;
+    const int j0 = pg * 64 + half * 32, j1 = min(tk, j0 + 32);
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int j = j0; j < j1; ++j) acc += bf2f(kv_row(kv, kv.k, hk, j)[c]);
+    __shared__ float hsum[128];
+    if (half == 1) hsum[c] = acc;
+    __syncthreads();
+    if (half == 0) kpart[((long)hk * npg + pg) * 128 + c] = acc + hsum[c];
+    return;
+  }
+  const int b = blockIdx.x, h = blockIdx.y;
+  if (h >= hq) return;
+  const int c8 = tid & 15, r0 = b * 64 + (tid >> 4);
+  float v[4][8];
+  bool valid[4];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + 16 * i;
+    valid[i] = r < tq;
+    if (valid[i]) {
+      load8_bf(q + ((long)h * tq + r) * 128 + c8 * 8, v[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(v[i][k]));
+    }
+  }
+  const float s = __fdiv_rn(block_absmax(m, red), 127.0f);
+  if (tid == 0) sq[(long)h * nqb + b] = s;
+  store_codes(v, s, valid, q8 + (long)h * tq * 128, r0, c8);
+}
+
+__global__ void __launch_bounds__(kSageThreads)
+    sage_k_kernel(KvView kv, int tk, int npg, const float* kpart, int8_t* k8, float* sk,
+                  long k8_stride)
+{
+  __shared__ float red[kSageThreads / 32];
+  __shared__ float km[128];
+  const int pg = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
+  if (tid < 128) {
+    float acc = 0.0f;
+    for (int i = 0; i < npg; ++i) acc += kpart[((long)hk * npg + i) * 128 + tid];
+    km[tid] = acc / (float)tk;
+  }
+  __syncthreads();
+  const int c8 = tid & 15, r0 = pg * 64 + (tid >> 4);
+  float v[4][8];
+  bool valid[4];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + 16 * i;
+    valid[i] = true;   // every row of the block is written; rows past tk as zeros
+    if (r < tk) {
+      load8_bf(kv_row(kv, kv.k, hk, r) + c8 * 8, v[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        v[i][k] -= km[c8 * 8 + k];
+        m = fmaxf(m, fabsf(v[i][k]));
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[i][k] = 0.0f;
+    }
+  }
+  const float s = __fdiv_rn(block_absmax(m, red), 127.0f);
+  if (tid == 0) sk[(long)hk * npg + pg] = s;
+  store_codes(v, s, valid, k8 + (long)hk * k8_stride * 128, r0, c8);
 }
 
 }  // namespace
@@ -503,11 +570,11 @@ int sage_prepare(const void* q, const KvView& kv, int hq, int hkv, int tq, int t
 {
   if (tq <= 0 || tk <= 0) return 0;
   const int nqb = (tq + 63) / 64, nkb = (tk + 63) / 64;
-  kmean_kernel<<<hkv, 1024, 0, st>>>(kv, tk, kmean);
-  sage_quant_kernel<false><<<dim3(nqb, hq), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(q), kv, kmean, tq, nqb, q8, sq, tq);
-  sage_quant_kernel<true><<<dim3(nkb, hkv), 256, 0, st>>>(nullptr, kv, kmean, tk, nkb, k8, sk,
-                                                           (long)nkb * 64);
+  // kmean holds the per-page partial sums [hkv][nkb][128]
+  sage_q_kernel<<<dim3(nqb + nkb, std::max(hq, hkv)), kSageThreads, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(q), kv, hq, hkv, tq, tk, nqb, nkb, q8, sq, kmean);
+  sage_k_kernel<<<dim3(nkb, hkv), kSageThreads, 0, st>>>(kv, tk, nkb, kmean, k8, sk,
+                                                         (long)nkb * 64);
   if (cudaGetLastError() != cudaSuccess) {
     *err = "sage_prepare: kernel launch failed";
     return 2;

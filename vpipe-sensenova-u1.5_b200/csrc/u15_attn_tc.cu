@@ -370,10 +370,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         f0 *= sqv * p.sk[(long)hk * p.nkb + kb0];
         f1 *= sqv * p.sk[(long)hk * p.nkb + kb1];
       }
+      // Sage scores are int32 sums of 128 int8 x int8 products, |S| <=
+      // 128 * 127 * 127 < 2^22: adding them to the bits of 1.5 * 2^23 gives
+      // the float 1.5 * 2^23 + S exactly, and subtracting 1.5 * 2^23 leaves
+      // S -- an integer add and a float add in place of a conversion.
       float s[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
-        if constexpr (SAGE) s[i] = (float)(int32_t)r[i];
+        if constexpr (SAGE) s[i] = __int_as_float((int)r[i] + 0x4B400000) - 12582912.0f;
         else s[i] = __uint_as_float(r[i]);
       }
       const int kmax = p.tk - j * kBlk;

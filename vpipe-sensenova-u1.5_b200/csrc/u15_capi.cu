@@ -119,7 +119,7 @@ size_t sage_bytes(int hq, int hkv, int tq, int tk)
   const size_t nqb = (size_t)(tq + 63) / 64, nkb = (size_t)(tk + 63) / 64;
   auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
   return al((size_t)hq * tq * 128) + al((size_t)hkv * nkb * 64 * 128) + al(4 * hq * nqb) +
-         al(4 * hkv * nkb) + al(4 * (size_t)hkv * 128);
+         al(4 * hkv * nkb) + al(4 * (size_t)hkv * nkb * 128);
 }
 
 SageWs sage_split(void* ws, int hq, int hkv, int tq, int tk)

@@ -246,34 +246,45 @@ __global__ void split_rope_kernel(__nv_bfloat16* __restrict__ x, const float* __
 }
 
 // ---------------------------------------------------------------------
-// RoPE tables on the device, angles in fp64 (src/u15-metal-ops.cc:547-605):
-// one thread per (token, column), column c in range [off, off + width).
+// RoPE tables on the device, angles in fp64 (src/u15-metal-ops.cc:547-605).
+// A block covers kRopeTok tokens x 128 columns; the 128 inverse frequencies
+// (column c in range [off, off + width)) are formed once per block.
 // ---------------------------------------------------------------------
+constexpr int kRopeTok = 16;
+
 __global__ void rope_tables_kernel(const int32_t* __restrict__ pt, const int32_t* __restrict__ ph,
                                    const int32_t* __restrict__ pw, int tokens, int d_t, int d_h,
                                    double theta_t, double theta_hw, float* __restrict__ cos_out,
                                    float* __restrict__ sin_out)
 {
-  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (long)tokens * 128) return;
-  const int t = (int)(idx / 128), c = (int)(idx % 128);
-  int off, width;
-  double theta;
-  const int32_t* pos;
-  if (c < d_t) { off = 0; width = d_t; theta = theta_t; pos = pt; }
-  else if (c < d_t + d_h) { off = d_t; width = d_h; theta = theta_hw; pos = ph; }
-  else { off = d_t + d_h; width = d_h; theta = theta_hw; pos = pw; }
-  const int half = width / 2;
-  const int i = (c - off) % half;
-  const double inv = 1.0 / pow(theta, (double)(2 * i) / (double)width);
-  const double ang = (double)pos[t] * inv;
-  cos_out[idx] = (float)cos(ang);
-  sin_out[idx] = (float)sin(ang);
+  __shared__ double inv_s[128];
+  if (threadIdx.x < 128) {
+    const int c = threadIdx.x;
+    int off, width;
+    double theta;
+    if (c < d_t) { off = 0; width = d_t; theta = theta_t; }
+    else if (c < d_t + d_h) { off = d_t; width = d_h; theta = theta_hw; }
+    else { off = d_t + d_h; width = d_h; theta = theta_hw; }
+    const int i = (c - off) % (width / 2);
+    inv_s[c] = 1.0 / pow(theta, (double)(2 * i) / (double)width);
+  }
+  __syncthreads();
+  const int c = threadIdx.x & 127;
+  const int32_t* pos = c < d_t ? pt : (c < d_t + d_h ? ph : pw);
+  const double inv = inv_s[c];
+  for (int r = threadIdx.x >> 7; r < kRopeTok; r += blockDim.x >> 7) {
+    const int t = blockIdx.x * kRopeTok + r;
+    if (t >= tokens) break;
+    const double ang = (double)pos[t] * inv;
+    const long idx = (long)t * 128 + c;
+    cos_out[idx] = (float)cos(ang);
+    sin_out[idx] = (float)sin(ang);
+  }
 }
 
 // ---------------------------------------------------------------------
 // Fused QKV post-processing of the token-major GEMM output
-// qkv [T][(NH + 2*KV) * 128]: per (token, head) warp,
+// qkv [T][(NH + 2*KV) * 128], per (token, head) row:
 //   q heads: split norm (q_norm, q_norm_hw of the row's expert) -> bf16 ->
 //            split rope -> bf16 -> q_out [NH][T][128]      (transpose_thd)
 //   k heads: the same with k_norm / k_norm_hw -> K cache @ kv_off (append)
@@ -283,60 +294,131 @@ __global__ void rope_tables_kernel(const int32_t* __restrict__ pt, const int32_t
 // after the norm and after the rope is kept.
 // norms: [E][4][64] bf16 = q_t, q_hw, k_t, k_hw per expert.
 // ---------------------------------------------------------------------
-__global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                const __nv_bfloat16* __restrict__ norms,
-                                const float* __restrict__ cosf_, const float* __restrict__ sinf_,
-                                __nv_bfloat16* __restrict__ q_out, KvView kv, int T, int nh,
-                                int nkv, int kv_off, float eps, SegInfo seg)
+constexpr int kQkvWarps = 8;
+constexpr int kQkvBatch = 4;     // rows a warp loads before it computes
+constexpr int kVtPad = 130;      // bf16 per staged V row: 65 words, odd, so the
+                                 // column reads of the transpose spread over banks
+
+// One launch, two kinds of block.
+// Blocks [0, T): one token each. Warp w takes heads w, w + 8, ... of the q
+// and k heads (and, for a cache with untransposed V, the v heads); the
+// token's cos / sin columns are loaded once per warp and serve all of them.
+// Blocks [T, T + nwin * nkv): one (64-token page window, v head) of a cache
+// whose V pages are transposed: the window's V rows are staged in shared
+// memory and written as [128 dims][64 tokens] rows, 16 bytes a thread.
+// Tokens of a window outside [0, T) (the frozen prefix, past the block) are
+// never written.
+__global__ void __launch_bounds__(kQkvWarps * 32)
+    qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ norms,
+                    const float* __restrict__ cosf_, const float* __restrict__ sinf_,
+                    __nv_bfloat16* __restrict__ q_out, KvView kv, int T, int nh, int nkv,
+                    int kv_off, float eps, SegInfo seg)
 {
   const int heads = nh + 2 * nkv;
-  const long row = (long)blockIdx.x * (blockDim.x / 32) + warp_id();
-  if (row >= (long)T * heads) return;
-  const int l = lane_id();
-  const int t = (int)(row / heads), h = (int)(row % heads);
-  const __nv_bfloat16* src = qkv + row * 128 + l * 4;
-  const uint2 u = *reinterpret_cast<const uint2*>(src);
-  const float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y);
-  float v[4] = {a.x, a.y, b.x, b.y};
-  __nv_bfloat16* dst;
-  if (h < nh + nkv) {
+  const int l = lane_id(), w = warp_id();
+  if ((int)blockIdx.x < T) {
+    const int t = blockIdx.x;
     const int e = expert_of(t, seg);
-    const __nv_bfloat16* nw = norms + (long)e * 256 + (h < nh ? 0 : 128) + (l < 16 ? 0 : 64) +
-                              (l & 15) * 4;
-    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-    ss = half_sum(ss);
-    const float inv = rsqrtf(ss / 64.0f + eps);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = bfround(v[i] * inv * bf2f(nw[i]));
+    const int nrow = nh + nkv + (kv.v_t ? 0 : nkv);
     const float4 c4 = *reinterpret_cast<const float4*>(cosf_ + (long)t * 128 + l * 4);
     const float4 s4 = *reinterpret_cast<const float4*>(sinf_ + (long)t * 128 + l * 4);
     const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-    rope4(v, cs, sn, l);
-    if (h < nh) {
-      dst = q_out + ((long)h * T + t) * 128;
-    } else {
-      const int j = kv_off + t;
-      const long page = kv.page_table ? kv.page_table[j >> 6] : (j >> 6);
-      dst = reinterpret_cast<__nv_bfloat16*>(kv.k) + page * kv.page_stride +
-            (long)(h - nh) * kv.head_stride + (long)(j & 63) * 128;
-    }
-  } else {
     const int j = kv_off + t;
     const long page = kv.page_table ? kv.page_table[j >> 6] : (j >> 6);
-    __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(kv.v) + page * kv.page_stride +
-                          (long)(h - nh - nkv) * kv.head_stride;
-    if (kv.v_t) {
-      // transposed page: dims are rows of 64 tokens
+    const long kv_row = page * kv.page_stride + (long)(j & 63) * 128 + l * 4;
+    const __nv_bfloat16* src = qkv + (long)t * heads * 128 + l * 4;
+    const int g = (l < 16 ? 0 : 64) + (l & 15) * 4;
+    for (int h0 = w; h0 < nrow; h0 += kQkvWarps * kQkvBatch) {
+      uint2 u[kQkvBatch];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) base[(long)(l * 4 + i) * 64 + (j & 63)] = f2bf(v[i]);
-      return;
+      for (int i = 0; i < kQkvBatch; ++i) {
+        const int h = h0 + i * kQkvWarps;
+        if (h < nrow) u[i] = *reinterpret_cast<const uint2*>(src + (long)h * 128);
+      }
+#pragma unroll
+      for (int i = 0; i < kQkvBatch; ++i) {
+        const int h = h0 + i * kQkvWarps;   // warp-uniform
+        if (h >= nrow) break;
+        const float2 a = unpack_bf2(u[i].x), b = unpack_bf2(u[i].y);
+        float v[4] = {a.x, a.y, b.x, b.y};
+        __nv_bfloat16* dst;
+        if (h < nh + nkv) {
+          const uint2 wn = *reinterpret_cast<const uint2*>(norms + (long)e * 256 +
+                                                           (h < nh ? 0 : 128) + g);
+          const float2 w0 = unpack_bf2(wn.x), w1 = unpack_bf2(wn.y);
+          const float wv[4] = {w0.x, w0.y, w1.x, w1.y};
+          float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+          ss = half_sum(ss);
+          const float inv = rsqrtf(ss / 64.0f + eps);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) v[k] = bfround(v[k] * inv * wv[k]);
+          rope4(v, cs, sn, l);
+          dst = h < nh ? q_out + ((long)h * T + t) * 128 + l * 4
+                       : reinterpret_cast<__nv_bfloat16*>(kv.k) + kv_row +
+                             (long)(h - nh) * kv.head_stride;
+        } else {
+          dst = reinterpret_cast<__nv_bfloat16*>(kv.v) + kv_row +
+                (long)(h - nh - nkv) * kv.head_stride;
+        }
+        uint2 o;
+        o.x = pack_bf2(v[0], v[1]);
+        o.y = pack_bf2(v[2], v[3]);
+        *reinterpret_cast<uint2*>(dst) = o;
+      }
     }
-    dst = base + (long)(j & 63) * 128;
+    return;
   }
-  uint2 o;
-  o.x = pack_bf2(v[0], v[1]);
-  o.y = pack_bf2(v[2], v[3]);
-  *reinterpret_cast<uint2*>(dst + l * 4) = o;
+  // ---- transposed V: one (window, v head)
+  __shared__ uint32_t tile[64 * kVtPad / 2];
+  const int vb = (int)blockIdx.x - T;
+  const int win = vb / nkv, hv = vb % nkv;
+  const int jw = (kv_off & ~63) + win * 64;       // first cache token of the window
+  const int t_lo = max(0, kv_off - jw), t_hi = min(64, kv_off + T - jw);   // valid [t_lo, t_hi)
+  // stage: 64 rows x 16 chunks of 8 dims, 4 per thread
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int item = threadIdx.x + it * kQkvWarps * 32;
+    const int r = item >> 4, q = item & 15;
+    if (r >= t_lo && r < t_hi) {
+      const int t = jw + r - kv_off;
+      const uint4 x = *reinterpret_cast<const uint4*>(
+          qkv + ((long)t * heads + nh + nkv + hv) * 128 + q * 8);
+      uint32_t* d = tile + r * (kVtPad / 2) + q * 4;
+      d[0] = x.x;
+      d[1] = x.y;
+      d[2] = x.z;
+      d[3] = x.w;
+    }
+  }
+  __syncthreads();
+  const long page = kv.page_table ? kv.page_table[jw >> 6] : (jw >> 6);
+  __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(kv.v) + page * kv.page_stride +
+                        (long)hv * kv.head_stride;
+  const unsigned short* tb = reinterpret_cast<const unsigned short*>(tile);
+  // write: 128 dim rows x 8 chunks of 8 tokens, 4 per thread; eight lanes
+  // fill one 128-byte dim row
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int item = threadIdx.x + it * kQkvWarps * 32;
+    const int c = item & 7, d = item >> 3;
+    unsigned short x[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[k] = tb[(8 * c + k) * kVtPad + d];
+    __nv_bfloat16* dst = base + (long)d * 64 + 8 * c;
+    if (8 * c >= t_lo && 8 * c + 8 <= t_hi) {
+      uint4 o;
+      o.x = x[0] | ((uint32_t)x[1] << 16);
+      o.y = x[2] | ((uint32_t)x[3] << 16);
+      o.z = x[4] | ((uint32_t)x[5] << 16);
+      o.w = x[6] | ((uint32_t)x[7] << 16);
+      *reinterpret_cast<uint4*>(dst) = o;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (8 * c + k >= t_lo && 8 * c + k < t_hi)
+          reinterpret_cast<unsigned short*>(dst)[k] = x[k];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------
@@ -562,7 +644,7 @@ int launch_rope_tables(const int32_t* pt, const int32_t* ph, const int32_t* pw, 
                        cudaStream_t st)
 {
   if (tokens <= 0) return 0;
-  rope_tables_kernel<<<blocks_for((long)tokens * 128, 256), 256, 0, st>>>(
+  rope_tables_kernel<<<(unsigned)((tokens + kRopeTok - 1) / kRopeTok), 256, 0, st>>>(
       pt, ph, pw, tokens, d_t, d_h, theta_t, theta_hw, c, s);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
@@ -571,9 +653,10 @@ int launch_qkv_post(const void* qkv, const void* norms, const float* c, const fl
                     void* q_out, const KvView& kv, int T, int nh, int nkv, int kv_off, float eps,
                     const SegInfo& seg, cudaStream_t st)
 {
-  const long rows = (long)T * (nh + 2 * nkv);
-  if (rows <= 0) return 0;
-  qkv_post_kernel<<<blocks_for(rows, 8), 256, 0, st>>>(
+  if (T <= 0 || nh + 2 * nkv <= 0) return 0;
+  // transposed-V windows: the 64-token pages the block [kv_off, kv_off + T) touches
+  const long nwin = kv.v_t ? ((kv_off & 63) + T + 63) / 64 : 0;
+  qkv_post_kernel<<<(unsigned)(T + nwin * nkv), kQkvWarps * 32, 0, st>>>(
       static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(norms), c, s,
       static_cast<__nv_bfloat16*>(q_out), kv, T, nh, nkv, kv_off, eps, seg);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
