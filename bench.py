@@ -531,7 +531,7 @@ def denoise_bench(args, rank, world, dist):
                  ("uncond", pre(13, 0), False)]
         return [Branch(nm, x, t, h, w, block_causal=bc) for nm, (x, t, h, w), bc in specs]
 
-    def run(gen, branches, seed):
+    def run(gen, branches, seed, int8=False):
         evs = []
 
         def cb(step, img):
@@ -541,7 +541,8 @@ def denoise_bench(args, rank, world, dist):
         if dist is not None:
             dist.barrier()
         gen.generate(branches, 2048, 2048, steps=1 + args.denoise_steps, shift=3.0, cfg=4.0,
-                     icfg=1.5, form=L.CFG_BOTH, i_img=1, i_unc=2, seed=seed, step_callback=cb)
+                     icfg=1.5, form=L.CFG_BOTH, i_img=1, i_unc=2, seed=seed, step_callback=cb,
+                     int8=int8)
         torch.cuda.synchronize()
         sps = evs[0].elapsed_time(evs[-1]) / 1e3 / args.denoise_steps
         if dist is not None:
@@ -550,12 +551,16 @@ def denoise_bench(args, rank, world, dist):
             sps = float(t.item())
         return sps
 
-    m = u15b200.Model(n_layers=42)
+    # bf16 weights and their per-channel int8 twin (BASELINE config 4 times both)
+    m = u15b200.Model(int8=True, n_layers=42)
     m.bind_random(seed=77, std=0.02, norm_mean=1.0, norm_std=0.2)
     for e in range(2):
         m.bind(0, e, "final_norm", torch.ones(H, device="cuda"))
+    m.finalize()
     s_rep = run(Generator(m), specs_on(5 + rank), rank)
+    s_rep8 = run(Generator(m), specs_on(5 + rank), rank, int8=True)
     out = {"steps_per_s": world / s_rep, "s_per_step_per_replica": s_rep,
+           "steps_per_s_i8": world / s_rep8, "s_per_step_per_replica_i8": s_rep8,
            "timed_steps": args.denoise_steps, "warmup_steps": 1,
            "config": "42 layers, 4096 gen tokens (BASELINE '1024^2' = 64x64 tokens = 2048^2 px),"
                      " 3 CFG forwards/step (prefix 320 / 8+1024 img block-causal / 13),"

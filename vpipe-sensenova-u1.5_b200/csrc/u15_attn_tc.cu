@@ -521,13 +521,13 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
     if (make_tma_2d(&mk, a.k_pages, (uint64_t)a.n_pages * a.hkv * 64, 128, 64, 2, err)) return 2;
   }
   if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, 64, 128, 2, err)) return 2;
-  // The Sage kernel computes a quarter of its exponentials on the FMA pipe
-  // (U15_SAGE_EMU=0 keeps them all on the MUFU; A/B checks); the bf16 kernel
-  // measured 5-10 % slower with it.
+  // Every exponential on the MUFU: a quarter of them on the FMA pipe measured
+  // 5-10 % slower for bf16 and 4 % slower for Sage (U15_SAGE_EMU=1 selects
+  // that form of the Sage kernel, for A/B checks).
   static std::atomic<uint64_t> set_attr[3];
   const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
   const char* emu_env = std::getenv("U15_SAGE_EMU");
-  const bool emu = emu_env == nullptr || *emu_env != '0';
+  const bool emu = emu_env != nullptr && *emu_env == '1';
   auto k = !sage ? attn_tc_kernel<false, false>
                  : (emu ? attn_tc_kernel<true, true> : attn_tc_kernel<true, false>);
   const int which = !sage ? 0 : (emu ? 1 : 2);
