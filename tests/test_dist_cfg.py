@@ -1,6 +1,6 @@
 """The CFG-branch placement and the per-step velocity exchange across ranks
 (the denoise loop's one collective), on CPU with the gloo backend and two
-ranks. No GPU: the exchange is host logic over torch.distributed."""
+and four ranks. No GPU: the exchange is host logic over torch.distributed."""
 import os
 import socket
 
@@ -33,13 +33,16 @@ def _worker(rank, world, port, n_branch, numel, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("n_branch", [1, 2, 3])
-def test_velocity_exchange_two_ranks(n_branch):
+@pytest.mark.parametrize("world,n_branch", [(2, 1), (2, 2), (2, 3), (4, 3)])
+def test_velocity_exchange(world, n_branch):
+    """Every rank ends with every branch's velocity; at 4 ranks and 3 branches
+    one rank owns none and contributes only padding."""
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, n_branch, 37, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n_branch, 37, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]

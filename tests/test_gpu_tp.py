@@ -1,7 +1,7 @@
-"""Tensor parallelism (one render over two GPUs): q/k/v heads, the KV cache
-and gate/up split column-wise, o_proj and down_proj row-wise with an
+"""Tensor parallelism (one render over two or four GPUs): q/k/v heads, the
+KV cache and gate/up split column-wise, o_proj and down_proj row-wise with an
 all-reduce of the f32 partial products (NCCL through torch.distributed).
-Two spawned ranks bind the same full weights; their outputs must be equal,
+Spawned ranks bind the same full weights; their outputs must be equal,
 match the CPU restatement of the layer (same bars as the one-GPU layer
 tests) and match a one-GPU model on the same weights. Both forms of the
 row-parallel reduction are checked: the all-reduce hook (NCCL) and the
@@ -19,6 +19,11 @@ pytestmark = pytest.mark.gpu
 
 TPCFG = dict(n_layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, inter=1024,
              n_experts=2)
+# four ranks: one kv head, two q heads and 512 of the MLP's columns per rank;
+# hidden 1024 gives every rank one 256-column block of the fused reduction
+TPCFG4 = dict(n_layers=2, hidden=1024, heads=8, kv_heads=4, head_dim=128, inter=2048,
+              n_experts=2)
+CFGS = {2: TPCFG, 4: TPCFG4}
 N_UND, GH, GW = 32, 8, 12
 
 
@@ -30,12 +35,12 @@ def _free_port():
     return p
 
 
-def _inputs():
+def _inputs(cfg):
     from test_gpu_layer import grid_positions
     T = N_UND + GH * GW
     segs = [(0, N_UND, 0), (N_UND, T, 1)]
     pos = grid_positions(N_UND, GH, GW, N_UND)
-    x = bf16_round(randn((T, TPCFG["hidden"]), 41))
+    x = bf16_round(randn((T, cfg["hidden"]), 41))
     return T, segs, pos, x
 
 
@@ -62,9 +67,10 @@ def _tp_worker(rank, world, port, q, fused=False):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     try:
-        T, segs, pos, x = _inputs()
-        m = u15b200.Model(tp_rank=rank, tp_size=world, **TPCFG)
-        _bind(m, TPCFG, 1)
+        cfg = CFGS[world]
+        T, segs, pos, x = _inputs(cfg)
+        m = u15b200.Model(tp_rank=rank, tp_size=world, **cfg)
+        _bind(m, cfg, 1)
         if fused:
             m.tp_connect(None, T)
         else:
@@ -88,12 +94,13 @@ def _tp_worker(rank, world, port, q, fused=False):
         dist.destroy_process_group()
 
 
-def _run_ranks(fused):
+def _run_ranks(fused, world):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q, fused)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q, fused))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
@@ -103,27 +110,35 @@ def _run_ranks(fused):
     return res
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("fused", [False, True], ids=["nccl_hook", "fused_peer"])
-def test_tp2_layer_and_stack(fused):
+def test_tp_layer_and_stack(fused, world):
     import u15b200
     from oracle import oracle as O
     from test_gpu_layer import check_layer, dims_of
-    (_, l0, k0, f0), (_, l1, k1, f1) = _run_ranks(fused)
-    # the all-reduce hands every rank the same sums: replicas stay identical
-    assert np.array_equal(l0, l1) and np.array_equal(f0, f1)
-    T, segs, pos, x = _inputs()
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} visible GPUs")
+    cfg = CFGS[world]
+    res = _run_ranks(fused, world)
+    l0, f0 = res[0][1], res[0][3]
+    # the reduction hands every rank the same sums: replicas stay identical
+    for _, lr, _, fr in res[1:]:
+        assert np.array_equal(l0, lr) and np.array_equal(f0, fr)
+    T, segs, pos, x = _inputs(cfg)
     # one-GPU model on the same weights, for the layer and the stack
-    m = u15b200.Model(**TPCFG)
-    W = _bind(m, TPCFG, 1)
+    m = u15b200.Model(**cfg)
+    W = _bind(m, cfg, 1)
     pd = [dev_i32(p) for p in pos]
     kv = m.make_cache(T)
     xd = dev_bf16(x)
     m.forward(xd, kv, 0, T, *pd, segments=segs)
     torch.cuda.synchronize()
     assert rel_l2(f0, host(xd)) < 1e-2
-    # layer 0 against the CPU restatement; rank r holds kv head r
-    ref, kn, _ = O.mot_layer(x, segs, W[0], dims_of(TPCFG), *pos)
+    # layer 0 against the CPU restatement; rank r holds kv heads
+    # [r * kv / world, (r + 1) * kv / world)
+    ref, kn, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos)
     check_layer(l0, x, ref)
-    assert rel_l2(np.concatenate([k0, k1]), kn) < 1e-2
-    assert rel_l2(k0, kn[:1]) < 1e-2 and rel_l2(k0, kn[1:]) > 1e-1   # negative control
+    ks = [r[2] for r in res]
+    assert rel_l2(np.concatenate(ks), kn) < 1e-2
+    per = cfg["kv_heads"] // world
+    assert rel_l2(ks[0], kn[:per]) < 1e-2 and rel_l2(ks[0], kn[per:2 * per]) > 1e-1   # negative control
