@@ -145,6 +145,40 @@ def quantised(ops, x):
     return q, s
 
 
+def _bf16_step(v, d):
+    """v (bf16-representable f32) moved d bf16 steps (toward +inf for d > 0
+    on positive values)."""
+    b = (v.view(np.uint32) >> 16).astype(np.int64) + d
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+@pytest.mark.parametrize("cols", [4096, 12288, 16384])
+def test_quant_rows_ties_bit_exact(ops, cols):
+    """Quotients at and one bf16 step either side of half-integers, for scales
+    that are exact (amax 127, 63.5) and inexact (amax 100, 3.3): the device's
+    reciprocal path must reproduce the division rule's codes, ties to even
+    included. Column counts cover the 16- and 48-per-thread register forms and
+    the two-pass form."""
+    rng = np.random.default_rng(5)
+    rows = []
+    for amax in (127.0, 63.5, 100.0, 3.3):
+        a = bf16_round(np.array([amax], np.float32))[0]
+        sc = np.float32(a) / np.float32(127.0)
+        for d in (0, 1, -1):
+            k = rng.integers(-126, 126, cols).astype(np.float32)
+            v = bf16_round(((k + np.float32(0.5)) * sc).astype(np.float32))
+            if d:
+                v = _bf16_step(v, d)
+            v = np.clip(v, -a, a)
+            v[0] = a
+            rows.append(v)
+    x = np.stack(rows).astype(np.float32)
+    q, s = quantised(ops, x)
+    rq, rs = O.quant_rows_i8(x)
+    assert np.array_equal(host(s), rs)
+    assert np.array_equal(host(q), rq)
+
+
 @pytest.mark.parametrize("M,K,N", [(128, 128, 256), (77, 4096, 1000), (256, 12288, 512)])
 def test_linear_i8_bit_exact(ops, M, K, N):
     x = bf16_round(randn((M, K), 20))

@@ -58,7 +58,65 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8])
 // y = bf16(x * rsqrt(mean(x^2) + eps) * w_e)
 // ---------------------------------------------------------------------
 constexpr int kRmsThreads = 256;
+constexpr int kRmsPer = 16;        // elements a thread keeps: 256 x 16 = 4096 columns
 
+// Symmetric int8 code of v at scale s: rn_even(v / s) clamped to +-127, with
+// the division's exact result. t = v * r (r = RN(1 / s)) is within 1.5 * 2^-23
+// relative of v / s, i.e. within 2.3e-5 for |v / s| <= 127, so rounding t to
+// the nearest integer (even on ties; the 1.5 * 2^23 add) gives the same code
+// as rounding the IEEE quotient unless t lies within that distance of a
+// half-integer; those rare values take the division itself.
+__device__ __forceinline__ uint32_t quant_code(float v, float s, float r)
+{
+  const float t = v * r;
+  const float tm = t + 12582912.0f;
+  const float d = t - (tm - 12582912.0f);
+  // |v| <= amax and s = RN(amax / 127) keep |t| <= 127 * (1 + 2^-23): the
+  // code never leaves [-127, 127], so no clamp is needed (s = 0 gives r = 0)
+  int k = __float_as_int(tm) - 0x4B400000;
+  if (fabsf(fabsf(d) - 0.5f) < 1e-4f) k = __float2int_rn(__fdiv_rn(v, s));
+  return (uint32_t)(k & 0xff);
+}
+
+__device__ __forceinline__ uint2 quant8(const float* v, float s, float r)
+{
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    lo |= quant_code(v[i], s, r) << (8 * i);
+    hi |= quant_code(v[4 + i], s, r) << (8 * i);
+  }
+  return make_uint2(lo, hi);
+}
+
+// block-wide sum / max over kRmsThreads threads; red[] holds 8 floats and is
+// reusable after the call
+__device__ __forceinline__ float block_sum(float v, float* red)
+{
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane_id() == 0) red[warp_id()] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kRmsThreads / 32; ++i) t += red[i];
+  return t;
+}
+__device__ __forceinline__ float block_max(float v, float* red)
+{
+  v = warp_max(v);
+  __syncthreads();
+  if (lane_id() == 0) red[warp_id()] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kRmsThreads / 32; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+// One CTA per row; thread i holds columns 8 (i + 256 k) .. + 8, k < 2 (the
+// row and its gains stay in registers, loaded before the reduction). One
+// warp per row (8 rows a CTA, shuffle-only reductions) measured 30 % slower.
 __global__ void __launch_bounds__(kRmsThreads)
     rms_norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                     __nv_bfloat16* __restrict__ y, int rows, int dim, float eps, SegInfo seg)
@@ -69,6 +127,36 @@ __global__ void __launch_bounds__(kRmsThreads)
   const __nv_bfloat16* wr = w + (long)expert_of(row, seg) * dim;
   __nv_bfloat16* yr = y + (long)row * dim;
   __shared__ float red[kRmsThreads / 32];
+  if (dim <= kRmsThreads * kRmsPer) {
+    float v[kRmsPer], g[kRmsPer];
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kRmsPer / 8; ++k) {
+      const int c = (k * kRmsThreads + threadIdx.x) * 8;
+      float t[8] = {0, 0, 0, 0, 0, 0, 0, 0}, u[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (c < dim) {
+        load8(xr + c, t);
+        load8(wr + c, u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[k * 8 + i] = t[i];
+        g[k * 8 + i] = u[i];
+        acc += t[i] * t[i];
+      }
+    }
+    const float inv = rsqrtf(block_sum(acc, red) / (float)dim + eps);
+#pragma unroll
+    for (int k = 0; k < kRmsPer / 8; ++k) {
+      const int c = (k * kRmsThreads + threadIdx.x) * 8;
+      if (c >= dim) continue;
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[k * 8 + i] * inv * g[k * 8 + i];
+      store8(yr + c, o);
+    }
+    return;
+  }
   float acc = 0.0f;
   for (int c = threadIdx.x * 8; c < dim; c += kRmsThreads * 8) {
     float v[8];
@@ -76,13 +164,7 @@ __global__ void __launch_bounds__(kRmsThreads)
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc += v[i] * v[i];
   }
-  acc = warp_sum(acc);
-  if (lane_id() == 0) red[warp_id()] = acc;
-  __syncthreads();
-  float tot = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kRmsThreads / 32; ++i) tot += red[i];
-  const float inv = rsqrtf(tot / (float)dim + eps);
+  const float inv = rsqrtf(block_sum(acc, red) / (float)dim + eps);
   for (int c = threadIdx.x * 8; c < dim; c += kRmsThreads * 8) {
     float v[8], g[8];
     load8(xr + c, v);
@@ -98,7 +180,7 @@ __global__ void __launch_bounds__(kRmsThreads)
 // registers (the value the unfused path would store), its absmax reduced
 // over the CTA, and the codes written directly: q = rn_even(y / (amax/127)).
 // Codes are bit-identical to rms_norm followed by quant_rows. dim <= 4096.
-constexpr int kRmsQuantPer = 16;   // elements per thread: 256 x 16 = 4096
+constexpr int kRmsQuantPer = kRmsPer;
 __global__ void __launch_bounds__(kRmsThreads)
     rms_norm_quant_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                           int8_t* __restrict__ q, float* __restrict__ scale, int rows, int dim,
@@ -109,61 +191,38 @@ __global__ void __launch_bounds__(kRmsThreads)
   const __nv_bfloat16* xr = x + (long)row * dim;
   const __nv_bfloat16* wr = w + (long)expert_of(row, seg) * dim;
   __shared__ float red[kRmsThreads / 32];
-  float v[kRmsQuantPer];
+  float v[kRmsQuantPer], g[kRmsQuantPer];
   float acc = 0.0f;
 #pragma unroll
   for (int k = 0; k < kRmsQuantPer / 8; ++k) {
     const int c = (k * kRmsThreads + threadIdx.x) * 8;
-    float t[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (c < dim) load8(xr + c, t);
+    float t[8] = {0, 0, 0, 0, 0, 0, 0, 0}, u[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c < dim) {
+      load8(xr + c, t);
+      load8(wr + c, u);
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       v[k * 8 + i] = t[i];
+      g[k * 8 + i] = u[i];
       acc += t[i] * t[i];
     }
   }
-  acc = warp_sum(acc);
-  if (lane_id() == 0) red[warp_id()] = acc;
-  __syncthreads();
-  float tot = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kRmsThreads / 32; ++i) tot += red[i];
-  const float inv = rsqrtf(tot / (float)dim + eps);
+  const float inv = rsqrtf(block_sum(acc, red) / (float)dim + eps);
   float m = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kRmsQuantPer / 8; ++k) {
-    const int c = (k * kRmsThreads + threadIdx.x) * 8;
-    float g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (c < dim) load8(wr + c, g);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float y = bfround(v[k * 8 + i] * inv * g[i]);
-      v[k * 8 + i] = y;
-      m = fmaxf(m, fabsf(y));
-    }
+  for (int i = 0; i < kRmsQuantPer; ++i) {
+    v[i] = bfround(v[i] * inv * g[i]);
+    m = fmaxf(m, fabsf(v[i]));
   }
-  m = warp_max(m);
-  __syncthreads();   // red[] reuse
-  if (lane_id() == 0) red[warp_id()] = m;
-  __syncthreads();
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kRmsThreads / 32; ++i) amax = fmaxf(amax, red[i]);
-  const float s = __fdiv_rn(amax, 127.0f);
+  const float s = __fdiv_rn(block_max(m, red), 127.0f);
+  const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
   if (threadIdx.x == 0) scale[row] = s;
 #pragma unroll
   for (int k = 0; k < kRmsQuantPer / 8; ++k) {
     const int c = (k * kRmsThreads + threadIdx.x) * 8;
     if (c >= dim) continue;
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      int code = 0;
-      if (s > 0.0f) code = max(-127, min(127, __float2int_rn(__fdiv_rn(v[k * 8 + i], s))));
-      const uint32_t b = (uint32_t)(code & 0xff);
-      if (i < 4) lo |= b << (8 * i); else hi |= b << (8 * (i - 4));
-    }
-    *reinterpret_cast<uint2*>(q + (long)row * dim + c) = make_uint2(lo, hi);
+    *reinterpret_cast<uint2*>(q + (long)row * dim + c) = quant8(&v[k * 8], s, r);
   }
 }
 
@@ -553,13 +612,40 @@ __global__ void silu_kernel(__nv_bfloat16* __restrict__ x, long n8)
 // Every step is a single correctly-rounded fp32 operation, so the codes
 // equal the CPU restatement's bit for bit.
 // ---------------------------------------------------------------------
+// One CTA per row: absmax, s = amax / 127, codes. PER > 0: rows up to 256 x
+// PER columns stay in registers between the two passes (PER = 16 for the
+// 4096-wide rows, 48 for the 12288-wide ones); PER = 0 reads the row twice.
+template <int PER>
 __global__ void __launch_bounds__(256)
     quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ q,
                       float* __restrict__ scale, int cols)
 {
+  constexpr int kQuantPer = PER > 0 ? PER : 8;
   const long row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * cols;
   __shared__ float red[8];
+  if (PER > 0) {
+    float v[kQuantPer];
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kQuantPer / 8; ++k) {
+      const int c = (k * 256 + threadIdx.x) * 8;
+      if (c < cols) {
+        load8(xr + c, *reinterpret_cast<float(*)[8]>(&v[k * 8]));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[k * 8 + i]));
+      }
+    }
+    const float s = __fdiv_rn(block_max(m, red), 127.0f);
+    const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+    if (threadIdx.x == 0) scale[row] = s;
+#pragma unroll
+    for (int k = 0; k < kQuantPer / 8; ++k) {
+      const int c = (k * 256 + threadIdx.x) * 8;
+      if (c < cols) *reinterpret_cast<uint2*>(q + row * cols + c) = quant8(&v[k * 8], s, r);
+    }
+    return;
+  }
   float m = 0.0f;
   for (int c = threadIdx.x * 8; c < cols; c += 256 * 8) {
     float v[8];
@@ -567,26 +653,13 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
   }
-  m = warp_max(m);
-  if (lane_id() == 0) red[warp_id()] = m;
-  __syncthreads();
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, red[i]);
-  const float s = __fdiv_rn(amax, 127.0f);
+  const float s = __fdiv_rn(block_max(m, red), 127.0f);
+  const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
   if (threadIdx.x == 0) scale[row] = s;
   for (int c = threadIdx.x * 8; c < cols; c += 256 * 8) {
     float v[8];
     load8(xr + c, v);
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      int k = 0;
-      if (s > 0.0f) k = max(-127, min(127, __float2int_rn(__fdiv_rn(v[i], s))));
-      const uint32_t b = (uint32_t)(k & 0xff);
-      if (i < 4) lo |= b << (8 * i); else hi |= b << (8 * (i - 4));
-    }
-    *reinterpret_cast<uint2*>(q + row * cols + c) = make_uint2(lo, hi);
+    *reinterpret_cast<uint2*>(q + row * cols + c) = quant8(v, s, r);
   }
 }
 
@@ -732,7 +805,13 @@ int launch_silu(void* x, long n, cudaStream_t st)
 int launch_quant_rows(const void* x, int8_t* q, float* s, int rows, int cols, cudaStream_t st)
 {
   if (rows <= 0) return 0;
-  quant_rows_kernel<<<rows, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), q, s, cols);
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  if (cols <= 256 * 16)
+    quant_rows_kernel<16><<<rows, 256, 0, st>>>(xb, q, s, cols);
+  else if (cols <= 256 * 48)
+    quant_rows_kernel<48><<<rows, 256, 0, st>>>(xb, q, s, cols);
+  else
+    quant_rows_kernel<0><<<rows, 256, 0, st>>>(xb, q, s, cols);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
