@@ -388,6 +388,9 @@ def run_ours(args, rank, world, local):
         tp = tp_bench(args, rank, world, dist, timed, pos, segs, x0)
         tp["speedup_vs_one_gpu"] = ms_step / tp["ms_per_layer_fused"]
 
+    # ---- the image path of one branch (rank 0) ----
+    img_line = image_bench(max(5, min(args.steps, 20))) if rank == 0 else None
+
     # ---- denoise steps/s (BASELINE config 5 geometry), one replica per rank ----
     den = None
     if args.denoise_steps > 0:
@@ -441,6 +444,7 @@ def run_ours(args, rank, world, local):
         "kernels": kern,
         "tensor_parallel": tp,
         "denoise": den,
+        "image_path": img_line,
         "clocks": clk.summary(),
         "cpu_baseline": cpu_line,
     }
@@ -494,6 +498,45 @@ def tp_bench(args, rank, world, dist, timed, pos, segs, x0):
         del m
         torch.cuda.empty_cache()
     return out
+
+
+IMG_FLOP = {"patch": 2.0 * 16384 * 1024 * 768, "dense": 2.0 * 4096 * 4096 * 4096,
+            "conv1": 2.0 * 16384 * 1024 * 9216, "conv2": 2.0 * 65536 * 192 * 2304}
+
+
+def image_bench(steps):
+    """The device image path of one CFG branch at the denoise geometry
+    (2048 x 2048 px, 4096 tokens): patchify + patch embedder (patch GEMM,
+    GELU / 2-D RoPE / merge, dense GEMM) and the pixel head (PS(2), im2col,
+    conv1 GEMM, GELU + PS(2), im2col, conv2 GEMM, PS(8)). Seeded random
+    weights and inputs; CUDA events, inputs resident."""
+    import torch
+    import u15b200
+    im = u15b200.ImagePath()
+    im.bind_random(seed=3)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    img = torch.randn(2048, 2048, 3, device="cuda", generator=g)
+    h = torch.randn(4096, 4096, device="cuda", generator=g).bfloat16()
+    emb = torch.empty(4096, 4096, device="cuda", dtype=torch.bfloat16)
+    dec = torch.empty(2048, 2048, 3, device="cuda", dtype=torch.float32)
+
+    def embed():
+        im.embed(im.patchify(img), 128, 128, gen=True, out=emb)
+
+    def decode():
+        im.decode(h, 64, 64, out=dec)
+    for _ in range(3):
+        embed()
+        decode()
+    t_e = ev_time(embed, steps)
+    t_d = ev_time(decode, steps)
+    im.close()
+    fe = IMG_FLOP["patch"] + IMG_FLOP["dense"]
+    fd = IMG_FLOP["conv1"] + IMG_FLOP["conv2"]
+    return {"embed_ms": t_e, "decode_ms": t_d, "embed_tflops": fe / t_e / 1e9,
+            "decode_tflops": fd / t_d / 1e9,
+            "config": "one branch at 2048x2048 px / 4096 tokens; embed = patchify + patch "
+                      "embedder (25.8 + 137.4 GFLOP), decode = pixel head (309.2 + 58.0 GFLOP)"}
 
 
 def denoise_bench(args, rank, world, dist):
@@ -603,7 +646,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--denoise-steps", type=int, default=3,
                     help="timed denoise steps after one warm-up step (0: skip)")
+    ap.add_argument("--image-only", action="store_true",
+                    help="time only the image path of one branch (a small case for profiling)")
     args = ap.parse_args()
+    if args.image_only:
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        print(json.dumps({"image_path": image_bench(max(1, args.steps))}))
+        return
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -26,6 +26,7 @@
 #include "u15_capi_internal.h"
 #include "u15_common.cuh"
 
+#include <algorithm>
 #include <cmath>
 #include <string>
 #include <vector>
@@ -37,6 +38,8 @@ using u15::fail;
 namespace {
 
 using bf16 = __nv_bfloat16;
+using u15::pack_bf2;
+using u15::unpack_bf2;
 inline unsigned nblk(long n, int t) { return (unsigned)((n + t - 1) / t); }
 
 __device__ __forceinline__ float gelu_erf(float v)
@@ -135,6 +138,154 @@ __global__ void ps8_out_kernel(const bf16* in, float* out, int H, int W)
   const int oy = (int)(pix / OW), ox = (int)(pix % OW);
   const int y = oy / 8, ii = oy % 8, x = ox / 8, jj = ox % 8;
   out[i] = __bfloat162float(in[((long)y * W + x) * 192 + c * 64 + ii * 8 + jj]);
+}
+
+// ---- the same layout moves, a run of values per thread (the forms above
+// stay for geometries these do not cover) ----
+
+// patchify for patch 16: one thread per (patch, patch row) reads the row's
+// 16 pixels x 3 channels (192 contiguous bytes) and writes the three
+// 16-value channel runs of the channel-first patch (32 bytes each).
+__global__ void patchify16_kernel(const float* img, bf16* px, int H, int W)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int gw = W / 16;
+  if (i >= (long)(H / 16) * gw * 16) return;
+  const long patch = i / 16;
+  const int pi = (int)(i % 16);
+  const int y = (int)(patch / gw) * 16 + pi, x0 = (int)(patch % gw) * 16;
+  const float4* src = reinterpret_cast<const float4*>(img + ((long)y * W + x0) * 3);
+  float v[48];
+#pragma unroll
+  for (int k = 0; k < 12; ++k) {
+    const float4 f = src[k];
+    v[4 * k] = f.x;
+    v[4 * k + 1] = f.y;
+    v[4 * k + 2] = f.z;
+    v[4 * k + 3] = f.w;
+  }
+#pragma unroll
+  for (int ci = 0; ci < 3; ++ci) {
+    uint32_t w[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) w[q] = pack_bf2(v[(2 * q) * 3 + ci], v[(2 * q + 1) * 3 + ci]);
+    uint4* dst = reinterpret_cast<uint4*>(px + patch * 768 + ci * 256 + pi * 16);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+// the vision RoPE's (cos, sin) for every (position, frequency):
+// rot[pos][k] = sincos((double)pos * inv[k]), the values vision_post forms
+__global__ void vision_rot_kernel(const float* inv, int quarter, int npos, double2* rot)
+{
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= npos * quarter) return;
+  const int pos = i / quarter, k = i % quarter;
+  double sn, cs;
+  sincos((double)pos * (double)inv[k], &sn, &cs);
+  rot[i] = make_double2(cs, sn);
+}
+
+// vision_post for a 2 x 2 merge: one thread per (merged token, channel pair
+// q) takes pair q of the token's four patches (GELU, rotation from the
+// table) and writes the 8 outputs (channels 2q, 2q+1 x the four patches,
+// channel (c, i, j) order) as one 16-byte run.
+__global__ void vision_post_m2_kernel(const bf16* emb, bf16* merged, int gh, int gw, int C,
+                                      const double2* rot)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int pairs = C / 2, ow = gw / 2;
+  if (i >= (long)(gh / 2) * ow * pairs) return;
+  const long t = i / pairs;
+  const int q = (int)(i % pairs);
+  const int quarter = C / 4;
+  const bool second = q >= quarter;
+  const int k = second ? q - quarter : q;
+  const int r0 = (int)(t / ow) * 2, c0 = (int)(t % ow) * 2;
+  float o[8];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int row = r0 + (s >> 1), col = c0 + (s & 1);
+    const float2 ab = unpack_bf2(*reinterpret_cast<const uint32_t*>(
+        emb + ((long)row * gw + col) * C + 2 * q));
+    const float a = gelu_erf(ab.x), b = gelu_erf(ab.y);
+    const double2 r = rot[(long)(second ? row : col) * quarter + k];
+    o[s] = (float)((double)a * r.x - (double)b * r.y);
+    o[4 + s] = (float)((double)a * r.y + (double)b * r.x);
+  }
+  *reinterpret_cast<uint4*>(merged + t * (long)C * 4 + 8 * q) =
+      make_uint4(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]), pack_bf2(o[4], o[5]),
+                 pack_bf2(o[6], o[7]));
+}
+
+// PixelShuffle(2) channel-last, 8 output channels per thread: reads the 32
+// input channels 4c0 .. 4c0 + 31 of one pixel (64 bytes) and writes 8
+// channels to each of its 2 x 2 output pixels (16 bytes each); GELU optional.
+__global__ void ps2_hwc_kernel(const bf16* in, bf16* out, int H, int W, int Cin, int gelu)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int Co = Cin / 4, g = Co / 8;
+  if (i >= (long)H * W * g) return;
+  const long pix = i / g;
+  const int c0 = (int)(i % g) * 8;
+  const uint4* src = reinterpret_cast<const uint4*>(in + pix * Cin + 4 * c0);
+  float v[32];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint4 u = src[k];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf2(w[j]);
+      v[8 * k + 2 * j] = gelu ? gelu_erf(f.x) : f.x;
+      v[8 * k + 2 * j + 1] = gelu ? gelu_erf(f.y) : f.y;
+    }
+  }
+  const int y = (int)(pix / W), x = (int)(pix % W);
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {   // input channel 4c + s -> output pixel (2y + s/2, 2x + s%2)
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = pack_bf2(v[4 * (2 * j) + s], v[4 * (2 * j + 1) + s]);
+    *reinterpret_cast<uint4*>(out + ((long)(2 * y + (s >> 1)) * (2 * W) + 2 * x + (s & 1)) * Co +
+                              c0) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// PixelShuffle(8) to the f32 image, one thread per (input pixel, output row
+// ii): reads channels c 64 + 8 ii .. + 8 for c < 3 and writes the 8 output
+// pixels x 3 channels of that row (96 contiguous bytes).
+__global__ void ps8_row_kernel(const bf16* in, float* out, int H, int W)
+{
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)H * W * 8) return;
+  const long pix = i / 8;
+  const int ii = (int)(i % 8);
+  float v[3][8];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(in + pix * 192 + c * 64 + ii * 8);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf2(w[j]);
+      v[c][2 * j] = f.x;
+      v[c][2 * j + 1] = f.y;
+    }
+  }
+  const int y = (int)(pix / W), x = (int)(pix % W);
+  float4* dst = reinterpret_cast<float4*>(out + ((long)(8 * y + ii) * (8 * W) + 8 * x) * 3);
+#pragma unroll
+  for (int k = 0; k < 6; ++k) {
+    float e[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int idx = 4 * k + j;   // = 3 jj + c
+      e[j] = v[idx % 3][idx / 3];
+    }
+    dst[k] = make_float4(e[0], e[1], e[2], e[3]);
+  }
 }
 
 // [H][W][3] model space ([-1, 1]) -> [3][H][W] u8: clamp(x/2 + 1/2) * 255,
@@ -258,6 +409,8 @@ struct u15c_image {
   bf16* conv2_b = nullptr;   // [192]
   bf16* mlp[8] = {};         // tstep w0 b0 w2 b2, nscale w0 b0 w2 b2
   float* inv = nullptr;      // vision RoPE inverse frequencies [C/4]
+  double2* rot = nullptr;    // (cos, sin) per (position, frequency), rot_pos positions
+  int rot_pos = 0;
   float* tvec = nullptr;     // [dim + 2 LLM] sinusoid | hidden | row
   std::vector<void*> allocs;
   // grow-only scratch
@@ -289,6 +442,7 @@ struct u15c_image {
   }
   ~u15c_image()
   {
+    if (rot) cudaFree(rot);
     if (scratch) cudaFree(scratch);
     for (void* p : allocs) cudaFree(p);
   }
@@ -461,8 +615,12 @@ int u15c_image_patchify(u15c_stream stream, const float* img, void* px, int H, i
     return fail(U15C_EINVAL, "image_patchify: H and W must be positive multiples of the patch");
   if (u15::dev() == nullptr) return U15C_ECUDA;
   const long n = (long)H * W * 3;
-  patchify_cf_kernel<<<nblk(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      img, static_cast<bf16*>(px), H, W, patch);
+  if (patch == 16 && reinterpret_cast<uintptr_t>(img) % 16 == 0)
+    patchify16_kernel<<<nblk(n / 48, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        img, static_cast<bf16*>(px), H, W);
+  else
+    patchify_cf_kernel<<<nblk(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        img, static_cast<bf16*>(px), H, W, patch);
   return launched("image_patchify");
 }
 
@@ -488,8 +646,28 @@ int u15c_image_embed(u15c_image* im, u15c_stream stream, const void* px, int gri
   if ((rc = gemm(im, st, px, im->patch_w + (size_t)expert * C * pin, im->patch_b + expert * C, emb,
                  (int)n, pin, C)))
     return rc;
-  vision_post_kernel<<<nblk(n * C / 2, 256), 256, 0, st>>>(emb, merged, grid_h, grid_w, C, m,
-                                                            im->inv);
+  if (m == 2 && C % 16 == 0) {
+    // the (cos, sin) table, grown to the grid's largest position on demand
+    const int npos = std::max(grid_h, grid_w);
+    if (npos > im->rot_pos) {
+      if (im->rot) cudaFree(im->rot);
+      im->rot = nullptr;
+      im->rot_pos = 0;
+      if (cudaMalloc(&im->rot, (size_t)npos * (C / 4) * sizeof(double2)) != cudaSuccess)
+        return fail(U15C_ENOMEM, "image_embed: out of device memory for the rotation table");
+      vision_rot_kernel<<<nblk((long)npos * (C / 4), 256), 256, 0, st>>>(im->inv, C / 4, npos,
+                                                                         im->rot);
+      // once per growth: later calls may come on other streams
+      if (cudaStreamSynchronize(st) != cudaSuccess)
+        return cuda_fail(cudaGetLastError(), "image_embed: rotation table");
+      im->rot_pos = npos;
+    }
+    vision_post_m2_kernel<<<nblk(n / 4 * C / 2, 256), 256, 0, st>>>(emb, merged, grid_h, grid_w,
+                                                                    C, im->rot);
+  } else {
+    vision_post_kernel<<<nblk(n * C / 2, 256), 256, 0, st>>>(emb, merged, grid_h, grid_w, C, m,
+                                                              im->inv);
+  }
   if ((rc = launched("image_embed: vision_post"))) return rc;
   const int rows = (int)(n / (m * m)), K = C * m * m;
   return gemm(im, st, merged, im->dense_w + (size_t)expert * L * K, im->dense_b + expert * L, out,
@@ -548,18 +726,28 @@ int u15c_image_decode(u15c_image* im, u15c_stream stream, const void* hidden, in
   bf16* col = a + std::max(a_el, c_el);
   bf16* b = col + col_el;                               // a conv's output
   // PS(2): [th][tw][L] -> [2th][2tw][L/4]; conv1 (+ bias) -> [2th][2tw][hid]
-  ps_hwc_kernel<<<nblk((long)th * tw * L, 256), 256, 0, st>>>(static_cast<const bf16*>(hidden), a,
-                                                              th, tw, L, 2, 0);
+  if (L % 32 == 0)
+    ps2_hwc_kernel<<<nblk((long)th * tw * (L / 32), 256), 256, 0, st>>>(
+        static_cast<const bf16*>(hidden), a, th, tw, L, 0);
+  else
+    ps_hwc_kernel<<<nblk((long)th * tw * L, 256), 256, 0, st>>>(static_cast<const bf16*>(hidden),
+                                                                a, th, tw, L, 2, 0);
   im2col3x3_kernel<<<nblk(p1 * 9 * (c1 / 8), 256), 256, 0, st>>>(a, col, 2 * th, 2 * tw, c1);
   if ((rc = launched("image_decode: conv1 gather"))) return rc;
   if ((rc = gemm(im, st, col, im->conv1_w, im->conv1_b, b, (int)p1, 9 * c1, hid))) return rc;
   // GELU + PS(2): [2th][2tw][hid] -> [4th][4tw][hid/4]; conv2 (+ bias) -> [4th][4tw][192]
-  ps_hwc_kernel<<<nblk(p1 * hid, 256), 256, 0, st>>>(b, a, 2 * th, 2 * tw, hid, 2, 1);
+  if (hid % 32 == 0)
+    ps2_hwc_kernel<<<nblk(p1 * (hid / 32), 256), 256, 0, st>>>(b, a, 2 * th, 2 * tw, hid, 1);
+  else
+    ps_hwc_kernel<<<nblk(p1 * hid, 256), 256, 0, st>>>(b, a, 2 * th, 2 * tw, hid, 2, 1);
   im2col3x3_kernel<<<nblk(p2 * 9 * (c2 / 8), 256), 256, 0, st>>>(a, col, 4 * th, 4 * tw, c2);
   if ((rc = launched("image_decode: conv2 gather"))) return rc;
   if ((rc = gemm(im, st, col, im->conv2_w, im->conv2_b, b, (int)p2, 9 * c2, 192))) return rc;
   // PS(8) -> [32th][32tw][3]
-  ps8_out_kernel<<<nblk(p2 * 192, 256), 256, 0, st>>>(b, out_px, 4 * th, 4 * tw);
+  if (reinterpret_cast<uintptr_t>(out_px) % 16 == 0)
+    ps8_row_kernel<<<nblk(p2 * 8, 256), 256, 0, st>>>(b, out_px, 4 * th, 4 * tw);
+  else
+    ps8_out_kernel<<<nblk(p2 * 192, 256), 256, 0, st>>>(b, out_px, 4 * th, 4 * tw);
   return launched("image_decode: pixel shuffle");
 }
 
