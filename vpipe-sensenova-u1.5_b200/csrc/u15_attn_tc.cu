@@ -207,6 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the set-up above overlaps the previous kernel; global memory waits for it
+  griddep_launch();
+  griddep_wait();
   if (w < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
     if (w == 0) {
@@ -533,8 +536,18 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   const int which = !sage ? 0 : (emu ? 1 : 2);
   cudaError_t e = cudaSuccess;
   if (smem_attr_once(k, kSmem, set_attr[which])) {
-    k<<<grid, kThreads, kSmem, st>>>(mq, mk, mv, p);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, k, mq, mk, mv, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
   } else {
     e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaErrorInvalidValue;

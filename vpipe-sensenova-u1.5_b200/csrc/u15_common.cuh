@@ -99,6 +99,20 @@ __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
 
 // ---------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with the PDL attribute
+// may be scheduled while the previous kernel of its stream still runs (on
+// SMs that kernel has freed); griddep_wait blocks until that kernel has
+// completed and its writes are visible, and is a no-op for a kernel launched
+// without the attribute. griddep_launch lets the next kernel be scheduled
+// once every CTA of this one has issued it (or exited).
+// ---------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch()
+{
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)

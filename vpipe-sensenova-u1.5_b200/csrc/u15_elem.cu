@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kRmsThreads)
     rms_norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                     __nv_bfloat16* __restrict__ y, int rows, int dim, float eps, SegInfo seg)
 {
+  griddep_launch();   // the next (tensor-core) kernel may start its set-up
   const int row = blockIdx.x;
   if (row >= rows) return;
   const __nv_bfloat16* xr = x + (long)row * dim;
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(kRmsThreads)
                           int8_t* __restrict__ q, float* __restrict__ scale, int rows, int dim,
                           float eps, SegInfo seg)
 {
+  griddep_launch();   // the next (tensor-core) kernel may start its set-up
   const int row = blockIdx.x;
   if (row >= rows) return;
   const __nv_bfloat16* xr = x + (long)row * dim;
@@ -373,6 +375,7 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
                     __nv_bfloat16* __restrict__ q_out, KvView kv, int T, int nh, int nkv,
                     int kv_off, float eps, SegInfo seg)
 {
+  griddep_launch();   // the next (tensor-core) kernel may start its set-up
   const int heads = nh + 2 * nkv;
   const int l = lane_id(), w = warp_id();
   if ((int)blockIdx.x < T) {
@@ -620,6 +623,7 @@ __global__ void __launch_bounds__(256)
     quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ q,
                       float* __restrict__ scale, int cols)
 {
+  griddep_launch();   // the next (tensor-core) kernel may start its set-up
   constexpr int kQuantPer = PER > 0 ? PER : 8;
   const long row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * cols;

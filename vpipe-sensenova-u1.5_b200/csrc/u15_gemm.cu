@@ -458,6 +458,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();   // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the set-up above overlaps the previous kernel; nothing in global memory
+  // is touched before it has completed
+  griddep_launch();
+  griddep_wait();
 
   const int n_tiles = launch_tiles(p);
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
@@ -703,10 +707,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n0 = nb * 256 + (half ? 128 * ti.half : 0);
         const int nchunk = half ? 4 : 8;
         __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.y) + (long)row * p.ldy;
+        // the residual row is fetched one 32-column chunk ahead, so its load
+        // latency overlaps the previous chunk (whole, aligned chunks only)
+        const __nv_bfloat16* rrow = EPI == kEpiResid ? p.resid + (long)row * p.ldr : nullptr;
+        const bool pre = EPI == kEpiResid && row_ok && n0 + nchunk * 32 <= p.N &&
+                         (reinterpret_cast<uintptr_t>(rrow + n0) & 15) == 0 && (p.ldr & 7) == 0;
+        uint4 rcur[4] = {}, rnext[4] = {};
+        if (pre) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) rcur[q] = reinterpret_cast<const uint4*>(rrow + n0)[q];
+        }
 #pragma unroll 1
         for (int c = 0; c < nchunk; ++c) {
           float v[32];
           const int col0 = n0 + c * 32;
+          if (pre && c + 1 < nchunk) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              rnext[q] = reinterpret_cast<const uint4*>(rrow + col0 + 32)[q];
+          }
           chunk_values<I8>(tb + c * 32, v, p, row, row_ok, col0, u.expert);
           if (!row_ok || col0 >= p.N) continue;
           if (p.bias != nullptr) {
@@ -717,7 +736,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if constexpr (EPI == kEpiResid) {
             float rr[32];
-            load_row32(p.resid + (long)row * p.ldr + col0, rr, col0, p.N);
+            if (pre) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float2 a = unpack_bf2(rcur[q].x), b = unpack_bf2(rcur[q].y),
+                             cc = unpack_bf2(rcur[q].z), d = unpack_bf2(rcur[q].w);
+                rr[q * 8 + 0] = a.x; rr[q * 8 + 1] = a.y; rr[q * 8 + 2] = b.x;
+                rr[q * 8 + 3] = b.y; rr[q * 8 + 4] = cc.x; rr[q * 8 + 5] = cc.y;
+                rr[q * 8 + 6] = d.x; rr[q * 8 + 7] = d.y;
+                rcur[q] = rnext[q];
+              }
+            } else {
+              load_row32(rrow + col0, rr, col0, p.N);
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = rr[i] + bfround(v[i]);
           }
@@ -890,6 +921,11 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   const int rest = tiles % pairs;
   p.n_full = (allow_split && rest > 0 && 2 * rest <= pairs && !no_split()) ? tiles - rest : tiles;
   cfg.gridDim = dim3(2 * pairs);
+  cudaLaunchAttribute attrs[2] = {attr[0], {}};
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, k, ma, mb, mbh, p) == cudaSuccess ? 0 : 2;
 }
 
@@ -905,6 +941,12 @@ bool use_pair(int M)
 }
 
 }  // namespace
+
+bool pdl_enabled()
+{
+  const char* e = std::getenv("U15_PDL");
+  return e == nullptr || *e != '0';
+}
 
 int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
 {

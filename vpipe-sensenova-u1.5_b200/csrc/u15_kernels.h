@@ -11,6 +11,10 @@
 
 namespace u15 {
 
+// Launch the layer's tensor-core kernels with programmatic dependent launch
+// (U15_PDL=0 turns it off; read per launch, for A/B checks).
+bool pdl_enabled();
+
 // Kernel attributes are per device: a process that drives several GPUs
 // (or that switches its current device between calls) must set a kernel's
 // dynamic shared-memory limit on each of them. `done` holds one bit per
