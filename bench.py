@@ -397,7 +397,11 @@ def run_ours(args, rank, world, local):
         if world == 1:
             del m, kv
         torch.cuda.empty_cache()
-        den = denoise_bench(args, rank, world, dist)
+        # the one-image tensor-parallel denoise uses the row-parallel reduction
+        # the layer measurement above found faster at this rank count
+        nccl_faster = tp is not None and (tp["ms_per_layer_nccl"] < tp["ms_per_layer_fused"] or
+                                          os.environ.get("U15_TP_NCCL") == "1")
+        den = denoise_bench(args, rank, world, dist, tp_nccl=nccl_faster)
     clk.__exit__(None, None, None)
 
     # ---- CPU baseline (rank 0, N=1 only): bounded sample, ~10-30 s ----
@@ -539,7 +543,7 @@ def image_bench(steps):
                       "embedder (25.8 + 137.4 GFLOP), decode = pixel head (309.2 + 58.0 GFLOP)"}
 
 
-def denoise_bench(args, rank, world, dist):
+def denoise_bench(args, rank, world, dist, tp_nccl=False):
     """Denoise steps/s at BASELINE config 5's geometry: 42 layers (random
     N(0, 0.02) weights, both experts), 4096 generation tokens (64x64 token
     grid, 2048x2048 px), three CFG forwards per step -- text-conditional
@@ -622,12 +626,17 @@ def denoise_bench(args, rank, world, dist):
         mt.bind_random(seed=77, std=0.02, norm_mean=1.0, norm_std=0.2)
         for e in range(2):
             mt.bind(0, e, "final_norm", torch.ones(H, device="cuda"))
-        mt.tp_connect(None, 3 * M_TOK)
+        if tp_nccl:
+            mt.set_allreduce(None, 3 * M_TOK)
+        else:
+            mt.tp_connect(None, 3 * M_TOK)
         s_tp = run(Generator(mt), specs_on(5), 0)
-        out["one_image_tensor_parallel"] = {"steps_per_s": 1.0 / s_tp, "s_per_step": s_tp,
-                                            "tp": world, "reduction": "fused, peer memory"}
+        out["one_image_tensor_parallel"] = {
+            "steps_per_s": 1.0 / s_tp, "s_per_step": s_tp, "tp": world,
+            "reduction": "NCCL all-reduce" if tp_nccl else "fused, peer memory"}
         torch.cuda.synchronize()
-        mt.tp_disconnect(None)
+        if not tp_nccl:
+            mt.tp_disconnect(None)
         mt.close()
         del mt
     else:
