@@ -591,10 +591,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (EPI == kEpiTpReduce) {
         // Row-parallel product over tensor-parallel ranks.
-        // 1) this rank's f32 partial -> the owner's inbox plane [rank]. A
-        //    warp's 32 rows x 32 columns of a chunk go through its 4 KB of
-        //    shared memory (XOR-swizzled rows) so that every global store
-        //    instruction writes 512 contiguous bytes over NVLink.
+        // 1) this rank's partial, rounded to bf16 (the exchange's dominant
+        //    bytes halved), -> the owner's inbox plane [rank]. A warp's 32
+        //    rows x 32 columns of a chunk go through its 4 KB of shared
+        //    memory (XOR-swizzled rows) so that every global store
+        //    instruction writes 256 contiguous bytes over NVLink.
         const TpPeers& tp = p.tp;
         const int owner = nb % tp.size;
         const int nbo = p.n_nblk / tp.size;
@@ -603,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* wsm = tp_stage + wq * 1024;   // [32 rows][32 floats]
         // chunk c of this warp's rows: plane + ((slot*2 + cta)*8 + c)*4096 + (32 wq)*32
         const long tile_off = (slot * 2 + rank) * 8 * 4096 + wq * 32 * 32;
-        float* mine = tp.inbox[owner] + (long)tp.rank * tp.plane + tile_off;
+        __nv_bfloat16* mine = tp.inbox[owner] + (long)tp.rank * tp.plane + tile_off;
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
           float v[32];
@@ -616,8 +617,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const int r = 4 * k + (lane >> 3), q4 = lane & 7;
-            *reinterpret_cast<float4*>(mine + c * 4096 + r * 32 + q4 * 4) =
-                *reinterpret_cast<const float4*>(wsm + r * 32 + ((q4 ^ (r & 7)) << 2));
+            const float4 f = *reinterpret_cast<const float4*>(wsm + r * 32 + ((q4 ^ (r & 7)) << 2));
+            *reinterpret_cast<uint2*>(mine + c * 4096 + r * 32 + q4 * 4) =
+                make_uint2(pack_bf2(f.x, f.y), pack_bf2(f.z, f.w));
           }
           __syncwarp();
         }
@@ -633,15 +635,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           continue;
         }
         // 2) owner: wait for the other ranks' partials of these rows, then
-        //    x = bf16(x + bf16(sum of the planes)) into every rank's x. Lanes
-        //    run along the columns: each plane read is 512 contiguous bytes,
-        //    each x store 64 bytes of a row.
+        //    x = bf16(x + bf16(f32 sum of the planes)) into every rank's x.
+        //    Lanes run along the columns: each plane read is 256 contiguous
+        //    bytes, each x store 64 bytes of a row.
         if (threadIdx.x == 64) {
           wait_counter_sys(arrive, (unsigned long long)(tp.size - 1), p.err, kDevWaitPeer);
           *arrive = 0ull;   // ready for the next pass: no rank adds to it before done below
         }
         named_bar_sync(1, 128);
-        const float* own = tp.inbox[tp.rank] + tile_off;
+        const __nv_bfloat16* own = tp.inbox[tp.rank] + tile_off;
         const int wrow0 = u.m0 + 128 * (int)rank + wq * 32;   // this warp's first row
         const int q4 = lane & 7;
         // two chunks per pass: 16 independent loads per plane in flight
@@ -654,19 +656,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) acc4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 1
           for (int q = 0; q < tp.size; ++q) {
-            const float* base = own + q * tp.plane + c * 4096;
-            float4 f[16];
+            const __nv_bfloat16* base = own + q * tp.plane + c * 4096;
+            uint2 f[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int r = 4 * (i & 7) + (lane >> 3);
-              f[i] = __ldcg(reinterpret_cast<const float4*>(base + (i >> 3) * 4096 + r * 32 + q4 * 4));
+              f[i] = __ldcg(reinterpret_cast<const uint2*>(base + (i >> 3) * 4096 + r * 32 + q4 * 4));
             }
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              acc4[i].x += f[i].x;
-              acc4[i].y += f[i].y;
-              acc4[i].z += f[i].z;
-              acc4[i].w += f[i].w;
+              const float2 a = unpack_bf2(f[i].x), b = unpack_bf2(f[i].y);
+              acc4[i].x += a.x;
+              acc4[i].y += a.y;
+              acc4[i].z += b.x;
+              acc4[i].w += b.y;
             }
           }
           const __nv_bfloat16* xme = static_cast<const __nv_bfloat16*>(tp.x[tp.rank]);

@@ -9,6 +9,8 @@
 #include <atomic>
 #include <string>
 
+#include <cuda_bf16.h>
+
 namespace u15 {
 
 // Launch the layer's tensor-core kernels with programmatic dependent launch
@@ -44,19 +46,18 @@ enum Epilogue {
 // Tensor-parallel peers for the fused row-parallel GEMM (kEpiTpReduce).
 // Column block nb (256 columns) of the [M][N] product is owned by rank
 // nb % size; tile (unit u, nb) is the owner's slot u * (N / 256 / size) +
-// nb / size. Every rank stores its f32 partial of a tile into the owner's
-// inbox plane [rank], chunk-major (32 columns x 128 rows of one CTA
-// contiguous, so a warp writes 512 contiguous bytes per store), and counts
-// it on the owner's arrive[tile][cta]; the
-// owner adds the planes and the residual x, rounds as the residual epilogue
-// does, stores the bf16 result into every rank's x and counts it on every
-// rank's done.
+// nb / size. Every rank stores its partial of a tile, rounded to bf16, into
+// the owner's inbox plane [rank], chunk-major (32 columns x 128 rows of one
+// CTA contiguous, so a warp writes 256 contiguous bytes per store), and
+// counts it on the owner's arrive[tile][cta]; the owner sums the planes in
+// f32, adds the residual x, rounds as the residual epilogue does, stores the
+// bf16 result into every rank's x and counts it on every rank's done.
 constexpr int kMaxTp = 8;
 struct TpPeers {
   int rank = 0, size = 1;
   long rows = 0;                              // rows of x (the largest pass)
-  long plane = 0;                             // floats of one inbox plane
-  float* inbox[kMaxTp] = {};                  // owner q: [size planes][slot][cta 2][chunk 8][128][32] f32
+  long plane = 0;                             // elements of one inbox plane
+  __nv_bfloat16* inbox[kMaxTp] = {};          // owner q: [size planes][slot][cta 2][chunk 8][128][32] bf16
   void* x[kMaxTp] = {};                       // rank q: residual stream [rows][N] bf16
   unsigned long long* arrive[kMaxTp] = {};    // owner q: [tiles][2] (reset by the owner)
   unsigned long long* done[kMaxTp] = {};      // rank q: cumulative count of finished tile halves

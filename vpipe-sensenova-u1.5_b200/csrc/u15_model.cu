@@ -587,14 +587,14 @@ int u15c_model_tp(const u15c_model* m, int* tp_rank, int* tp_size)
 }
 
 namespace {
-// the peer region of one rank: [inbox: P planes of f32 tile slots | x bf16
+// the peer region of one rank: [inbox: P planes of bf16 tile slots | x bf16
 // rows x H | arrive u64 [tiles][2] | done u64], sections 256-byte aligned.
 // A pass of `rows` tokens has at most rows/256 + 8 row units (one more per
 // segment boundary) and H/256 column blocks, P-th of them owned here; a
-// slot holds one 256 x 256 f32 tile (2 CTAs x 8 chunks x 128 x 32).
+// slot holds one 256 x 256 tile of partials (2 CTAs x 8 chunks x 128 x 32).
 struct TpLayout {
   size_t inbox, x, arrive, done, total;
-  long plane;   // floats
+  long plane;   // elements
   TpLayout(long rows, long H, int P)
   {
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
@@ -602,7 +602,7 @@ struct TpLayout {
     const long tiles = units * (H / 256);
     plane = units * (H / 256 / P) * 2 * 8 * 4096;
     inbox = 0;
-    x = up(inbox + (size_t)plane * P * 4);
+    x = up(inbox + (size_t)plane * P * 2);
     arrive = up(x + (size_t)rows * H * 2);
     done = up(arrive + (size_t)tiles * 2 * 8);
     total = up(done + 8);
@@ -693,7 +693,7 @@ int u15c_model_tp_import(u15c_model* m, const void* blobs)
   m->tpp.rows = m->tp_rows;
   for (int q = 0; q < P; ++q) {
     char* base = static_cast<char*>(m->tp_peer[q]);
-    m->tpp.inbox[q] = reinterpret_cast<float*>(base + lay.inbox);
+    m->tpp.inbox[q] = reinterpret_cast<__nv_bfloat16*>(base + lay.inbox);
     m->tpp.x[q] = base + lay.x;
     m->tpp.arrive[q] = reinterpret_cast<unsigned long long*>(base + lay.arrive);
     m->tpp.done[q] = reinterpret_cast<unsigned long long*>(base + lay.done);
