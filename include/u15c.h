@@ -446,9 +446,9 @@ typedef int (*u15c_allreduce_fn)(void* ctx, long count, u15c_stream stream);
 int u15c_model_set_allreduce(u15c_model* m, u15c_allreduce_fn fn, void* ctx, float* buf,
                              long buf_elems);
 /* The fused form: o_proj / down_proj and their all-reduce in ONE kernel over
- * NVLink peer memory (each rank's f32 partial tile goes to the tile's owner,
- * the owner adds the ranks' partials and the residual and stores the bf16
- * result into every rank's activations). Each rank exports a region sized
+ * NVLink peer memory (each rank's partial tile, rounded to bf16, goes to the
+ * tile's owner; the owner adds the ranks' partials in f32 and the residual
+ * and stores the bf16 result into every rank's activations). Each rank exports a region sized
  * for passes of up to max_tokens tokens and gets a U15C_TP_BLOB_BYTES blob
  * (a CUDA IPC handle and the GPU's UUID); the caller gathers the blobs of
  * all ranks in rank order (e.g. an all-gather) and imports them. Then every
