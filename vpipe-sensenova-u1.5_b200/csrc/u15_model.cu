@@ -157,6 +157,12 @@ struct u15c_model {
   // layer_forward_host's copy stream and its chunk events (made on first use)
   cudaStream_t copy_st = nullptr;
   cudaEvent_t copy_ev[2 * 4 + 1] = {};
+  // forward_many's branch attentions run on these beside the model's stream
+  // (made on first use), so one branch's last part-empty round of CTAs is
+  // filled by the next branch's
+  static constexpr int kSideStreams = 3;
+  cudaStream_t side_st[kSideStreams] = {};
+  cudaEvent_t side_ev[kSideStreams + 1] = {};   // [i]: side i done; [last]: inputs ready
   std::vector<void*> scratch_allocs;
 
   int qkv_n() const { return (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim; }
@@ -217,6 +223,10 @@ struct u15c_model {
     for (cudaEvent_t e : copy_ev)
       if (e) cudaEventDestroy(e);
     if (copy_st) cudaStreamDestroy(copy_st);
+    for (cudaEvent_t e : side_ev)
+      if (e) cudaEventDestroy(e);
+    for (cudaStream_t s : side_st)
+      if (s) cudaStreamDestroy(s);
     free_scratch();
     for (int q = 0; q < u15::kMaxTp; ++q)
       if (tp_peer[q] != nullptr && tp_peer[q] != tp_mem) cudaIpcCloseMemHandle(tp_peer[q]);
@@ -416,25 +426,57 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x_all, int M,
                    m->qkv + (long)r0 * m->qkv_n(), fuse_q)))
       return rc;
   }
-  for (const SlotRun& sl : slots) {
-    if (!(parts & kPartAttn)) break;
-    const u15::SegInfo& seg = seg_all;
-    const u15::KvView view = sl.kv->view(li);
-    const u15::SegInfo sseg = slice_seg(seg, sl.row0, sl.n);
-    bf16* qh = m->qh + (long)sl.row0 * m->qd();
-    bf16* out = m->attn + (long)sl.row0 * m->qd();
-    if (u15::launch_qkv_post(m->qkv + (long)sl.row0 * m->qkv_n(), L.norms,
-                             m->rcos + (long)sl.row0 * 128, m->rsin + (long)sl.row0 * 128, qh,
-                             view, sl.n, c.heads, c.kv_heads, sl.kv_off, (float)c.eps, sseg, st))
-      return fail(U15C_ECUDA, "qkv_post launch failed");
-    const bool sage = (flags & U15C_FWD_SAGE) != 0 && sl.attn == U15C_ATTN_BIDIRECTIONAL;
-    if (sl.attn == U15C_ATTN_BIDIRECTIONAL)
-      rc = u15::run_attention_tc(st, qh, view, sl.kv->pages, out, c.heads, c.kv_heads, sl.n,
-                                 sl.kv_len, sage ? m->sage_ws : nullptr);
-    else
-      rc = u15::run_attention(st, qh, view, out, c.heads, c.kv_heads, sl.n, sl.kv_len, sl.attn,
-                              sl.kv_off, sl.t_index, nullptr);
-    if (rc) return rc;
+  if (parts & kPartAttn) {
+    // q / K / V of every slot first; then the attentions. Two or more bf16
+    // bidirectional slots run their attentions on side streams beside `st`
+    // (forked after the qkv_post kernels, joined before o_proj), so the
+    // GPU schedules their CTAs as one pool.
+    int n_par = 0;
+    for (const SlotRun& sl : slots)
+      n_par += sl.attn == U15C_ATTN_BIDIRECTIONAL && !(flags & U15C_FWD_SAGE) ? 1 : 0;
+    const bool fork = n_par >= 2 && n_par <= u15c_model::kSideStreams;
+    if (fork && m->side_st[0] == nullptr) {
+      for (cudaStream_t& s : m->side_st)
+        if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+          return fail(U15C_ECUDA, "forward: attention side streams");
+      for (cudaEvent_t& e : m->side_ev)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+          return fail(U15C_ECUDA, "forward: attention side events");
+    }
+    for (const SlotRun& sl : slots) {
+      const u15::SegInfo sseg = slice_seg(seg_all, sl.row0, sl.n);
+      if (u15::launch_qkv_post(m->qkv + (long)sl.row0 * m->qkv_n(), L.norms,
+                               m->rcos + (long)sl.row0 * 128, m->rsin + (long)sl.row0 * 128,
+                               m->qh + (long)sl.row0 * m->qd(), sl.kv->view(li), sl.n, c.heads,
+                               c.kv_heads, sl.kv_off, (float)c.eps, sseg, st))
+        return fail(U15C_ECUDA, "qkv_post launch failed");
+    }
+    if (fork) cudaEventRecord(m->side_ev[u15c_model::kSideStreams], st);
+    int k_side = 0;
+    for (const SlotRun& sl : slots) {
+      const u15::KvView view = sl.kv->view(li);
+      bf16* qh = m->qh + (long)sl.row0 * m->qd();
+      bf16* out = m->attn + (long)sl.row0 * m->qd();
+      const bool sage = (flags & U15C_FWD_SAGE) != 0 && sl.attn == U15C_ATTN_BIDIRECTIONAL;
+      if (sl.attn == U15C_ATTN_BIDIRECTIONAL) {
+        cudaStream_t as = st;
+        if (fork) {
+          as = m->side_st[k_side];
+          cudaStreamWaitEvent(as, m->side_ev[u15c_model::kSideStreams], 0);
+        }
+        rc = u15::run_attention_tc(as, qh, view, sl.kv->pages, out, c.heads, c.kv_heads, sl.n,
+                                   sl.kv_len, sage ? m->sage_ws : nullptr);
+        if (!rc && fork) {
+          cudaEventRecord(m->side_ev[k_side], as);
+          cudaStreamWaitEvent(st, m->side_ev[k_side], 0);
+          ++k_side;
+        }
+      } else {
+        rc = u15::run_attention(st, qh, view, out, c.heads, c.kv_heads, sl.n, sl.kv_len, sl.attn,
+                                sl.kv_off, sl.t_index, nullptr);
+      }
+      if (rc) return rc;
+    }
   }
   if (!(parts & kPartPost)) return U15C_OK;
   if ((rc = row_parallel(m->attn + (long)r0 * m->qd(), m->qd(), L.o, L.o8, L.o_s))) return rc;
