@@ -60,33 +60,39 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8])
 constexpr int kRmsThreads = 256;
 constexpr int kRmsPer = 16;        // elements a thread keeps: 256 x 16 = 4096 columns
 
-// Symmetric int8 code of v at scale s: rn_even(v / s) clamped to +-127, with
+// Symmetric int8 codes of v at scale s: rn_even(v / s) clamped to +-127, with
 // the division's exact result. t = v * r (r = RN(1 / s)) is within 1.5 * 2^-23
 // relative of v / s, i.e. within 2.3e-5 for |v / s| <= 127, so rounding t to
 // the nearest integer (even on ties; the 1.5 * 2^23 add) gives the same code
 // as rounding the IEEE quotient unless t lies within that distance of a
-// half-integer; those rare values take the division itself.
-__device__ __forceinline__ uint32_t quant_code(float v, float s, float r)
+// half-integer; a group of 8 holding such a value takes the division itself.
+// |v| <= amax and s = RN(amax / 127) keep |t| <= 127 * (1 + 2^-23): the code
+// never leaves [-127, 127], so no clamp is needed (s = 0 gives r = 0).
+// The low byte of t + 1.5 * 2^23's bit pattern is the code's low byte.
+__device__ __forceinline__ uint32_t code_bits(float v, float r, bool& tie)
 {
   const float t = v * r;
   const float tm = t + 12582912.0f;
   const float d = t - (tm - 12582912.0f);
-  // |v| <= amax and s = RN(amax / 127) keep |t| <= 127 * (1 + 2^-23): the
-  // code never leaves [-127, 127], so no clamp is needed (s = 0 gives r = 0)
-  int k = __float_as_int(tm) - 0x4B400000;
-  if (fabsf(fabsf(d) - 0.5f) < 1e-4f) k = __float2int_rn(__fdiv_rn(v, s));
-  return (uint32_t)(k & 0xff);
+  tie |= fabsf(fabsf(d) - 0.5f) < 1e-4f;
+  return __float_as_uint(tm);
+}
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 __device__ __forceinline__ uint2 quant8(const float* v, float s, float r)
 {
-  uint32_t lo = 0, hi = 0;
+  bool tie = false;
+  uint32_t c[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    lo |= quant_code(v[i], s, r) << (8 * i);
-    hi |= quant_code(v[4 + i], s, r) << (8 * i);
+  for (int i = 0; i < 8; ++i) c[i] = code_bits(v[i], r, tie);
+  if (tie) {   // rare: the IEEE quotient of every value of the group
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = (uint32_t)__float2int_rn(__fdiv_rn(v[i], s));
   }
-  return make_uint2(lo, hi);
+  return make_uint2(pack_low_bytes(c[0], c[1], c[2], c[3]), pack_low_bytes(c[4], c[5], c[6], c[7]));
 }
 
 // block-wide sum / max over kRmsThreads threads; red[] holds 8 floats and is
@@ -182,6 +188,11 @@ __global__ void __launch_bounds__(kRmsThreads)
 // over the CTA, and the codes written directly: q = rn_even(y / (amax/127)).
 // Codes are bit-identical to rms_norm followed by quant_rows. dim <= 4096.
 constexpr int kRmsQuantPer = kRmsPer;
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8])
+{
+  float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
 __global__ void __launch_bounds__(kRmsThreads)
     rms_norm_quant_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                           int8_t* __restrict__ q, float* __restrict__ scale, int rows, int dim,
@@ -193,38 +204,50 @@ __global__ void __launch_bounds__(kRmsThreads)
   const __nv_bfloat16* xr = x + (long)row * dim;
   const __nv_bfloat16* wr = w + (long)expert_of(row, seg) * dim;
   __shared__ float red[kRmsThreads / 32];
-  float v[kRmsQuantPer], g[kRmsQuantPer];
+  constexpr int kW = kRmsQuantPer / 8;
+  uint4 xv[kW], gv[kW];
   float acc = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kRmsQuantPer / 8; ++k) {
+  for (int k = 0; k < kW; ++k) {
     const int c = (k * kRmsThreads + threadIdx.x) * 8;
-    float t[8] = {0, 0, 0, 0, 0, 0, 0, 0}, u[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    xv[k] = gv[k] = make_uint4(0, 0, 0, 0);
     if (c < dim) {
-      load8(xr + c, t);
-      load8(wr + c, u);
+      xv[k] = *reinterpret_cast<const uint4*>(xr + c);
+      gv[k] = *reinterpret_cast<const uint4*>(wr + c);
     }
+    float t[8];
+    unpack8(xv[k], t);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[k * 8 + i] = t[i];
-      g[k * 8 + i] = u[i];
-      acc += t[i] * t[i];
-    }
+    for (int i = 0; i < 8; ++i) acc += t[i] * t[i];
   }
   const float inv = rsqrtf(block_sum(acc, red) / (float)dim + eps);
+  // The normed row rounded to bf16 (the value the unfused path stores), kept
+  // packed. Rounding to bf16 is monotone, so the absmax of the rounded row is
+  // the rounded absmax of the f32 row.
   float m = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kRmsQuantPer; ++i) {
-    v[i] = bfround(v[i] * inv * g[i]);
-    m = fmaxf(m, fabsf(v[i]));
+  for (int k = 0; k < kW; ++k) {
+    float t[8], u[8];
+    unpack8(xv[k], t);
+    unpack8(gv[k], u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      t[i] = t[i] * inv * u[i];
+      m = fmaxf(m, fabsf(t[i]));
+    }
+    xv[k] = make_uint4(pack_bf2(t[0], t[1]), pack_bf2(t[2], t[3]), pack_bf2(t[4], t[5]),
+                       pack_bf2(t[6], t[7]));
   }
-  const float s = __fdiv_rn(block_max(m, red), 127.0f);
+  const float s = __fdiv_rn(bfround(block_max(m, red)), 127.0f);
   const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
   if (threadIdx.x == 0) scale[row] = s;
 #pragma unroll
-  for (int k = 0; k < kRmsQuantPer / 8; ++k) {
+  for (int k = 0; k < kW; ++k) {
     const int c = (k * kRmsThreads + threadIdx.x) * 8;
     if (c >= dim) continue;
-    *reinterpret_cast<uint2*>(q + (long)row * dim + c) = quant8(&v[k * 8], s, r);
+    float t[8];
+    unpack8(xv[k], t);
+    *reinterpret_cast<uint2*>(q + (long)row * dim + c) = quant8(t, s, r);
   }
 }
 
@@ -629,24 +652,30 @@ __global__ void __launch_bounds__(256)
   const __nv_bfloat16* xr = x + row * cols;
   __shared__ float red[8];
   if (PER > 0) {
-    float v[kQuantPer];
-    float m = 0.0f;
+    // the row stays packed; its absmax is taken on bf16 pairs (exact)
+    uint4 raw[kQuantPer / 8];
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
 #pragma unroll
     for (int k = 0; k < kQuantPer / 8; ++k) {
       const int c = (k * 256 + threadIdx.x) * 8;
-      if (c < cols) {
-        load8(xr + c, *reinterpret_cast<float(*)[8]>(&v[k * 8]));
+      raw[k] = make_uint4(0, 0, 0, 0);
+      if (c < cols) raw[k] = *reinterpret_cast<const uint4*>(xr + c);
+      const uint32_t w4[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[k * 8 + i]));
-      }
+      for (int i = 0; i < 4; ++i)
+        m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w4[i])));
     }
-    const float s = __fdiv_rn(block_max(m, red), 127.0f);
+    const float2 mf = __bfloat1622float2(m2);
+    const float s = __fdiv_rn(block_max(fmaxf(mf.x, mf.y), red), 127.0f);
     const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
     if (threadIdx.x == 0) scale[row] = s;
 #pragma unroll
     for (int k = 0; k < kQuantPer / 8; ++k) {
       const int c = (k * 256 + threadIdx.x) * 8;
-      if (c < cols) *reinterpret_cast<uint2*>(q + row * cols + c) = quant8(&v[k * 8], s, r);
+      if (c >= cols) continue;
+      float t[8];
+      unpack8(raw[k], t);
+      *reinterpret_cast<uint2*>(q + row * cols + c) = quant8(t, s, r);
     }
     return;
   }
