@@ -179,6 +179,25 @@ def test_quant_rows_ties_bit_exact(ops, cols):
     assert np.array_equal(host(q), rq)
 
 
+@pytest.mark.parametrize("cols", [4096, 12288, 16384])
+def test_quant_rows_tiny_scales_bit_exact(ops, cols):
+    """Rows whose scale is subnormal (amax below 127 * 2^-126, down to bf16
+    subnormals), rows at that edge, and an all-zero row: the device takes the
+    clamped division for the subnormal scales and must match the oracle."""
+    rng = np.random.default_rng(6)
+    rows = []
+    for amax in (1.6e-36, 1.5e-36, 1.4e-36, 1e-37, 1e-38, 3e-39, 1e-40, 0.0, 1.0):
+        v = bf16_round(rng.uniform(-1, 1, cols).astype(np.float32) * np.float32(amax))
+        if amax:
+            v[7] = bf16_round(np.array([amax], np.float32))[0]
+        rows.append(v)
+    x = np.stack(rows).astype(np.float32)
+    q, s = quantised(ops, x)
+    rq, rs = O.quant_rows_i8(x)
+    assert np.array_equal(host(s), rs)
+    assert np.array_equal(host(q), rq)
+
+
 @pytest.mark.parametrize("M,K,N", [(128, 128, 256), (77, 4096, 1000), (256, 12288, 512)])
 def test_linear_i8_bit_exact(ops, M, K, N):
     x = bf16_round(randn((M, K), 20))

@@ -1,10 +1,13 @@
-"""The int8 row quantizers' fast path, restated in float32 numpy: the code of
-v at scale s is rn_even(v / s); the kernels form t = RN(v * RN(1 / s)), round
-it to the nearest integer (ties to even) and fall back to the division only
-when t lies within 1e-4 of a half-integer. Here every rounding step is the
-same IEEE float32 step the device takes, over millions of bf16 values and
-scales, ties and near-ties included: the fast path must give the division
-rule's codes everywhere (the device itself is checked against the oracle in
+"""The int8 quantizers' fast path, restated in numpy: the code of v at scale
+s is rn_even(v / s) clamped to +-127; the kernels round the exact product
+p = v * RN(1 / s) to the nearest integer k (ties to even; one fma with
+1.5 * 2^23), form d = p - k rounded once to float32 (a second fma), and fall
+back to the clamped division for a group of 8 holding a value with
+|d| > 0.4999, or for every value when the scale is subnormal (1 / s > 2^126).
+p is exact in float64 (24 x 24 significant bits), so np.rint(p) and
+float32(p - k) are the fma results. Over millions of bf16 values and scales,
+ties and near-ties included, the fast path must give the division rule's codes
+everywhere (the device itself is checked against the oracle in
 tests/test_gpu_gemm.py)."""
 import numpy as np
 
@@ -15,18 +18,26 @@ def _bf16(a):
 
 
 def _codes_div(v, s):
-    return np.clip(np.rint((v / s).astype(np.float32)), -127, 127).astype(np.int32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        t = np.where(s > 0, (v / s).astype(np.float32), np.float32(0.0))
+    return np.clip(np.rint(t), -127, 127).astype(np.int32)
 
 
 def _codes_fast(v, s):
-    r = (np.float32(1.0) / s).astype(np.float32)
-    t = (v * r).astype(np.float32)
-    k = np.rint(t).astype(np.int32)          # numpy rounds half to even, as the device add does
-    d = (t - np.rint(t)).astype(np.float32)
-    near = np.abs(np.abs(d) - np.float32(0.5)) < np.float32(1e-4)
+    v = np.asarray(v, np.float32)
     sb = np.broadcast_to(np.asarray(s, np.float32), v.shape)
-    k[near] = _codes_div(v[near], sb[near])
-    return np.clip(k, -127, 127)
+    with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
+        r = np.where(sb > 0, np.float32(1.0) / sb, np.float32(0.0)).astype(np.float32)
+        p = v.astype(np.float64) * r.astype(np.float64)
+        k = np.rint(p)
+        d = (p - k).astype(np.float32)
+    tie = (np.abs(d) > np.float32(0.4999)) | (r > np.float32(2.0 ** 126))
+    g = tie.reshape(v.shape[:-1] + (-1, 8)).any(axis=-1)      # whole groups of 8
+    tie = np.repeat(g, 8, axis=-1).reshape(v.shape)
+    codes = np.zeros(v.shape, np.int32)
+    codes[~tie] = k[~tie].astype(np.int32)
+    codes[tie] = _codes_div(v[tie], sb[tie])
+    return codes
 
 
 def test_random_rows():
@@ -49,3 +60,19 @@ def test_ties_and_near_ties():
             bits = (v.view(np.uint32) >> 16).astype(np.int64) + d
             w = np.clip((bits.astype(np.uint32) << 16).view(np.float32), -a, a)
             assert np.array_equal(_codes_fast(w, s), _codes_div(w, s))
+
+
+def test_tiny_and_zero_scales():
+    """amax around 127 * 2^-126, where the scale turns subnormal, and below,
+    down to bf16 subnormals, plus an all-zero row."""
+    rng = np.random.default_rng(2)
+    rows = []
+    for amax in (1.6e-36, 1.5e-36, 1.4e-36, 1e-37, 1e-38, 3e-39, 1e-40, 0.0):
+        v = _bf16(rng.uniform(-1, 1, 4096).astype(np.float32) * np.float32(amax))
+        if amax:
+            v[7] = _bf16(np.float32(amax))
+        rows.append(v)
+    x = np.stack(rows)
+    amax = np.abs(x).max(axis=1, keepdims=True)
+    s = (amax / np.float32(127.0)).astype(np.float32)
+    assert np.array_equal(_codes_fast(x, s), _codes_div(x, s))

@@ -409,16 +409,11 @@ __device__ __forceinline__ float block_absmax(float m, float* red)
 __device__ __forceinline__ void store_codes(const float (&v)[4][8], float s, bool (&valid)[4],
                                             int8_t* out, long row0, int c8)
 {
+  const float r = quant_recip(s);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     if (!valid[i]) continue;
-    uint32_t w[2] = {0u, 0u};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int q = s > 0.0f ? max(-127, min(127, __float2int_rn(__fdiv_rn(v[i][k], s)))) : 0;
-      w[k >> 2] |= (uint32_t)(q & 0xff) << (8 * (k & 3));
-    }
-    *reinterpret_cast<uint2*>(out + (row0 + 16 * i) * 128 + c8 * 8) = make_uint2(w[0], w[1]);
+    *reinterpret_cast<uint2*>(out + (row0 + 16 * i) * 128 + c8 * 8) = quant8(v[i], s, r);
   }
 }
 

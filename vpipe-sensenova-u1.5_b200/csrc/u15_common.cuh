@@ -56,6 +56,51 @@ __device__ __forceinline__ float2 unpack_bf2(uint32_t v)
   return __bfloat1622float2(h);
 }
 
+// Symmetric int8 codes of v at scale s = RN(amax / 127): rn_even(v / s)
+// clamped to +-127, equal to the IEEE division rule's codes bit for bit.
+// With r = RN(1 / s) (quant_recip), the exact product p = v * r and the exact
+// quotient v / s differ by at most |v / s| * 2^-24 <= 7.6e-6, and the IEEE
+// quotient by as much again, so p rounds to the same integer as the quotient
+// unless p lies within 1.6e-5 of a half-integer. tm = fma(v, r, 1.5 * 2^23)
+// rounds p to the nearest integer k (even on ties), and
+// d = fma(v, r, 1.5 * 2^23 - tm) is p - k rounded once (|d| <= 0.5), so
+// |d| > 0.4999 marks the values within 1e-4 of a half-integer; a group of 8
+// holding one takes the division itself. For a normal s, |v| <= amax keeps
+// |p| <= 127 * (1 + 2^-23), so the fast code never leaves [-127, 127]; a
+// subnormal s (amax < 127 * 2^-126) can be rounded far enough that v / s
+// passes 127, so its rows take the clamped division for every value (their
+// r = 1 / s is above 2^126). s = 0 (an all-zero row) has r = 0 and codes 0.
+// The low byte of tm's bit pattern is the code's low byte.
+__device__ __forceinline__ float quant_recip(float s) { return s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f; }
+
+__device__ __forceinline__ uint32_t code_bits(float v, float r, bool& tie)
+{
+  const float tm = __fmaf_rn(v, r, 12582912.0f);
+  const float d = __fmaf_rn(v, r, 12582912.0f - tm);
+  tie |= fabsf(d) > 0.4999f;
+  return __float_as_uint(tm);
+}
+
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// codes of v[0..8) as 8 bytes, v[0] lowest
+__device__ __forceinline__ uint2 quant8(const float* v, float s, float r)
+{
+  bool tie = r > 8.5070592e37f;   // 2^126: the scale is subnormal
+  uint32_t c[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = code_bits(v[i], r, tie);
+  if (tie) {   // rare: the IEEE quotient of every value of the group
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      c[i] = (uint32_t)max(-127, min(127, __float2int_rn(__fdiv_rn(v[i], s))));
+  }
+  return make_uint2(pack_low_bytes(c[0], c[1], c[2], c[3]), pack_low_bytes(c[4], c[5], c[6], c[7]));
+}
+
 // ---------------------------------------------------------------------
 // timers / smem addresses
 // ---------------------------------------------------------------------

@@ -60,41 +60,6 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8])
 constexpr int kRmsThreads = 256;
 constexpr int kRmsPer = 16;        // elements a thread keeps: 256 x 16 = 4096 columns
 
-// Symmetric int8 codes of v at scale s: rn_even(v / s) clamped to +-127, with
-// the division's exact result. t = v * r (r = RN(1 / s)) is within 1.5 * 2^-23
-// relative of v / s, i.e. within 2.3e-5 for |v / s| <= 127, so rounding t to
-// the nearest integer (even on ties; the 1.5 * 2^23 add) gives the same code
-// as rounding the IEEE quotient unless t lies within that distance of a
-// half-integer; a group of 8 holding such a value takes the division itself.
-// |v| <= amax and s = RN(amax / 127) keep |t| <= 127 * (1 + 2^-23): the code
-// never leaves [-127, 127], so no clamp is needed (s = 0 gives r = 0).
-// The low byte of t + 1.5 * 2^23's bit pattern is the code's low byte.
-__device__ __forceinline__ uint32_t code_bits(float v, float r, bool& tie)
-{
-  const float t = v * r;
-  const float tm = t + 12582912.0f;
-  const float d = t - (tm - 12582912.0f);
-  tie |= fabsf(fabsf(d) - 0.5f) < 1e-4f;
-  return __float_as_uint(tm);
-}
-__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d)
-{
-  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
-}
-
-__device__ __forceinline__ uint2 quant8(const float* v, float s, float r)
-{
-  bool tie = false;
-  uint32_t c[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = code_bits(v[i], r, tie);
-  if (tie) {   // rare: the IEEE quotient of every value of the group
-#pragma unroll
-    for (int i = 0; i < 8; ++i) c[i] = (uint32_t)__float2int_rn(__fdiv_rn(v[i], s));
-  }
-  return make_uint2(pack_low_bytes(c[0], c[1], c[2], c[3]), pack_low_bytes(c[4], c[5], c[6], c[7]));
-}
-
 // block-wide sum / max over kRmsThreads threads; red[] holds 8 floats and is
 // reusable after the call
 __device__ __forceinline__ float block_sum(float v, float* red)
@@ -239,7 +204,7 @@ __global__ void __launch_bounds__(kRmsThreads)
                        pack_bf2(t[6], t[7]));
   }
   const float s = __fdiv_rn(bfround(block_max(m, red)), 127.0f);
-  const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+  const float r = quant_recip(s);
   if (threadIdx.x == 0) scale[row] = s;
 #pragma unroll
   for (int k = 0; k < kW; ++k) {
@@ -667,7 +632,7 @@ __global__ void __launch_bounds__(256)
     }
     const float2 mf = __bfloat1622float2(m2);
     const float s = __fdiv_rn(block_max(fmaxf(mf.x, mf.y), red), 127.0f);
-    const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+    const float r = quant_recip(s);
     if (threadIdx.x == 0) scale[row] = s;
 #pragma unroll
     for (int k = 0; k < kQuantPer / 8; ++k) {
@@ -687,7 +652,7 @@ __global__ void __launch_bounds__(256)
     for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
   }
   const float s = __fdiv_rn(block_max(m, red), 127.0f);
-  const float r = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+  const float r = quant_recip(s);
   if (threadIdx.x == 0) scale[row] = s;
   for (int c = threadIdx.x * 8; c < cols; c += 256 * 8) {
     float v[8];
