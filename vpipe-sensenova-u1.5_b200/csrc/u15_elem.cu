@@ -340,6 +340,49 @@ __global__ void rope_tables_kernel(const int32_t* __restrict__ pt, const int32_t
   }
 }
 
+// The same tables when the sections are even and fill the 128 columns
+// (d_t + 2 d_h = 128): column c and c + width / 2 of a section share their
+// frequency, so a thread forms one angle of the 64 distinct ones per token,
+// takes its sine and cosine together and writes both columns.
+__global__ void rope_tables_pair_kernel(const int32_t* __restrict__ pt,
+                                        const int32_t* __restrict__ ph,
+                                        const int32_t* __restrict__ pw, int tokens, int d_t,
+                                        int d_h, double theta_t, double theta_hw,
+                                        float* __restrict__ cos_out, float* __restrict__ sin_out)
+{
+  __shared__ double inv_s[64];
+  __shared__ int col_s[64], half_s[64], sec_s[64];
+  if (threadIdx.x < 64) {
+    const int u = threadIdx.x, ht = d_t / 2, hh = d_h / 2;
+    int off, width, i, sec;
+    double theta;
+    if (u < ht) { off = 0; width = d_t; i = u; theta = theta_t; sec = 0; }
+    else if (u < ht + hh) { off = d_t; width = d_h; i = u - ht; theta = theta_hw; sec = 1; }
+    else { off = d_t + d_h; width = d_h; i = u - ht - hh; theta = theta_hw; sec = 2; }
+    inv_s[u] = 1.0 / pow(theta, (double)(2 * i) / (double)width);
+    col_s[u] = off + i;
+    half_s[u] = width / 2;
+    sec_s[u] = sec;
+  }
+  __syncthreads();
+  const int u = threadIdx.x & 63;
+  const int32_t* pos = sec_s[u] == 0 ? pt : (sec_s[u] == 1 ? ph : pw);
+  const double inv = inv_s[u];
+  const int c0 = col_s[u], c1 = c0 + half_s[u];
+  for (int r = threadIdx.x >> 6; r < kRopeTok; r += blockDim.x >> 6) {
+    const int t = blockIdx.x * kRopeTok + r;
+    if (t >= tokens) break;
+    const double ang = (double)pos[t] * inv;
+    double sv, cv;
+    sincos(ang, &sv, &cv);
+    const long row = (long)t * 128;
+    cos_out[row + c0] = (float)cv;
+    cos_out[row + c1] = (float)cv;
+    sin_out[row + c0] = (float)sv;
+    sin_out[row + c1] = (float)sv;
+  }
+}
+
 // ---------------------------------------------------------------------
 // Fused QKV post-processing of the token-major GEMM output
 // qkv [T][(NH + 2*KV) * 128], per (token, head) row:
@@ -725,8 +768,13 @@ int launch_rope_tables(const int32_t* pt, const int32_t* ph, const int32_t* pw, 
                        cudaStream_t st)
 {
   if (tokens <= 0) return 0;
-  rope_tables_kernel<<<(unsigned)((tokens + kRopeTok - 1) / kRopeTok), 256, 0, st>>>(
-      pt, ph, pw, tokens, d_t, d_h, theta_t, theta_hw, c, s);
+  const unsigned blocks = (unsigned)((tokens + kRopeTok - 1) / kRopeTok);
+  if (d_t > 0 && d_h >= 0 && d_t % 2 == 0 && d_h % 2 == 0 && d_t + 2 * d_h == 128)
+    rope_tables_pair_kernel<<<blocks, 256, 0, st>>>(pt, ph, pw, tokens, d_t, d_h, theta_t,
+                                                    theta_hw, c, s);
+  else
+    rope_tables_kernel<<<blocks, 256, 0, st>>>(pt, ph, pw, tokens, d_t, d_h, theta_t, theta_hw,
+                                               c, s);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
