@@ -588,7 +588,7 @@ def denoise_bench(args, rank, world, dist, tp_nccl=False):
                  ("uncond", pre(13, 0), False)]
         return [Branch(nm, x, t, h, w, block_causal=bc) for nm, (x, t, h, w), bc in specs]
 
-    def run(gen, branches, seed, int8=False):
+    def run(gen, branches, seed, int8=False, sage=False):
         evs = []
 
         def cb(step, img):
@@ -599,7 +599,7 @@ def denoise_bench(args, rank, world, dist, tp_nccl=False):
             dist.barrier()
         gen.generate(branches, 2048, 2048, steps=1 + args.denoise_steps, shift=3.0, cfg=4.0,
                      icfg=1.5, form=L.CFG_BOTH, i_img=1, i_unc=2, seed=seed, step_callback=cb,
-                     int8=int8)
+                     int8=int8, sage=sage)
         torch.cuda.synchronize()
         sps = evs[0].elapsed_time(evs[-1]) / 1e3 / args.denoise_steps
         if dist is not None:
@@ -616,8 +616,11 @@ def denoise_bench(args, rank, world, dist, tp_nccl=False):
     m.finalize()
     s_rep = run(Generator(m), specs_on(5 + rank), rank)
     s_rep8 = run(Generator(m), specs_on(5 + rank), rank, int8=True)
+    # the W8A8 twin with Sage int8 QK on the bidirectional denoise passes
+    s_rep8s = run(Generator(m), specs_on(5 + rank), rank, int8=True, sage=True)
     out = {"steps_per_s": world / s_rep, "s_per_step_per_replica": s_rep,
            "steps_per_s_i8": world / s_rep8, "s_per_step_per_replica_i8": s_rep8,
+           "steps_per_s_i8_sage": world / s_rep8s, "s_per_step_per_replica_i8_sage": s_rep8s,
            "timed_steps": args.denoise_steps, "warmup_steps": 1,
            "config": "42 layers, 4096 gen tokens (BASELINE '1024^2' = 64x64 tokens = 2048^2 px),"
                      " 3 CFG forwards/step (prefix 320 / 8+1024 img block-causal / 13),"

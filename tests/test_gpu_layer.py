@@ -196,9 +196,11 @@ def test_stop_and_determinism(small):
     assert np.array_equal(outs[0], outs[1])
 
 
-def test_forward_many_equals_separate_passes(small):
+@pytest.mark.parametrize("int8,sage", [(False, False), (True, True)])
+def test_forward_many_equals_separate_passes(small, int8, sage):
     """Branches through the stack together (one GEMM over all branches' rows)
-    give bit-identical results to one pass per branch."""
+    give bit-identical results to one pass per branch, in bf16 and in W8A8
+    with Sage int8 QK (the W8A8 denoise configuration)."""
     m, _ = small
     T = 64
     pos = [dev_i32(p) for p in grid_positions(0, 8, 8, 5)]
@@ -220,13 +222,13 @@ def test_forward_many_equals_separate_passes(small):
     for x, kv, kp in zip(xs, caches(), pres):
         xd = dev_bf16(x)
         npre = kp.shape[1]
-        m.forward(xd, kv, npre, npre + T, *pos, segments=[(0, T, 1)])
+        m.forward(xd, kv, npre, npre + T, *pos, segments=[(0, T, 1)], int8=int8, sage=sage)
         sep.append(xd)
     kvs = caches()
     xb = dev_bf16(np.concatenate(xs))
     slots = [{"kv": kv, "kv_off": kp.shape[1], "kv_len": kp.shape[1] + T, "pos": pos}
              for kv, kp in zip(kvs, pres)]
-    m.forward_many(xb, T, slots)
+    m.forward_many(xb, T, slots, int8=int8, sage=sage)
     torch.cuda.synchronize()
     for i in range(3):
         assert np.array_equal(host(xb[i * T:(i + 1) * T]), host(sep[i]))
