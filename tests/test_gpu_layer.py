@@ -201,7 +201,7 @@ def test_forward_many_equals_separate_passes(small, int8, sage):
     """Branches through the stack together (one GEMM over all branches' rows)
     give bit-identical results to one pass per branch, in bf16 and in W8A8
     with Sage int8 QK (the W8A8 denoise configuration)."""
-    m, _ = small
+    m = build(SMALL, 1, int8=True)[0] if int8 else small[0]
     T = 64
     pos = [dev_i32(p) for p in grid_positions(0, 8, 8, 5)]
     rng = np.random.default_rng(13)
