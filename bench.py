@@ -48,7 +48,7 @@ GEMMS = {"qkv": (H, (NH + 2 * KV) * HD), "o": (NH * HD, H), "gate_up": (H, 2 * I
 PROJ_FLOP = sum(2.0 * M_TOK * k * n for k, n in GEMMS.values())      # 1.5806e12
 ATTN_FLOP = 4.0 * NH * M_TOK * TK * HD                                  # 2.964e11
 LAYER_FLOP = PROJ_FLOP + ATTN_FLOP
-PUBLISHED_MS = 148.0   # Apple M5, bf16 (README.md:112-114 of the reference)
+PUBLISHED_MS = 148.0   # the published figure: Apple M5, bf16 (README.md:112-114 of the reference)
 WORKLOAD = ("MoT layer @4096 tok: 512 und + 3584 gen routed, frozen 320-token prefix, "
             "bidirectional GQA 32/8x128 over 4416 keys (paged KV)")
 
