@@ -163,6 +163,10 @@ struct u15c_model {
   static constexpr int kSideStreams = 3;
   cudaStream_t side_st[kSideStreams] = {};
   cudaEvent_t side_ev[kSideStreams + 1] = {};   // [i]: side i done; [last]: inputs ready
+  // a Sage workspace per side stream, so that Sage slots can run side by side
+  // (grown on first use to the largest slot's size)
+  void* side_sage[kSideStreams] = {};
+  size_t side_sage_bytes = 0;
   std::vector<void*> scratch_allocs;
 
   int qkv_n() const { return (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim; }
@@ -178,6 +182,29 @@ struct u15c_model {
     return U15C_OK;
   }
 
+  void free_side_sage()
+  {
+    for (void*& p : side_sage) {
+      if (p) cudaFree(p);
+      p = nullptr;
+    }
+    side_sage_bytes = 0;
+  }
+
+  int ensure_side_sage(size_t bytes)
+  {
+    if (bytes <= side_sage_bytes) return U15C_OK;
+    free_side_sage();
+    for (void*& p : side_sage)
+      if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        free_side_sage();
+        return fail(U15C_ENOMEM, "out of device memory (Sage side workspaces, " +
+                                     std::to_string(bytes >> 20) + " MB each)");
+      }
+    side_sage_bytes = bytes;
+    return U15C_OK;
+  }
+
   void free_scratch()
   {
     for (void* p : scratch_allocs) cudaFree(p);
@@ -186,6 +213,7 @@ struct u15c_model {
     scratch_tk = 0;
     sage_ws = nullptr;
     sage_ws_bytes = 0;
+    free_side_sage();
   }
 
   int ensure_scratch(int n, int tk)
@@ -427,14 +455,22 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x_all, int M,
       return rc;
   }
   if (parts & kPartAttn) {
-    // q / K / V of every slot first; then the attentions. Two or more bf16
+    // q / K / V of every slot first; then the attentions. Two or more
     // bidirectional slots run their attentions on side streams beside `st`
     // (forked after the qkv_post kernels, joined before o_proj), so the
-    // GPU schedules their CTAs as one pool.
+    // GPU schedules their CTAs as one pool; with Sage each side stream has
+    // its own workspace.
     int n_par = 0;
+    size_t side_sage_need = 0;
     for (const SlotRun& sl : slots)
-      n_par += sl.attn == U15C_ATTN_BIDIRECTIONAL && !(flags & U15C_FWD_SAGE) ? 1 : 0;
+      if (sl.attn == U15C_ATTN_BIDIRECTIONAL) {
+        ++n_par;
+        if (flags & U15C_FWD_SAGE)
+          side_sage_need = std::max(side_sage_need,
+                                    u15::sage_bytes(c.heads, c.kv_heads, sl.n, sl.kv_len));
+      }
     const bool fork = n_par >= 2 && n_par <= u15c_model::kSideStreams;
+    if (fork && side_sage_need && (rc = m->ensure_side_sage(side_sage_need))) return rc;
     if (fork && m->side_st[0] == nullptr) {
       for (cudaStream_t& s : m->side_st)
         if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
@@ -464,8 +500,9 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x_all, int M,
           as = m->side_st[k_side];
           cudaStreamWaitEvent(as, m->side_ev[u15c_model::kSideStreams], 0);
         }
+        void* ws = !sage ? nullptr : fork ? m->side_sage[k_side] : m->sage_ws;
         rc = u15::run_attention_tc(as, qh, view, sl.kv->pages, out, c.heads, c.kv_heads, sl.n,
-                                   sl.kv_len, sage ? m->sage_ws : nullptr);
+                                   sl.kv_len, ws);
         if (!rc && fork) {
           cudaEventRecord(m->side_ev[k_side], as);
           cudaStreamWaitEvent(st, m->side_ev[k_side], 0);
