@@ -9,6 +9,8 @@
 #include "u15_common.cuh"
 #include "u15_kernels.h"
 
+#include <utility>
+
 #include <algorithm>
 
 namespace u15 {
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(kRmsThreads)
                     __nv_bfloat16* __restrict__ y, int rows, int dim, float eps, SegInfo seg)
 {
   griddep_launch();   // the next (tensor-core) kernel may start its set-up
+  griddep_wait();     // launched early (PDL): the previous kernel's writes first
   const int row = blockIdx.x;
   if (row >= rows) return;
   const __nv_bfloat16* xr = x + (long)row * dim;
@@ -173,6 +176,7 @@ __global__ void __launch_bounds__(kRmsThreads)
                           float eps, SegInfo seg)
 {
   griddep_launch();   // the next (tensor-core) kernel may start its set-up
+  griddep_wait();     // launched early (PDL): the previous kernel's writes first
   const int row = blockIdx.x;
   if (row >= rows) return;
   const __nv_bfloat16* xr = x + (long)row * dim;
@@ -315,6 +319,8 @@ __global__ void rope_tables_kernel(const int32_t* __restrict__ pt, const int32_t
                                    double theta_t, double theta_hw, float* __restrict__ cos_out,
                                    float* __restrict__ sin_out)
 {
+  griddep_launch();
+  griddep_wait();
   __shared__ double inv_s[128];
   if (threadIdx.x < 128) {
     const int c = threadIdx.x;
@@ -350,6 +356,8 @@ __global__ void rope_tables_pair_kernel(const int32_t* __restrict__ pt,
                                         int d_h, double theta_t, double theta_hw,
                                         float* __restrict__ cos_out, float* __restrict__ sin_out)
 {
+  griddep_launch();
+  griddep_wait();
   __shared__ double inv_s[64];
   __shared__ int col_s[64], half_s[64], sec_s[64];
   if (threadIdx.x < 64) {
@@ -416,6 +424,7 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
                     int kv_off, float eps, SegInfo seg)
 {
   griddep_launch();   // the next (tensor-core) kernel may start its set-up
+  griddep_wait();     // launched early (PDL): the previous kernel's writes first
   const int heads = nh + 2 * nkv;
   const int l = lane_id(), w = warp_id();
   if ((int)blockIdx.x < T) {
@@ -665,6 +674,7 @@ __global__ void __launch_bounds__(NT)
                       float* __restrict__ scale, int cols)
 {
   griddep_launch();   // the next (tensor-core) kernel may start its set-up
+  griddep_wait();     // launched early (PDL): the previous kernel's writes first
   constexpr int kQuantPer = PER > 0 ? PER : 8;
   const long row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * cols;
@@ -721,14 +731,36 @@ inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads
 // ---------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------
+// The layer's row kernels are launched with programmatic stream
+// serialisation (unless U15_PDL=0): their CTAs may be placed while the
+// previous kernel drains, and each waits (griddepcontrol.wait) before it
+// touches global memory.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st,
+                       Args&&... args)
+{
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
 int launch_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,
                     const SegInfo& seg, cudaStream_t st)
 {
   if (rows <= 0) return 0;
-  rms_norm_kernel<<<rows, kRmsThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
-                                                static_cast<const __nv_bfloat16*>(w),
-                                                static_cast<__nv_bfloat16*>(y), rows, dim, eps, seg);
-  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+  const cudaError_t e = launch_pdl(rms_norm_kernel, dim3(rows), dim3(kRmsThreads), st,
+                                   static_cast<const __nv_bfloat16*>(x),
+                                   static_cast<const __nv_bfloat16*>(w),
+                                   static_cast<__nv_bfloat16*>(y), rows, dim, eps, seg);
+  return e == cudaSuccess ? 0 : 2;
 }
 
 int launch_rms_norm_quant(const void* x, const void* w, int8_t* q, float* s, int rows, int dim,
@@ -736,10 +768,11 @@ int launch_rms_norm_quant(const void* x, const void* w, int8_t* q, float* s, int
 {
   if (rows <= 0) return 0;
   if (dim > kRmsThreads * kRmsPer || dim % 8) return 1;
-  rms_norm_quant_kernel<<<rows, kRmsThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
-                                                      static_cast<const __nv_bfloat16*>(w), q, s,
-                                                      rows, dim, eps, seg);
-  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+  const cudaError_t e = launch_pdl(rms_norm_quant_kernel, dim3(rows), dim3(kRmsThreads), st,
+                                   static_cast<const __nv_bfloat16*>(x),
+                                   static_cast<const __nv_bfloat16*>(w), q, s, rows, dim, eps,
+                                   seg);
+  return e == cudaSuccess ? 0 : 2;
 }
 
 int launch_split_qk_norm(void* x, const void* w_t, const void* w_hw, int heads, int tokens,
@@ -769,13 +802,13 @@ int launch_rope_tables(const int32_t* pt, const int32_t* ph, const int32_t* pw, 
 {
   if (tokens <= 0) return 0;
   const unsigned blocks = (unsigned)((tokens + kRopeTok - 1) / kRopeTok);
-  if (d_t > 0 && d_h >= 0 && d_t % 2 == 0 && d_h % 2 == 0 && d_t + 2 * d_h == 128)
-    rope_tables_pair_kernel<<<blocks, 256, 0, st>>>(pt, ph, pw, tokens, d_t, d_h, theta_t,
-                                                    theta_hw, c, s);
-  else
-    rope_tables_kernel<<<blocks, 256, 0, st>>>(pt, ph, pw, tokens, d_t, d_h, theta_t, theta_hw,
-                                               c, s);
-  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+  const cudaError_t e =
+      d_t > 0 && d_h >= 0 && d_t % 2 == 0 && d_h % 2 == 0 && d_t + 2 * d_h == 128
+          ? launch_pdl(rope_tables_pair_kernel, dim3(blocks), dim3(256), st, pt, ph, pw, tokens,
+                       d_t, d_h, theta_t, theta_hw, c, s)
+          : launch_pdl(rope_tables_kernel, dim3(blocks), dim3(256), st, pt, ph, pw, tokens, d_t,
+                       d_h, theta_t, theta_hw, c, s);
+  return e == cudaSuccess ? 0 : 2;
 }
 
 int launch_qkv_post(const void* qkv, const void* norms, const float* c, const float* s,
@@ -785,10 +818,11 @@ int launch_qkv_post(const void* qkv, const void* norms, const float* c, const fl
   if (T <= 0 || nh + 2 * nkv <= 0) return 0;
   // transposed-V windows: the 64-token pages the block [kv_off, kv_off + T) touches
   const long nwin = kv.v_t ? ((kv_off & 63) + T + 63) / 64 : 0;
-  qkv_post_kernel<<<(unsigned)(T + nwin * nkv), kQkvWarps * 32, 0, st>>>(
+  const cudaError_t e = launch_pdl(
+      qkv_post_kernel, dim3((unsigned)(T + nwin * nkv)), dim3(kQkvWarps * 32), st,
       static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(norms), c, s,
       static_cast<__nv_bfloat16*>(q_out), kv, T, nh, nkv, kv_off, eps, seg);
-  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+  return e == cudaSuccess ? 0 : 2;
 }
 
 int launch_transpose(const void* in, void* out, int T, int H, int D, bool to_head_major,
@@ -862,13 +896,15 @@ int launch_quant_rows(const void* x, int8_t* q, float* s, int rows, int cols, cu
 {
   if (rows <= 0) return 0;
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  cudaError_t e;
   if (cols <= kRmsThreads * kRmsPer)
-    quant_rows_kernel<kRmsThreads, kRmsPer><<<rows, kRmsThreads, 0, st>>>(xb, q, s, cols);
+    e = launch_pdl(quant_rows_kernel<kRmsThreads, kRmsPer>, dim3(rows), dim3(kRmsThreads), st,
+                   xb, q, s, cols);
   else if (cols <= 256 * 48)
-    quant_rows_kernel<256, 48><<<rows, 256, 0, st>>>(xb, q, s, cols);
+    e = launch_pdl(quant_rows_kernel<256, 48>, dim3(rows), dim3(256), st, xb, q, s, cols);
   else
-    quant_rows_kernel<256, 0><<<rows, 256, 0, st>>>(xb, q, s, cols);
-  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+    e = launch_pdl(quant_rows_kernel<256, 0>, dim3(rows), dim3(256), st, xb, q, s, cols);
+  return e == cudaSuccess ? 0 : 2;
 }
 
 }  // namespace u15
