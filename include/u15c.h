@@ -78,6 +78,22 @@ int u15c_device_status(int device, unsigned* code);
 /* cudaStreamSynchronize + the status word: U15C_EDEVICE if a watchdog fired. */
 int u15c_sync(u15c_stream stream);
 
+/* The bound of every device-side wait of `device`'s kernels, in ns (0: the
+ * default, 2 s). Waits that run out record a code in the status word and
+ * unwind instead of hanging. Set it between passes, with no kernel of this
+ * library in flight on the device. No reference counterpart: the reference's
+ * kernels do not wait on one another. */
+int u15c_set_wait_limit(int device, unsigned long long ns);
+
+/* One device thread waits (bounded by the wait limit) until *counter >=
+ * target with acquire semantics at system scope, so the stream's later work
+ * sees what the counter's writers stored before incrementing it; the gate
+ * the fused tensor-parallel reduction puts after each row-parallel product.
+ * On a wait that runs out the status word holds 0x106 and the stream moves
+ * on. counter: device or peer-mapped memory, 8-byte aligned. */
+int u15c_wait_counter(u15c_stream stream, const unsigned long long* counter,
+                      unsigned long long target);
+
 /* ------------------------------------------------------------------ */
 /* GEMMs                                                               */
 /* ------------------------------------------------------------------ */
@@ -215,10 +231,13 @@ int u15c_attention(u15c_stream stream, const void* q, const void* k, const void*
 /* The same over the model's paged cache layout: K pages
  * [n_pages][hkv][64][128], V pages TRANSPOSED [n_pages][hkv][128][64] (dims as
  * rows of 64 tokens, the operand layout of the tensor-core P.V), page table
- * device int32 (NULL = identity). mode U15C_ATTN_BIDIRECTIONAL runs the
- * tcgen05/TMEM flash kernel (Sage int8-QK when sage_ws is non-NULL); the
- * causal rules run the masked kernel. Replaces MetalOps::sdpa_steel for the
- * denoise pass (src/u15-metal-ops.cc:835-882). */
+ * device int32 (NULL = identity). Every rule runs the tcgen05/TMEM flash
+ * kernel: bidirectional (Sage int8-QK when sage_ws is non-NULL), causal and
+ * block-causal (fully masked key blocks skipped per 128-row query tile; a
+ * block-causal t_index that is not 16-byte aligned, or more than 32768 keys,
+ * runs on the mma.sync kernel instead). Replaces MetalOps::sdpa_steel for
+ * the denoise pass (src/u15-metal-ops.cc:835-882) and ::sdpa /
+ * ::sdpa_block_causal for the prefill (:648-677, 884-908). */
 int u15c_attention_paged(u15c_stream stream, const void* q, const void* k_pages,
                          const void* vt_pages, const int32_t* page_table, int n_pages, void* out,
                          int hq, int hkv, int tq, int tk, int head_dim, int mode, int q_offset,
@@ -283,6 +302,28 @@ int u15c_cfg_combine(u15c_stream stream, const float* v_cond, const float* v_unc
                      double icfg, int step, void* workspace);
 /* img += dt * v in fp64 (src/u15-generator.cc:701-705). */
 int u15c_euler(u15c_stream stream, float* img, const float* v, long n, double dt);
+
+/* The start image (Generator::generate, src/u15-generator.cc:394-417), on the
+ * host: out[i] = (float)(noise_scale * d(rng)) for i in [0, n) in order,
+ * rng = std::mt19937_64(seed), d = std::normal_distribution<float>(0, 1) --
+ * the reference's engine and distribution (the distribution's algorithm is
+ * the C++ library's: the same seed gives the reference's image wherever the
+ * standard library is the same; the init_noise file is the exact path
+ * across libraries). out: HOST float[n] ([H][W][3] channel-last). */
+int u15c_init_noise(uint64_t seed, double noise_scale, float* out, long n);
+
+/* GenConfig::init_noise_scale (src/u15-config.cc:106-122): the noise scale
+ * for an image of `image_tokens` tokens. mode (GenConfig::noise_scale_mode):
+ * U15C_NOISE_CONSTANT = min(noise_scale, max_value); U15C_NOISE_RESOLUTION
+ * ("resolution" / "dynamic") = min(sqrt(L / base) * noise_scale, max_value);
+ * U15C_NOISE_DYNAMIC_SQRT = min(sqrt(sqrt(L / base) * noise_scale), max_value);
+ * base = base_seq_len (64 when <= 0). The reference's defaults: RESOLUTION,
+ * noise_scale 1, max_value 16, base 64. Host arithmetic. */
+#define U15C_NOISE_CONSTANT 0
+#define U15C_NOISE_RESOLUTION 1
+#define U15C_NOISE_DYNAMIC_SQRT 2
+int u15c_init_noise_scale(int image_tokens, int mode, double noise_scale, double max_value,
+                          int base_seq_len, double* out);
 /* [H][W][3] f32 <-> [(H/32)*(W/32)][32*32*3] bf16 token rows, channel-last
  * packing (the reference's patchify_channel_last, src/u15-ref.cc). */
 int u15c_patchify(u15c_stream stream, const float* img, void* rows, int H, int W);
@@ -514,6 +555,13 @@ int u15c_kv_write(u15c_kv* kv, u15c_stream stream, int layer, int which_v, const
 
 #define U15C_FWD_INT8 1u /* W8A8 projections (i8_gemm) */
 #define U15C_FWD_SAGE 2u /* Sage int8-QK on the bidirectional pass */
+
+/* The Sage tier's `dense_layers` (vpipe::genai::sage::Config, set through
+ * MetalOps::set_sage, src/u15-metal-ops.cc:789-814, and honoured by
+ * sdpa_steel, :852-855): under U15C_FWD_SAGE, layers [0, n) keep the bf16
+ * attention and layers >= n take the int8-QK one. Default 0 (the
+ * reference's default, every layer Sage). */
+int u15c_model_set_sage_dense_layers(u15c_model* m, int n);
 
 /* One MoT layer for one branch: U15Backbone::layer_step_
  * (src/u15-backbone.cc:173-257), x [n][hidden] updated in place, tokens

@@ -31,8 +31,14 @@ _i8p = C.POINTER(C.c_int8)
 
 
 def build(ref: bool = False) -> None:
-    """Build the restatement (and, if asked and present, the reference)."""
-    target = ["all"] if ref else ["oracle"]
+    """Build the restatement (and, if asked and present, the reference: the
+    checkout named by U15_REFERENCE_DIR, else a `reference` directory beside
+    the repository)."""
+    target = ["oracle"]
+    if ref:
+        d = os.environ.get("U15_REFERENCE_DIR") or os.path.join(
+            os.path.dirname(os.path.dirname(HERE)), "reference")
+        target = ["all", f"REF={d}"]
     subprocess.run(["make", "-s", "-C", HERE] + target, check=True)
 
 
@@ -88,11 +94,20 @@ def lib():
                                     C.POINTER(_Expert), C.POINTER(_Dims), _i32p, _i32p,
                                     _i32p, C.c_long, _f32p, _f32p, C.c_int, _i32p, _f32p,
                                     _f32p, _f32p]
+        L.orc_mot_layer_ex.argtypes = [_f32p, C.c_long, C.c_int, _i32p, _i32p,
+                                       C.POINTER(_Expert), C.POINTER(_Dims), _i32p, _i32p,
+                                       _i32p, C.c_long, _f32p, _f32p, C.c_int, _i32p, C.c_int,
+                                       _f32p, _f32p, _f32p]
         L.orc_quant_rows_i8.argtypes = [_f32p, C.c_long, C.c_long, _i8p, _f32p]
         L.orc_gemm_i8.argtypes = [_i8p, _i8p, C.c_long, C.c_long, C.c_long, _i32p]
         L.orc_dequant_i8.argtypes = [_i32p, _f32p, _f32p, C.c_long, C.c_long, _f32p]
         L.orc_sage_attention.argtypes = [_f32p, _f32p, _f32p] + [C.c_long] * 8 + [_f32p]
         L.orc_time_schedule.argtypes = [C.c_int, C.c_double, _f32p]
+        L.orc_init_noise.argtypes = [C.c_uint64, C.c_double, _f32p, C.c_long]
+        L.orc_mt19937_64_nth.argtypes = [C.c_uint64, C.c_long]
+        L.orc_mt19937_64_nth.restype = C.c_uint64
+        L.orc_init_noise_scale.argtypes = [C.c_int, C.c_int, C.c_double, C.c_double, C.c_int]
+        L.orc_init_noise_scale.restype = C.c_double
         L.orc_velocity.argtypes = [_f32p, _f32p, C.c_long, C.c_double, _f32p]
         L.orc_optimized_scale.argtypes = [_f32p, _f32p, C.c_long]
         L.orc_optimized_scale.restype = C.c_double
@@ -191,8 +206,10 @@ def sage_attention(q, k, v, tk=None, bq=64, bk=64):
 
 
 def mot_layer(x, segments, experts, dims, pos_t, pos_h, pos_w, k_prefix=None,
-              v_prefix=None, mode=BIDIR, t_index=None):
+              v_prefix=None, mode=BIDIR, t_index=None, int8=False, sage=False):
     """The joint MoT layer. segments: list of (start, end, expert_id).
+    int8: every projection under the W8A8 rule; sage: the bidirectional
+    attention as Sage int8 QK (64-row / 32-key blocks).
     experts: list of two dicts keyed by EXPERT_KEYS (fp32 arrays).
     dims: dict(hidden, heads, kv_heads, head_dim, inter, eps, theta_t, theta_hw).
     Returns (out [T][H], k_new [hkv][T][hd], v_new [hkv][T][hd])."""
@@ -218,9 +235,10 @@ def mot_layer(x, segments, experts, dims, pos_t, pos_h, pos_w, k_prefix=None,
     hkv, hd = dims["kv_heads"], dims["head_dim"]
     kn = np.empty((hkv, T, hd), np.float32)
     vn = np.empty((hkv, T, hd), np.float32)
-    lib().orc_mot_layer(_fp(x), T, len(segments), _ip(off), _ip(ex), E, C.byref(D),
-                        _ip(pt), _ip(ph), _ip(pw), npre, _fp(kp), _fp(vp), mode,
-                        _ip(ti), _fp(out), _fp(kn), _fp(vn))
+    flags = (1 if int8 else 0) | (2 if sage else 0)
+    lib().orc_mot_layer_ex(_fp(x), T, len(segments), _ip(off), _ip(ex), E, C.byref(D),
+                           _ip(pt), _ip(ph), _ip(pw), npre, _fp(kp), _fp(vp), mode,
+                           _ip(ti), flags, _fp(out), _fp(kn), _fp(vn))
     return out, kn, vn
 
 
@@ -248,6 +266,25 @@ def dequant_i8(acc, s_tok, s_ch):
     y = np.empty((M, N), np.float32)
     lib().orc_dequant_i8(_ip(acc), _fp(_f32(s_tok)), _fp(_f32(s_ch)), M, N, _fp(y))
     return y
+
+
+def init_noise(seed, noise_scale, n):
+    """The render's start image, flat channel-last (src/u15-generator.cc:413-417)."""
+    out = np.empty(n, np.float32)
+    lib().orc_init_noise(seed, noise_scale, _fp(out), n)
+    return out
+
+
+def mt19937_64_nth(seed, nth):
+    return int(lib().orc_mt19937_64_nth(seed, nth))
+
+
+NOISE_CONSTANT, NOISE_RESOLUTION, NOISE_DYNAMIC_SQRT = 0, 1, 2
+
+
+def init_noise_scale(image_tokens, mode=NOISE_RESOLUTION, noise_scale=1.0, max_value=16.0,
+                     base=64):
+    return float(lib().orc_init_noise_scale(image_tokens, mode, noise_scale, max_value, base))
 
 
 def time_schedule(n, shift):

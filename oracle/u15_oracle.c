@@ -245,6 +245,46 @@ void orc_attention(const float* q, const float* k, const float* v, long hq,
  *
  * Outputs: out [tokens][hidden]; k_new/v_new (optional) [hkv][tokens][hd],
  * the block this layer appended to the cache. */
+/* Round to the nearest bf16 (ties to even), returned as float. */
+static float bf16_rne(float v)
+{
+  uint32_t u;
+  memcpy(&u, &v, sizeof u);
+  u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+  memcpy(&v, &u, sizeof v);
+  return v;
+}
+
+/* One projection of the layer: y[n][N] = x[n][K] w[N][K]^T, in fp32 with
+ * double accumulation (orc_linear), or under the W8A8 rule. The int8 tier
+ * quantizes the activation buffer the GEMM reads, which the reference keeps
+ * in bf16 (MetalOps::linear_mma_ hands its bf16 `x` to I8GemmContext::gemm,
+ * src/u15-metal-ops.cc:283-306), so the activations are rounded to bf16
+ * before the per-token codes are formed. The codes move with that rounding
+ * (a W8A8 layer computed from the f32 activations differs from this one by
+ * ~3e-2 of the layer's update at full width), so the rounding point is part
+ * of the rule. */
+static void layer_linear(const float* x, const float* w, long n, long K, long N,
+                         float* y, int w8a8)
+{
+  if (!w8a8) {
+    orc_linear(x, w, NULL, n, K, N, y);
+    return;
+  }
+  float* xb = malloc(sizeof(float) * n * K);
+  int8_t* xq = malloc((size_t)(n * K));
+  int8_t* wq = malloc((size_t)(N * K));
+  float* st = malloc(sizeof(float) * n);
+  float* sc = malloc(sizeof(float) * N);
+  int32_t* acc = malloc(sizeof(int32_t) * n * N);
+  for (long i = 0; i < n * K; ++i) xb[i] = bf16_rne(x[i]);
+  orc_quant_rows_i8(xb, n, K, xq, st);
+  orc_quant_rows_i8(w, N, K, wq, sc);
+  orc_gemm_i8(xq, wq, n, K, N, acc);
+  orc_dequant_i8(acc, st, sc, n, N, y);
+  free(xb); free(xq); free(wq); free(st); free(sc); free(acc);
+}
+
 void orc_mot_layer(const float* x, long T, int nseg, const int* seg_off,
                    const int* seg_expert, const orc_expert* E,
                    const orc_dims* d, const int* pos_t, const int* pos_h,
@@ -252,6 +292,19 @@ void orc_mot_layer(const float* x, long T, int nseg, const int* seg_off,
                    const float* v_prefix, int mode, const int* t_index,
                    float* out, float* k_new, float* v_new)
 {
+  orc_mot_layer_ex(x, T, nseg, seg_off, seg_expert, E, d, pos_t, pos_h, pos_w,
+                   n_prefix, k_prefix, v_prefix, mode, t_index, 0, out, k_new,
+                   v_new);
+}
+
+void orc_mot_layer_ex(const float* x, long T, int nseg, const int* seg_off,
+                      const int* seg_expert, const orc_expert* E,
+                      const orc_dims* d, const int* pos_t, const int* pos_h,
+                      const int* pos_w, long n_prefix, const float* k_prefix,
+                      const float* v_prefix, int mode, const int* t_index,
+                      int flags, float* out, float* k_new, float* v_new)
+{
+  const int i8 = (flags & ORC_LAYER_W8A8) != 0;
   const long H = d->hidden, NH = d->heads, KV = d->kv_heads,
              HD = d->head_dim, I = d->inter;
   const float eps = (float)d->eps;
@@ -282,12 +335,12 @@ void orc_mot_layer(const float* x, long T, int nseg, const int* seg_off,
     const orc_expert* w = &E[seg_expert[s]];
     orc_rms_norm(x + r0 * H, w->input_layernorm, eps, n, H,
                  normed + r0 * H);
-    orc_linear(normed + r0 * H, w->q_proj, NULL, n, H, NH * HD,
-               q + r0 * NH * HD);
-    orc_linear(normed + r0 * H, w->k_proj, NULL, n, H, KV * HD,
-               kk + r0 * KV * HD);
-    orc_linear(normed + r0 * H, w->v_proj, NULL, n, H, KV * HD,
-               vv + r0 * KV * HD);
+    layer_linear(normed + r0 * H, w->q_proj, n, H, NH * HD, q + r0 * NH * HD,
+                 i8);
+    layer_linear(normed + r0 * H, w->k_proj, n, H, KV * HD, kk + r0 * KV * HD,
+                 i8);
+    layer_linear(normed + r0 * H, w->v_proj, n, H, KV * HD, vv + r0 * KV * HD,
+                 i8);
     orc_split_qk_norm(q + r0 * NH * HD, w->q_norm, w->q_norm_hw, NH, n, HD,
                       eps);
     orc_split_qk_norm(kk + r0 * KV * HD, w->k_norm, w->k_norm_hw, KV, n, HD,
@@ -323,23 +376,26 @@ void orc_mot_layer(const float* x, long T, int nseg, const int* seg_off,
              sizeof(float) * T * HD);
     }
   }
-  orc_attention(qh, kc, vc, NH, KV, T, TK, HD, TK, mode, n_prefix, t_index,
-                att);
+  if ((flags & ORC_LAYER_SAGE) && mode == ORC_BIDIR)
+    orc_sage_attention(qh, kc, vc, NH, KV, T, TK, HD, TK, 64, 32, att);
+  else
+    orc_attention(qh, kc, vc, NH, KV, T, TK, HD, TK, mode, n_prefix, t_index,
+                  att);
 
   /* o_proj + residual, then the MLP half, per segment */
   for (int s = 0; s < nseg; ++s) {
     const long r0 = seg_off[s], n = seg_off[s + 1] - seg_off[s];
     if (n <= 0) continue;
     const orc_expert* w = &E[seg_expert[s]];
-    orc_linear(att + r0 * NH * HD, w->o_proj, NULL, n, NH * HD, H,
-               proj + r0 * H);
+    layer_linear(att + r0 * NH * HD, w->o_proj, n, NH * HD, H, proj + r0 * H,
+                 i8);
     for (long i = 0; i < n * H; ++i) proj[r0 * H + i] += x[r0 * H + i];
     orc_rms_norm(proj + r0 * H, w->post_attention_layernorm, eps, n, H,
                  normed + r0 * H);
-    orc_linear(normed + r0 * H, w->gate_proj, NULL, n, H, I, g + r0 * I);
-    orc_linear(normed + r0 * H, w->up_proj, NULL, n, H, I, u + r0 * I);
+    layer_linear(normed + r0 * H, w->gate_proj, n, H, I, g + r0 * I, i8);
+    layer_linear(normed + r0 * H, w->up_proj, n, H, I, u + r0 * I, i8);
     orc_swiglu(g + r0 * I, u + r0 * I, g + r0 * I, n * I);
-    orc_linear(g + r0 * I, w->down_proj, NULL, n, I, H, out + r0 * H);
+    layer_linear(g + r0 * I, w->down_proj, n, I, H, out + r0 * H, i8);
     for (long i = 0; i < n * H; ++i) out[r0 * H + i] += proj[r0 * H + i];
   }
 

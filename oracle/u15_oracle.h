@@ -82,6 +82,22 @@ void orc_mot_layer(const float* x, long tokens, int nseg, const int* seg_off,
                    const float* v_prefix, int mode, const int* t_index,
                    float* out, float* k_new, float* v_new);
 
+/* The same layer under the two lossy tiers (flags may combine):
+ * ORC_LAYER_W8A8  every projection through the W8A8 rule (per-token int8
+ *                 activations, per-output-channel int8 weights, exact int32
+ *                 accumulators, the fp32 dequant) -- the i8_gemm tier;
+ * ORC_LAYER_SAGE  the bidirectional attention through orc_sage_attention
+ *                 with the reference's Sage tiles (64 query rows, 32 keys)
+ *                 -- the sage_attn tier; the masked rules stay exact. */
+#define ORC_LAYER_W8A8 1
+#define ORC_LAYER_SAGE 2
+void orc_mot_layer_ex(const float* x, long tokens, int nseg, const int* seg_off,
+                      const int* seg_expert, const orc_expert* experts,
+                      const orc_dims* d, const int* pos_t, const int* pos_h,
+                      const int* pos_w, long n_prefix, const float* k_prefix,
+                      const float* v_prefix, int mode, const int* t_index,
+                      int flags, float* out, float* k_new, float* v_new);
+
 void orc_quant_rows_i8(const float* x, long rows, long cols, int8_t* q,
                        float* scale);
 void orc_gemm_i8(const int8_t* a, const int8_t* w, long M, long K, long N,

@@ -6,7 +6,10 @@ negative controls (GQA factor 1 must differ, plain causal must differ from
 block-causal, the kv stride is the capacity), plus the BASELINE attention
 shape (4096 queries over a 320-token prefix + 4096) on sampled heads, the
 paged cache with a permuted page table, and the Sage int8-QK path against its
-own restatement and against exact attention.
+own restatement (the reference's Sage tiles: 64 query rows and 32 keys per
+scale) and against exact attention. The tcgen05 kernel's masked rules are
+held to the same bar, up to the BASELINE block-causal prefill (64 text
+tokens + 2 reference images of 1024 tokens, t from thw_indexes).
 """
 import numpy as np
 import pytest
@@ -123,7 +126,7 @@ def test_baseline_shape_sampled_heads(ops):
 def test_sage_matches_restatement(ops):
     q, k, v = qkv(8, 2, 130, 200, 13, k_mean=0.7)
     got = run(ops, q, k, v, 170, sage=True)
-    sage_ref = O.sage_attention(q, k, v, tk=170, bq=64, bk=64)
+    sage_ref = O.sage_attention(q, k, v, tk=170, bq=64, bk=32)
     exact = O.attention(q, k, v, tk=170)
     assert rel_l2(got, sage_ref) < 1e-2
     assert rel_l2(got, exact) < 3e-2
@@ -201,7 +204,7 @@ def test_tc_baseline_shape_sampled(ops):
 def test_tc_sage(ops):
     q, k, v = qkv(8, 2, 300, 256, 25, k_mean=0.7)
     got = run_paged(ops, q, k, v, 230, sage=True)
-    assert rel_l2(got, O.sage_attention(q, k, v, tk=230, bq=64, bk=64)) < 1e-2
+    assert rel_l2(got, O.sage_attention(q, k, v, tk=230, bq=64, bk=32)) < 1e-2
     assert rel_l2(got, O.attention(q, k, v, tk=230)) < 3e-2
 
 
@@ -213,3 +216,97 @@ def test_paged_masked_rules_transposed_v(ops):
     q2, k2, v2 = qkv(8, 2, t.size, 64, 27)
     got = run_paged(ops, q2, k2, v2, t.size, mode=2, t_index=t)
     assert rel_l2(got, O.attention(q2, k2, v2, tk=t.size, mode=O.BLOCK_CAUSAL, t_index=t)) < BAR
+
+
+# ---------------------------------------------------------------------------
+# the tcgen05 kernel's prefill rules (causal, block-causal)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("hq,hkv,tq,cap,tk,off", [(8, 2, 48, 88, 67, 19), (4, 1, 300, 640, 600, 300),
+                                                  (32, 8, 257, 320, 257, 0),
+                                                  (8, 8, 640, 768, 700, 60)])
+def test_tc_causal(ops, hq, hkv, tq, cap, tk, off):
+    q, k, v = qkv(hq, hkv, tq, cap, 31)
+    got = run_paged(ops, q, k, v, tk, mode=1, q_offset=off)
+    ref = O.attention(q, k, v, tk=tk, mode=O.CAUSAL, q_offset=off)
+    assert rel_l2(got, ref) < BAR
+    # negative control: the bidirectional rule over the same keys differs
+    assert rel_l2(got, O.attention(q, k, v, tk=tk)) > 1e-2
+
+
+def test_tc_block_causal_reference_pattern(ops):
+    # the reference kernel test's t pattern (tests/u15-kernels-test.cc:612),
+    # stretched so an image run crosses 128-key blocks and query tiles
+    t = np.array([0, 1, 2] + [3] * 300 + [4, 5, 6] + [7] * 40 + [8], np.int32)
+    T = t.size
+    q, k, v = qkv(8, 2, T, T + 20, 32)
+    got = run_paged(ops, q, k, v, T, table=np.random.default_rng(3).permutation((T + 83) // 64),
+                    mode=2, t_index=t)
+    ref = O.attention(q, k, v, tk=T, mode=O.BLOCK_CAUSAL, t_index=t)
+    assert rel_l2(got, ref) < BAR
+    assert rel_l2(got, O.attention(q, k, v, tk=T, mode=O.CAUSAL)) > 1e-2
+
+
+def test_tc_block_causal_offset_and_unsorted_t(ops):
+    # queries after a prefix (q_offset), and a t vector that is not sorted:
+    # rows see later keys wherever their t matches
+    rng = np.random.default_rng(5)
+    T, off = 520, 200
+    t = rng.integers(0, 6, T).astype(np.int32)
+    q, k, v = qkv(4, 2, T - off, T, 33)
+    got = run_paged(ops, q, k, v, T, mode=2, q_offset=off, t_index=t)
+    ref = O.attention(q, k, v, tk=T, mode=O.BLOCK_CAUSAL, q_offset=off, t_index=t)
+    assert rel_l2(got, ref) < BAR
+
+
+def c4_prefill_ids():
+    """BASELINE config 4's prefill: 64 text tokens around two reference
+    images of 1024 tokens each (a 64 x 64 patch grid, merge 2), with their
+    <img> / </img> markers."""
+    IMG, CTX, END = 151665, 151667, 151666
+    text = list(range(1000, 1064))
+    ids = (text[:32] + [IMG] + [CTX] * 1024 + [END] + text[32:48] + [IMG] + [CTX] * 1024 +
+           [END] + text[48:])
+    return np.array(ids, np.int32), IMG, CTX, [(64, 64), (64, 64)]
+
+
+def test_tc_block_causal_c4_prefill(ops):
+    """The whole C4 prefill (2116 tokens, GQA 32/8) through the tcgen05
+    kernel, t from u15c_thw_indexes; sampled heads and rows against the CPU
+    restatement, and the causal rule as the negative control."""
+    import ctypes as C
+    from u15b200 import _lib as L
+    ids, IMG, CTX, grids = c4_prefill_ids()
+    T = ids.size
+    t, hh, ww = (np.zeros(T, np.int32) for _ in range(3))
+    g = np.ascontiguousarray(np.array(grids, np.int32).reshape(-1))
+    vp = lambda a: C.c_void_p(a.ctypes.data)  # noqa: E731
+    assert L.lib().u15c_thw_indexes(vp(ids), T, IMG, CTX, vp(g), 2, vp(t), vp(hh), vp(ww)) == 0
+    assert np.array_equal(t, O.thw_indexes(ids, IMG, CTX, grids)[0])
+    q, k, v = qkv(32, 8, T, T, 34)
+    got = run_paged(ops, q, k, v, T, mode=2, t_index=t)
+    rng = np.random.default_rng(35)
+    # rows in the text, inside each image (early, middle, last) and after it
+    rows = np.unique(np.concatenate([rng.choice(T, 40, replace=False), [0, 31, 32, 33, 600, 1057,
+                                     1058, 1075, 2000, 2114, T - 1]]))
+    for h in (0, 17, 31):
+        hk = h // 4
+        ref = np.concatenate([O.attention(q[h:h + 1, r:r + 1], k[hk:hk + 1], v[hk:hk + 1], tk=T,
+                                          mode=O.BLOCK_CAUSAL, q_offset=int(r), t_index=t)
+                              for r in rows])
+        cau = np.concatenate([O.attention(q[h:h + 1, r:r + 1], k[hk:hk + 1], v[hk:hk + 1], tk=T,
+                                          mode=O.CAUSAL, q_offset=int(r)) for r in rows])
+        mine = got[rows, h * 128:(h + 1) * 128]
+        assert rel_l2(mine, ref) < BAR, h
+        assert rel_l2(mine, cau) > 1e-2, h
+
+
+def test_tc_masked_matches_mma_sync_kernel(ops):
+    """The tcgen05 and mma.sync kernels on one cache (the op-level contiguous
+    layout for the latter): the same rule, the same answer within the bar."""
+    t = np.array([0] * 10 + [1] * 200 + list(range(2, 60)) + [60] * 130, np.int32)
+    T = t.size
+    q, k, v = qkv(16, 4, T, T, 36)
+    for mode, kw in ((1, {}), (2, {"t_index": t})):
+        a = run_paged(ops, q, k, v, T, mode=mode, **kw)
+        b = run(ops, q, k, v, T, mode=mode, **kw)
+        assert rel_l2(a, b) < BAR

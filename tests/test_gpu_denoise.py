@@ -232,3 +232,32 @@ def test_denoise_with_device_image_path():
     assert np.isfinite(got).all()
     assert rel_l2(got - noise, z - noise) < 5e-2
     assert isinstance(im, u15b200.ImagePath)
+
+
+def test_start_image_is_the_reference_draw(tmp_path):
+    """The generator's start image on the device: the reference's seeded draw
+    (std::mt19937_64 + std::normal_distribution<float>) scaled by
+    GenConfig::init_noise_scale of the image's token count, bit for bit
+    against the CPU checker; the init_noise file is taken as is, and one of
+    the wrong size is refused (src/u15-generator.cc:400-412)."""
+    import u15b200
+    from u15b200.generator import Generator
+    H, W = 256, 192
+    L_tok = (H // 32) * (W // 32)
+    scale = Generator.noise_scale(L_tok)
+    assert scale == O.init_noise_scale(L_tok)
+    img = Generator.initial_image(H, W, 1234, scale)
+    want = O.init_noise(1234, scale, H * W * 3).reshape(H, W, 3)
+    got = host(img)
+    assert img.is_cuda and np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # injected noise, raw f32 channel-last
+    noise = randn((H, W, 3), 99)
+    f = tmp_path / "noise.f32"
+    noise.tofile(f)
+    assert np.array_equal(host(Generator.initial_image(H, W, 0, scale, init_noise_path=str(f))),
+                          noise)
+    noise[:-1].tofile(f)
+    with pytest.raises(u15b200.U15Error, match="wrong size"):
+        Generator.initial_image(H, W, 0, scale, init_noise_path=str(f))
+    with pytest.raises(u15b200.U15Error, match="cannot read"):
+        Generator.initial_image(H, W, 0, scale, init_noise_path=str(tmp_path / "absent"))

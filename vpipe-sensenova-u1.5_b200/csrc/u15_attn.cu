@@ -20,8 +20,8 @@
 //
 // The Sage variant (bidirectional only) computes QK^T with mma.sync
 // m16n8k32 s8 x s8 -> s32 from int8 Q and smoothed int8 K prepared by
-// sage_prepare(), with one scale per 64-row Q block and per 64-key K
-// block; P.V stays bf16.
+// sage_prepare(), with one scale per 64-row Q block and per 32-key K
+// block (the reference's Sage tiles, bq 64 / bk 32); P.V stays bf16.
 #include "u15_common.cuh"
 #include "u15_kernels.h"
 
@@ -241,10 +241,13 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
           mma_s8_16832(si[2 * np + 1], a, b2, b3);
         }
       }
-      const float skv = p.sk[(long)hk * p.nkb + t] * p.scale_log2;
-      const float f0 = sq0 * skv, f1 = sq1 * skv;
+      // keys [0, 32) and [32, 64) of the tile are two K blocks (columns n * 8 + ..)
+      const float ska = p.sk[(long)hk * p.nkb + 2 * t] * p.scale_log2;
+      const float skb = p.sk[(long)hk * p.nkb + 2 * t + 1] * p.scale_log2;
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
+        const float skv = n < 4 ? ska : skb;
+        const float f0 = sq0 * skv, f1 = sq1 * skv;
         s[n][0] = (float)si[n][0] * f0;
         s[n][1] = (float)si[n][1] * f0;
         s[n][2] = (float)si[n][2] * f1;
@@ -381,9 +384,11 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
 // block of one head per CTA: absmax, s = amax / 127, int8 codes) and the
 // K-mean partials (one 64-key page of one kv head per CTA: the page's
 // channel sums). The second runs the K blocks: each CTA forms kmean[c] =
-// sum of the page partials / tk (fixed page order), smooths its 64 keys by
-// it and quantizes them like Q. Rows stay in registers between the absmax
-// and the codes: 32 elements a thread, 16-byte loads, 8-byte stores.
+// sum of the page partials / tk (fixed page order), smooths its page's 64
+// keys by it and quantizes them like Q as two 32-key blocks, one scale each
+// (the reference's key block, bk = 32, src/u15-metal-ops.cc:702). Rows stay
+// in registers between the absmax and the codes: 32 elements a thread,
+// 16-byte loads, 8-byte stores.
 constexpr int kSageThreads = 256;
 
 __device__ __forceinline__ void load8_bf(const __nv_bfloat16* p, float (&v)[8])
@@ -463,7 +468,7 @@ __global__ void __launch_bounds__(kSageThreads)
     sage_k_kernel(KvView kv, int tk, int npg, const float* kpart, int8_t* k8, float* sk,
                   long k8_stride)
 {
-  __shared__ float red[kSageThreads / 32];
+  __shared__ float red[2][kSageThreads / 32];
   __shared__ float km[128];
   const int pg = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
   if (tid < 128) {
@@ -472,29 +477,49 @@ __global__ void __launch_bounds__(kSageThreads)
     km[tid] = acc / (float)tk;
   }
   __syncthreads();
+  // rows r0 + 16 i: i = 0, 1 are the page's first 32-key block, i = 2, 3 its second
   const int c8 = tid & 15, r0 = pg * 64 + (tid >> 4);
   float v[4][8];
-  bool valid[4];
-  float m = 0.0f;
+  float m[2] = {0.0f, 0.0f};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = r0 + 16 * i;
-    valid[i] = true;   // every row of the block is written; rows past tk as zeros
-    if (r < tk) {
+    if (r < tk) {   // every row of the page is written; rows past tk as zeros
       load8_bf(kv_row(kv, kv.k, hk, r) + c8 * 8, v[i]);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         v[i][k] -= km[c8 * 8 + k];
-        m = fmaxf(m, fabsf(v[i][k]));
+        m[i >> 1] = fmaxf(m[i >> 1], fabsf(v[i][k]));
       }
     } else {
 #pragma unroll
       for (int k = 0; k < 8; ++k) v[i][k] = 0.0f;
     }
   }
-  const float s = __fdiv_rn(block_absmax(m, red), 127.0f);
-  if (tid == 0) sk[(long)hk * npg + pg] = s;
-  store_codes(v, s, valid, k8 + (long)hk * k8_stride * 128, r0, c8);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m[0] = fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], o));
+    m[1] = fmaxf(m[1], __shfl_xor_sync(0xffffffffu, m[1], o));
+  }
+  if (lane_id() == 0) {
+    red[0][warp_id()] = m[0];
+    red[1][warp_id()] = m[1];
+  }
+  __syncthreads();
+  float amax[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < kSageThreads / 32; ++i) {
+    amax[0] = fmaxf(amax[0], red[0][i]);
+    amax[1] = fmaxf(amax[1], red[1][i]);
+  }
+  const float s[2] = {__fdiv_rn(amax[0], 127.0f), __fdiv_rn(amax[1], 127.0f)};
+  if (tid < 2) sk[(long)hk * 2 * npg + 2 * pg + tid] = s[tid];
+  const float rc[2] = {quant_recip(s[0]), quant_recip(s[1])};
+  int8_t* out = k8 + (long)hk * k8_stride * 128;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<uint2*>(out + (long)(r0 + 16 * i) * 128 + c8 * 8) =
+        quant8(v[i], s[i >> 1], rc[i >> 1]);
 }
 
 }  // namespace
@@ -539,8 +564,8 @@ int attention(const AttnArgs& a, cudaStream_t st, std::string* err)
   p.sq = a.sq;
   p.sk = a.sk;
   p.nqb = (a.tq + 63) / 64;
-  p.nkb = (a.tk + 63) / 64;
-  p.k8_stride = (long)p.nkb * 64;
+  p.nkb = 2 * ((a.tk + 63) / 64);   // 32-key K blocks, two per page
+  p.k8_stride = (long)p.nkb * 32;
   const dim3 grid((a.tq + p.R - 1) / p.R, a.hkv);
   const int smem = sage ? (kRows * 128 + 2 * kKeys * 128 + 2 * kKeys * 256)
                         : (kRows * 256 + 2 * kKeys * 256 + 2 * kKeys * 256);
@@ -564,12 +589,13 @@ int sage_prepare(const void* q, const KvView& kv, int hq, int hkv, int tq, int t
                  std::string* err)
 {
   if (tq <= 0 || tk <= 0) return 0;
-  const int nqb = (tq + 63) / 64, nkb = (tk + 63) / 64;
-  // kmean holds the per-page partial sums [hkv][nkb][128]
-  sage_q_kernel<<<dim3(nqb + nkb, std::max(hq, hkv)), kSageThreads, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(q), kv, hq, hkv, tq, tk, nqb, nkb, q8, sq, kmean);
-  sage_k_kernel<<<dim3(nkb, hkv), kSageThreads, 0, st>>>(kv, tk, nkb, kmean, k8, sk,
-                                                         (long)nkb * 64);
+  const int nqb = (tq + 63) / 64, npg = (tk + 63) / 64;
+  // kmean holds the per-page partial sums [hkv][npg][128]; sk two 32-key
+  // block scales per page [hkv][2 * npg]
+  sage_q_kernel<<<dim3(nqb + npg, std::max(hq, hkv)), kSageThreads, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(q), kv, hq, hkv, tq, tk, nqb, npg, q8, sq, kmean);
+  sage_k_kernel<<<dim3(npg, hkv), kSageThreads, 0, st>>>(kv, tk, npg, kmean, k8, sk,
+                                                         (long)npg * 64);
   if (cudaGetLastError() != cudaSuccess) {
     *err = "sage_prepare: kernel launch failed";
     return 2;

@@ -1,6 +1,8 @@
-// Bidirectional flash attention on sm_100a tensor cores (tcgen05 + TMEM +
-// TMA), the denoise pass's attention (src/u15-metal-ops.cc:835-882 in the
-// reference: q head-major, every key of [prefix || block]).
+// Flash attention on sm_100a tensor cores (tcgen05 + TMEM + TMA): the
+// denoise pass's bidirectional attention (src/u15-metal-ops.cc:835-882 in
+// the reference: q head-major, every key of [prefix || block]) and the
+// prefill's masked rules (src/u15-metal-ops.cc:648-677, 884-908;
+// src/u15-kernels.metal:186-252), over the paged cache.
 //
 // One CTA = 256 query rows of one head as two 128-row tiles sharing every
 // K/V block it loads; keys in blocks of 128 (two 64-token pages of the
@@ -37,7 +39,23 @@
 //
 // The Sage variant (int8 QK, SageAttention) feeds S from int8 Q and smoothed
 // int8 K (kind::i8, s32 accumulators) and scales the scores by the per-64-row
-// Q block and per-64-key K block scales; P.V stays bf16.
+// Q block and per-32-key K block scales (the reference's bq 64 / bk 32, so a
+// 128-key block carries four K scales, one per 32-column chunk of a score
+// row); P.V stays bf16.
+//
+// Masked rules (MODE 1 causal: key j visible to query row i iff
+// j <= q_offset + i; MODE 2 block-causal: iff j <= q_offset + i or
+// t[j] == t[q_offset + i], t the caller's int32 t-index vector). Each tile
+// runs only the key blocks up to its last visible one (n_t blocks; the
+// CTA's producer loads max(n_0, n_1)), and per (tile, block) a uniform test
+// says whether every pair is visible -- the block lies wholly at or below
+// the tile's first row, or (block-causal) the tile's rows and the block's
+// keys all carry one t value -- in which case the softmax runs as in the
+// bidirectional pass; only the other blocks test the rule per element. For
+// the block-causal rule a prologue forms each key block's t range
+// (min, max) in shared memory and each tile's last block: a block can hold
+// a key visible to row i only if it starts at or below i or its t range
+// holds t[i].
 //
 // K/V come from the paged cache: K page [64 tokens][128] and V page
 // transposed [128 dims][64 tokens], per kv head, page index from the page
@@ -46,6 +64,7 @@
 #include "u15_kernels.h"
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 
@@ -68,15 +87,19 @@ constexpr int kRegsLow = 72, kRegsHigh = 216;
 constexpr int kQBytes = 2 * kTile * 256;        // bf16 Q, 2 tiles; int8 uses half
 constexpr int kKBytes = kBlk * 256;             // [2 dims blocks][128 keys][128 B]
 constexpr int kVBytes = 128 * kBlk * 2;         // [2 key blocks][128 dims][128 B]
-constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256;
+// block-causal: per key block the t range (min, max); tk <= kMaxBlk * 128
+constexpr int kMaxBlk = 256;
+constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256 + 2 * kMaxBlk * 4 + 64;
 
 struct TcAttnP {
   int hq, hkv, tq, tk, G;
+  int q_offset;
+  const int32_t* t_index;   // block-causal: [tk], 16-byte aligned
   float scale_log2;
   const int32_t* page_table;
   __nv_bfloat16* out;
   const float* sq;   // Sage: [hq][nqb]
-  const float* sk;   // Sage: [hkv][nkb]
+  const float* sk;   // Sage: [hkv][nkb], one scale per 32-key block
   int nqb, nkb;
   long k8_stride;    // Sage: rows per kv head in the int8 K copy
   unsigned* err;
@@ -149,7 +172,15 @@ __device__ __forceinline__ float ex2_fma(float x)
   return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
 }
 
-template <bool SAGE, bool EMU>
+// Per-tile key-block schedule of the masked rules, shared by every warp
+// (see the file comment): n[t] blocks for tile t, and for block-causal the
+// tile's t range and each key block's t range.
+struct MaskPlan {
+  int n[2];
+  int tlo[2], thi[2];
+};
+
+template <bool SAGE, bool EMU, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
@@ -171,12 +202,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t p_full = s_full + 16;            // [2 tiles], 128 arrivals
   const uint32_t drain = p_full + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages + 2 + 2 + 1);
+  MaskPlan* plan = reinterpret_cast<MaskPlan*>(bars + 32);
+  int* blk_tlo = reinterpret_cast<int*>(bars + 40);   // [kMaxBlk] (block-causal)
+  int* blk_thi = blk_tlo + kMaxBlk;
 
   const int w = (int)warp_id();
   const int h = blockIdx.y;
   const int hk = h / p.G;
   const int q0 = blockIdx.x * 2 * kTile;
-  const int n = (p.tk + kBlk - 1) / kBlk;
+  const int n_all = (p.tk + kBlk - 1) / kBlk;
   const int n_pg = (p.tk + 63) / 64;
 
   if (threadIdx.x == 0) {
@@ -190,6 +224,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full + 8 * t, 1);
       mbar_init(p_full + 8 * t, 128);
+      // blocks of tile t: none when the tile holds no query row; the causal
+      // rule ends at the block of the tile's last row
+      const int r_lo = q0 + t * kTile, r_hi = min(r_lo + kTile, p.tq) - 1;
+      int nt = r_lo < p.tq ? n_all : 0;
+      if (MODE == 1 && nt > 0) nt = min(n_all, (p.q_offset + r_hi) / kBlk + 1);
+      plan->n[t] = MODE == 2 ? 0 : nt;
+      plan->tlo[t] = INT_MAX;
+      plan->thi[t] = INT_MIN;
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -210,6 +252,56 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the set-up above overlaps the previous kernel; global memory waits for it
   griddep_launch();
   griddep_wait();
+  if constexpr (MODE == 2) {
+    // t range of every key block (each warp a block at a time, 4 keys a lane)
+    for (int kb = w; kb < n_all; kb += kThreads / 32) {
+      int lo = INT_MAX, hi = INT_MIN;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = kb * kBlk + q * 32 + (int)lane_id();
+        if (j < p.tk) {
+          const int tj = p.t_index[j];
+          lo = min(lo, tj);
+          hi = max(hi, tj);
+        }
+      }
+      lo = __reduce_min_sync(0xffffffffu, lo);
+      hi = __reduce_max_sync(0xffffffffu, hi);
+      if (lane_id() == 0) {
+        blk_tlo[kb] = lo;
+        blk_thi[kb] = hi;
+      }
+    }
+    __syncthreads();
+    if (w >= 4) {
+      // each softmax thread's row: its last block that can hold a visible key
+      const int t = (w - 4) >> 2;
+      const int qi = q0 + t * kTile + (w & 3) * 32 + (int)lane_id();
+      int last = -1, ti = 0;
+      if (qi < p.tq) {
+        const int gi = p.q_offset + qi;
+        ti = p.t_index[gi];
+        last = min(gi / kBlk, n_all - 1);
+        for (int kb = n_all - 1; kb > last; --kb)
+          if (blk_tlo[kb] <= ti && ti <= blk_thi[kb]) {
+            last = kb;
+            break;
+          }
+      }
+      const bool valid = qi < p.tq;
+      last = __reduce_max_sync(0xffffffffu, last);
+      const int lo = __reduce_min_sync(0xffffffffu, valid ? ti : INT_MAX);
+      const int hi = __reduce_max_sync(0xffffffffu, valid ? ti : INT_MIN);
+      if (lane_id() == 0) {
+        atomicMax(&plan->n[t], last + 1);
+        atomicMin(&plan->tlo[t], lo);
+        atomicMax(&plan->thi[t], hi);
+      }
+    }
+    __syncthreads();
+  }
+  const int n_t0 = plan->n[0], n_t1 = plan->n[1];
+  const int n = max(n_t0, n_t1);   // blocks the producer loads
   if (w < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
     if (w == 0) {
@@ -278,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane_id() == 0) {
         const uint32_t id_s = SAGE ? idesc_s8(kTile, kBlk) : idesc_bf16(kTile, kBlk);
         const uint32_t id_o = idesc_bf16(kTile, 128);
+        const int nt[2] = {n_t0, n_t1};
         auto issue_s = [&](int t, int j) {
           const uint32_t d = tmem + t * 256;
           const uint32_t kb = smem_u32(sK + (j % kStages) * kKBytes);
@@ -300,6 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ok) {
             tc_fence_after();
             for (int t = 0; t < 2; ++t) {
+              if (nt[t] == 0) continue;
               issue_s(t, 0);
               mma_commit(s_full + 8 * t);
             }
@@ -310,7 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = j % kStages, s1 = (j + 1) % kStages;
           if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull)) break;
           const uint32_t vb = smem_u32(sV + s * kVBytes);
+          bool k_next = false;   // K of block j + 1 has landed
           for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= nt[t]) continue;
             if (!mbar_wait(p_full + 8 * t, j & 1, p.err, kDevWaitFull)) {
               ok = false;
               break;
@@ -321,12 +417,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < 8; ++k)
               mma_bf16_ts(d, a + k * 8, smem_desc_sw128(vb + (k >> 2) * 128 * 128 + (k & 3) * 32),
                           id_o, (j | k) != 0);
-            if (j + 1 < n) {
-              if (t == 0 && !mbar_wait(k_full + 8 * s1, ((j + 1) / kStages) & 1, p.err,
-                                       kDevWaitFull)) {
+            if (j + 1 < nt[t]) {
+              if (!k_next && !mbar_wait(k_full + 8 * s1, ((j + 1) / kStages) & 1, p.err,
+                                        kDevWaitFull)) {
                 ok = false;
                 break;
               }
+              k_next = true;
               tc_fence_after();
               issue_s(t, j + 1);
             }
@@ -334,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!ok) break;
           mma_commit(v_empty + 8 * s);
+          // n = max(n_0, n_1): some tile ran block j + 1's S, so its K was waited for
           if (j + 1 < n) mma_commit(k_empty + 8 * s1);
         }
         mma_commit(drain);
@@ -347,13 +445,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wq = w & 3;
     const int row = wq * 32 + (int)lane_id();
     const int qi = q0 + t * kTile + row;
+    const int n_mine = t == 0 ? n_t0 : n_t1;
     const uint32_t tS = tmem + t * 256 + ((uint32_t)(wq * 32) << 16);
     const uint32_t tO = tS + 128;
     float sqv = 1.0f;
     if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
+    // masked rules: this row's position among the keys, its t, and the
+    // tile's first position (blocks wholly at or below it are visible)
+    const int gi = p.q_offset + qi;
+    const int g_first = p.q_offset + q0 + t * kTile;
+    int ti = 0;
+    bool t_uniform = false;
+    if constexpr (MODE == 2) {
+      ti = qi < p.tq ? p.t_index[gi] : 0;
+      t_uniform = plan->tlo[t] == plan->thi[t];
+    }
+    // the last 32-key block that holds a key (Sage scales past it are clamped to it)
+    const int kb_last = (p.tk - 1) >> 5;
     float m_ref = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    for (int j = 0; j < n_mine; ++j) {
       // warp-uniform: the TMEM loads and stores below are warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait(s_full + 8 * t, j & 1, p.err, kDevWaitAccFull))) {
         ok = false;
@@ -366,12 +477,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
       tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
       tmem_ld_wait();
-      // base-2 scale of each 64-key half (Sage: per-block Q and K scales)
-      float f0 = p.scale_log2, f1 = p.scale_log2;
-      if constexpr (SAGE) {
-        const int kb0 = 2 * j, kb1 = min(2 * j + 1, p.nkb - 1);
-        f0 *= sqv * p.sk[(long)hk * p.nkb + kb0];
-        f1 *= sqv * p.sk[(long)hk * p.nkb + kb1];
+      // base-2 scale of each 32-key chunk (Sage: the Q block's and the chunk's
+      // K block's scales; never zero, so a masked -inf score stays -inf)
+      float f[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        f[c] = p.scale_log2;
+        if constexpr (SAGE)
+          f[c] = fmaxf(f[c] * sqv * p.sk[(long)hk * p.nkb + min(4 * j + c, kb_last)], 1e-30f);
       }
       // Sage scores are int32 sums of 128 int8 x int8 products, |S| <=
       // 128 * 127 * 127 < 2^22: adding them to the bits of 1.5 * 2^23 gives
@@ -383,35 +496,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (SAGE) s[i] = __int_as_float((int)r[i] + 0x4B400000) - 12582912.0f;
         else s[i] = __uint_as_float(r[i]);
       }
-      const int kmax = p.tk - j * kBlk;
-      if (kmax < kBlk) {
+      const int j0 = j * kBlk;
+      const int kmax = p.tk - j0;
+      if constexpr (MODE == 0) {
+        if (kmax < kBlk) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= kmax) s[i] = -INFINITY;
-      }
-      // row maxima of the two 64-key halves, four independent chains each
-      // (one serial chain of 64 would put its latency on the critical path)
-      float ma[4], mb[4];
+          for (int i = 0; i < 128; ++i)
+            if (i >= kmax) s[i] = -INFINITY;
+        }
+      } else {
+        // tile-uniform: is every (row, key) pair of this block visible?
+        bool full = kmax >= kBlk && j0 + kBlk - 1 <= g_first;
+        if constexpr (MODE == 2)
+          full = full || (kmax >= kBlk && t_uniform && blk_tlo[j] == blk_thi[j] &&
+                          blk_tlo[j] == plan->tlo[t]);
+        if (!full) {
+          if constexpr (MODE == 1) {
+            const int lim = min(kmax - 1, gi - j0);   // visible columns [0, lim]
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        ma[k] = s[k];
-        mb[k] = s[64 + k];
-      }
+            for (int i = 0; i < 128; ++i)
+              if (i > lim) s[i] = -INFINITY;
+          } else {
+            const int lim = gi - j0;
+            const int4* t4 = reinterpret_cast<const int4*>(p.t_index + j0);
 #pragma unroll
-      for (int i = 4; i < 64; i += 4) {
+            for (int qd = 0; qd < 32; ++qd) {
+              int tt[4];
+              if (4 * qd + 3 < kmax) {
+                const int4 v = __ldg(t4 + qd);
+                tt[0] = v.x; tt[1] = v.y; tt[2] = v.z; tt[3] = v.w;
+              } else {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          ma[k] = fmaxf(ma[k], s[i + k]);
-          mb[k] = fmaxf(mb[k], s[64 + i + k]);
+                for (int e = 0; e < 4; ++e) tt[e] = 4 * qd + e < kmax ? p.t_index[j0 + 4 * qd + e] : 0;
+              }
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = 4 * qd + e;
+                const bool vis = i < kmax && (i <= lim || tt[e] == ti);
+                if (!vis) s[i] = -INFINITY;
+              }
+            }
+          }
         }
       }
-      const float mt = fmaxf(fmaxf(fmaxf(ma[0], ma[1]), fmaxf(ma[2], ma[3])) * f0,
-                             fmaxf(fmaxf(mb[0], mb[1]), fmaxf(mb[2], mb[3])) * f1);
+      // row maxima of the four 32-key chunks, two independent chains each
+      // (one serial chain of 128 would put its latency on the critical path)
+      float mc[4][2];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        mc[c][0] = s[32 * c];
+        mc[c][1] = s[32 * c + 1];
+      }
+#pragma unroll
+      for (int i = 2; i < 32; i += 2) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          mc[c][0] = fmaxf(mc[c][0], s[32 * c + i]);
+          mc[c][1] = fmaxf(mc[c][1], s[32 * c + i + 1]);
+        }
+      }
+      const float mt = fmaxf(fmaxf(fmaxf(mc[0][0], mc[0][1]) * f[0], fmaxf(mc[1][0], mc[1][1]) * f[1]),
+                             fmaxf(fmaxf(mc[2][0], mc[2][1]) * f[2], fmaxf(mc[3][0], mc[3][1]) * f[3]));
       const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
       const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // O_t is final up to P.V(j-1): s_full[t] completed after it
-        const float fac = need ? ex2(m_ref - m_new) : 1.0f;
+        const float fac = (need && m_ref != -INFINITY) ? ex2(m_ref - m_new) : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -424,11 +574,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= fac;
       }
       m_ref = m_new;
-      const float nm = -m_ref;
+      // a row with no visible key yet keeps m_ref = -inf: its exponentials are
+      // of -inf scores and give 0 with a zero offset
+      const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;
       float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // four independent partial sums
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const float fc = c < 2 ? f0 : f1;
+        const float fc = f[c];
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -450,7 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(p_full + 8 * t);
     }
     // the commit after the last P.V of this tile
-    const bool fin = ok && n > 0 && mbar_wait(s_full + 8 * t, n & 1, p.err, kDevWaitAccFull);
+    const bool fin = ok && n_mine > 0 &&
+                     mbar_wait(s_full + 8 * t, n_mine & 1, p.err, kDevWaitAccFull);
     if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
@@ -487,14 +640,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
+bool attention_tc_serves(int mode, int tk, const int32_t* t_index)
+{
+  if (mode == 0 || mode == 1) return true;
+  return mode == 2 && t_index != nullptr && tk <= kMaxBlk * kBlk &&
+         (reinterpret_cast<uintptr_t>(t_index) & 15) == 0;
+}
+
 int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
 {
   if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv) {
     *err = "attention: hq must be a positive multiple of hkv";
     return 1;
   }
-  if (a.tq <= 0 || a.tk <= 0) return 0;
+  if (a.mode < 0 || a.mode > 2) {
+    *err = "attention: unknown mode";
+    return 1;
+  }
   const bool sage = a.q8 != nullptr;
+  if (sage && a.mode != 0) {
+    *err = "attention: the int8-QK path serves the bidirectional pass only";
+    return 1;
+  }
+  if (a.mode == 2 && !attention_tc_serves(2, a.tk, a.t_index)) {
+    *err = "attention (tcgen05): block-causal needs a 16-byte aligned t-index vector and at most " +
+           std::to_string(kMaxBlk * kBlk) + " keys";
+    return 1;
+  }
+  if (a.mode != 0 && (a.q_offset < 0 || (a.mode == 2 && (long)a.q_offset + a.tq > a.tk))) {
+    *err = "attention: the queries' positions must lie within the key range";
+    return 1;
+  }
+  if (a.tq <= 0 || a.tk <= 0) return 0;
   const int n_pages_needed = (a.tk + 63) / 64;
   if (a.n_pages < n_pages_needed && a.page_table == nullptr) {
     *err = "attention: the page pool holds fewer pages than the key length needs";
@@ -506,14 +683,16 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   p.tq = a.tq;
   p.tk = a.tk;
   p.G = a.hq / a.hkv;
+  p.q_offset = a.q_offset;
+  p.t_index = a.t_index;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
   p.page_table = a.page_table;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.sq = a.sq;
   p.sk = a.sk;
   p.nqb = (a.tq + 63) / 64;
-  p.nkb = (a.tk + 63) / 64;
-  p.k8_stride = (long)p.nkb * 64;
+  p.nkb = 2 * ((a.tk + 63) / 64);   // 32-key K blocks, two per page
+  p.k8_stride = (long)p.nkb * 32;
   p.err = a.dev_err;
   CUtensorMap mq, mk, mv;
   if (sage) {
@@ -527,13 +706,22 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   // Every exponential on the MUFU: a quarter of them on the FMA pipe measured
   // 5-10 % slower for bf16 and 4 % slower for Sage (U15_SAGE_EMU=1 selects
   // that form of the Sage kernel, for A/B checks).
-  static std::atomic<uint64_t> set_attr[3];
+  static std::atomic<uint64_t> set_attr[5];
   const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
   const char* emu_env = std::getenv("U15_SAGE_EMU");
   const bool emu = emu_env != nullptr && *emu_env == '1';
-  auto k = !sage ? attn_tc_kernel<false, false>
-                 : (emu ? attn_tc_kernel<true, true> : attn_tc_kernel<true, false>);
-  const int which = !sage ? 0 : (emu ? 1 : 2);
+  auto k = attn_tc_kernel<false, false, 0>;
+  int which = 0;
+  if (sage) {
+    k = emu ? attn_tc_kernel<true, true, 0> : attn_tc_kernel<true, false, 0>;
+    which = emu ? 1 : 2;
+  } else if (a.mode == 1) {
+    k = attn_tc_kernel<false, false, 1>;
+    which = 3;
+  } else if (a.mode == 2) {
+    k = attn_tc_kernel<false, false, 2>;
+    which = 4;
+  }
   cudaError_t e = cudaSuccess;
   if (smem_attr_once(k, kSmem, set_attr[which])) {
     cudaLaunchConfig_t cfg = {};

@@ -25,6 +25,7 @@ int cuda_fail(cudaError_t e, const char* what)
 
 namespace {
 constexpr int kMaxDev = 64;
+constexpr size_t kStatusBytes = 16;
 DevState g_dev[kMaxDev];
 std::mutex g_dev_mu;
 }  // namespace
@@ -45,9 +46,10 @@ int dev_init(int device)
                                  prop.name + " sm_" + std::to_string(prop.major) +
                                  std::to_string(prop.minor));
   d.sms = prop.multiProcessorCount;
-  e = cudaMalloc(&d.err, sizeof(unsigned));
+  // the status block: the first error code, then the wait limit (0 = default)
+  e = cudaMalloc(&d.err, kStatusBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(status word)");
-  e = cudaMemset(d.err, 0, sizeof(unsigned));
+  e = cudaMemset(d.err, 0, kStatusBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status word)");
   d.ready = true;
   return U15C_OK;
@@ -114,30 +116,52 @@ KvView kv_view(void* k, void* v, const int32_t* page_table, int cap, int hkv)
   return kv;
 }
 
+// Sage workspace: int8 Q [hq][tq][128], int8 smoothed K [hkv][npg * 64][128]
+// (rows past tk zero), Q scales [hq][ceil(tq / 64)], K scales [hkv][2 * npg]
+// (one per 32-key block), K-mean page partials [hkv][npg][128].
 size_t sage_bytes(int hq, int hkv, int tq, int tk)
 {
-  const size_t nqb = (size_t)(tq + 63) / 64, nkb = (size_t)(tk + 63) / 64;
+  const size_t nqb = (size_t)(tq + 63) / 64, npg = (size_t)(tk + 63) / 64;
   auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
-  return al((size_t)hq * tq * 128) + al((size_t)hkv * nkb * 64 * 128) + al(4 * hq * nqb) +
-         al(4 * hkv * nkb) + al(4 * (size_t)hkv * nkb * 128);
+  return al((size_t)hq * tq * 128) + al((size_t)hkv * npg * 64 * 128) + al(4 * hq * nqb) +
+         al(4 * hkv * 2 * npg) + al(4 * (size_t)hkv * npg * 128);
 }
 
 SageWs sage_split(void* ws, int hq, int hkv, int tq, int tk)
 {
-  const size_t nqb = (size_t)(tq + 63) / 64, nkb = (size_t)(tk + 63) / 64;
+  const size_t nqb = (size_t)(tq + 63) / 64, npg = (size_t)(tk + 63) / 64;
   auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
   uint8_t* p = static_cast<uint8_t*>(ws);
   SageWs s;
   s.q8 = reinterpret_cast<int8_t*>(p);
   p += al((size_t)hq * tq * 128);
   s.k8 = reinterpret_cast<int8_t*>(p);
-  p += al((size_t)hkv * nkb * 64 * 128);
+  p += al((size_t)hkv * npg * 64 * 128);
   s.sq = reinterpret_cast<float*>(p);
   p += al(4 * hq * nqb);
   s.sk = reinterpret_cast<float*>(p);
-  p += al(4 * hkv * nkb);
+  p += al(4 * hkv * 2 * npg);
   s.kmean = reinterpret_cast<float*>(p);
   return s;
+}
+
+int check_attention(int hq, int hkv, int tq, int tk, int mode, int q_offset,
+                    const int32_t* t_index, bool sage, bool legacy)
+{
+  if (hq <= 0 || hkv <= 0 || hq % hkv != 0)
+    return fail(U15C_EINVAL, "attention: hq must be a positive multiple of hkv");
+  if (legacy && (hq / hkv > 8 || 128 % (hq / hkv) != 0))
+    return fail(U15C_EINVAL, "attention: GQA group size must divide 128 and be at most 8");
+  if (tq < 0 || tk < 0)
+    return fail(U15C_EINVAL, "attention: token counts must be non-negative");
+  if (mode < 0 || mode > 2) return fail(U15C_EINVAL, "attention: unknown mode");
+  if (sage && mode != 0)
+    return fail(U15C_EINVAL, "attention: Sage serves the bidirectional pass only");
+  if (mode == 2 && t_index == nullptr)
+    return fail(U15C_EINVAL, "attention: block-causal needs the t-index vector");
+  if (mode != 0 && (q_offset < 0 || (mode == 2 && tq > 0 && (long)q_offset + tq > tk)))
+    return fail(U15C_EINVAL, "attention: the queries' positions must lie within the key range");
+  return U15C_OK;
 }
 
 int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, int hq, int hkv,
@@ -147,7 +171,8 @@ int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, i
   if (d == nullptr) return U15C_ECUDA;
   if (q == nullptr || kv.k == nullptr || kv.v == nullptr || out == nullptr)
     return fail(U15C_EINVAL, "attention: null buffer");
-  if (mode < 0 || mode > 2) return fail(U15C_EINVAL, "attention: unknown mode");
+  int rc = check_attention(hq, hkv, tq, tk, mode, q_offset, t_index, sage_ws != nullptr, true);
+  if (rc) return rc;
   AttnArgs a;
   a.q = q;
   a.kv = kv;
@@ -162,7 +187,6 @@ int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, i
   a.dev_err = d->err;
   std::string err;
   if (sage_ws != nullptr) {
-    if (mode != 0) return fail(U15C_EINVAL, "attention: Sage serves the bidirectional pass only");
     SageWs s = sage_split(sage_ws, hq, hkv, tq, tk);
     if (sage_prepare(q, kv, hq, hkv, tq, tk, s.q8, s.k8, s.sq, s.sk, s.kmean, st, &err))
       return fail(U15C_ECUDA, err);
@@ -171,13 +195,14 @@ int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, i
     a.sq = s.sq;
     a.sk = s.sk;
   }
-  const int rc = attention(a, st, &err);
+  rc = attention(a, st, &err);
   if (rc) return fail(rc == 1 ? U15C_EINVAL : U15C_ECUDA, err);
   return U15C_OK;
 }
 
 int run_attention_tc(cudaStream_t st, const void* q, const KvView& kv, int n_pages, void* out,
-                     int hq, int hkv, int tq, int tk, void* sage_ws)
+                     int hq, int hkv, int tq, int tk, int mode, int q_offset,
+                     const int32_t* t_index, void* sage_ws)
 {
   DevState* d = dev();
   if (d == nullptr) return U15C_ECUDA;
@@ -188,6 +213,10 @@ int run_attention_tc(cudaStream_t st, const void* q, const KvView& kv, int n_pag
     return fail(U15C_EINVAL, "attention: the tcgen05 path needs the paged layout with transposed V");
   if ((tk + kPageTokens - 1) / kPageTokens > n_pages)
     return fail(U15C_EINVAL, "attention: key length exceeds the page pool");
+  if (!attention_tc_serves(mode, tk, t_index))
+    return run_attention(st, q, kv, out, hq, hkv, tq, tk, mode, q_offset, t_index, sage_ws);
+  int rc = check_attention(hq, hkv, tq, tk, mode, q_offset, t_index, sage_ws != nullptr, false);
+  if (rc) return rc;
   TcAttnArgs a;
   a.q = q;
   a.k_pages = kv.k;
@@ -199,6 +228,9 @@ int run_attention_tc(cudaStream_t st, const void* q, const KvView& kv, int n_pag
   a.hkv = hkv;
   a.tq = tq;
   a.tk = tk;
+  a.mode = mode;
+  a.q_offset = q_offset;
+  a.t_index = t_index;
   a.dev_err = d->err;
   std::string err;
   if (sage_ws != nullptr) {
@@ -210,7 +242,7 @@ int run_attention_tc(cudaStream_t st, const void* q, const KvView& kv, int n_pag
     a.sq = s.sq;
     a.sk = s.sk;
   }
-  const int rc = attention_tc(a, st, &err);
+  rc = attention_tc(a, st, &err);
   if (rc) return fail(rc == 1 ? U15C_EINVAL : U15C_ECUDA, err);
   return U15C_OK;
 }
@@ -274,6 +306,35 @@ int u15c_device_status(int device, unsigned* code)
   }
   if (cur != device) cudaSetDevice(cur);
   return rc;
+}
+
+int u15c_set_wait_limit(int device, unsigned long long ns)
+{
+  if (device < 0 || device >= 64) return fail(U15C_EINVAL, "device index out of range");
+  int cur = 0;
+  cudaGetDevice(&cur);
+  int rc = dev_init(device);
+  if (rc == U15C_OK) {
+    const uint64_t v = ns;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(reinterpret_cast<uint8_t*>(g_dev[device].err) + 8, &v, sizeof v,
+                     cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) rc = cuda_fail(e, "setting the wait limit");
+  }
+  cudaSetDevice(cur);
+  return rc;
+}
+
+int u15c_wait_counter(u15c_stream stream, const unsigned long long* counter,
+                      unsigned long long target)
+{
+  if (counter == nullptr) return fail(U15C_EINVAL, "wait_counter: null counter");
+  DevState* d = dev();
+  if (d == nullptr) return U15C_ECUDA;
+  if (launch_tp_wait(counter, target, d->err, ST(stream)))
+    return fail(U15C_ECUDA, "wait_counter: kernel launch failed");
+  return U15C_OK;
 }
 
 int u15c_sync(u15c_stream stream)
@@ -566,11 +627,8 @@ int u15c_attention_paged(u15c_stream stream, const void* q, const void* k_pages,
   kv.page_stride = (long)hkv * kPageTokens * kHeadDim;
   kv.head_stride = (long)kPageTokens * kHeadDim;
   kv.v_t = true;
-  if (mode == U15C_ATTN_BIDIRECTIONAL)
-    return run_attention_tc(ST(stream), q, kv, n_pages, out, hq, hkv, tq, tk, sage_ws);
-  if (sage_ws != nullptr)
-    return fail(U15C_EINVAL, "attention: Sage serves the bidirectional pass only");
-  return run_attention(ST(stream), q, kv, out, hq, hkv, tq, tk, mode, q_offset, t_index, nullptr);
+  return run_attention_tc(ST(stream), q, kv, n_pages, out, hq, hkv, tq, tk, mode, q_offset,
+                          t_index, sage_ws);
 }
 
 int u15c_sdpa(u15c_stream stream, const void* q, const void* k, const void* v, void* out, int hq,

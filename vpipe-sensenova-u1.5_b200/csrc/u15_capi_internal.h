@@ -13,7 +13,7 @@ namespace u15 {
 struct DevState {
   bool ready = false;
   int sms = 148;
-  unsigned* err = nullptr;   // device status word (watchdog codes)
+  unsigned* err = nullptr;   // device status block: watchdog code, then the wait limit
 };
 
 // Set this thread's last error and return `code`.
@@ -57,12 +57,22 @@ struct SageWs {
 size_t sage_bytes(int hq, int hkv, int tq, int tk);
 SageWs sage_split(void* ws, int hq, int hkv, int tq, int tk);
 
+// The checks every attention entry makes before it launches anything (the
+// Sage prologue included): head counts and, for the mma.sync kernel
+// (`legacy`), its GQA group limit; the rule, its t-index vector and the
+// queries' place among the keys. U15C_OK or the refusal (message set).
+int check_attention(int hq, int hkv, int tq, int tk, int mode, int q_offset,
+                    const int32_t* t_index, bool sage, bool legacy);
+// The mma.sync kernel: any K/V layout (contiguous, paged, transposed V).
 int run_attention(cudaStream_t st, const void* q, const KvView& kv, void* out, int hq, int hkv,
                   int tq, int tk, int mode, int q_offset, const int32_t* t_index, void* sage_ws);
 int run_gemm(GemmArgs& a, cudaStream_t st);
-// Bidirectional attention on the tcgen05 kernel over a paged cache with
-// transposed V pages (the model's layout); Sage when sage_ws is non-null.
+// The tcgen05 kernel over a paged cache with transposed V pages (the model's
+// layout): every rule, Sage (bidirectional) when sage_ws is non-null. A
+// block-causal call the kernel does not serve (an unaligned t-index vector,
+// more than 32768 keys) runs on the mma.sync kernel.
 int run_attention_tc(cudaStream_t st, const void* q, const KvView& kv, int n_pages, void* out,
-                     int hq, int hkv, int tq, int tk, void* sage_ws);
+                     int hq, int hkv, int tq, int tk, int mode, int q_offset,
+                     const int32_t* t_index, void* sage_ws);
 
 }  // namespace u15

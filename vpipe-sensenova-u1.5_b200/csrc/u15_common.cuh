@@ -3,10 +3,15 @@
 // sm_100a machinery (mbarrier, TMA bulk-tensor copies, tcgen05 MMA/TMEM).
 //
 // Every wait in this library is BOUNDED: a spin on an mbarrier gives up
-// after U15_WAIT_LIMIT_NS of %globaltimer time, records where it gave up in
-// the caller-visible error word and returns false, and the kernel unwinds
-// (waiting, again bounded, for its own copies and MMAs in flight) instead
-// of hanging the GPU. The host reads the word with u15c_device_status().
+// after the device's wait limit (U15_WAIT_LIMIT_NS, 2 s, unless
+// u15c_set_wait_limit set another) of %globaltimer time, records where it
+// gave up in the caller-visible error word and returns false, and the
+// kernel unwinds (waiting, again bounded, for its own copies and MMAs in
+// flight) instead of hanging the GPU. The host reads the word with
+// u15c_device_status().
+//
+// The status block of a device is 16 bytes: word 0 the first error code,
+// bytes 8-15 the wait limit in ns (0 = U15_WAIT_LIMIT_NS).
 #pragma once
 
 #include <cuda.h>
@@ -35,6 +40,15 @@ enum DevErr : unsigned {
 __device__ __forceinline__ void dev_fail(unsigned* err, unsigned code)
 {
   if (err != nullptr) atomicCAS(err, 0u, code);
+}
+
+// The wait limit of the device whose status block `err` is (read once per
+// wait that outlasts its fast tries).
+__device__ __forceinline__ uint64_t wait_limit_ns(const unsigned* err)
+{
+  if (err == nullptr) return U15_WAIT_LIMIT_NS;
+  const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(err + 2);
+  return v != 0 ? v : U15_WAIT_LIMIT_NS;
 }
 
 // ---------------------------------------------------------------------
@@ -197,11 +211,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
 #pragma unroll 1
   for (int i = 0; i < 128; ++i)
     if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), lim = wait_limit_ns(err);
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > U15_WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > lim) {
       dev_fail(err, code);
       return false;
     }
@@ -213,12 +227,12 @@ __device__ __forceinline__ bool wait_counter_sys(const unsigned long long* p,
                                                  unsigned code)
 {
   if (ld_acquire_sys(p) >= target) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), lim = wait_limit_ns(err);
 #pragma unroll 1
   while (true) {
     __nanosleep(64);
     if (ld_acquire_sys(p) >= target) return true;
-    if (globaltimer() - t0 > U15_WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > lim) {
       dev_fail(err, code);
       return false;
     }
@@ -405,11 +419,11 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
 #pragma unroll 1
   for (int i = 0; i < 128; ++i)
     if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), lim = wait_limit_ns(err);
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (globaltimer() - t0 > U15_WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > lim) {
       dev_fail(err, code);
       return false;
     }

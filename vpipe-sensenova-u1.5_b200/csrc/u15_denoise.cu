@@ -15,6 +15,10 @@
 #include "u15_capi_internal.h"
 #include "u15_common.cuh"
 
+#include <algorithm>
+#include <cmath>
+#include <random>
+
 namespace {
 
 constexpr int kRedBlocks = 256;   // fixed partial count: deterministic order
@@ -277,6 +281,42 @@ int u15c_unpatchify(u15c_stream stream, const void* rows, float* img, int H, int
   unpatchify_kernel<<<nb(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(rows), img, W, W / kTok, n);
   return cudaGetLastError() == cudaSuccess ? U15C_OK : fail(U15C_ECUDA, "unpatchify: launch failed");
+}
+
+
+// The start image of a render (Generator::generate, src/u15-generator.cc:394-417):
+// pixel space, channel-last [H][W][3], one draw per value in that order from
+// std::mt19937_64(seed) through std::normal_distribution<float>(0, 1), each
+// scaled in double by the resolution's noise scale and rounded to float --
+// the reference's own engine and distribution, so the image is the
+// reference's for the same seed wherever the C++ standard library is the
+// same (the distribution's algorithm is the library's choice).
+int u15c_init_noise(uint64_t seed, double noise_scale, float* out, long n)
+{
+  if (out == nullptr || n < 0) return u15::fail(U15C_EINVAL, "init_noise: bad output");
+  std::mt19937_64 rng(seed);
+  std::normal_distribution<float> nd(0.0f, 1.0f);
+  for (long i = 0; i < n; ++i) out[i] = (float)(noise_scale * nd(rng));
+  return U15C_OK;
+}
+
+// GenConfig::init_noise_scale (src/u15-config.cc:106-122): sqrt(L / base)
+// times noise_scale for the resolution-dependent modes (its square root
+// for dynamic_sqrt), noise_scale itself otherwise; capped at max_value.
+int u15c_init_noise_scale(int image_tokens, int mode, double noise_scale, double max_value,
+                          int base_seq_len, double* out)
+{
+  if (out == nullptr || image_tokens < 0 || mode < 0 || mode > 2)
+    return u15::fail(U15C_EINVAL, "init_noise_scale: bad argument");
+  if (mode == U15C_NOISE_CONSTANT) {
+    *out = std::min(noise_scale, max_value);
+    return U15C_OK;
+  }
+  const double base = (double)(base_seq_len > 0 ? base_seq_len : 64);
+  double v = std::sqrt((double)image_tokens / base) * noise_scale;
+  if (mode == U15C_NOISE_DYNAMIC_SQRT) v = std::sqrt(v);
+  *out = std::min(v, max_value);
+  return U15C_OK;
 }
 
 }  // extern "C"

@@ -135,14 +135,16 @@ struct AttnArgs {
   const int8_t* q8 = nullptr;   // [hq][tq][128]
   const int8_t* k8 = nullptr;   // [hkv][tk_pad][128]
   const float* sq = nullptr;    // [hq][ceil(tq/64)]
-  const float* sk = nullptr;    // [hkv][ceil(tk/64)]
+  const float* sk = nullptr;    // [hkv][2 * ceil(tk/64)]: one per 32-key block
   unsigned* dev_err = nullptr;
 };
 
 int attention(const AttnArgs& a, cudaStream_t st, std::string* err);
 
-// The tcgen05 bidirectional attention (u15_attn_tc.cu) over the paged cache:
-// K pages [n_pages][hkv][64][128], V pages transposed [n_pages][hkv][128][64].
+// The tcgen05 attention (u15_attn_tc.cu) over the paged cache: K pages
+// [n_pages][hkv][64][128], V pages transposed [n_pages][hkv][128][64]; the
+// bidirectional rule (bf16 or Sage int8 QK) and the causal / block-causal
+// prefill rules (bf16).
 struct TcAttnArgs {
   const void* q = nullptr;          // [hq][tq][128] bf16
   const void* k_pages = nullptr;
@@ -151,7 +153,10 @@ struct TcAttnArgs {
   int n_pages = 0;                  // pages in the pool (tensor-map extent)
   void* out = nullptr;              // [tq][hq*128] bf16
   int hq = 0, hkv = 0, tq = 0, tk = 0;
-  // Sage int8 QK (from sage_prepare): q8 [hq][tq][128], k8 [hkv][nkb*64][128]
+  int mode = 0;                     // 0 bidirectional, 1 causal, 2 block-causal
+  int q_offset = 0;                 // the queries' first position among the keys
+  const int32_t* t_index = nullptr; // block-causal: device [tk], 16-byte aligned
+  // Sage int8 QK (from sage_prepare): q8 [hq][tq][128], k8 [hkv][npg*64][128]
   const int8_t* q8 = nullptr;
   const int8_t* k8 = nullptr;
   const float* sq = nullptr;
@@ -159,6 +164,10 @@ struct TcAttnArgs {
   unsigned* dev_err = nullptr;
 };
 int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err);
+// Whether the tcgen05 kernel serves this rule (block-causal: a 16-byte
+// aligned t-index vector and at most 32768 keys); the callers route the
+// rest to the mma.sync kernel.
+bool attention_tc_serves(int mode, int tk, const int32_t* t_index);
 
 // A cached 2-D TMA map over a row-major [rows][cols] tensor (elsize 2 = bf16,
 // 1 = int8): box of 128 bytes x box_rows, 128-byte swizzle, zero fill.
@@ -166,7 +175,8 @@ int make_tma_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols,
                 uint32_t box_rows, int elsize, std::string* err);
 
 // Sage prologue: K smoothing (mean over tk keys per kv head and channel),
-// per-64-row block int8 quantisation of Q and of the smoothed K.
+// int8 quantisation of Q per 64-row block and of the smoothed K per 32-key
+// block (the reference's bq = 64, bk = 32).
 int sage_prepare(const void* q, const KvView& kv, int hq, int hkv, int tq, int tk, int8_t* q8,
                  int8_t* k8, float* sq, float* sk, float* kmean, cudaStream_t st,
                  std::string* err);

@@ -134,6 +134,8 @@ struct u15c_model {
   unsigned long long tp_done_target = 0;
   unsigned flags = 0;
   int device = 0;
+  // layers [0, sage_dense_layers) keep the bf16 attention under U15C_FWD_SAGE
+  int sage_dense_layers = 0;
   std::vector<LayerW> layers;
   bf16* final_norm = nullptr;   // [E][H]
   size_t weight_bytes = 0;
@@ -356,6 +358,9 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x_all, int M,
   const LayerW& L = m->layers[li];
   const int E = c.n_experts, H = c.hidden, I = c.inter;
   const bool i8 = (flags & U15C_FWD_INT8) != 0;
+  // the Sage tier leaves a prefix of the stack on the bf16 attention
+  // (sdpa_steel's `sage_layer >= dense_layers`, src/u15-metal-ops.cc:852-855)
+  if (li < m->sage_dense_layers) flags &= ~U15C_FWD_SAGE;
   if (i8 && L.qkv8 == nullptr)
     return fail(U15C_EINVAL, "W8A8 requested but the model has no int8 twins "
                              "(create with U15C_MODEL_INT8 and call u15c_model_finalize)");
@@ -502,15 +507,16 @@ int layer_impl(u15c_model* m, cudaStream_t st, int li, bf16* x_all, int M,
         }
         void* ws = !sage ? nullptr : fork ? m->side_sage[k_side] : m->sage_ws;
         rc = u15::run_attention_tc(as, qh, view, sl.kv->pages, out, c.heads, c.kv_heads, sl.n,
-                                   sl.kv_len, ws);
+                                   sl.kv_len, U15C_ATTN_BIDIRECTIONAL, 0, nullptr, ws);
         if (!rc && fork) {
           cudaEventRecord(m->side_ev[k_side], as);
           cudaStreamWaitEvent(st, m->side_ev[k_side], 0);
           ++k_side;
         }
       } else {
-        rc = u15::run_attention(st, qh, view, out, c.heads, c.kv_heads, sl.n, sl.kv_len, sl.attn,
-                                sl.kv_off, sl.t_index, nullptr);
+        // the prefill rules: the queries sit at kv_off among the keys
+        rc = u15::run_attention_tc(st, qh, view, sl.kv->pages, out, c.heads, c.kv_heads, sl.n,
+                                   sl.kv_len, sl.attn, sl.kv_off, sl.t_index, nullptr);
       }
       if (rc) return rc;
     }
@@ -654,6 +660,14 @@ int u15c_model_set_allreduce(u15c_model* m, u15c_allreduce_fn fn, void* ctx, flo
   m->ar_ctx = ctx;
   m->part = fn ? buf : nullptr;
   m->part_elems = fn ? buf_elems : 0;
+  return U15C_OK;
+}
+
+int u15c_model_set_sage_dense_layers(u15c_model* m, int n)
+{
+  if (m == nullptr) return fail(U15C_EINVAL, "null model");
+  if (n < 0) return fail(U15C_EINVAL, "sage_dense_layers must be non-negative");
+  m->sage_dense_layers = n;
   return U15C_OK;
 }
 

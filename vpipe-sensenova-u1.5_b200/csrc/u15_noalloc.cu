@@ -67,8 +67,9 @@ int u15c_attention_sage_static(u15c_stream stream, const void* q, const void* k,
   if (head_dim != 128) return u15::fail(U15C_EINVAL, "attention: head_dim must be 128");
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
     return u15::fail(U15C_EINVAL, "attention: null buffer");
-  if (hq <= 0 || hkv <= 0 || tq < 0 || tk < 0)
-    return u15::fail(U15C_EINVAL, "attention: head and token counts must be non-negative");
+  // every refusal comes before anything is launched or the array is touched
+  int rc = u15::check_attention(hq, hkv, tq, tk, 0, 0, nullptr, true, true);
+  if (rc) return rc;
   if (page_table == nullptr && tk > cap)
     return u15::fail(U15C_EINVAL, "attention: key length exceeds the cache capacity");
   const size_t need = u15::sage_bytes(hq, hkv, tq, tk);
@@ -79,7 +80,7 @@ int u15c_attention_sage_static(u15c_stream stream, const void* q, const void* k,
                                       " (use u15c_attention with a caller-provided workspace)");
   if (tq == 0 || tk == 0) return U15C_OK;
   void* ws = nullptr;
-  int rc = static_workspace(&ws);
+  rc = static_workspace(&ws);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const u15::KvView kv =

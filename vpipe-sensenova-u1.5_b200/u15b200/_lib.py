@@ -25,6 +25,7 @@ FWD_INT8, FWD_SAGE = 1, 2
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 CFG_NONE, CFG_IMG, CFG_UNC, CFG_BOTH = 0, 1, 2, 3
 NORM_NONE, NORM_GLOBAL, NORM_CHANNEL, NORM_ZERO_STAR = 0, 1, 2, 3
+NOISE_CONSTANT, NOISE_RESOLUTION, NOISE_DYNAMIC_SQRT = 0, 1, 2
 TENSORS = ["input_layernorm", "post_attention_layernorm", "q_proj", "k_proj", "v_proj",
            "o_proj", "q_norm", "k_norm", "q_norm_hw", "k_norm_hw", "gate_proj", "up_proj",
            "down_proj", "final_norm"]
@@ -70,6 +71,11 @@ SIGNATURES = {
     "u15c_init": (ip, [ip, C.c_uint]),
     "u15c_device_status": (ip, [ip, C.POINTER(C.c_uint)]),
     "u15c_sync": (ip, [vp]),
+    "u15c_set_wait_limit": (ip, [ip, C.c_ulonglong]),
+    "u15c_init_noise": (ip, [C.c_uint64, C.c_double, vp, C.c_long]),
+    "u15c_init_noise_scale": (ip, [ip, ip, C.c_double, C.c_double, ip,
+                                   C.POINTER(C.c_double)]),
+    "u15c_wait_counter": (ip, [vp, vp, C.c_ulonglong]),
     "u15c_linear_bf16": (ip, [vp, vp, vp, vp, vp, ip, ip, ip]),
     "u15c_mot_linear_bf16": (ip, [vp, vp, vp, ip, i32p, i32p, ip, ip, vp, vp, vp, ip, ip, ip]),
     "u15c_quant_rows_i8": (ip, [vp, vp, vp, vp, ip, ip]),
@@ -127,6 +133,7 @@ SIGNATURES = {
     "u15c_model_destroy": (None, [vp]),
     "u15c_model_create_tp": (ip, [C.POINTER(Config), C.c_uint, ip, ip, C.POINTER(vp)]),
     "u15c_model_tp": (ip, [vp, i32p, i32p]),
+    "u15c_model_set_sage_dense_layers": (ip, [vp, ip]),
     "u15c_model_set_allreduce": (ip, [vp, ALLREDUCE_FN, vp, vp, C.c_long]),
     "u15c_model_tp_export": (ip, [vp, ip, vp]),
     "u15c_model_tp_import": (ip, [vp, vp]),

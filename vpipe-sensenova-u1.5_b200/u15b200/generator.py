@@ -32,7 +32,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
-from ._lib import check, lib
+from ._lib import U15Error, check, lib
 from .ops import CudaOps, _p, _stream
 
 PIX = 32   # pixels per LLM token side (src/u15-config.h:23-28)
@@ -270,15 +270,51 @@ class Generator:
         th_tw = self._geom
         b.pos = [torch.from_numpy(a).cuda() for a in image_positions(int(b.t.max()) + 1, *th_tw)]
 
+    @staticmethod
+    def noise_scale(image_tokens: int, mode: int = L.NOISE_RESOLUTION, scale: float = 1.0,
+                    max_value: float = 16.0, base: int = 64) -> float:
+        """GenConfig::init_noise_scale (src/u15-config.cc:106-122), the
+        reference's defaults: sqrt(L / 64), capped at 16."""
+        out = C.c_double()
+        check(lib().u15c_init_noise_scale(image_tokens, mode, scale, max_value, base,
+                                          C.byref(out)))
+        return out.value
+
+    @staticmethod
+    def initial_image(H: int, W: int, seed: int, noise_scale: float, init_noise=None,
+                      init_noise_path: str = None) -> torch.Tensor:
+        """The start image on the device (src/u15-generator.cc:394-417): the
+        injected noise (a tensor, or a file of H*W*3 raw f32 values,
+        channel-last), or the seeded draw of u15c_init_noise."""
+        n = H * W * 3
+        if init_noise_path:
+            try:
+                with open(init_noise_path, "rb") as f:
+                    raw = f.read(n * 4 + 1)
+            except OSError as e:
+                raise U15Error(L.EINVAL, f"cannot read init_noise {init_noise_path}") from e
+            if len(raw) < n * 4:
+                raise U15Error(L.EINVAL, f"init_noise is the wrong size: want {n} f32")
+            host = np.frombuffer(raw[:n * 4], np.float32).copy()
+        elif init_noise is not None:
+            return init_noise.clone().reshape(H, W, 3).float().cuda()
+        else:
+            host = np.empty(n, np.float32)
+            check(lib().u15c_init_noise(seed, noise_scale, C.c_void_p(host.ctypes.data), n))
+        return torch.from_numpy(host).reshape(H, W, 3).cuda()
+
     def generate(self, branches: list, H: int, W: int, steps: int = 20, shift: float = 3.0,
                  cfg: float = 4.0, icfg: float = 1.0, cfg_norm: int = L.NORM_NONE,
-                 t_eps: float = 0.05, seed: int = 0, noise_scale: float = 1.0,
+                 t_eps: float = 0.05, seed: int = 0, noise_scale: float = None,
                  form: int = None, i_img: int = -1, i_unc: int = -1,
                  cfg_interval=(0.0, 1.0), int8: bool = False, sage: bool = False,
-                 init_noise: torch.Tensor = None, step_callback=None,
-                 noise_scale_max: float = 16.0):
+                 init_noise: torch.Tensor = None, init_noise_path: str = None,
+                 step_callback=None, noise_scale_max: float = 16.0):
         """Run the loop; returns the final [H][W][3] f32 image (device).
-        `branches` are already ordered cond, [img_cond], [uncond]."""
+        `branches` are already ordered cond, [img_cond], [uncond]. The start
+        image is the reference's seeded draw scaled by the resolution's noise
+        scale (noise_scale None: GenConfig::init_noise_scale of the image's
+        token count), or the injected init_noise / init_noise_path."""
         th, tw = H // PIX, W // PIX
         Ltok = th * tw
         self._geom = (th, tw)
@@ -294,11 +330,9 @@ class Generator:
         if form is None:
             form = {(-1, -1): L.CFG_NONE}.get((i_img, i_unc), L.CFG_NONE)
         n = H * W * 3
-        if init_noise is not None:
-            img = init_noise.clone().reshape(H, W, 3).float().cuda()
-        else:
-            gen = torch.Generator(device="cuda").manual_seed(seed)
-            img = torch.randn(H, W, 3, device="cuda", generator=gen) * noise_scale
+        if noise_scale is None:
+            noise_scale = self.noise_scale(Ltok, max_value=noise_scale_max)
+        img = self.initial_image(H, W, seed, noise_scale, init_noise, init_noise_path)
         ts = time_schedule(steps, shift)
         emb = torch.empty(Ltok, self.hidden, device="cuda", dtype=torch.bfloat16)
         # the noise-scale embedder sees the scale as a ratio of its maximum

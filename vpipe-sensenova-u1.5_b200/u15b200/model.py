@@ -111,6 +111,11 @@ class Model:
     def finalize(self) -> None:
         check(lib().u15c_model_finalize(self.h, _stream()))
 
+    def set_sage_dense_layers(self, n: int) -> None:
+        """Sage's `dense_layers`: with sage=True, layers [0, n) keep the bf16
+        attention (src/u15-metal-ops.cc:852-855)."""
+        check(lib().u15c_model_set_sage_dense_layers(self.h, n))
+
     def weight_bytes(self) -> int:
         return lib().u15c_model_weight_bytes(self.h)
 
