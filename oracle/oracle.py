@@ -206,10 +206,12 @@ def sage_attention(q, k, v, tk=None, bq=64, bk=64):
 
 
 def mot_layer(x, segments, experts, dims, pos_t, pos_h, pos_w, k_prefix=None,
-              v_prefix=None, mode=BIDIR, t_index=None, int8=False, sage=False):
+              v_prefix=None, mode=BIDIR, t_index=None, int8=False, sage=False,
+              bf16_buffers=False):
     """The joint MoT layer. segments: list of (start, end, expert_id).
     int8: every projection under the W8A8 rule; sage: the bidirectional
-    attention as Sage int8 QK (64-row / 32-key blocks).
+    attention as Sage int8 QK (64-row / 32-key blocks); bf16_buffers: the
+    activations rounded to bf16 wherever the reference's layer stores them.
     experts: list of two dicts keyed by EXPERT_KEYS (fp32 arrays).
     dims: dict(hidden, heads, kv_heads, head_dim, inter, eps, theta_t, theta_hw).
     Returns (out [T][H], k_new [hkv][T][hd], v_new [hkv][T][hd])."""
@@ -235,7 +237,7 @@ def mot_layer(x, segments, experts, dims, pos_t, pos_h, pos_w, k_prefix=None,
     hkv, hd = dims["kv_heads"], dims["head_dim"]
     kn = np.empty((hkv, T, hd), np.float32)
     vn = np.empty((hkv, T, hd), np.float32)
-    flags = (1 if int8 else 0) | (2 if sage else 0)
+    flags = (1 if int8 else 0) | (2 if sage else 0) | (4 if bf16_buffers else 0)
     lib().orc_mot_layer_ex(_fp(x), T, len(segments), _ip(off), _ip(ex), E, C.byref(D),
                            _ip(pt), _ip(ph), _ip(pw), npre, _fp(kp), _fp(vp), mode,
                            _ip(ti), flags, _fp(out), _fp(kn), _fp(vn))

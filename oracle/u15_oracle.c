@@ -255,6 +255,14 @@ static float bf16_rne(float v)
   return v;
 }
 
+/* With `on`, round a buffer to bf16 in place (the reference's activation
+ * buffers are bf16 SharedBuffers). */
+static void store_bf16(float* a, long n, int on)
+{
+  if (!on) return;
+  for (long i = 0; i < n; ++i) a[i] = bf16_rne(a[i]);
+}
+
 /* One projection of the layer: y[n][N] = x[n][K] w[N][K]^T, in fp32 with
  * double accumulation (orc_linear), or under the W8A8 rule. The int8 tier
  * quantizes the activation buffer the GEMM reads, which the reference keeps
@@ -305,6 +313,7 @@ void orc_mot_layer_ex(const float* x, long T, int nseg, const int* seg_off,
                       int flags, float* out, float* k_new, float* v_new)
 {
   const int i8 = (flags & ORC_LAYER_W8A8) != 0;
+  const int bf = (flags & ORC_LAYER_BF16) != 0;
   const long H = d->hidden, NH = d->heads, KV = d->kv_heads,
              HD = d->head_dim, I = d->inter;
   const float eps = (float)d->eps;
@@ -335,19 +344,27 @@ void orc_mot_layer_ex(const float* x, long T, int nseg, const int* seg_off,
     const orc_expert* w = &E[seg_expert[s]];
     orc_rms_norm(x + r0 * H, w->input_layernorm, eps, n, H,
                  normed + r0 * H);
+    store_bf16(normed + r0 * H, n * H, bf);
     layer_linear(normed + r0 * H, w->q_proj, n, H, NH * HD, q + r0 * NH * HD,
                  i8);
     layer_linear(normed + r0 * H, w->k_proj, n, H, KV * HD, kk + r0 * KV * HD,
                  i8);
     layer_linear(normed + r0 * H, w->v_proj, n, H, KV * HD, vv + r0 * KV * HD,
                  i8);
+    store_bf16(q + r0 * NH * HD, n * NH * HD, bf);
+    store_bf16(kk + r0 * KV * HD, n * KV * HD, bf);
+    store_bf16(vv + r0 * KV * HD, n * KV * HD, bf);
     orc_split_qk_norm(q + r0 * NH * HD, w->q_norm, w->q_norm_hw, NH, n, HD,
                       eps);
     orc_split_qk_norm(kk + r0 * KV * HD, w->k_norm, w->k_norm_hw, KV, n, HD,
                       eps);
   }
+  store_bf16(q, T * NH * HD, bf);
+  store_bf16(kk, T * KV * HD, bf);
   orc_split_rope(q, ctab, stab, NH, T, HD, d_t, d_h);
   orc_split_rope(kk, ctab, stab, KV, T, HD, d_t, d_h);
+  store_bf16(q, T * NH * HD, bf);
+  store_bf16(kk, T * KV * HD, bf);
 
   /* head-major q; the cache holds [prefix || block] per kv head */
   for (long t = 0; t < T; ++t)
@@ -381,6 +398,7 @@ void orc_mot_layer_ex(const float* x, long T, int nseg, const int* seg_off,
   else
     orc_attention(qh, kc, vc, NH, KV, T, TK, HD, TK, mode, n_prefix, t_index,
                   att);
+  store_bf16(att, T * NH * HD, bf);
 
   /* o_proj + residual, then the MLP half, per segment */
   for (int s = 0; s < nseg; ++s) {
@@ -389,14 +407,22 @@ void orc_mot_layer_ex(const float* x, long T, int nseg, const int* seg_off,
     const orc_expert* w = &E[seg_expert[s]];
     layer_linear(att + r0 * NH * HD, w->o_proj, n, NH * HD, H, proj + r0 * H,
                  i8);
+    store_bf16(proj + r0 * H, n * H, bf);
     for (long i = 0; i < n * H; ++i) proj[r0 * H + i] += x[r0 * H + i];
+    store_bf16(proj + r0 * H, n * H, bf);
     orc_rms_norm(proj + r0 * H, w->post_attention_layernorm, eps, n, H,
                  normed + r0 * H);
+    store_bf16(normed + r0 * H, n * H, bf);
     layer_linear(normed + r0 * H, w->gate_proj, n, H, I, g + r0 * I, i8);
     layer_linear(normed + r0 * H, w->up_proj, n, H, I, u + r0 * I, i8);
+    store_bf16(g + r0 * I, n * I, bf);
+    store_bf16(u + r0 * I, n * I, bf);
     orc_swiglu(g + r0 * I, u + r0 * I, g + r0 * I, n * I);
+    store_bf16(g + r0 * I, n * I, bf);
     layer_linear(g + r0 * I, w->down_proj, n, I, H, out + r0 * H, i8);
+    store_bf16(out + r0 * H, n * H, bf);
     for (long i = 0; i < n * H; ++i) out[r0 * H + i] += proj[r0 * H + i];
+    store_bf16(out + r0 * H, n * H, bf);
   }
 
   free(normed); free(q); free(kk); free(vv); free(qh); free(kc); free(vc);

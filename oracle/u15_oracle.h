@@ -88,9 +88,15 @@ void orc_mot_layer(const float* x, long tokens, int nseg, const int* seg_off,
  *                 accumulators, the fp32 dequant) -- the i8_gemm tier;
  * ORC_LAYER_SAGE  the bidirectional attention through orc_sage_attention
  *                 with the reference's Sage tiles (64 query rows, 32 keys)
- *                 -- the sage_attn tier; the masked rules stay exact. */
+ *                 -- the sage_attn tier; the masked rules stay exact;
+ * ORC_LAYER_BF16  every activation buffer of the reference's layer_step_
+ *                 (src/u15-backbone.cc:173-257: _normed, _q/_k/_v after the
+ *                 projection, the split norm and the rope, _attn, _proj, x
+ *                 after each add, _gate/_up/_ff) rounded to bf16 where the
+ *                 reference stores it, instead of u15-ref's fp32 throughout. */
 #define ORC_LAYER_W8A8 1
 #define ORC_LAYER_SAGE 2
+#define ORC_LAYER_BF16 4
 void orc_mot_layer_ex(const float* x, long tokens, int nseg, const int* seg_off,
                       const int* seg_expert, const orc_expert* experts,
                       const orc_dims* d, const int* pos_t, const int* pos_h,

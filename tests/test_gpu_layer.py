@@ -387,11 +387,24 @@ def test_42_layer_drift_c1_width():
     m.close()
 
 
+# The W8A8 layer's bar against its CPU restatement. Int8 codes move with any
+# bf16-level change of a quantizer's input (a value within one bf16 ulp of a
+# code boundary lands on the other side), and a moved code changes its
+# product by a whole step, so two correct W8A8 layers that round a single
+# intermediate differently already differ by ~2.8e-2 of the layer's update at
+# full width (measured on the restatement: bf16- vs f32-rounded activations).
+# The int32 accumulators themselves are bit-exact (tests/test_gpu_gemm.py);
+# the layer is held to 3e-2 and must sit closer to the W8A8 restatement than
+# to the bf16 one (it carries the same quantization pattern).
+W8A8_LAYER_BAR = 3e-2
+
+
 @pytest.mark.parametrize("int8", [False, True], ids=["bf16", "w8a8"])
 def test_full_width_c1_layer(int8):
     """BASELINE config 1 at full width (one layer, both experts); the W8A8
-    layer against the oracle's W8A8 layer (BASELINE config 3's rule on every
-    projection) at the same bars."""
+    layer against the restatement's W8A8 layer (BASELINE config 3's rule on
+    every projection, the activations rounded to bf16 where the reference
+    stores them)."""
     cfg = dict(n_layers=1, hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=12288,
                n_experts=2)
     m, W = build(cfg, 70, int8=int8)
@@ -404,8 +417,15 @@ def test_full_width_c1_layer(int8):
     xd = dev_bf16(x)
     m.layer_forward(0, xd, kv, 0, T, *(dev_i32(p) for p in pos), segments=segs, int8=int8)
     torch.cuda.synchronize()
-    ref, _, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos, int8=int8)
-    check_layer(host(xd), x, ref, delta_bar=2e-2)
+    out = host(xd)
+    if not int8:
+        ref, _, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos)
+        check_layer(out, x, ref, delta_bar=2e-2)
+    else:
+        ref, _, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos, int8=True, bf16_buffers=True)
+        dense, _, _ = O.mot_layer(x, segs, W[0], dims_of(cfg), *pos, bf16_buffers=True)
+        check_layer(out, x, ref, bar=W8A8_LAYER_BAR, delta_bar=W8A8_LAYER_BAR)
+        assert rel_l2(out - x, ref - x) < 0.8 * rel_l2(out - x, dense - x)
     m.close()
 
 

@@ -89,6 +89,8 @@ constexpr int kKBytes = kBlk * 256;             // [2 dims blocks][128 keys][128
 constexpr int kVBytes = 128 * kBlk * 2;         // [2 key blocks][128 dims][128 B]
 // block-causal: per key block the t range (min, max); tk <= kMaxBlk * 128
 constexpr int kMaxBlk = 256;
+// the exponential form a launch takes unless U15_ATTN_EXP says otherwise
+constexpr int kDefaultExp = 0;
 constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256 + 2 * kMaxBlk * 4 + 64;
 
 struct TcAttnP {
@@ -127,6 +129,18 @@ __device__ __forceinline__ float ex2(float x)
 {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x of both halves of a bf16 pair on the MUFU unit (PTX
+// ex2.approx.ftz.bf16x2): one instruction for two exponentials. The input
+// pair is x rounded to bf16 (the rounding moves a result by at most
+// 2^-9 * |x| * ln 2 relative, and bf16's 8-bit exponent keeps every
+// exponential down to 2^-126 without flushing); the results are bf16.
+__device__ __forceinline__ uint32_t ex2_bf2(uint32_t x)
+{
+  uint32_t y;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
@@ -180,7 +194,7 @@ struct MaskPlan {
   int tlo[2], thi[2];
 };
 
-template <bool SAGE, bool EMU, int MODE>
+template <bool SAGE, int EXPM, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
@@ -207,9 +221,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* blk_thi = blk_tlo + kMaxBlk;
 
   const int w = (int)warp_id();
-  const int h = blockIdx.y;
+  // bidirectional: grid (query blocks, heads), the query blocks of a head
+  // side by side (they share its K/V in L2); masked rules: grid (heads,
+  // query blocks) with the last query block first -- the longest CTAs start
+  // first, so the short ones fill the tail
+  const int h = MODE == 0 ? (int)blockIdx.y : (int)blockIdx.x;
+  const int qb = MODE == 0 ? (int)blockIdx.x : (int)(gridDim.y - 1 - blockIdx.y);
   const int hk = h / p.G;
-  const int q0 = blockIdx.x * 2 * kTile;
+  const int q0 = qb * 2 * kTile;
   const int n_all = (p.tk + kBlk - 1) / kBlk;
   const int n_pg = (p.tk + 63) / 64;
 
@@ -585,13 +604,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
-          // EMU: every fourth pair on the FMA pipe, interleaved with the MUFU
-          // ones (i is a constant after unrolling); the Sage instantiation
-          const bool fma_pipe = EMU && (i & 3) == 3;
-          const float a = fma_pipe ? ex2_fma(x0) : ex2(x0);
-          const float b = fma_pipe ? ex2_fma(x1) : ex2(x1);
-          rs[i & 3] += a + b;
-          pk[i] = pack_bf2(a, b);
+          if constexpr (EXPM == 2) {
+            // both exponentials of the pair in one MUFU instruction, in bf16:
+            // P's own format, and the row sum adds the very values P.V uses
+            pk[i] = ex2_bf2(pack_bf2(x0, x1));
+            rs[i & 3] += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xFFFF0000u);
+          } else {
+            // EXPM 1: every fourth pair on the FMA pipe, interleaved with the
+            // MUFU ones (i is a constant after unrolling)
+            const bool fma_pipe = EXPM == 1 && (i & 3) == 3;
+            const float a = fma_pipe ? ex2_fma(x0) : ex2(x0);
+            const float b = fma_pipe ? ex2_fma(x1) : ex2(x1);
+            rs[i & 3] += a + b;
+            pk[i] = pack_bf2(a, b);
+          }
         }
         // P chunk c -> columns [16c, 16c+16), whose scores were all read
         tmem_st16(tS + 16 * c, pk);
@@ -703,25 +729,26 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
     if (make_tma_2d(&mk, a.k_pages, (uint64_t)a.n_pages * a.hkv * 64, 128, 64, 2, err)) return 2;
   }
   if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, 64, 128, 2, err)) return 2;
-  // Every exponential on the MUFU: a quarter of them on the FMA pipe measured
-  // 5-10 % slower for bf16 and 4 % slower for Sage (U15_SAGE_EMU=1 selects
-  // that form of the Sage kernel, for A/B checks).
-  static std::atomic<uint64_t> set_attr[5];
-  const dim3 grid((a.tq + 2 * kTile - 1) / (2 * kTile), a.hq);
-  const char* emu_env = std::getenv("U15_SAGE_EMU");
-  const bool emu = emu_env != nullptr && *emu_env == '1';
-  auto k = attn_tc_kernel<false, false, 0>;
-  int which = 0;
-  if (sage) {
-    k = emu ? attn_tc_kernel<true, true, 0> : attn_tc_kernel<true, false, 0>;
-    which = emu ? 1 : 2;
-  } else if (a.mode == 1) {
-    k = attn_tc_kernel<false, false, 1>;
-    which = 3;
-  } else if (a.mode == 2) {
-    k = attn_tc_kernel<false, false, 2>;
-    which = 4;
-  }
+  // The exponentials (U15_ATTN_EXP, read per launch for A/B checks): 0 every
+  // one a float ex2 on the MUFU; 1 a quarter of them on the FMA pipe (5-10 %
+  // slower for bf16, 4 % for Sage, measured); 2 two bf16 exponentials per
+  // MUFU instruction.
+  static std::atomic<uint64_t> set_attr[15];
+  const int nqblk = (a.tq + 2 * kTile - 1) / (2 * kTile);
+  const dim3 grid = a.mode == 0 ? dim3(nqblk, a.hq) : dim3(a.hq, nqblk);
+  const char* exp_env = std::getenv("U15_ATTN_EXP");
+  const int expm = exp_env != nullptr && *exp_env >= '0' && *exp_env <= '2' ? *exp_env - '0'
+                                                                               : kDefaultExp;
+  using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, TcAttnP);
+  static const KFn table[5][3] = {
+      {attn_tc_kernel<false, 0, 0>, attn_tc_kernel<false, 1, 0>, attn_tc_kernel<false, 2, 0>},
+      {attn_tc_kernel<true, 0, 0>, attn_tc_kernel<true, 1, 0>, attn_tc_kernel<true, 2, 0>},
+      {attn_tc_kernel<false, 0, 1>, attn_tc_kernel<false, 1, 1>, attn_tc_kernel<false, 2, 1>},
+      {attn_tc_kernel<false, 0, 2>, attn_tc_kernel<false, 1, 2>, attn_tc_kernel<false, 2, 2>},
+      {nullptr, nullptr, nullptr}};
+  const int row = sage ? 1 : (a.mode == 0 ? 0 : a.mode + 1);
+  const KFn k = table[row][expm];
+  const int which = row * 3 + expm;
   cudaError_t e = cudaSuccess;
   if (smem_attr_once(k, kSmem, set_attr[which])) {
     cudaLaunchConfig_t cfg = {};
