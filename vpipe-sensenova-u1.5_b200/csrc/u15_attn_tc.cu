@@ -132,18 +132,6 @@ __device__ __forceinline__ float ex2(float x)
   return y;
 }
 
-// 2^x of both halves of a bf16 pair on the MUFU unit (PTX
-// ex2.approx.ftz.bf16x2): one instruction for two exponentials. The input
-// pair is x rounded to bf16 (the rounding moves a result by at most
-// 2^-9 * |x| * ln 2 relative, and bf16's 8-bit exponent keeps every
-// exponential down to 2^-126 without flushing); the results are bf16.
-__device__ __forceinline__ uint32_t ex2_bf2(uint32_t x)
-{
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16])
 {
   asm volatile(
@@ -604,20 +592,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
-          if constexpr (EXPM == 2) {
-            // both exponentials of the pair in one MUFU instruction, in bf16:
-            // P's own format, and the row sum adds the very values P.V uses
-            pk[i] = ex2_bf2(pack_bf2(x0, x1));
-            rs[i & 3] += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xFFFF0000u);
-          } else {
-            // EXPM 1: every fourth pair on the FMA pipe, interleaved with the
-            // MUFU ones (i is a constant after unrolling)
-            const bool fma_pipe = EXPM == 1 && (i & 3) == 3;
-            const float a = fma_pipe ? ex2_fma(x0) : ex2(x0);
-            const float b = fma_pipe ? ex2_fma(x1) : ex2(x1);
-            rs[i & 3] += a + b;
-            pk[i] = pack_bf2(a, b);
-          }
+          // EXPM 1: every fourth pair on the FMA pipe, interleaved with the
+          // MUFU ones (i is a constant after unrolling)
+          const bool fma_pipe = EXPM == 1 && (i & 3) == 3;
+          const float a = fma_pipe ? ex2_fma(x0) : ex2(x0);
+          const float b = fma_pipe ? ex2_fma(x1) : ex2(x1);
+          rs[i & 3] += a + b;
+          pk[i] = pack_bf2(a, b);
         }
         // P chunk c -> columns [16c, 16c+16), whose scores were all read
         tmem_st16(tS + 16 * c, pk);
@@ -731,24 +712,22 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   if (make_tma_2d(&mv, a.vt_pages, (uint64_t)a.n_pages * a.hkv * 128, 64, 128, 2, err)) return 2;
   // The exponentials (U15_ATTN_EXP, read per launch for A/B checks): 0 every
   // one a float ex2 on the MUFU; 1 a quarter of them on the FMA pipe (5-10 %
-  // slower for bf16, 4 % for Sage, measured); 2 two bf16 exponentials per
-  // MUFU instruction.
-  static std::atomic<uint64_t> set_attr[15];
+  // slower for bf16, 4 % for Sage, measured).
+  static std::atomic<uint64_t> set_attr[10];
   const int nqblk = (a.tq + 2 * kTile - 1) / (2 * kTile);
   const dim3 grid = a.mode == 0 ? dim3(nqblk, a.hq) : dim3(a.hq, nqblk);
   const char* exp_env = std::getenv("U15_ATTN_EXP");
-  const int expm = exp_env != nullptr && *exp_env >= '0' && *exp_env <= '2' ? *exp_env - '0'
-                                                                               : kDefaultExp;
+  const int expm = exp_env != nullptr && (*exp_env == '0' || *exp_env == '1') ? *exp_env - '0'
+                                                                                : kDefaultExp;
   using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, TcAttnP);
-  static const KFn table[5][3] = {
-      {attn_tc_kernel<false, 0, 0>, attn_tc_kernel<false, 1, 0>, attn_tc_kernel<false, 2, 0>},
-      {attn_tc_kernel<true, 0, 0>, attn_tc_kernel<true, 1, 0>, attn_tc_kernel<true, 2, 0>},
-      {attn_tc_kernel<false, 0, 1>, attn_tc_kernel<false, 1, 1>, attn_tc_kernel<false, 2, 1>},
-      {attn_tc_kernel<false, 0, 2>, attn_tc_kernel<false, 1, 2>, attn_tc_kernel<false, 2, 2>},
-      {nullptr, nullptr, nullptr}};
+  static const KFn table[4][2] = {
+      {attn_tc_kernel<false, 0, 0>, attn_tc_kernel<false, 1, 0>},
+      {attn_tc_kernel<true, 0, 0>, attn_tc_kernel<true, 1, 0>},
+      {attn_tc_kernel<false, 0, 1>, attn_tc_kernel<false, 1, 1>},
+      {attn_tc_kernel<false, 0, 2>, attn_tc_kernel<false, 1, 2>}};
   const int row = sage ? 1 : (a.mode == 0 ? 0 : a.mode + 1);
   const KFn k = table[row][expm];
-  const int which = row * 3 + expm;
+  const int which = row * 2 + expm;
   cudaError_t e = cudaSuccess;
   if (smem_attr_once(k, kSmem, set_attr[which])) {
     cudaLaunchConfig_t cfg = {};

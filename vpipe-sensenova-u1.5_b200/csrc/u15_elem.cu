@@ -404,15 +404,18 @@ __global__ void rope_tables_pair_kernel(const int32_t* __restrict__ pt,
 // norms: [E][4][64] bf16 = q_t, q_hw, k_t, k_hw per expert.
 // ---------------------------------------------------------------------
 constexpr int kQkvWarps = 8;
+constexpr int kQkvTok = 4;       // tokens per token block (two warps a token)
 constexpr int kQkvBatch = 4;     // rows a warp loads before it computes
 constexpr int kVtPad = 130;      // bf16 per staged V row: 65 words, odd, so the
                                  // column reads of the transpose spread over banks
 
 // One launch, two kinds of block.
-// Blocks [0, T): one token each. Warp w takes heads w, w + 8, ... of the q
-// and k heads (and, for a cache with untransposed V, the v heads); the
-// token's cos / sin columns are loaded once per warp and serve all of them.
-// Blocks [T, T + nwin * nkv): one (64-token page window, v head) of a cache
+// Blocks [0, ntb): four tokens each, two warps a token. Warp w takes token
+// w / 2 of the block and its heads w % 2, w % 2 + 2, ... of the q and k heads
+// (and, for a cache with untransposed V, the v heads); the token's cos / sin
+// columns are loaded once per warp and serve all of them. (One token per
+// block spent a quarter of the kernel launching and retiring blocks.)
+// Blocks [ntb, ntb + nwin * nkv): one (64-token page window, v head) of a cache
 // whose V pages are transposed: the window's V rows are staged in shared
 // memory and written as [128 dims][64 tokens] rows, 16 bytes a thread.
 // Tokens of a window outside [0, T) (the frozen prefix, past the block) are
@@ -427,8 +430,11 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
   griddep_wait();     // launched early (PDL): the previous kernel's writes first
   const int heads = nh + 2 * nkv;
   const int l = lane_id(), w = warp_id();
-  if ((int)blockIdx.x < T) {
-    const int t = blockIdx.x;
+  const int ntb = (T + kQkvTok - 1) / kQkvTok;
+  if ((int)blockIdx.x < ntb) {
+    constexpr int kWpt = kQkvWarps / kQkvTok;   // warps per token
+    const int t = (int)blockIdx.x * kQkvTok + w / kWpt;
+    if (t >= T) return;
     const int e = expert_of(t, seg);
     const int nrow = nh + nkv + (kv.v_t ? 0 : nkv);
     const float4 c4 = *reinterpret_cast<const float4*>(cosf_ + (long)t * 128 + l * 4);
@@ -439,16 +445,16 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
     const long kv_row = page * kv.page_stride + (long)(j & 63) * 128 + l * 4;
     const __nv_bfloat16* src = qkv + (long)t * heads * 128 + l * 4;
     const int g = (l < 16 ? 0 : 64) + (l & 15) * 4;
-    for (int h0 = w; h0 < nrow; h0 += kQkvWarps * kQkvBatch) {
+    for (int h0 = w % kWpt; h0 < nrow; h0 += kWpt * kQkvBatch) {
       uint2 u[kQkvBatch];
 #pragma unroll
       for (int i = 0; i < kQkvBatch; ++i) {
-        const int h = h0 + i * kQkvWarps;
+        const int h = h0 + i * kWpt;
         if (h < nrow) u[i] = *reinterpret_cast<const uint2*>(src + (long)h * 128);
       }
 #pragma unroll
       for (int i = 0; i < kQkvBatch; ++i) {
-        const int h = h0 + i * kQkvWarps;   // warp-uniform
+        const int h = h0 + i * kWpt;   // warp-uniform
         if (h >= nrow) break;
         const float2 a = unpack_bf2(u[i].x), b = unpack_bf2(u[i].y);
         float v[4] = {a.x, a.y, b.x, b.y};
@@ -481,7 +487,7 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
   }
   // ---- transposed V: one (window, v head)
   __shared__ uint32_t tile[64 * kVtPad / 2];
-  const int vb = (int)blockIdx.x - T;
+  const int vb = (int)blockIdx.x - ntb;
   const int win = vb / nkv, hv = vb % nkv;
   const int jw = (kv_off & ~63) + win * 64;       // first cache token of the window
   const int t_lo = max(0, kv_off - jw), t_hi = min(64, kv_off + T - jw);   // valid [t_lo, t_hi)
@@ -818,8 +824,9 @@ int launch_qkv_post(const void* qkv, const void* norms, const float* c, const fl
   if (T <= 0 || nh + 2 * nkv <= 0) return 0;
   // transposed-V windows: the 64-token pages the block [kv_off, kv_off + T) touches
   const long nwin = kv.v_t ? ((kv_off & 63) + T + 63) / 64 : 0;
+  const long ntb = (T + kQkvTok - 1) / kQkvTok;
   const cudaError_t e = launch_pdl(
-      qkv_post_kernel, dim3((unsigned)(T + nwin * nkv)), dim3(kQkvWarps * 32), st,
+      qkv_post_kernel, dim3((unsigned)(ntb + nwin * nkv)), dim3(kQkvWarps * 32), st,
       static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(norms), c, s,
       static_cast<__nv_bfloat16*>(q_out), kv, T, nh, nkv, kv_off, eps, seg);
   return e == cudaSuccess ? 0 : 2;

@@ -54,6 +54,8 @@ struct Unit {
 };
 
 constexpr int kMaxUnits = 200;
+// the pair kernel's L2 policy unless U15_GEMM_L2HINT says otherwise
+constexpr int kDefaultL2Hint = 0;
 
 struct Params {
   int M, N, K;          // N: weight rows per expert (SWIGLU: 2x the output width)
@@ -62,6 +64,7 @@ struct Params {
   int group;            // tile order: units (row blocks) per group, >= 1
   int implicit_bm;      // > 0: units are implicit row blocks of this size (one segment)
   int implicit_expert;
+  int l2hint;           // 0 none; 1 B (weights) evict-first; 2 also A evict-last
   void* y;
   long ldy;             // output row stride, elements
   const __nv_bfloat16* resid;
@@ -472,6 +475,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane_id() == 0) {
       uint32_t it = 0;
       bool ok = true;
+      // the weights stream through L2 once per launch; the activations are
+      // read again by every round of the schedule
+      const uint64_t pol_b = l2_evict_first_policy(), pol_a = l2_evict_last_policy();
       for (int t = pair; t < n_tiles && ok; t += n_pairs) {
         const TileIdx ti = tile_at(p, t);
         const Unit u = unit_at(p, ti.unit);
@@ -494,8 +500,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t fb = mapa_shared(full0 + 8 * s, 0);
           mbar_arrive_expect_tx_cluster(fb, tx);
-          tma_load_2d_pair(smem_u32(sA + s * kAStageP), &tmA, kb * kBK, arow, fb);
-          tma_load_2d_pair(smem_u32(sB + s * kBStageP), mb, kb * kBK, brow, fb);
+          if (p.l2hint >= 2)
+            tma_load_2d_pair_hint(smem_u32(sA + s * kAStageP), &tmA, kb * kBK, arow, fb, pol_a);
+          else
+            tma_load_2d_pair(smem_u32(sA + s * kAStageP), &tmA, kb * kBK, arow, fb);
+          if (p.l2hint >= 1)
+            tma_load_2d_pair_hint(smem_u32(sB + s * kBStageP), mb, kb * kBK, brow, fb, pol_b);
+          else
+            tma_load_2d_pair(smem_u32(sB + s * kBStageP), mb, kb * kBK, brow, fb);
         }
       }
       // unwinding (leader): the last fill of every stage, both CTAs' halves,
@@ -1056,6 +1068,12 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
       return e != nullptr ? std::atoi(e) : 0;
     }();
     if (grp > 0 && grp < n_units) p.group = grp;
+  }
+  {
+    // U15_GEMM_L2HINT (read per launch, for A/B checks): the L2 policy of
+    // the pair kernel's operand loads
+    const char* e = std::getenv("U15_GEMM_L2HINT");
+    p.l2hint = e != nullptr ? std::atoi(e) : kDefaultL2Hint;
   }
   const int bk = a.int8 ? 128 : 64;
   p.n_kblk = (a.K + bk - 1) / bk;
