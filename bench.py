@@ -712,17 +712,20 @@ def denoise_bench(args, rank, world, dist, tp_nccl=False):
     cfg 4.0, img_cfg 1.5. The image path is the device ImagePath (patch
     embedder, timestep + noise-scale row, pixel head) with seeded weights.
 
-    Three placements (N > 1; at N = 1 only the first):
+    Four placements (N > 1; at N = 1 only the first):
       replicas    every rank runs its own seed: job steps/s = N / max-over-ranks s/step
       branches    ONE image, its three CFG branches placed round-robin over the
                   ranks, one velocity all-gather per step (NCCL)
       tensor_par  ONE image, every branch on all ranks, the model split by
                   tensor parallelism (fused row-parallel reduction over NVLink)
+      hybrid      ONE image, its branches over tensor-parallel groups of ranks
+                  (plan_groups; at 6 and 8 ranks three two-rank groups), run
+                  where the plan differs from the two above
     """
     import torch
     import u15b200
     from u15b200 import _lib as L
-    from u15b200.generator import Branch, Generator
+    from u15b200.generator import Branch, Generator, plan_groups
 
     def specs_on(seed):
         g = torch.Generator(device="cuda").manual_seed(seed)
@@ -802,6 +805,35 @@ def denoise_bench(args, rank, world, dist, tp_nccl=False):
             mt.tp_disconnect(None)
         mt.close()
         del mt
+        torch.cuda.empty_cache()
+        # one image, hybrid: the branches over tensor-parallel groups of ranks
+        # (plan_groups), where that differs from both placements above
+        plan = plan_groups(3, world)
+        sizes = [len(g.ranks) for g in plan]
+        if max(sizes) > 1 and not (len(plan) == 1 and sizes[0] == world):
+            subs = [dist.new_group(g.ranks) for g in plan]   # every rank, same order
+            mine = [i for i, g in enumerate(plan) if rank in g.ranks]
+            mh = None
+            if mine:
+                g, sub = plan[mine[0]], subs[mine[0]]
+                mh = u15b200.Model(n_layers=42, tp_rank=g.ranks.index(rank),
+                                   tp_size=len(g.ranks))
+                mh.bind_random(seed=77, std=0.02, norm_mean=1.0, norm_std=0.2)
+                for e in range(2):
+                    mh.bind(0, e, "final_norm", torch.ones(H, device="cuda"))
+                if len(g.ranks) > 1:
+                    mh.tp_connect(sub, 3 * M_TOK)
+            s_hy = run(Generator(mh, group=dist.group.WORLD, groups=plan), specs_on(5), 0)
+            out["one_image_hybrid"] = {
+                "steps_per_s": 1.0 / s_hy, "s_per_step": s_hy,
+                "groups": [{"ranks": g.ranks, "branches": g.branches} for g in plan],
+                "reduction": "fused, peer memory, within each group"}
+            torch.cuda.synchronize()
+            if mh is not None:
+                if len(plan[mine[0]].ranks) > 1:
+                    mh.tp_disconnect(subs[mine[0]])
+                mh.close()
+            dist.barrier()
     else:
         del m
     torch.cuda.empty_cache()

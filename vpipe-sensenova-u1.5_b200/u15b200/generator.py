@@ -81,26 +81,91 @@ def placement(n_branch: int, world: int) -> list[int]:
     return [b % world for b in range(n_branch)]
 
 
-def exchange_velocities(local: dict, n_branch: int, numel: int, group=None, device=None):
+# Per-layer speed-up of a tensor-parallel group of 1, 2, 4 and 8 GPUs over one
+# GPU on the 4096-token layer (the bench's `tensor_parallel` section, fused
+# reduction): the cost model of plan_groups.
+TP_SPEEDUP = {1: 1.0, 2: 1.58, 4: 1.79, 8: 1.38}
+
+
+@dataclass
+class Group:
+    ranks: list           # consecutive global ranks; tensor-parallel over them when > 1
+    branches: list        # branch indices this group runs (through forward_many)
+
+
+def plan_groups(n_branch: int, world: int, speedup: dict = None,
+                weights: list = None) -> list:
+    """Place ONE image's CFG branches over `world` ranks: disjoint groups of
+    consecutive ranks (1, 2, 4 or 8 of them, the tensor-parallel sizes the
+    model splits into), each running a run of consecutive branches, every
+    rank in at most one group. The plan minimises the step time
+    max_g(sum of its branches' weights / speedup[size]); ties go to fewer
+    ranks. world <= n_branch gives branch placement (groups of one rank);
+    e.g. 3 branches: 4 ranks keep 1 + 1 + 1, 6 and 8 ranks run three
+    two-rank groups."""
+    sp = TP_SPEEDUP if speedup is None else speedup
+    w = [1.0] * n_branch if weights is None else list(weights)
+    sizes = sorted(k for k in sp if k <= world)
+    best = None
+
+    def rec(b0, used, acc):
+        nonlocal best
+        if b0 == n_branch:
+            t = max(x[2] for x in acc)
+            key = (round(t, 9), used)
+            if best is None or key < best[0]:
+                best = (key, list(acc))
+            return
+        for b1 in range(b0 + 1, n_branch + 1):
+            load = sum(w[b0:b1])
+            for sz in sizes:
+                if used + sz > world:
+                    continue
+                acc.append((list(range(b0, b1)), sz, load / sp[sz]))
+                rec(b1, used + sz, acc)
+                acc.pop()
+
+    rec(0, 0, [])
+    groups, r0 = [], 0
+    for br, sz, _ in best[1]:
+        groups.append(Group(list(range(r0, r0 + sz)), br))
+        r0 += sz
+    return groups
+
+
+def owners_of(groups: list, n_branch: int) -> list:
+    """The rank that contributes each branch's velocity: its group's first."""
+    own = [0] * n_branch
+    for g in groups:
+        for b in g.branches:
+            own[b] = g.ranks[0]
+    return own
+
+
+def exchange_velocities(local: dict, n_branch: int, numel: int, group=None, device=None,
+                        owner: list = None):
     """All-gather per-branch velocities so every rank holds all of them.
 
     `local` maps branch index -> flat f32 tensor of `numel` elements for the
-    branches this rank ran. Each rank contributes ceil(n_branch / world)
-    slots (unused slots zero); returns a list of n_branch tensors."""
+    branches this rank contributes; `owner[b]` is the rank that contributes
+    branch b (default: round-robin placement). Each rank sends as many slots
+    as the busiest owner (unused slots zero); returns a list of n_branch
+    tensors."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    per = (n_branch + world - 1) // world
+    own = placement(n_branch, world) if owner is None else list(owner)
+    per = max(1, max(own.count(r) for r in range(world)))
     dev = device if device is not None else next(iter(local.values())).device
     send = torch.zeros(per, numel, dtype=torch.float32, device=dev)
-    mine = [b for b in range(n_branch) if b % world == rank]
+    mine = [b for b in range(n_branch) if own[b] == rank]
     for i, b in enumerate(mine):
         send[i].copy_(local[b].reshape(-1))
     recv = torch.empty(world * per, numel, dtype=torch.float32, device=dev)
     dist.all_gather_into_tensor(recv, send, group=group)
     out = [None] * n_branch
     for r in range(world):
-        owned = [b for b in range(n_branch) if b % world == r]
+        owned = [b for b in range(n_branch) if own[b] == r]
         for i, b in enumerate(owned):
             out[b] = recv[r * per + i]
     return out
@@ -237,11 +302,19 @@ class Generator:
     """Generator::generate over a u15b200.Model (both experts bound)."""
 
     def __init__(self, model, image_path=None, device: int | None = None, group=None,
-                 image_seed: int = 0):
+                 image_seed: int = 0, groups: list = None):
+        """group: the ranks that share ONE image (torch.distributed group,
+        None for a single process). groups: how that image's branches sit on
+        those ranks (plan_groups); None places the branches round-robin, one
+        rank each. A rank of a multi-rank group passes that group's
+        tensor-parallel model as `model`."""
         self.m = model
+        self.groups = groups
         # the model's device is the caller's current one (one process per GPU)
         self.ops = CudaOps(torch.cuda.current_device() if device is None else device)
-        self.hidden = model.cfg["hidden"]
+        # a rank that runs no branch of the plan holds no model (it still
+        # takes part in each step's velocity exchange)
+        self.hidden = model.cfg["hidden"] if model is not None else 4096
         if image_path is None:
             # no checkpoint here: the device image path with seeded weights
             from .image import ImagePath
@@ -323,9 +396,21 @@ class Generator:
         if self.group is not None:
             import torch.distributed as dist
             world, rank = dist.get_world_size(self.group), dist.get_rank(self.group)
-        owner = placement(len(branches), world)
+        nb = len(branches)
+        if self.groups is not None:
+            covered = sorted(b for g in self.groups for b in g.branches)
+            ranks = [r for g in self.groups for r in g.ranks]
+            if covered != list(range(nb)) or len(set(ranks)) != len(ranks) or \
+                    any(r >= world for r in ranks):
+                raise ValueError("groups must cover every branch once on distinct ranks")
+            owner = owners_of(self.groups, nb)
+            runs = [any(rank in g.ranks and bi in g.branches for g in self.groups)
+                    for bi in range(nb)]
+        else:
+            owner = placement(nb, world)
+            runs = [owner[bi] == rank for bi in range(nb)]
         for bi, b in enumerate(branches):
-            if owner[bi] == rank:
+            if runs[bi]:
                 self.prefill(b, Ltok)
         if form is None:
             form = {(-1, -1): L.CFG_NONE}.get((i_img, i_unc), L.CFG_NONE)
@@ -340,7 +425,7 @@ class Generator:
         ns_ratio = noise_scale / max(1e-9, noise_scale_max)
         # one hidden state per branch this rank runs, contiguous, so the
         # branches go through the stack together (u15c_forward_many)
-        mine = [bi for bi in range(len(branches)) if owner[bi] == rank]
+        mine = [bi for bi in range(nb) if runs[bi]]
         hstate = torch.empty(max(len(mine), 1), Ltok, self.hidden, device="cuda",
                              dtype=torch.bfloat16)
         x_pred = torch.empty(H, W, 3, device="cuda", dtype=torch.float32)
@@ -375,9 +460,11 @@ class Generator:
                     self.image.decode(hstate[i], H, W, x_pred)
                     check(lib().u15c_velocity(_stream(), _p(x_pred), _p(img), _p(b.v), n,
                                               denom))
-                    local[bi] = b.v
+                    if owner[bi] == rank:   # a group's first rank speaks for it
+                        local[bi] = b.v
             if world > 1:
-                vs = exchange_velocities(local, n_branch, n, self.group, device=img.device)
+                vs = exchange_velocities(local, n_branch, n, self.group, device=img.device,
+                                         owner=owner[:n_branch])
                 vs = [v.reshape(H, W, 3) for v in vs]
             else:
                 vs = [branches[bi].v for bi in range(n_branch)]
