@@ -53,7 +53,7 @@ WORKLOAD = ("MoT layer @4096 tok: 512 und + 3584 gen routed, frozen 320-token pr
             "bidirectional GQA 32/8x128 over 4416 keys (paged KV)")
 
 
-LONG_WINDOW_S = 2.5
+LONG_WINDOW_S = 2.5   # the sustained window's default length (--sustained-s)
 
 
 def bench_config(world):
@@ -152,6 +152,59 @@ def prefill_bench(ops, steps):
         out[name] = {"ms": ms, "tflops": 4.0 * HD * NH * pairs / ms / 1e9}
     out["kernel"] = "attn_tc_kernel<MODE 2> (tcgen05, paged KV, masked key blocks skipped)"
     return out
+
+
+def profile_case(case, steps):
+    """A small workload of one kind of kernel for ncu captures (the kernels
+    the bench times, on the bench's inputs); returns the mean ms of a step."""
+    import torch
+    import u15b200
+    ops = u15b200.CudaOps(0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    if case == "prefill":
+        t = c4_prefill()
+        T = t.size
+        npg = (T + 63) // 64
+        q = torch.randn(NH, T, HD, device="cuda", generator=g).bfloat16()
+        kp = torch.randn(npg, KV, 64, HD, device="cuda", generator=g).bfloat16()
+        vp = torch.randn(npg, KV, HD, 64, device="cuda", generator=g).bfloat16()
+        table = torch.arange(npg, dtype=torch.int32, device="cuda")
+        td = torch.from_numpy(t).cuda()
+        o = torch.empty(T, NH * HD, device="cuda").bfloat16()
+        fn = lambda: ops.attention_paged(q, kp, vp, o, NH, KV, T, T, page_table=table, mode=2,  # noqa
+                                         t_index=td)
+    elif case == "attention":
+        npg = (TK + 63) // 64
+        q = torch.randn(NH, M_TOK, HD, device="cuda", generator=g).bfloat16()
+        kp = torch.randn(npg, KV, 64, HD, device="cuda", generator=g).bfloat16()
+        vp = torch.randn(npg, KV, HD, 64, device="cuda", generator=g).bfloat16()
+        table = torch.arange(npg, dtype=torch.int32, device="cuda")
+        o = torch.empty(M_TOK, NH * HD, device="cuda").bfloat16()
+        ws = ops.sage_workspace(NH, KV, M_TOK, TK)
+        state = {"i": 0}
+
+        def fn():   # bf16 and Sage launches alternate
+            ops.attention_paged(q, kp, vp, o, NH, KV, M_TOK, TK, page_table=table,
+                                sage_ws=ws if state["i"] % 2 else None)
+            state["i"] += 1
+    else:
+        m = u15b200.Model(int8=True, n_layers=1)
+        m.bind_random(seed=1234, std=0.02, norm_mean=1.0, norm_std=0.2)
+        m.finalize()
+        kv = m.make_cache(TK)
+        for v in (False, True):
+            kv.write(0, v, torch.randn(KV, N_PRE, HD, device="cuda", generator=g).bfloat16())
+        pos = [torch.from_numpy(p).cuda() for p in positions()]
+        x = torch.randn(M_TOK, H, device="cuda", generator=g).bfloat16()
+        segs = [(0, N_UND, 0), (N_UND, M_TOK, 1)]
+        state = {"i": 0}
+
+        def fn():   # bf16 and W8A8 layers alternate
+            m.layer_forward(0, x, kv, N_PRE, TK, *pos, segments=segs, int8=state["i"] % 2 == 1)
+            state["i"] += 1
+    fn()
+    torch.cuda.synchronize()
+    return ev_time(fn, steps)
 
 
 def peaks():
@@ -434,7 +487,7 @@ def run_ours(args, rank, world, local):
 
     # ---- the same loop held for seconds: the clock a render settles at ----
     # (the burst window above is tens of ms; a denoise step streams 126 layers)
-    n_long = max(args.steps, int(np.ceil(LONG_WINDOW_S * 1e3 / ms_step)))
+    n_long = max(args.steps, int(np.ceil(args.sustained_s * 1e3 / ms_step)))
     x.copy_(x0)
     t0 = time.time()
     ms_long = timed(step, n_long) / n_long
@@ -595,7 +648,7 @@ def run_ours(args, rank, world, local):
                       "burst_clock": clk.window(*win["burst"]),
                       "note": "the burst line's loop held for >= %.1f s (same layers, same "
                               "inputs); frac against the sustained (power-capped) cuBLAS bf16 "
-                              "rate in MEASURED_PEAKS.json" % LONG_WINDOW_S},
+                              "rate in MEASURED_PEAKS.json" % args.sustained_s},
         "prefill": prefill,
         "e2e": {"value": ms_e2e / world, "unit": UNIT,
                 "h2d_bytes_per_step": M_TOK * H * 2, "d2h_bytes_per_step": M_TOK * H * 2},
@@ -852,11 +905,22 @@ def main():
                     help="timed denoise steps after one warm-up step (0: skip)")
     ap.add_argument("--image-only", action="store_true",
                     help="time only the image path of one branch (a small case for profiling)")
+    ap.add_argument("--sustained-s", type=float, default=LONG_WINDOW_S,
+                    help="length of the sustained layer window (0: --steps layers only)")
+    ap.add_argument("--case", choices=["prefill", "attention", "layer"],
+                    help="one small workload for a profiler, then exit: the C4 prefill "
+                         "attention (block-causal, tcgen05), the bidirectional attention at "
+                         "4096 x 4416 (bf16 then Sage), or --steps bf16 + W8A8 layers")
     args = ap.parse_args()
     if args.image_only:
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         print(json.dumps({"image_path": image_bench(max(1, args.steps))}))
+        return
+    if args.case:
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        print(json.dumps({"case": args.case, "ms": profile_case(args.case, max(1, args.steps))}))
         return
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))

@@ -713,12 +713,12 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   // The exponentials (U15_ATTN_EXP, read per launch for A/B checks): 0 every
   // one a float ex2 on the MUFU; 1 a quarter of them on the FMA pipe (5-10 %
   // slower for bf16, 4 % for Sage, measured).
-  static std::atomic<uint64_t> set_attr[10];
+  static std::atomic<uint64_t> set_attr[8];
   const int nqblk = (a.tq + 2 * kTile - 1) / (2 * kTile);
   const dim3 grid = a.mode == 0 ? dim3(nqblk, a.hq) : dim3(a.hq, nqblk);
   const char* exp_env = std::getenv("U15_ATTN_EXP");
-  const int expm = exp_env != nullptr && (*exp_env == '0' || *exp_env == '1') ? *exp_env - '0'
-                                                                                : kDefaultExp;
+  int expm = exp_env != nullptr ? std::atoi(exp_env) : kDefaultExp;
+  if (expm < 0 || expm > 1) expm = kDefaultExp;
   using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, TcAttnP);
   static const KFn table[4][2] = {
       {attn_tc_kernel<false, 0, 0>, attn_tc_kernel<false, 1, 0>},

@@ -1063,10 +1063,9 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   }
   p.group = n_units;
   {
-    static const int grp = [] {
-      const char* e = std::getenv("U15_GEMM_GROUP");
-      return e != nullptr ? std::atoi(e) : 0;
-    }();
+    // U15_GEMM_GROUP (read per launch, for A/B checks): row units per group
+    const char* e = std::getenv("U15_GEMM_GROUP");
+    const int grp = e != nullptr ? std::atoi(e) : 0;
     if (grp > 0 && grp < n_units) p.group = grp;
   }
   {
