@@ -77,6 +77,32 @@ def test_mot_routing(ops, segs):
         assert rel_l2(host(y), O.linear(x, w[segs[0][2]])) > 1e-2
 
 
+def test_mot_routing_many_rows(ops):
+    """A routed pass of 60000 rows over five segments (the row units come from
+    the segment table, so M has no cap), checked on rows around every segment
+    boundary and the last row against the CPU restatement; blocks of the
+    CTA-pair kernel straddle three of the boundaries; every row against
+    torch's product of the same bf16 operands."""
+    M, K, N = 60000, 256, 256
+    segs = [(0, 7000, 0), (7000, 7001, 1), (7001, 30000, 0), (30000, 41000, 1), (41000, M, 0)]
+    torch.manual_seed(16)
+    xd = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    wd = (torch.randn(2, N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.mot_linear(xd, wd, segs, y, M, K, N)
+    ops.sync()
+    rows = np.unique(np.concatenate([[b + d for b in (0, 7000, 7001, 30000, 41000) for d in
+                                      (-2, -1, 0, 1, 2)], [M - 1]]))
+    rows = rows[(rows >= 0) & (rows < M)]
+    want = np.stack([O.linear(host(xd[r:r + 1]), host(wd[[s[2] for s in segs if s[0] <= r < s[1]][0]]))[0]
+                     for r in rows])
+    assert rel_l2(host(y[torch.from_numpy(rows).cuda()]), want) < BAR
+    full = torch.empty_like(y, dtype=torch.float32)
+    for lo, hi, e in segs:
+        full[lo:hi] = xd[lo:hi].float() @ wd[e].float().t()
+    assert ((y.float() - full).norm() / full.norm()).item() < BAR
+
+
 def test_residual_epilogue_in_place(ops):
     M, K, N = 256, 1024, 512
     x = bf16_round(randn((M, K), 8))

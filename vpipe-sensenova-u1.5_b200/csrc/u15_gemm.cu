@@ -53,7 +53,6 @@ struct Unit {
   int m0, row_lo, row_hi, expert;
 };
 
-constexpr int kMaxUnits = 200;
 // the pair kernel's L2 policy unless U15_GEMM_L2HINT says otherwise
 constexpr int kDefaultL2Hint = 0;
 
@@ -62,8 +61,13 @@ struct Params {
   int n_units, n_nblk, n_kblk;
   int n_full;           // tiles before the split tail (== n_units * n_nblk when none)
   int group;            // tile order: units (row blocks) per group, >= 1
-  int implicit_bm;      // > 0: units are implicit row blocks of this size (one segment)
-  int implicit_expert;
+  // row units: a unit_bm-row block intersected with one routing segment,
+  // segment-major (segment s holds units [unit_start[s], unit_start[s + 1]))
+  int unit_bm;
+  int nseg;
+  int seg_off[kMaxSeg + 1];
+  int seg_expert[kMaxSeg];
+  int unit_start[kMaxSeg + 1];
   int l2hint;           // 0 none; 1 B (weights) evict-first; 2 also A evict-last
   void* y;
   long ldy;             // output row stride, elements
@@ -75,7 +79,6 @@ struct Params {
   int32_t* acc_dump;           // int8 debug: [M][N] raw accumulators, or null
   unsigned* err;
   TpPeers tp;           // kEpiTpReduce
-  Unit units[kMaxUnits];
 };
 
 // Tile t of a launch. Tiles [0, n_full) are full width; each tile after
@@ -105,16 +108,18 @@ __device__ __forceinline__ TileIdx tile_at(const Params& p, int t)
   return r;
 }
 
-// Row unit i: from the table, or (one routing segment) the implicit
-// block [i * bm, (i + 1) * bm) of that segment's expert, so a single-expert
-// GEMM has no limit on M.
+// Row unit i, computed from the segment table (no per-unit table, so M has
+// no limit): its segment s is the last whose first unit is <= i, its block
+// the segment's first block plus the offset, its rows the block's rows
+// inside the segment.
 __device__ __forceinline__ Unit unit_at(const Params& p, int i)
 {
-  if (p.implicit_bm > 0) {
-    const int m0 = i * p.implicit_bm;
-    return Unit{m0, m0, min(m0 + p.implicit_bm, p.M), p.implicit_expert};
-  }
-  return p.units[i];
+  int s = 0;
+#pragma unroll 1
+  for (int k = 1; k < p.nseg; ++k)
+    if (i >= p.unit_start[k]) s = k;
+  const int m0 = (p.seg_off[s] / p.unit_bm + (i - p.unit_start[s])) * p.unit_bm;
+  return Unit{m0, max(m0, p.seg_off[s]), min(m0 + p.unit_bm, p.seg_off[s + 1]), p.seg_expert[s]};
 }
 
 __host__ __device__ __forceinline__ int launch_tiles(const Params& p)
@@ -1024,36 +1029,31 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
   }
   const bool pair = tp || use_pair(a.M);   // the fused TP epilogue exists in the pair kernel
   const int bm = pair ? 256 : kBM;
+  if (nseg > kMaxSeg) {
+    *err = "gemm: at most 8 routing segments";
+    return 1;
+  }
+  // units segment-major: a block that straddles a boundary appears once per
+  // segment and each pass stores only its own rows
+  p.unit_bm = bm;
+  p.nseg = nseg;
   int n_units = 0;
-  if (nseg == 1) {
-    if (ex[0] < 0 || ex[0] >= a.n_experts) {
+  for (int s = 0; s < nseg; ++s) {
+    if (off[s + 1] < off[s]) {
+      *err = "gemm: segment offsets must be non-decreasing";
+      return 1;
+    }
+    if (ex[s] < 0 || ex[s] >= a.n_experts) {
       *err = "gemm: segment expert out of range";
       return 1;
     }
-    p.implicit_bm = bm;
-    p.implicit_expert = ex[0];
-    n_units = (a.M + bm - 1) / bm;
+    p.seg_off[s] = off[s];
+    p.seg_expert[s] = ex[s];
+    p.unit_start[s] = n_units;
+    if (off[s + 1] > off[s]) n_units += (off[s + 1] + bm - 1) / bm - off[s] / bm;
   }
-  for (int m0 = 0; nseg > 1 && m0 < a.M; m0 += bm) {
-    const int m1 = std::min(m0 + bm, a.M);
-    for (int s = 0; s < nseg; ++s) {
-      if (off[s + 1] < off[s]) {
-        *err = "gemm: segment offsets must be non-decreasing";
-        return 1;
-      }
-      if (ex[s] < 0 || ex[s] >= a.n_experts) {
-        *err = "gemm: segment expert out of range";
-        return 1;
-      }
-      const int lo = std::max(m0, off[s]), hi = std::min(m1, off[s + 1]);
-      if (lo >= hi) continue;
-      if (n_units >= kMaxUnits) {
-        *err = "gemm: too many row blocks for one launch (M too large)";
-        return 1;
-      }
-      p.units[n_units++] = Unit{m0, lo, hi, ex[s]};
-    }
-  }
+  p.seg_off[nseg] = off[nseg];
+  p.unit_start[nseg] = n_units;
   p.n_units = n_units;
   p.n_nblk = (a.N + kBN - 1) / kBN;
   p.n_full = n_units * p.n_nblk;
