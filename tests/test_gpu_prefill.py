@@ -68,3 +68,40 @@ def test_embed_tokens_bad_id_reports():
         ops.sync()
     o = host(out)
     assert (o[0] == 1).all() and (o[1] == 0).all() and (o[2] == 1).all()
+
+
+def test_c4_prefill_through_the_model():
+    """BASELINE config 4's image-conditional prefill through the backbone: 64
+    text tokens around two reference images of 1024 tokens (2116 tokens, t, h,
+    w from u15c_thw_indexes) in one block-causal pass of both layers of a
+    small-width model over the paged cache (a permuted page table), against
+    the CPU restatement layer by layer: the output and each layer's K / V."""
+    import ctypes as C
+    from u15b200 import _lib as L
+    from test_gpu_attention import c4_prefill_ids
+    from test_gpu_layer import SMALL, build, check_layer, dims_of
+
+    ids, IMG, CTX, grids = c4_prefill_ids()
+    T = ids.size
+    t, h, w = (np.zeros(T, np.int32) for _ in range(3))
+    g = np.ascontiguousarray(np.array(grids, np.int32).reshape(-1))
+    vp = lambda a: C.c_void_p(a.ctypes.data)  # noqa: E731
+    assert L.lib().u15c_thw_indexes(vp(ids), T, IMG, CTX, vp(g), 2, vp(t), vp(h), vp(w)) == 0
+    m, Wts = build(SMALL, 600)
+    x = bf16_round(randn((T, SMALL["hidden"]), 601))
+    kv = m.make_cache(T)
+    kv.set_page_table(np.random.default_rng(602).permutation((T + 63) // 64).astype(np.int32))
+    xd = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    pos = [torch.from_numpy(a).cuda() for a in (t, h, w)]
+    m.forward(xd, kv, 0, T, *pos, segments=[(0, T, 0)], attn=L.ATTN_BLOCK_CAUSAL,
+              t_index=torch.from_numpy(t).cuda())
+    torch.cuda.synchronize()
+    ref = x
+    for li in range(SMALL["n_layers"]):
+        cur = host(xd) if li == SMALL["n_layers"] - 1 else None
+        ref_in = ref
+        ref, kn, vn = O.mot_layer(ref_in, [(0, T, 0)], Wts[li], dims_of(SMALL), t, h, w,
+                                  mode=O.BLOCK_CAUSAL, t_index=t)
+        assert rel_l2(host(kv.read(li, False, T)), kn) < 1e-2, li
+        assert rel_l2(host(kv.read(li, True, T)), vn) < 1e-2, li
+    check_layer(cur, x, ref, bar=5e-2, delta_bar=5e-2)
