@@ -23,12 +23,22 @@
 //               earlier P.V of the tile has finished: the softmax may
 //               rescale O_t and overwrite the S columns with P without
 //               another wait.
-//   warps 2-3   idle (they complete the first warpgroup)
+//               (with the key-split softmax: warp 1 + t issues tile t's
+//               MMAs alone, the same sequence)
+//   warps 2-3   idle (they complete the first warpgroup; warp 2 is tile 1's
+//               issuer in the key-split form)
 //   warps 4-11  softmax, four warps per tile, one row per thread: the whole
 //               128-score row in registers, base-2 online softmax with lazy
 //               rescale (O is rescaled only when a row max grows by more
 //               than 2^8), P as bf16 pairs into TMEM, final O / l to global
-//               token-major [tq][hq*128]
+//               token-major [tq][hq*128]. The block-causal rule takes the
+//               key-split form instead: the eight warps serve both tiles in
+//               turn, two warps per lane quadrant, lanes l and l + 16 holding
+//               keys [0, 64) and [64, 128) of one row (TMEM shape 16x32bx2),
+//               which halves the per-thread mask tests and exponentials of
+//               that rule (0.118 -> 0.103 ms at BASELINE config 4's prefill;
+//               0.317 -> 0.325 ms bidirectional, so that pass keeps the
+//               one-row form)
 // TMEM (512 columns): tile t at t*256: S_t / P_t [0,128) | O_t [128,256).
 //
 // The exponentials stay on the MUFU unit: moving a quarter or half of them
@@ -91,6 +101,7 @@ constexpr int kVBytes = 128 * kBlk * 2;         // [2 key blocks][128 dims][128 
 constexpr int kMaxBlk = 256;
 // the exponential form a launch takes unless U15_ATTN_EXP says otherwise
 constexpr int kDefaultExp = 0;
+
 constexpr int kSmem = kQBytes + kStages * (kKBytes + kVBytes) + 1024 + 256 + 2 * kMaxBlk * 4 + 64;
 
 struct TcAttnP {
@@ -105,6 +116,7 @@ struct TcAttnP {
   int nqb, nkb;
   long k8_stride;    // Sage: rows per kv head in the int8 K copy
   unsigned* err;
+  int issuers;       // MMA issuing warps: 1 (warp 1, both tiles) or 2 (warp 1 + t, tile t)
 };
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
@@ -140,6 +152,60 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
+      : "memory");
+}
+
+// 64 32-bit columns per thread in the 16x32bx2 shape: threads 0-15 read
+// lanes taddr.lane + (0..15) at columns [c, c + 64), threads 16-31 the same
+// lanes at [c + OFF, c + OFF + 64)
+template <int OFF>
+__device__ __forceinline__ void tmem_ld_pair64(uint32_t taddr, uint32_t (&r)[64])
+{
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,"
+      "%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,"
+      "%58,%59,%60,%61,%62,%63}, [%64], %65;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr), "n"(OFF)
+      : "memory");
+}
+
+// the store of the same shape: threads 0-15 write columns [c, c + 16),
+// threads 16-31 [c + OFF, c + OFF + 16) of the same 16 lanes
+template <int OFF>
+__device__ __forceinline__ void tmem_st_pair16(uint32_t taddr, const uint32_t (&r)[16])
+{
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], %17, {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
+      "%12,%13,%14,%15,%16};"
+      :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "n"(OFF)
+      : "memory");
+}
+
+// 32 32-bit columns per thread in the 16x32bx2 shape: threads 0-15 read
+// lanes taddr.lane + (0..15) at columns [c, c + 32), threads 16-31 the same
+// lanes at [c + OFF, c + OFF + 32)
+template <int OFF>
+__device__ __forceinline__ void tmem_ld_pair32(uint32_t taddr, uint32_t (&r)[32])
+{
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], %33;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr), "n"(OFF)
+      : "memory");
+}
+
+// the store of the same shape: threads 0-15 write columns [c, c + 32),
+// threads 16-31 [c + OFF, c + OFF + 32) of the same 16 lanes
+template <int OFF>
+__device__ __forceinline__ void tmem_st_pair32(uint32_t taddr, const uint32_t (&r)[32])
+{
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x32.b32 [%0], %33, {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,"
+      "%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "n"(OFF)
       : "memory");
 }
 
@@ -182,7 +248,217 @@ struct MaskPlan {
   int tlo[2], thi[2];
 };
 
+// The softmax in the key-split layout. Warp w of 4..11 serves rows
+// 32 * (w & 3) + 16 * ((w - 4) >> 2) + (0..15) of BOTH tiles, the tiles in
+// turn (tile 0 of block j, tile 1 of block j, tile 0 of block j + 1, ...);
+// it reads them through the 16x32bx2 TMEM shape, so lane l < 16 holds keys
+// [0, 64) of its row and lane l + 16 keys [64, 128) of the same row. Two
+// warps share each lane quadrant: every warp exponentiates 64 scores a row
+// instead of 128, and the two keep the SM sub-partition's MUFU busy where a
+// single warp issuing 128 dependent-chain exponentials could not. The row
+// max takes one shuffle between the two lanes of a row; the row sum stays
+// split until the end. P lands where the one-row-per-thread layout puts it
+// (key k of the block at bf16 column k of the tile's S columns), so the
+// MMA issuer is unchanged.
 template <bool SAGE, int EXPM, int MODE>
+__device__ __forceinline__ void softmax_key_split(const TcAttnP& p, const MaskPlan* plan,
+                                                  const int* blk_tlo, const int* blk_thi,
+                                                  uint32_t tmem, uint32_t s_full, uint32_t p_full,
+                                                  int h, int hk, int q0, int n_t0, int n_t1)
+{
+  const int w = (int)warp_id();
+  const int q4 = w & 3, hf = (w - 4) >> 2;
+  const int kh = (int)lane_id() >> 4;   // key half of the block this lane holds
+  const int kb0 = 64 * kh;
+  const int row = q4 * 32 + hf * 16 + ((int)lane_id() & 15);
+  const uint32_t lane_off = (uint32_t)(q4 * 32 + hf * 16) << 16;
+  const int nt[2] = {n_t0, n_t1};
+  const int n = max(n_t0, n_t1);
+  float m_ref[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+  float sqv[2] = {1.0f, 1.0f};
+  int qi[2], gi[2], g_first[2], ti[2] = {0, 0};
+  bool t_uniform[2] = {false, false};
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    qi[t] = q0 + t * kTile + row;
+    gi[t] = p.q_offset + qi[t];
+    g_first[t] = p.q_offset + q0 + t * kTile;
+    if constexpr (SAGE) sqv[t] = (qi[t] < p.tq) ? p.sq[(long)h * p.nqb + qi[t] / 64] : 0.0f;
+    if constexpr (MODE == 2) {
+      ti[t] = qi[t] < p.tq ? p.t_index[gi[t]] : 0;
+      t_uniform[t] = plan->tlo[t] == plan->thi[t];
+    }
+  }
+  const int kb_last = (p.tk - 1) >> 5;
+  bool ok = true;
+  for (int j = 0; j < n && ok; ++j) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (j >= nt[t]) continue;
+      // warp-uniform: the TMEM loads and stores below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full + 8 * t, j & 1, p.err, kDevWaitAccFull))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tS = tmem + t * 256 + lane_off;
+      const uint32_t tO = tS + 128;
+      uint32_t r[64];
+      tmem_ld_pair64<64>(tS, r);
+      tmem_ld_wait();
+      // base-2 scale of this lane's two 32-key chunks (Sage: the Q block's and
+      // the chunk's K block's scales; never zero, so -inf stays -inf)
+      float f[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        f[c] = p.scale_log2;
+        if constexpr (SAGE)
+          f[c] = fmaxf(f[c] * sqv[t] * p.sk[(long)hk * p.nkb + min(4 * j + 2 * kh + c, kb_last)],
+                       1e-30f);
+      }
+      float s[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        if constexpr (SAGE) s[i] = __int_as_float((int)r[i] + 0x4B400000) - 12582912.0f;
+        else s[i] = __uint_as_float(r[i]);
+      }
+      const int j0 = j * kBlk;
+      const int kmax = p.tk - j0;
+      if constexpr (MODE == 0) {
+        if (kmax < kBlk) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (kb0 + i >= kmax) s[i] = -INFINITY;
+        }
+      } else {
+        bool full = kmax >= kBlk && j0 + kBlk - 1 <= g_first[t];
+        if constexpr (MODE == 2)
+          full = full || (kmax >= kBlk && t_uniform[t] && blk_tlo[j] == blk_thi[j] &&
+                          blk_tlo[j] == plan->tlo[t]);
+        if (!full) {
+          if constexpr (MODE == 1) {
+            const int lim = min(kmax - 1, gi[t] - j0);   // visible keys [0, lim] of the block
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if (kb0 + i > lim) s[i] = -INFINITY;
+          } else {
+            const int lim = gi[t] - j0;
+            const int4* t4 = reinterpret_cast<const int4*>(p.t_index + j0 + kb0);
+#pragma unroll
+            for (int qd = 0; qd < 16; ++qd) {
+              int tt[4];
+              if (kb0 + 4 * qd + 3 < kmax) {
+                const int4 v = __ldg(t4 + qd);
+                tt[0] = v.x; tt[1] = v.y; tt[2] = v.z; tt[3] = v.w;
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  tt[e] = kb0 + 4 * qd + e < kmax ? p.t_index[j0 + kb0 + 4 * qd + e] : 0;
+              }
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = kb0 + 4 * qd + e;
+                const bool vis = i < kmax && (i <= lim || tt[e] == ti[t]);
+                if (!vis) s[4 * qd + e] = -INFINITY;
+              }
+            }
+          }
+        }
+      }
+      // row max: this lane's two chunks in two chains each, then the partner lane
+      float mc[2][2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        mc[c][0] = s[32 * c];
+        mc[c][1] = s[32 * c + 1];
+      }
+#pragma unroll
+      for (int i = 2; i < 32; i += 2) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          mc[c][0] = fmaxf(mc[c][0], s[32 * c + i]);
+          mc[c][1] = fmaxf(mc[c][1], s[32 * c + i + 1]);
+        }
+      }
+      float mt = fmaxf(fmaxf(mc[0][0], mc[0][1]) * f[0], fmaxf(mc[1][0], mc[1][1]) * f[1]);
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+      const bool need = (m_ref[t] == -INFINITY) || (mt > m_ref[t] + 8.0f);
+      const float m_new = need ? fmaxf(mt, m_ref[t]) : m_ref[t];
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O_t is final up to P.V(j-1): s_full[t] completed after it. Lane
+        // l < 16 rescales dims [0, 64) of its row, lane l + 16 dims [64, 128)
+        const float fac = (need && m_ref[t] != -INFINITY) ? ex2(m_ref[t] - m_new) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld_pair32<64>(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
+          tmem_st_pair32<64>(tO + c * 32, o);
+        }
+        l[t] *= fac;
+      }
+      m_ref[t] = m_new;
+      const float nm = m_ref[t] == -INFINITY ? 0.0f : -m_ref[t];
+      float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float fc = f[c];
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
+          const bool fma_pipe = EXPM == 1 && (i & 3) == 3;
+          const float a = fma_pipe ? ex2_fma(x0) : ex2(x0);
+          const float b = fma_pipe ? ex2_fma(x1) : ex2(x1);
+          rs[i & 3] += a + b;
+          pk[i] = pack_bf2(a, b);
+        }
+        // keys [kb0 + 32c, kb0 + 32c + 32) -> bf16 columns [kb0/2 + 16c, +16):
+        // lanes < 16 write columns 16c.., lanes >= 16 columns 32 + 16c..
+        tmem_st_pair16<32>(tS + 16 * c, pk);
+      }
+      tmem_st_wait();
+      l[t] += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane_id() == 0) mbar_arrive(p_full + 8 * t);
+    }
+  }
+  // the commit after each tile's last P.V, then O / l of this lane's 64 dims
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const bool fin = ok && nt[t] > 0 &&
+                     mbar_wait(s_full + 8 * t, nt[t] & 1, p.err, kDevWaitAccFull);
+    if (!__all_sync(0xffffffffu, fin)) continue;
+    tc_fence_after();
+    const float lt = l[t] + __shfl_xor_sync(0xffffffffu, l[t], 16);
+    const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+    const uint32_t tO = tmem + t * 256 + lane_off + 128;
+    __nv_bfloat16* dst = p.out + (long)qi[t] * p.hq * 128 + (long)h * 128 + kb0;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t o[32];
+      tmem_ld_pair32<64>(tO + c * 32, o);
+      tmem_ld_wait();
+      if (qi[t] < p.tq) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) {
+          uint4 v;
+          v.x = pack_bf2(__uint_as_float(o[qd * 8 + 0]) * inv, __uint_as_float(o[qd * 8 + 1]) * inv);
+          v.y = pack_bf2(__uint_as_float(o[qd * 8 + 2]) * inv, __uint_as_float(o[qd * 8 + 3]) * inv);
+          v.z = pack_bf2(__uint_as_float(o[qd * 8 + 4]) * inv, __uint_as_float(o[qd * 8 + 5]) * inv);
+          v.w = pack_bf2(__uint_as_float(o[qd * 8 + 6]) * inv, __uint_as_float(o[qd * 8 + 7]) * inv);
+          d4[qd] = v;
+        }
+      }
+    }
+  }
+}
+
+template <bool SAGE, int EXPM, int MODE, bool KS>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
@@ -225,12 +501,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(k_full + 8 * s, 1);
       mbar_init(v_full + 8 * s, 1);
-      mbar_init(k_empty + 8 * s, 1);
-      mbar_init(v_empty + 8 * s, 1);
+      // a K / V stage is free once every issuing warp's MMAs that read it are done
+      mbar_init(k_empty + 8 * s, p.issuers);
+      mbar_init(v_empty + 8 * s, p.issuers);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full + 8 * t, 1);
-      mbar_init(p_full + 8 * t, 128);
+      // P_t ready: one arrival per softmax thread of the tile, or (key-split
+      // layout) one per softmax warp, every warp serving both tiles
+      mbar_init(p_full + 8 * t, KS ? 8 : 128);
       // blocks of tile t: none when the tile holds no query row; the causal
       // rule ends at the block of the tile's last row
       const int r_lo = q0 + t * kTile, r_hi = min(r_lo + kTile, p.tq) - 1;
@@ -240,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       plan->tlo[t] = INT_MAX;
       plan->thi[t] = INT_MIN;
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, p.issuers);
     fence_barrier_init();
   }
   if (w == 0) {
@@ -372,6 +651,87 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+    } else if ((w == 1 || w == 2) && p.issuers == 2) {
+      // ------------------------------------------------------------ MMA, one warp a tile
+      // Warp 1 + t issues tile t's MMAs (the key-split softmax's partner). A
+      // single issuer's barrier operations after its MMAs return late (the
+      // stage commits and the V and P waits between the two tiles took ~700
+      // of every ~3900 cycles in a clock trace), and the key-split softmax
+      // serves the tiles in turn, so the tiles' MMAs do not interleave: one
+      // issuer a tile overlaps each tile's waits with the other's MMAs.
+      if (lane_id() == 0) {
+        const int t = w - 1;
+        const int n_mine = t == 0 ? n_t0 : n_t1;
+        const uint32_t id_s = SAGE ? idesc_s8(kTile, kBlk) : idesc_bf16(kTile, kBlk);
+        const uint32_t id_o = idesc_bf16(kTile, 128);
+        auto issue_s = [&](int j) {
+          const uint32_t d = tmem + t * 256;
+          const uint32_t kb = smem_u32(sK + (j % kStages) * kKBytes);
+          if constexpr (SAGE) {
+            const uint32_t a0 = smem_u32(sQ + t * kTile * 128);
+  #pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(kb + k * 32), id_s, k != 0);
+          } else {
+            const uint32_t a0 = smem_u32(sQ + t * kTile * 256);
+  #pragma unroll
+            for (int k = 0; k < 8; ++k)
+              mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
+                       smem_desc_sw128(kb + (k >> 2) * kBlk * 128 + (k & 3) * 32), id_s, k != 0);
+          }
+        };
+        bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
+        if (ok && n > 0) {
+          ok = mbar_wait(k_full, 0, p.err, kDevWaitFull);
+          if (ok) {
+            tc_fence_after();
+            if (n_mine > 0) {
+              issue_s(0);
+              mma_commit(s_full + 8 * t);
+            }
+            mma_commit(k_empty);
+          }
+        }
+        // Every block the producer loads is released by both issuers, each
+        // only after that fill has landed (the V and next K waits below, also
+        // where this tile has no MMA to issue): with two arrivals a phase, a
+        // release issued before its fill landed could complete the previous
+        // fill's phase alone, while the other tile still reads that fill.
+        for (int j = 0; j < n && ok; ++j) {
+          const int s = j % kStages, s1 = (j + 1) % kStages;
+          const bool mine = j < n_mine;
+          if (!mbar_wait(v_full + 8 * s, (j / kStages) & 1, p.err, kDevWaitFull) ||
+              (mine && !mbar_wait(p_full + 8 * t, j & 1, p.err, kDevWaitFull))) {
+            ok = false;
+            break;
+          }
+          if (mine) {
+            tc_fence_after();
+            const uint32_t vb = smem_u32(sV + s * kVBytes);
+            const uint32_t d = tmem + t * 256 + 128, a = tmem + t * 256;
+  #pragma unroll
+            for (int k = 0; k < 8; ++k)
+              mma_bf16_ts(d, a + k * 8, smem_desc_sw128(vb + (k >> 2) * 128 * 128 + (k & 3) * 32),
+                          id_o, (j | k) != 0);
+          }
+          if (j + 1 < n &&
+              !mbar_wait(k_full + 8 * s1, ((j + 1) / kStages) & 1, p.err, kDevWaitFull)) {
+            ok = false;
+            break;
+          }
+          if (mine) {
+            if (j + 1 < n_mine) {
+              tc_fence_after();
+              issue_s(j + 1);
+            }
+            mma_commit(s_full + 8 * t);
+          }
+          mma_commit(v_empty + 8 * s);
+          if (j + 1 < n) mma_commit(k_empty + 8 * s1);
+        }
+        mma_commit(drain);
+        mbar_wait(drain, 0, p.err, kDevWaitDrain);
+      }
     } else if (w == 1) {
       // ------------------------------------------------------------ MMA
       if (lane_id() == 0) {
@@ -445,6 +805,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(drain, 0, p.err, kDevWaitDrain);
       }
     }
+  } else if constexpr (KS) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    softmax_key_split<SAGE, EXPM, MODE>(p, plan, blk_tlo, blk_thi, tmem, s_full, p_full, h, hk, q0,
+                                        n_t0, n_t1);
+    tc_fence_before();
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------------------------------------ softmax
@@ -645,6 +1010,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
+
 }  // namespace
 
 bool attention_tc_serves(int mode, int tk, const int32_t* t_index)
@@ -701,6 +1067,8 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   p.nkb = 2 * ((a.tk + 63) / 64);   // 32-key K blocks, two per page
   p.k8_stride = (long)p.nkb * 32;
   p.err = a.dev_err;
+  const char* iss_env = std::getenv("U15_ATTN_ISSUERS");
+  p.issuers = iss_env != nullptr ? (std::atoi(iss_env) == 2 ? 2 : 1) : (a.mode == 2 ? 2 : 1);
   CUtensorMap mq, mk, mv;
   if (sage) {
     if (make_tma_2d(&mq, a.q8, (uint64_t)a.hq * a.tq, 128, kTile, 1, err)) return 2;
@@ -713,27 +1081,41 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   // The exponentials (U15_ATTN_EXP, read per launch for A/B checks): 0 every
   // one a float ex2 on the MUFU; 1 a quarter of them on the FMA pipe (5-10 %
   // slower for bf16, 4 % for Sage, measured).
-  static std::atomic<uint64_t> set_attr[8];
+  static std::atomic<uint64_t> set_attr[16];
   const int nqblk = (a.tq + 2 * kTile - 1) / (2 * kTile);
   const dim3 grid = a.mode == 0 ? dim3(nqblk, a.hq) : dim3(a.hq, nqblk);
   const char* exp_env = std::getenv("U15_ATTN_EXP");
   int expm = exp_env != nullptr ? std::atoi(exp_env) : kDefaultExp;
   if (expm < 0 || expm > 1) expm = kDefaultExp;
+  // The softmax layout and the MMA issuers per rule (measured, 4096 x 4416
+  // and BASELINE config 4's prefill): the bidirectional and causal rules take
+  // one query row a thread with one issuer; the block-causal rule, whose
+  // per-element test loads the softmax warps' issue slots, the key-split
+  // layout (64 keys a thread, two warps per lane quadrant) with one issuer a
+  // tile. U15_ATTN_KS and U15_ATTN_ISSUERS override both (read per launch,
+  // for A/B checks).
+  const char* ks_env = std::getenv("U15_ATTN_KS");
+  const int ks = ks_env != nullptr ? (std::atoi(ks_env) != 0) : (a.mode == 2 ? 1 : 0);
   using KFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, TcAttnP);
-  static const KFn table[4][2] = {
-      {attn_tc_kernel<false, 0, 0>, attn_tc_kernel<false, 1, 0>},
-      {attn_tc_kernel<true, 0, 0>, attn_tc_kernel<true, 1, 0>},
-      {attn_tc_kernel<false, 0, 1>, attn_tc_kernel<false, 1, 1>},
-      {attn_tc_kernel<false, 0, 2>, attn_tc_kernel<false, 1, 2>}};
+  static const KFn table[4][2][2] = {
+      {{attn_tc_kernel<false, 0, 0, false>, attn_tc_kernel<false, 0, 0, true>},
+       {attn_tc_kernel<false, 1, 0, false>, attn_tc_kernel<false, 1, 0, true>}},
+      {{attn_tc_kernel<true, 0, 0, false>, attn_tc_kernel<true, 0, 0, true>},
+       {attn_tc_kernel<true, 1, 0, false>, attn_tc_kernel<true, 1, 0, true>}},
+      {{attn_tc_kernel<false, 0, 1, false>, attn_tc_kernel<false, 0, 1, true>},
+       {attn_tc_kernel<false, 1, 1, false>, attn_tc_kernel<false, 1, 1, true>}},
+      {{attn_tc_kernel<false, 0, 2, false>, attn_tc_kernel<false, 0, 2, true>},
+       {attn_tc_kernel<false, 1, 2, false>, attn_tc_kernel<false, 1, 2, true>}}};
   const int row = sage ? 1 : (a.mode == 0 ? 0 : a.mode + 1);
-  const KFn k = table[row][expm];
-  const int which = row * 2 + expm;
+  const KFn k = table[row][expm][ks];
+  const int which = (row * 2 + expm) * 2 + ks;
+  const int smem = kSmem;
   cudaError_t e = cudaSuccess;
-  if (smem_attr_once(k, kSmem, set_attr[which])) {
+  if (smem_attr_once(k, smem, set_attr[which])) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmem;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -751,7 +1133,7 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
     cudaFuncGetAttributes(&fa, k);
     *err = std::string("attention (tcgen05): kernel launch failed: ") + cudaGetErrorString(e) +
            " (registers " + std::to_string(fa.numRegs) + ", max threads " +
-           std::to_string(fa.maxThreadsPerBlock) + ", dynamic smem " + std::to_string(kSmem) + ")";
+           std::to_string(fa.maxThreadsPerBlock) + ", dynamic smem " + std::to_string(smem) + ")";
     return 2;
   }
   return 0;
