@@ -615,6 +615,29 @@ int u15c_layer_forward_host(u15c_model* m, u15c_stream stream, int layer, const 
                             const int32_t* pos_h, const int32_t* pos_w, int attn,
                             const int32_t* t_index, unsigned flags);
 
+/* The same layer through host memory, enqueued without waiting (a serving
+ * loop's form of u15c_layer_forward_host; the reference's layer calls are
+ * synchronous, so this entry has no counterpart there). The upload runs on
+ * the model's upload stream, the layer on `stream` once it has landed, the
+ * download on the model's download stream once the layer is done. Two device
+ * staging buffers are used in turn, so call k + 1's upload and call k - 1's
+ * download run during call k's layer: back-to-back calls keep the copies off
+ * the critical path. x_host must stay unchanged and out_host unread until the
+ * call's results are drained: u15c_layer_host_drain makes `stream` wait for
+ * every download enqueued so far, after which synchronising `stream` (or
+ * u15c_sync) completes them. Both host buffers should be pinned. Not for
+ * tensor-parallel models (U15C_EINVAL). */
+int u15c_layer_forward_host_async(u15c_model* m, u15c_stream stream, int layer,
+                                  const void* x_host, void* out_host, int n, const int* seg_off,
+                                  const int* seg_expert, int nseg, u15c_kv* kv, int kv_off,
+                                  int kv_len, const int32_t* pos_t, const int32_t* pos_h,
+                                  const int32_t* pos_w, int attn, const int32_t* t_index,
+                                  unsigned flags);
+
+/* Make `stream` wait for every download u15c_layer_forward_host_async has
+ * enqueued on this model so far (no host wait). */
+int u15c_layer_host_drain(u15c_model* m, u15c_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -316,6 +316,36 @@ def test_layer_forward_host_pipelined(int8):
     assert np.array_equal(oh.float().numpy(), host(xd))
 
 
+@pytest.mark.parametrize("n_und,gh,gw", [(700, 20, 40), (16, 6, 8)], ids=["1500-row", "64-row"])
+def test_layer_forward_host_async_back_to_back(n_und, gh, gw):
+    """Three async host-buffer passes enqueued back to back (two staging
+    buffers used in turn, so the third reuses the first's while the uploads
+    and downloads of neighbouring calls overlap): each result equals the
+    synchronous device pass of the same input, bit for bit."""
+    import u15b200
+    m, _ = build(SMALL, 78)
+    T = n_und + gh * gw
+    segs = [(0, n_und, 0), (n_und, T, 1)]
+    pos = [dev_i32(p) for p in grid_positions(n_und, gh, gw, n_und)]
+    xs = [bf16_round(randn((T, SMALL["hidden"]), 30 + i)) for i in range(3)]
+    kv = m.make_cache(T)
+    want = []
+    for i, x in enumerate(xs):
+        xd = dev_bf16(x)
+        m.layer_forward(i % 2, xd, kv, 0, T, *pos, segments=segs)
+        torch.cuda.synchronize()
+        want.append(host(xd))
+    xh = [torch.from_numpy(x).to(torch.bfloat16).pin_memory() for x in xs]
+    oh = [torch.zeros_like(h).pin_memory() for h in xh]
+    for i in range(3):
+        m.layer_forward_host_async(i % 2, xh[i], oh[i], kv, 0, T, *pos, segments=segs)
+    m.host_drain()
+    torch.cuda.synchronize()
+    u15b200.CudaOps(0).sync()
+    for i in range(3):
+        assert np.array_equal(oh[i].float().numpy(), want[i]), i
+
+
 def test_42_layer_drift():
     cfg = dict(SMALL, n_layers=42)
     m, W = build(cfg, 50)

@@ -159,6 +159,17 @@ struct u15c_model {
   // layer_forward_host's copy stream and its chunk events (made on first use)
   cudaStream_t copy_st = nullptr;
   cudaEvent_t copy_ev[2 * 4 + 1] = {};
+  // layer_forward_host_async: two staging buffers used in turn, an upload and
+  // a download stream (so one call's upload overlaps the previous call's
+  // download), per staging buffer its upload-landed, layer-done and
+  // download-done events (the last: the buffer is free again); made on first
+  // use, grow-only
+  bf16* hio[2] = {};
+  int hio_n = 0;
+  int hio_next = 0;
+  bool hio_used[2] = {};
+  cudaStream_t up_st = nullptr, down_st = nullptr;
+  cudaEvent_t hio_in[2][1] = {}, hio_out[2][1] = {}, hio_free[2] = {};
   // forward_many's branch attentions run on these beside the model's stream
   // (made on first use), so one branch's last part-empty round of CTAs is
   // filled by the next branch's
@@ -248,8 +259,54 @@ struct u15c_model {
     return U15C_OK;
   }
 
+  // the async host path's staging and streams (grow-only; a regrowth waits
+  // for the copies in flight)
+  int ensure_host_staging(int n)
+  {
+    if (up_st == nullptr) {
+      if (cudaStreamCreateWithFlags(&up_st, cudaStreamNonBlocking) != cudaSuccess ||
+          cudaStreamCreateWithFlags(&down_st, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(U15C_ECUDA, "layer_forward_host_async: copy streams");
+      for (int b = 0; b < 2; ++b) {
+        if (cudaEventCreateWithFlags(&hio_in[b][0], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&hio_out[b][0], cudaEventDisableTiming) != cudaSuccess)
+          return fail(U15C_ECUDA, "layer_forward_host_async: copy events");
+        if (cudaEventCreateWithFlags(&hio_free[b], cudaEventDisableTiming) != cudaSuccess)
+          return fail(U15C_ECUDA, "layer_forward_host_async: copy events");
+      }
+    }
+    if (n <= hio_n) return U15C_OK;
+    cudaStreamSynchronize(up_st);
+    cudaStreamSynchronize(down_st);
+    for (bf16*& b : hio) {
+      if (b) cudaFree(b);
+      b = nullptr;
+    }
+    hio_n = 0;
+    for (bf16*& b : hio)
+      if (cudaMalloc(reinterpret_cast<void**>(&b), (size_t)n * cfg.hidden * 2) != cudaSuccess) {
+        for (bf16*& c : hio) {
+          if (c) cudaFree(c);
+          c = nullptr;
+        }
+        return fail(U15C_ENOMEM, "out of device memory (host-path staging)");
+      }
+    hio_n = n;
+    return U15C_OK;
+  }
+
   ~u15c_model()
   {
+    if (up_st) cudaStreamSynchronize(up_st);
+    if (down_st) cudaStreamSynchronize(down_st);
+    for (int b = 0; b < 2; ++b) {
+      if (hio_in[b][0]) cudaEventDestroy(hio_in[b][0]);
+      if (hio_out[b][0]) cudaEventDestroy(hio_out[b][0]);
+      if (hio_free[b]) cudaEventDestroy(hio_free[b]);
+      if (hio[b]) cudaFree(hio[b]);
+    }
+    if (up_st) cudaStreamDestroy(up_st);
+    if (down_st) cudaStreamDestroy(down_st);
     for (cudaEvent_t e : copy_ev)
       if (e) cudaEventDestroy(e);
     if (copy_st) cudaStreamDestroy(copy_st);
@@ -1282,6 +1339,76 @@ int u15c_layer_forward_host(u15c_model* m, u15c_stream stream, int layer, const 
   e = cudaMemcpyAsync(out_host, m->io, bytes, cudaMemcpyDeviceToHost, st);
   if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host: download");
   return u15c_sync(stream);
+}
+
+int u15c_layer_forward_host_async(u15c_model* m, u15c_stream stream, int layer,
+                                  const void* x_host, void* out_host, int n, const int* seg_off,
+                                  const int* seg_expert, int nseg, u15c_kv* kv, int kv_off,
+                                  int kv_len, const int32_t* pos_t, const int32_t* pos_h,
+                                  const int32_t* pos_w, int attn, const int32_t* t_index,
+                                  unsigned flags)
+{
+  if (m == nullptr || x_host == nullptr || out_host == nullptr)
+    return fail(U15C_EINVAL, "layer_forward_host_async: null argument");
+  DeviceScope ds(m->device);
+  if (m->tp_size != 1)
+    return fail(U15C_EINVAL, "layer_forward_host_async: tensor-parallel models take the "
+                             "synchronous u15c_layer_forward_host");
+  int rc = validate_pass(m, n, kv, kv_off, kv_len, attn, pos_t, pos_h, pos_w, t_index);
+  if (rc) return rc;
+  if (layer < 0 || layer >= m->cfg.n_layers) return fail(U15C_EINVAL, "layer out of range");
+  u15::SegInfo seg;
+  std::string err;
+  if (!u15::fill_seg(&seg, seg_off, seg_expert, nseg, n, m->cfg.n_experts, &err))
+    return fail(U15C_EINVAL, err);
+  if ((rc = m->ensure_scratch(n, kv_len)) || (rc = m->ensure_host_staging(n))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t bytes = (size_t)n * m->cfg.hidden * 2;
+  const int b = m->hio_next;
+  m->hio_next ^= 1;
+  bf16* io = m->hio[b];
+  // The staging buffer is free once the call two back (the last one that
+  // used it) has downloaded its result. Back to back, call k + 1's upload
+  // runs during call k's layer and call k's download during call k + 1's, so
+  // the pass is not cut into row chunks (whole-pass GEMMs), unlike the
+  // synchronous form, which can only overlap copies within its own call.
+  if (m->hio_used[b]) cudaStreamWaitEvent(m->up_st, m->hio_free[b], 0);
+  m->hio_used[b] = true;
+  cudaError_t e = cudaMemcpyAsync(io, x_host, bytes, cudaMemcpyHostToDevice, m->up_st);
+  if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host_async: upload");
+  cudaEventRecord(m->hio_in[b][0], m->up_st);
+  cudaStreamWaitEvent(st, m->hio_in[b][0], 0);
+  if (u15::launch_rope_tables(pos_t, pos_h, pos_w, n, 64, 32, m->cfg.theta_t, m->cfg.theta_hw,
+                              m->rcos, m->rsin, st))
+    return fail(U15C_ECUDA, "rope tables launch failed");
+  SlotRun sl;
+  sl.n = n;
+  sl.kv = kv;
+  sl.kv_off = kv_off;
+  sl.kv_len = kv_len;
+  sl.attn = attn;
+  sl.t_index = t_index;
+  const std::vector<SlotRun> slots{sl};
+  if ((rc = layer_impl(m, st, layer, io, n, seg, seg_off, seg_expert, nseg, slots, flags)))
+    return rc;
+  cudaEventRecord(m->hio_out[b][0], st);
+  cudaStreamWaitEvent(m->down_st, m->hio_out[b][0], 0);
+  e = cudaMemcpyAsync(out_host, io, bytes, cudaMemcpyDeviceToHost, m->down_st);
+  if (e != cudaSuccess) return cuda_fail(e, "layer_forward_host_async: download");
+  cudaEventRecord(m->hio_free[b], m->down_st);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? U15C_OK : cuda_fail(e, "layer_forward_host_async");
+}
+
+int u15c_layer_host_drain(u15c_model* m, u15c_stream stream)
+{
+  if (m == nullptr) return fail(U15C_EINVAL, "layer_host_drain: null model");
+  DeviceScope ds(m->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int b = 0; b < 2; ++b)
+    if (m->hio_used[b]) cudaStreamWaitEvent(st, m->hio_free[b], 0);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? U15C_OK : cuda_fail(e, "layer_host_drain");
 }
 
 }  // extern "C"

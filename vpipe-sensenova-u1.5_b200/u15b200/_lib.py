@@ -161,6 +161,9 @@ SIGNATURES = {
     "u15c_final_norm": (ip, [vp, vp, vp, ip, ip]),
     "u15c_layer_forward_host": (ip, [vp, vp, ip, vp, vp, ip, i32p, i32p, ip, vp, ip, ip, vp, vp,
                                      vp, ip, vp, C.c_uint]),
+    "u15c_layer_forward_host_async": (ip, [vp, vp, ip, vp, vp, ip, i32p, i32p, ip, vp, ip, ip, vp,
+                                           vp, vp, ip, vp, C.c_uint]),
+    "u15c_layer_host_drain": (ip, [vp, vp]),
 }
 
 _lib = None

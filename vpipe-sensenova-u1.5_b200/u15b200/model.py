@@ -176,6 +176,25 @@ class Model:
                                             n, off, ex, ns, kv.h, kv_off, kv_len, _p(pos_t),
                                             _p(pos_h), _p(pos_w), attn, _p(t_index), flags))
 
+    def layer_forward_host_async(self, layer, x_host, out_host, kv, kv_off, kv_len, pos_t, pos_h,
+                                 pos_w, segments=None, attn=L.ATTN_BIDIRECTIONAL, t_index=None,
+                                 int8=False, sage=False):
+        """Enqueue the layer through pinned host buffers without waiting
+        (u15c_layer_forward_host_async): x_host must stay unchanged and
+        out_host unread until host_drain() and a stream synchronisation."""
+        n = x_host.shape[0]
+        off, ex, ns = segments_arrays(segments, n)
+        flags = (L.FWD_INT8 if int8 else 0) | (L.FWD_SAGE if sage else 0)
+        check(lib().u15c_layer_forward_host_async(self.h, _stream(), layer, _p(x_host),
+                                                  _p(out_host), n, off, ex, ns, kv.h, kv_off,
+                                                  kv_len, _p(pos_t), _p(pos_h), _p(pos_w), attn,
+                                                  _p(t_index), flags))
+
+    def host_drain(self):
+        """Make the current stream wait for every download the async host
+        path has enqueued (u15c_layer_host_drain)."""
+        check(lib().u15c_layer_host_drain(self.h, _stream()))
+
 
 class KvCache:
     """Paged bf16 KV cache for every layer of one branch."""
