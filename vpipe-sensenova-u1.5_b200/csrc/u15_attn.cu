@@ -429,18 +429,35 @@ __global__ void __launch_bounds__(kSageThreads)
   __shared__ float red[kSageThreads / 32];
   const int tid = threadIdx.x;
   if ((int)blockIdx.x >= nqb) {
-    // K-mean partial of one page: two threads per channel, 32 keys each
+    // K-mean partial of one page: thread (key slot kr, 8-channel group c8)
+    // sums keys kr, kr + 16, kr + 32, kr + 48 of the page with 16-byte loads,
+    // then the 16 key slots of each channel are added in slot order (the
+    // first form, a 2-byte load per key and channel in a 32-deep chain, took
+    // 21 us of the Sage prologue at BASELINE config 4)
     const int pg = (int)blockIdx.x - nqb, hk = blockIdx.y;
     if (hk >= hkv) return;
-    const int c = tid & 127, half = tid >> 7;
-    const int j0 = pg * 64 + half * 32, j1 = min(tk, j0 + 32);
-    float acc = 0.0f;
-#pragma unroll 8
-    for (int j = j0; j < j1; ++j) acc += bf2f(kv_row(kv, kv.k, hk, j)[c]);
-    __shared__ float hsum[128];
-    if (half == 1) hsum[c] = acc;
+    const int c8 = tid & 15, kr = tid >> 4;
+    float acc[8] = {};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int j = pg * 64 + kr + 16 * i;
+      if (j < tk) {
+        float v[8];
+        load8_bf(kv_row(kv, kv.k, hk, j) + c8 * 8, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += v[k];
+      }
+    }
+    __shared__ float part[16][129];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) part[kr][c8 * 8 + k] = acc[k];
     __syncthreads();
-    if (half == 0) kpart[((long)hk * npg + pg) * 128 + c] = acc + hsum[c];
+    if (tid < 128) {
+      float t = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) t += part[r][tid];
+      kpart[((long)hk * npg + pg) * 128 + tid] = t;
+    }
     return;
   }
   const int b = blockIdx.x, h = blockIdx.y;
@@ -471,10 +488,23 @@ __global__ void __launch_bounds__(kSageThreads)
   __shared__ float red[2][kSageThreads / 32];
   __shared__ float km[128];
   const int pg = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
-  if (tid < 128) {
-    float acc = 0.0f;
-    for (int i = 0; i < npg; ++i) acc += kpart[((long)hk * npg + i) * 128 + tid];
-    km[tid] = acc / (float)tk;
+  {
+    // kmean over the pages: two threads a channel, each over every other
+    // page with four independent sums, combined in a fixed order
+    const int c = tid & 127, h2 = tid >> 7;
+    const float* kp = kpart + (long)hk * npg * 128 + c;
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int i = h2;
+    for (; i + 6 < npg; i += 8) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] += kp[(long)(i + 2 * u) * 128];
+    }
+    for (; i < npg; i += 2) a[0] += kp[(long)i * 128];
+    __shared__ float hsum[128];
+    const float t = (a[0] + a[1]) + (a[2] + a[3]);
+    if (h2 == 1) hsum[c] = t;
+    __syncthreads();
+    if (h2 == 0) km[c] = (t + hsum[c]) / (float)tk;
   }
   __syncthreads();
   // rows r0 + 16 i: i = 0, 1 are the page's first 32-key block, i = 2, 3 its second
