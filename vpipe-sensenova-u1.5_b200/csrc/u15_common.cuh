@@ -203,6 +203,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
       : "memory");
   return ok != 0;
 }
+// Whether the phase with parity `parity` has completed, without waiting.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity)
+{
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Wait until the phase with parity `parity` has completed. Bounded: gives up
 // after U15_WAIT_LIMIT_NS, records `code` and returns false.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned* err,
@@ -220,6 +233,16 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
       return false;
     }
   }
+}
+
+// mbar_wait for a thread whose barrier is usually complete already: one
+// non-blocking probe first. A tcgen05.mma issuer's try_wait returned ~200
+// cycles after its call even on a phase completed long before (a clock
+// trace of the attention's issuer); the probe returns in a few.
+__device__ __forceinline__ bool mbar_wait_probe(uint32_t bar, uint32_t parity, unsigned* err,
+                                                unsigned code)
+{
+  return mbar_test(bar, parity) || mbar_wait(bar, parity, err, code);
 }
 
 __device__ __forceinline__ bool wait_counter_sys(const unsigned long long* p,
@@ -412,6 +435,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity)
+{
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait with cluster-scope acquire (for barriers other CTAs arrive on).
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, unsigned* err,
                                                   unsigned code)
@@ -428,6 +463,12 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
       return false;
     }
   }
+}
+// mbar_wait_cluster with one non-blocking probe first (see mbar_wait_probe).
+__device__ __forceinline__ bool mbar_wait_cluster_probe(uint32_t bar, uint32_t parity,
+                                                        unsigned* err, unsigned code)
+{
+  return mbar_test_cluster(bar, parity) || mbar_wait_cluster(bar, parity, err, code);
 }
 // 2-D tiled load into this CTA's shared memory whose completion is counted
 // on an mbarrier of either CTA of the pair (no multicast).

@@ -296,12 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++lt) {
         const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
-        if (!mbar_wait(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
+        if (!mbar_wait_probe(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
           const uint32_t s = it % kStages, ph = (it / kStages) & 1;
-          if (!mbar_wait(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
+          if (!mbar_wait_probe(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
             ok = false;
             break;
           }
@@ -538,12 +538,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = pair; t < n_tiles && ok; t += n_pairs, ++lt) {
           const uint32_t idesc = t < p.n_full ? idesc_full : idesc_half;
           const uint32_t acc = lt & 1, aph = (lt >> 1) & 1;
-          if (!mbar_wait_cluster(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
+          if (!mbar_wait_cluster_probe(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + acc * 256;
           for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
             const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
-            if (!mbar_wait(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
+            if (!mbar_wait_probe(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
               ok = false;
               break;
             }
