@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float gg = bfround(g[i]), uu = bfround(v[i]);
-            g[i] = (gg / (1.0f + expf(-gg))) * uu;
+            g[i] = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
           }
           const int oc = nb * 128 + c * 32;
           if (row_ok) store_row32(yrow + oc, g, oc, nout);
@@ -601,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float gg = bfround(g[i]), uu = bfround(v[i]);
-            g[i] = (gg / (1.0f + expf(-gg))) * uu;
+            g[i] = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
           }
           const int oc = nb * 128 + gsub + c * 32;
           if (row_ok) store_row32(yrow + oc, g, oc, nout);
