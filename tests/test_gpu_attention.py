@@ -310,3 +310,37 @@ def test_tc_masked_matches_mma_sync_kernel(ops):
         a = run_paged(ops, q, k, v, T, mode=mode, **kw)
         b = run(ops, q, k, v, T, mode=mode, **kw)
         assert rel_l2(a, b) < BAR
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2], ids=["bidirectional", "causal", "block_causal"])
+def test_tc_forms_agree(ops, mode, monkeypatch):
+    """The tcgen05 kernel's forms, chosen per launch by the A/B switches (the
+    softmax layout, one or two MMA issuers, who releases the K/V stages),
+    give the same answer: bit for bit where only the hand-off differs, and
+    within 1e-3 of each other where the softmax sums a row in another order;
+    each form within the attention bar of the CPU restatement."""
+    t = np.array([0] * 40 + [1] * 300 + list(range(2, 150)) + [150] * 160, np.int32)
+    T = t.size
+    q, k, v = qkv(8, 2, T - 130, T, 37)
+    kw = {"mode": mode, "q_offset": 130 if mode else 0}
+    if mode == 2:
+        kw["t_index"] = t
+    forms = [{}, {"U15_ATTN_RELEASE": "0"}, {"U15_ATTN_KS": "0", "U15_ATTN_ISSUERS": "1"},
+             {"U15_ATTN_KS": "1", "U15_ATTN_ISSUERS": "2"}, {"U15_ATTN_KS": "1", "U15_ATTN_ISSUERS": "1"}]
+    outs = []
+    for f in forms:
+        for key in ("U15_ATTN_RELEASE", "U15_ATTN_KS", "U15_ATTN_ISSUERS"):
+            monkeypatch.delenv(key, raising=False)
+        for key, val in f.items():
+            monkeypatch.setenv(key, val)
+        outs.append(run_paged(ops, q, k, v, T, **kw))
+    for key in ("U15_ATTN_RELEASE", "U15_ATTN_KS", "U15_ATTN_ISSUERS"):
+        monkeypatch.delenv(key, raising=False)
+    ref = O.attention(q, k, v, tk=T, mode={0: O.BIDIR, 1: O.CAUSAL, 2: O.BLOCK_CAUSAL}[mode],
+                      q_offset=kw["q_offset"], t_index=kw.get("t_index"))
+    for i, o in enumerate(outs):
+        assert rel_l2(o, ref) < BAR, (mode, forms[i])
+        assert rel_l2(o, outs[0]) < 1e-3, (mode, forms[i])
+    # the release form and the issuer's commits differ only in the hand-off
+    if mode == 0:
+        assert np.array_equal(outs[0], outs[1])
