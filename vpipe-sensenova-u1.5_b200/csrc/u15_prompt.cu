@@ -58,30 +58,35 @@ int u15c_thw_indexes(const int32_t* ids, int n, int img_id, int img_ctx_id, cons
   if (ids == nullptr || t == nullptr || h == nullptr || w == nullptr || n < 0 || n_imgs < 0 ||
       (n_imgs > 0 && grid_hw == nullptr))
     return fail(U15C_EINVAL, "thw_indexes: bad argument");
-  // t: +1 for every token that is not <IMG_CONTEXT>, +1 more right after an
-  // <img>; a run of context tokens therefore shares one t
-  int cum = 0;
+  // One pass over the prompt. The sequence position steps on every token
+  // outside an image's context run and once more on the token that follows
+  // an <img> marker, so all of a run's tokens share the position one past
+  // their marker's. Context tokens also take the next cell of their
+  // image's merged grid (half the patch grid each way), row by row; an
+  // image whose grid is exhausted (or empty) hands over to the next one,
+  // and context tokens beyond the last image keep row and column 0.
+  int pos = -1;
+  int image = 0;   // the image whose grid the next context token fills
+  int cell = 0;    // the next free cell of that grid
+  auto grid_cells = [&](int k) { return (grid_hw[2 * k] / 2) * (grid_hw[2 * k + 1] / 2); };
   for (int i = 0; i < n; ++i) {
-    cum += ((i > 0 && ids[i - 1] == img_id) ? 1 : 0) + (ids[i] != img_ctx_id ? 1 : 0);
-    t[i] = cum - 1;
+    const bool context = ids[i] == img_ctx_id;
+    const bool after_marker = i > 0 && ids[i - 1] == img_id;
+    pos += (after_marker ? 1 : 0) + (context ? 0 : 1);
+    t[i] = pos;
     h[i] = 0;
     w[i] = 0;
-  }
-  // h / w over each image's context tokens, row-major on the merged grid
-  // (grid_w / 2 tokens per row), restarting per image
-  int img = 0, seen = 0;
-  for (int i = 0; i < n; ++i) {
-    if (ids[i] != img_ctx_id) continue;
-    while (img < n_imgs && seen >= (grid_hw[2 * img] / 2) * (grid_hw[2 * img + 1] / 2)) {
-      ++img;
-      seen = 0;
+    if (!context) continue;
+    while (image < n_imgs && cell >= grid_cells(image)) {
+      ++image;
+      cell = 0;
     }
-    if (img >= n_imgs) break;
-    const int tw = grid_hw[2 * img + 1] / 2;
-    if (tw <= 0) return fail(U15C_EINVAL, "thw_indexes: an image grid is smaller than 2x2");
-    h[i] = seen / tw;
-    w[i] = seen % tw;
-    ++seen;
+    if (image >= n_imgs) continue;
+    const int cols = grid_hw[2 * image + 1] / 2;
+    if (cols <= 0) return fail(U15C_EINVAL, "thw_indexes: an image grid is smaller than 2x2");
+    h[i] = cell / cols;
+    w[i] = cell % cols;
+    ++cell;
   }
   return U15C_OK;
 }
