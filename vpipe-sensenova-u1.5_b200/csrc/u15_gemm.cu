@@ -55,6 +55,8 @@ struct Unit {
 
 // the pair kernel's L2 policy unless U15_GEMM_L2HINT says otherwise
 constexpr int kDefaultL2Hint = 0;
+// the pair kernel's k-blocks per stage unless U15_GEMM_KPS says otherwise
+constexpr int kDefaultKps = 2;
 
 struct Params {
   int M, N, K;          // N: weight rows per expert (SWIGLU: 2x the output width)
@@ -69,6 +71,7 @@ struct Params {
   int seg_expert[kMaxSeg];
   int unit_start[kMaxSeg + 1];
   int l2hint;           // 0 none; 1 B (weights) evict-first; 2 also A evict-last
+  int kps;              // pair kernel: k-blocks per pipeline stage, 1, 2 or 3
   void* y;
   long ldy;             // output row stride, elements
   const __nv_bfloat16* resid;
@@ -474,6 +477,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = launch_tiles(p);
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
   constexpr int kBK = I8 ? 128 : 64;
+  // k-blocks per pipeline stage (1 or 2) and the stages of the ring: the
+  // same shared memory as kStagesP stages of one k-block
+  const int kps = p.kps;
+  const uint32_t nst = kStagesP / kps;
 
   if (w == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -497,31 +504,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int brow = u.expert * p.N + ti.nb * 256 + boff;
         const CUtensorMap* mb = half ? &tmBh : &tmB;
         const uint32_t tx = kAStageP + (half ? kBStageP / 2 : kBStageP);
-        for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
-          const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
+        for (int kb = 0; kb < p.n_kblk; kb += kps, ++it) {
+          const uint32_t s = it % nst, ph = (it / nst) & 1;
           if (!mbar_wait(empty0 + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) {
             ok = false;
             break;
           }
+          const int nk = min(kps, p.n_kblk - kb);   // k-blocks in this stage
           const uint32_t fb = mapa_shared(full0 + 8 * s, 0);
-          mbar_arrive_expect_tx_cluster(fb, tx);
-          if (p.l2hint >= 2)
-            tma_load_2d_pair_hint(smem_u32(sA + s * kAStageP), &tmA, kb * kBK, arow, fb, pol_a);
-          else
-            tma_load_2d_pair(smem_u32(sA + s * kAStageP), &tmA, kb * kBK, arow, fb);
-          if (p.l2hint >= 1)
-            tma_load_2d_pair_hint(smem_u32(sB + s * kBStageP), mb, kb * kBK, brow, fb, pol_b);
-          else
-            tma_load_2d_pair(smem_u32(sB + s * kBStageP), mb, kb * kBK, brow, fb);
+          mbar_arrive_expect_tx_cluster(fb, nk * tx);
+          for (int hk = 0; hk < nk; ++hk) {
+            const uint32_t slot = s * kps + hk;
+            const int kx = (kb + hk) * kBK;
+            if (p.l2hint >= 2)
+              tma_load_2d_pair_hint(smem_u32(sA + slot * kAStageP), &tmA, kx, arow, fb, pol_a);
+            else
+              tma_load_2d_pair(smem_u32(sA + slot * kAStageP), &tmA, kx, arow, fb);
+            if (p.l2hint >= 1)
+              tma_load_2d_pair_hint(smem_u32(sB + slot * kBStageP), mb, kx, brow, fb, pol_b);
+            else
+              tma_load_2d_pair(smem_u32(sB + slot * kBStageP), mb, kx, brow, fb);
+          }
         }
       }
       // unwinding (leader): the last fill of every stage, both CTAs' halves,
       // has landed once the leader's full barrier for it completes
       if (leader) {
-        for (uint32_t s = 0; s < kStagesP; ++s) {
+        for (uint32_t s = 0; s < nst; ++s) {
           if (it > s) {
-            const uint32_t last = ((it - 1 - s) / kStagesP) * kStagesP + s;
-            mbar_wait(full0 + 8 * s, (last / kStagesP) & 1, p.err, kDevWaitDrain);
+            const uint32_t last = ((it - 1 - s) / nst) * nst + s;
+            mbar_wait(full0 + 8 * s, (last / nst) & 1, p.err, kDevWaitDrain);
           }
         }
       }
@@ -541,23 +553,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait_cluster_probe(acce0 + 8 * acc, aph ^ 1, p.err, kDevWaitAccEmpty)) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + acc * 256;
-          for (int kb = 0; kb < p.n_kblk; ++kb, ++it) {
-            const uint32_t s = it % kStagesP, ph = (it / kStagesP) & 1;
+          for (int kb = 0; kb < p.n_kblk; kb += kps, ++it) {
+            const uint32_t s = it % nst, ph = (it / nst) & 1;
             if (!mbar_wait_probe(full0 + 8 * s, ph, p.err, kDevWaitFull)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a0 = smem_u32(sA + s * kAStageP);
-            const uint32_t b0 = smem_u32(sB + s * kBStageP);
+            const int nk = min(kps, p.n_kblk - kb);
+            for (int hk = 0; hk < nk; ++hk) {
+              const uint32_t slot = s * kps + hk;
+              const uint32_t a0 = smem_u32(sA + slot * kAStageP);
+              const uint32_t b0 = smem_u32(sB + slot * kBStageP);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = smem_desc_sw128(a0 + k * 32);
-              const uint64_t bd = smem_desc_sw128(b0 + k * 32);
-              if constexpr (I8)
-                mma_i8_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
-              else
-                mma_bf16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+              for (int k = 0; k < 4; ++k) {
+                const uint64_t ad = smem_desc_sw128(a0 + k * 32);
+                const uint64_t bd = smem_desc_sw128(b0 + k * 32);
+                if constexpr (I8)
+                  mma_i8_pair(d_tmem, ad, bd, idesc, ((kb + hk) | k) != 0);
+                else
+                  mma_bf16_pair(d_tmem, ad, bd, idesc, ((kb + hk) | k) != 0);
+              }
             }
             mma_commit_pair_mc(empty0 + 8 * s, 0x3);
           }
@@ -1073,6 +1089,13 @@ int gemm_tc(const GemmArgs& a, cudaStream_t st, std::string* err)
     // the pair kernel's operand loads
     const char* e = std::getenv("U15_GEMM_L2HINT");
     p.l2hint = e != nullptr ? std::atoi(e) : kDefaultL2Hint;
+  }
+  {
+    // U15_GEMM_KPS (read per launch, for A/B checks): k-blocks per stage of
+    // the pair kernel's ring
+    const char* e = std::getenv("U15_GEMM_KPS");
+    const int v = e != nullptr ? std::atoi(e) : 0;
+    p.kps = v == 1 || v == 2 || v == 3 ? v : kDefaultKps;
   }
   const int bk = a.int8 ? 128 : 64;
   p.n_kblk = (a.K + bk - 1) / bk;
