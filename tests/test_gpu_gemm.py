@@ -34,7 +34,7 @@ def sample_rows(M, n, seed):
 
 
 @pytest.mark.parametrize("M,K,N", [(128, 64, 256), (1, 64, 8), (200, 136, 48), (333, 4096, 1024),
-                                   (130, 12288, 512)])
+                                   (130, 12288, 512), (300, 1160, 520)])
 def test_linear_bf16(ops, M, K, N):
     x = bf16_round(randn((M, K), 1))
     w = bf16_round(randn((N, K), 2, 0.02))
@@ -224,7 +224,8 @@ def test_quant_rows_tiny_scales_bit_exact(ops, cols):
     assert np.array_equal(host(q), rq)
 
 
-@pytest.mark.parametrize("M,K,N", [(128, 128, 256), (77, 4096, 1000), (256, 12288, 512)])
+@pytest.mark.parametrize("M,K,N", [(128, 128, 256), (77, 4096, 1000), (256, 12288, 512),
+                                   (200, 384, 256), (300, 1104, 520)])
 def test_linear_i8_bit_exact(ops, M, K, N):
     x = bf16_round(randn((M, K), 20))
     w = bf16_round(randn((N, K), 21, 0.02))
@@ -336,3 +337,47 @@ def test_single_segment_unbounded_rows(ops):
     got = host(y[idx])
     ref = O.linear(host(xd[idx]), host(wd), host(bd))
     assert rel_l2(got, ref) < BAR
+
+
+@pytest.mark.parametrize("int8", [False, True], ids=["bf16", "i8"])
+@pytest.mark.parametrize("K", [1160, 4096], ids=["odd-kblocks", "even-kblocks"])
+def test_pair_stage_forms_agree(ops, monkeypatch, int8, K):
+    """The CTA-pair GEMM stages one, two or three k-blocks per pipeline stage
+    (U15_GEMM_KPS, read per launch); an odd k-block count leaves a last stage
+    part full. Every form sums the same products in the same order, so the
+    routed outputs are bit-identical, and the default form matches the
+    oracle."""
+    M, N = 640, 768
+    segs = [(0, 192, 0), (192, M, 1)]
+    g = torch.Generator(device="cuda").manual_seed(41)
+    if int8:
+        K -= K % 16   # int8 rows: 16-byte TMA strides
+        xq = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+        xs = torch.rand(M, device="cuda", generator=g) * 0.01 + 0.01
+        wq = torch.randint(-127, 128, (2, N, K), dtype=torch.int8, device="cuda", generator=g)
+        ws = torch.rand(2, N, device="cuda", generator=g) * 0.001 + 0.001
+    else:
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(2, N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    outs = {}
+    for kps in ("1", "2", "3"):
+        monkeypatch.setenv("U15_GEMM_KPS", kps)
+        y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+        if int8:
+            acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+            ops.mot_linear_i8(xq, xs, wq, ws, segs, y, M, K, N, acc_dump=acc)
+            outs[kps] = (y, acc)
+        else:
+            ops.mot_linear(x, w, segs, y, M, K, N)
+            outs[kps] = (y,)
+        ops.sync()
+    for kps in ("1", "3"):
+        for a, b in zip(outs["2"], outs[kps]):
+            assert torch.equal(a, b), kps
+    if int8:
+        racc = np.concatenate([O.gemm_i8(host(xq)[lo:hi], host(wq)[e]) for lo, hi, e in segs])
+        assert np.array_equal(host(outs["2"][1]), racc)
+    else:
+        xh, wh = host(x), host(w)
+        ref = np.concatenate([O.linear(xh[lo:hi], wh[e]) for lo, hi, e in segs])
+        assert rel_l2(host(outs["2"][0]), ref) < BAR
