@@ -380,22 +380,29 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
 // ---------------------------------------------------------------------
 // Sage prologue
 // ---------------------------------------------------------------------
-// Two launches. The first runs, side by side, the Q blocks (one 64-row
-// block of one head per CTA: absmax, s = amax / 127, int8 codes) and the
-// K-mean partials (one 64-key page of one kv head per CTA: the page's
-// channel sums). The second runs the K blocks: each CTA forms kmean[c] =
-// sum of the page partials / tk (fixed page order), smooths its page's 64
-// keys by it and quantizes them like Q as two 32-key blocks, one scale each
-// (the reference's key block, bk = 32, src/u15-metal-ops.cc:702). Rows stay
-// in registers between the absmax and the codes: 32 elements a thread,
-// 16-byte loads, 8-byte stores.
+// Two launches, both with programmatic dependent launch. The first runs,
+// side by side, the Q blocks (four 64-row blocks of one head per CTA, each
+// block: absmax, s = amax / 127, int8 codes) and the K-mean partials (one
+// 64-key page of one kv head per CTA: the page's channel sums; these CTAs
+// follow the Q CTAs, pages of every kv head packed with no empty CTA). The
+// second runs the K blocks: each CTA forms kmean[c] = sum of the page
+// partials / tk (each warp sums every eighth page, four channels a lane,
+// the eight warp sums added in warp order), smooths its page's 64 keys by
+// it and quantizes them like Q as two 32-key blocks, one scale each (the
+// reference's key block, bk = 32, src/u15-metal-ops.cc:702). Rows stay in
+// registers between the absmax and the codes: 16-byte loads, 8-byte stores.
 constexpr int kSageThreads = 256;
+constexpr int kSageQBlocks = 2;   // 64-row Q blocks per CTA
+
+__device__ __forceinline__ void unpack8_bf(const uint4 u, float (&v)[8])
+{
+  const float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
 
 __device__ __forceinline__ void load8_bf(const __nv_bfloat16* p, float (&v)[8])
 {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const float2 a = unpack_bf2(u.x), b = unpack_bf2(u.y), c = unpack_bf2(u.z), d = unpack_bf2(u.w);
-  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+  unpack8_bf(*reinterpret_cast<const uint4*>(p), v);
 }
 
 __device__ __forceinline__ float block_absmax(float m, float* red)
@@ -426,16 +433,17 @@ __global__ void __launch_bounds__(kSageThreads)
     sage_q_kernel(const __nv_bfloat16* q, KvView kv, int hq, int hkv, int tq, int tk, int nqb,
                   int npg, int8_t* q8, float* sq, float* kpart)
 {
-  __shared__ float red[kSageThreads / 32];
+  griddep_wait();
+  griddep_launch();
   const int tid = threadIdx.x;
-  if ((int)blockIdx.x >= nqb) {
+  const int nqc = (nqb + kSageQBlocks - 1) / kSageQBlocks;   // Q CTAs a head
+  if ((int)blockIdx.x >= nqc) {
     // K-mean partial of one page: thread (key slot kr, 8-channel group c8)
     // sums keys kr, kr + 16, kr + 32, kr + 48 of the page with 16-byte loads,
-    // then the 16 key slots of each channel are added in slot order (the
-    // first form, a 2-byte load per key and channel in a 32-deep chain, took
-    // 21 us of the Sage prologue at BASELINE config 4)
-    const int pg = (int)blockIdx.x - nqb, hk = blockIdx.y;
-    if (hk >= hkv) return;
+    // then the 16 key slots of each channel are added in slot order
+    const int f = ((int)blockIdx.x - nqc) * hq + (int)blockIdx.y;
+    if (f >= hkv * npg) return;
+    const int hk = f / npg, pg = f % npg;
     const int c8 = tid & 15, kr = tid >> 4;
     float acc[8] = {};
 #pragma unroll
@@ -460,51 +468,103 @@ __global__ void __launch_bounds__(kSageThreads)
     }
     return;
   }
-  const int b = blockIdx.x, h = blockIdx.y;
-  if (h >= hq) return;
-  const int c8 = tid & 15, r0 = b * 64 + (tid >> 4);
-  float v[4][8];
-  bool valid[4];
-  float m = 0.0f;
+  // Q: blocks b0 .. b0 + 3 of head h; thread (row slot rr, 8-column group
+  // c8) holds rows 64 b + rr + 16 i of each block, all 16 loads in flight
+  const int h = blockIdx.y, b0 = (int)blockIdx.x * kSageQBlocks;
+  const int c8 = tid & 15, rr = tid >> 4;
+  const __nv_bfloat16* qh = q + (long)h * tq * 128;
+  uint4 raw[kSageQBlocks][4];
+  float m[kSageQBlocks];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = r0 + 16 * i;
-    valid[i] = r < tq;
-    if (valid[i]) {
-      load8_bf(q + ((long)h * tq + r) * 128 + c8 * 8, v[i]);
+  for (int g = 0; g < kSageQBlocks; ++g) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(v[i][k]));
+    for (int i = 0; i < 4; ++i) {
+      const int r = (b0 + g) * 64 + rr + 16 * i;
+      raw[g][i] = r < tq ? *reinterpret_cast<const uint4*>(qh + (long)r * 128 + c8 * 8)
+                         : make_uint4(0u, 0u, 0u, 0u);
     }
   }
-  const float s = __fdiv_rn(block_absmax(m, red), 127.0f);
-  if (tid == 0) sq[(long)h * nqb + b] = s;
-  store_codes(v, s, valid, q8 + (long)h * tq * 128, r0, c8);
+#pragma unroll
+  for (int g = 0; g < kSageQBlocks; ++g) {
+    m[g] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float v[8];
+      unpack8_bf(raw[g][i], v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m[g] = fmaxf(m[g], fabsf(v[k]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
+  }
+  __shared__ float red[kSageQBlocks][kSageThreads / 32];
+  if (lane_id() == 0) {
+#pragma unroll
+    for (int g = 0; g < kSageQBlocks; ++g) red[g][warp_id()] = m[g];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < kSageQBlocks; ++g) {
+    const int b = b0 + g;
+    if (b >= nqb) break;
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kSageThreads / 32; ++i) amax = fmaxf(amax, red[g][i]);
+    const float sc = __fdiv_rn(amax, 127.0f);
+    if (tid == 0) sq[(long)h * nqb + b] = sc;
+    const float rc = quant_recip(sc);
+    int8_t* out = q8 + (long)h * tq * 128;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = b * 64 + rr + 16 * i;
+      if (r >= tq) continue;
+      float v[8];
+      unpack8_bf(raw[g][i], v);
+      *reinterpret_cast<uint2*>(out + (long)r * 128 + c8 * 8) = quant8(v, sc, rc);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kSageThreads)
     sage_k_kernel(KvView kv, int tk, int npg, const float* kpart, int8_t* k8, float* sk,
                   long k8_stride)
 {
+  griddep_wait();
+  griddep_launch();
   __shared__ float red[2][kSageThreads / 32];
   __shared__ float km[128];
   const int pg = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
   {
-    // kmean over the pages: two threads a channel, each over every other
-    // page with four independent sums, combined in a fixed order
-    const int c = tid & 127, h2 = tid >> 7;
-    const float* kp = kpart + (long)hk * npg * 128 + c;
-    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    int i = h2;
-    for (; i + 6 < npg; i += 8) {
+    // kmean over the pages: warp w sums pages w, w + 8, ... in page order
+    // (lane l: channels 4 l .. 4 l + 3, four pages' loads in flight), then
+    // the eight warp sums are added in warp order
+    __shared__ float4 wsum[kSageThreads / 32][32];
+    const int wp = (int)warp_id();
+    const float4* kp = reinterpret_cast<const float4*>(kpart + (long)hk * npg * 128) + lane_id();
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    int i = wp;
+    for (; i + 24 < npg; i += 32) {
+      float4 t[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) a[u] += kp[(long)(i + 2 * u) * 128];
+      for (int u = 0; u < 4; ++u) t[u] = kp[(long)(i + 8 * u) * 32];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        a.x += t[u].x; a.y += t[u].y; a.z += t[u].z; a.w += t[u].w;
+      }
     }
-    for (; i < npg; i += 2) a[0] += kp[(long)i * 128];
-    __shared__ float hsum[128];
-    const float t = (a[0] + a[1]) + (a[2] + a[3]);
-    if (h2 == 1) hsum[c] = t;
+    for (; i < npg; i += 8) {
+      const float4 t = kp[(long)i * 32];
+      a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
+    }
+    wsum[wp][lane_id()] = a;
     __syncthreads();
-    if (h2 == 0) km[c] = (t + hsum[c]) / (float)tk;
+    if (tid < 128) {
+      const float* ws = reinterpret_cast<const float*>(&wsum[0][0]);
+      float t = 0.0f;
+#pragma unroll
+      for (int u = 0; u < kSageThreads / 32; ++u) t += ws[u * 128 + tid];
+      km[tid] = t / (float)tk;
+    }
   }
   __syncthreads();
   // rows r0 + 16 i: i = 0, 1 are the page's first 32-key block, i = 2, 3 its second
@@ -618,15 +678,24 @@ int sage_prepare(const void* q, const KvView& kv, int hq, int hkv, int tq, int t
                  int8_t* k8, float* sq, float* sk, float* kmean, cudaStream_t st,
                  std::string* err)
 {
+  if (hq <= 0 || hkv <= 0 || hq % hkv != 0) {
+    *err = "sage_prepare: hq must be a positive multiple of hkv";
+    return 1;
+  }
   if (tq <= 0 || tk <= 0) return 0;
   const int nqb = (tq + 63) / 64, npg = (tk + 63) / 64;
   // kmean holds the per-page partial sums [hkv][npg][128]; sk two 32-key
   // block scales per page [hkv][2 * npg]
-  sage_q_kernel<<<dim3(nqb + npg, std::max(hq, hkv)), kSageThreads, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(q), kv, hq, hkv, tq, tk, nqb, npg, q8, sq, kmean);
-  sage_k_kernel<<<dim3(npg, hkv), kSageThreads, 0, st>>>(kv, tk, npg, kmean, k8, sk,
-                                                         (long)npg * 64);
-  if (cudaGetLastError() != cudaSuccess) {
+  // Q CTAs, then the K-mean page CTAs packed over the grid's hq rows
+  const int nqc = (nqb + kSageQBlocks - 1) / kSageQBlocks;
+  const int nkc = (hkv * npg + hq - 1) / hq;
+  cudaError_t e = launch_pdl(sage_q_kernel, dim3(nqc + nkc, hq), dim3(kSageThreads), st,
+                             static_cast<const __nv_bfloat16*>(q), kv, hq, hkv, tq, tk, nqb,
+                             npg, q8, sq, kmean);
+  if (e == cudaSuccess)
+    e = launch_pdl(sage_k_kernel, dim3(npg, hkv), dim3(kSageThreads), st, kv, tk, npg,
+                   static_cast<const float*>(kmean), k8, sk, (long)npg * 64);
+  if (e != cudaSuccess || cudaGetLastError() != cudaSuccess) {
     *err = "sage_prepare: kernel launch failed";
     return 2;
   }

@@ -737,26 +737,6 @@ inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads
 // ---------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------
-// The layer's row kernels are launched with programmatic stream
-// serialisation (unless U15_PDL=0): their CTAs may be placed while the
-// previous kernel drains, and each waits (griddepcontrol.wait) before it
-// touches global memory.
-template <class... KArgs, class... Args>
-cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st,
-                       Args&&... args)
-{
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
-}
 
 int launch_rms_norm(const void* x, const void* w, void* y, int rows, int dim, float eps,
                     const SegInfo& seg, cudaStream_t st)

@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <string>
+#include <utility>
 
 #include <cuda_bf16.h>
 
@@ -16,6 +17,27 @@ namespace u15 {
 // Launch the layer's tensor-core kernels with programmatic dependent launch
 // (U15_PDL=0 turns it off; read per launch, for A/B checks).
 bool pdl_enabled();
+
+// The layer's row kernels are launched with programmatic stream
+// serialisation (unless U15_PDL=0): their CTAs may be placed while the
+// previous kernel drains, and each waits (griddepcontrol.wait) before it
+// touches global memory.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st,
+                       Args&&... args)
+{
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
 
 // Kernel attributes are per device: a process that drives several GPUs
 // (or that switches its current device between calls) must set a kernel's
