@@ -326,21 +326,47 @@ def test_tc_forms_agree(ops, mode, monkeypatch):
     if mode == 2:
         kw["t_index"] = t
     forms = [{}, {"U15_ATTN_RELEASE": "0"}, {"U15_ATTN_KS": "0", "U15_ATTN_ISSUERS": "1"},
-             {"U15_ATTN_KS": "1", "U15_ATTN_ISSUERS": "2"}, {"U15_ATTN_KS": "1", "U15_ATTN_ISSUERS": "1"}]
+             {"U15_ATTN_KS": "1", "U15_ATTN_ISSUERS": "2"}, {"U15_ATTN_KS": "1", "U15_ATTN_ISSUERS": "1"},
+             {"U15_ATTN_TILES": "1"}]
+    keys = ("U15_ATTN_RELEASE", "U15_ATTN_KS", "U15_ATTN_ISSUERS", "U15_ATTN_TILES")
     outs = []
     for f in forms:
-        for key in ("U15_ATTN_RELEASE", "U15_ATTN_KS", "U15_ATTN_ISSUERS"):
+        for key in keys:
             monkeypatch.delenv(key, raising=False)
         for key, val in f.items():
             monkeypatch.setenv(key, val)
         outs.append(run_paged(ops, q, k, v, T, **kw))
-    for key in ("U15_ATTN_RELEASE", "U15_ATTN_KS", "U15_ATTN_ISSUERS"):
+    for key in keys:
         monkeypatch.delenv(key, raising=False)
     ref = O.attention(q, k, v, tk=T, mode={0: O.BIDIR, 1: O.CAUSAL, 2: O.BLOCK_CAUSAL}[mode],
                       q_offset=kw["q_offset"], t_index=kw.get("t_index"))
     for i, o in enumerate(outs):
         assert rel_l2(o, ref) < BAR, (mode, forms[i])
         assert rel_l2(o, outs[0]) < 1e-3, (mode, forms[i])
-    # the release form and the issuer's commits differ only in the hand-off
+    # the release form and the issuer's commits differ only in the hand-off;
+    # the one-tile kernel runs the key-split softmax's arithmetic in the same
+    # order as the two-tile key-split form
     if mode == 0:
         assert np.array_equal(outs[0], outs[1])
+        assert np.array_equal(outs[5], outs[4])
+
+
+@pytest.mark.parametrize("hq,hkv,tq,cap,tk", [(8, 2, 48, 88, 67), (4, 1, 300, 320, 320),
+                                              (32, 8, 257, 200, 130), (8, 8, 512, 640, 577),
+                                              (8, 2, 130, 1100, 1025)])
+def test_tc_one_tile_kernel(ops, monkeypatch, hq, hkv, tq, cap, tk):
+    """The bidirectional pass with one 128-row tile a CTA (U15_ATTN_TILES=1,
+    two or three S buffers in TMEM): bf16 and Sage against the CPU
+    restatements, ragged query and key counts, one to nine key blocks; the
+    two buffer counts run the same arithmetic in the same order."""
+    q, k, v = qkv(hq, hkv, tq, cap, 23)
+    monkeypatch.setenv("U15_ATTN_TILES", "1")
+    outs = []
+    for sbuf in ("2", "3"):
+        monkeypatch.setenv("U15_ATTN_SBUF", sbuf)
+        got = run_paged(ops, q, k, v, tk)
+        assert rel_l2(got, O.attention(q, k, v, tk=tk)) < BAR
+        got8 = run_paged(ops, q, k, v, tk, sage=True)
+        assert rel_l2(got8, O.sage_attention(q, k, v, tk=tk, bq=64, bk=32)) < 1e-2
+        outs.append((got, got8))
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])

@@ -1033,6 +1033,375 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
+// ---------------------------------------------------------------------
+// The bidirectional pass with ONE 128-row tile a CTA (U15_ATTN_TILES=1, an
+// A/B form; the two-tile kernel above is the default). TMEM holds kSBuf (2
+// or 3, U15_ATTN_SBUF) S buffers of 128 columns (block j in buffer
+// j % kSBuf, its P written over the buffer's first 64 columns) and O after
+// them. The MMA issuer runs S(0) .. S(kSBuf - 1), then P.V(j) followed by
+// S(j + kSBuf) into the buffer P.V(j) has just read, so the next blocks' S
+// are ready while the softmax works on block j: the tile's chain per block
+// is its softmax, with S and P.V on the tensor core beneath it. The
+// softmax is the key-split layout (eight warps, two a lane quadrant, 64
+// keys a lane). A lazy O rescale first waits for P.V(j - 1) (o_done: two
+// slots, block parity; the slot's previous phase, P.V(j - 3), completed
+// before S(j) ran). K and V in three stages (224 KB with Q). At 4096 x 32
+// heads: 1024 CTAs, 6.92 rounds on 148 SMs (the two-tile kernel: 512, 3.46).
+constexpr int kStages1 = 3;
+constexpr int kQBytes1 = kTile * 256;   // bf16 Q, one tile; int8 uses half
+// + 1024 for the base alignment, + 512 for the mbarriers (at most 23) and the TMEM slot
+constexpr int kSmem1 = kQBytes1 + kStages1 * (kKBytes + kVBytes) + 1024 + 512;
+static_assert(kSmem1 <= 232448, "one-tile attention: over the 227 KB shared-memory limit");
+
+template <bool SAGE, int kSBuf>
+__device__ __forceinline__ void softmax_single(const TcAttnP& p, uint32_t tmem, uint32_t s_full,
+                                               uint32_t p_full, uint32_t o_done, uint32_t o_final,
+                                               int h, int hk, int q0, int n)
+{
+  const int w = (int)warp_id();
+  const int q4 = w & 3, hf = (w - 4) >> 2;
+  const int kh = (int)lane_id() >> 4;   // key half of the block this lane holds
+  const int kb0 = 64 * kh;
+  const int row = q4 * 32 + hf * 16 + ((int)lane_id() & 15);
+  const uint32_t lane_off = (uint32_t)(q4 * 32 + hf * 16) << 16;
+  const uint32_t tO = tmem + kSBuf * 128 + lane_off;
+  const int qi = q0 + row;
+  float sqv = 1.0f;
+  if constexpr (SAGE) sqv = (qi < p.tq) ? p.sq[(long)h * p.nqb + qi / 64] : 0.0f;
+  const int kb_last = (p.tk - 1) >> 5;
+  float m_ref = -INFINITY, l = 0.0f;
+  bool ok = true;
+  for (int j = 0; j < n; ++j) {
+    // warp-uniform: the TMEM loads and stores below are warp-collective
+    const int b = j % kSBuf;
+    const uint32_t ph = (uint32_t)(j / kSBuf) & 1;
+    if (!__all_sync(0xffffffffu, mbar_wait(s_full + 8 * b, ph, p.err, kDevWaitAccFull))) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t tS = tmem + (uint32_t)b * 128 + lane_off;
+    uint32_t r[64];
+    tmem_ld_pair64<64>(tS, r);
+    tmem_ld_wait();
+    float f[2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      f[c] = p.scale_log2;
+      if constexpr (SAGE)
+        f[c] = fmaxf(f[c] * sqv * p.sk[(long)hk * p.nkb + min(4 * j + 2 * kh + c, kb_last)],
+                     1e-30f);
+    }
+    float s[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      if constexpr (SAGE) s[i] = __int_as_float((int)r[i] + 0x4B400000) - 12582912.0f;
+      else s[i] = __uint_as_float(r[i]);
+    }
+    const int kmax = p.tk - j * kBlk;
+    if (kmax < kBlk) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i)
+        if (kb0 + i >= kmax) s[i] = -INFINITY;
+    }
+    float mc[2][2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      mc[c][0] = fmax3(s[32 * c], s[32 * c + 1], s[32 * c + 2]);
+      mc[c][1] = fmax3(s[32 * c + 3], s[32 * c + 4], s[32 * c + 5]);
+    }
+#pragma unroll
+    for (int i = 6; i < 32; i += 4) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        mc[c][0] = fmax3(mc[c][0], s[32 * c + i], s[32 * c + i + 1]);
+        if (i + 3 < 32) mc[c][1] = fmax3(mc[c][1], s[32 * c + i + 2], s[32 * c + i + 3]);
+      }
+    }
+    float mt = fmaxf(fmaxf(mc[0][0], mc[0][1]) * f[0], fmaxf(mc[1][0], mc[1][1]) * f[1]);
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+    const bool need = (m_ref == -INFINITY) || (mt > m_ref + 8.0f);
+    const float m_new = need ? fmaxf(mt, m_ref) : m_ref;
+    if (j > 0 && __any_sync(0xffffffffu, need)) {
+      // O is final up to P.V(j - 1) once its commit has landed (P.V(j - 3),
+      // the slot's previous phase, had before S(j) ran)
+      if (!__all_sync(0xffffffffu, mbar_wait(o_done + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1,
+                                             p.err, kDevWaitAccFull))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float fac = (need && m_ref != -INFINITY) ? ex2(m_ref - m_new) : 1.0f;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld_pair32<64>(tO + c * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * fac);
+        tmem_st_pair32<64>(tO + c * 32, o);
+      }
+      l *= fac;
+    }
+    m_ref = m_new;
+    const float nm = m_ref == -INFINITY ? 0.0f : -m_ref;
+    float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const float fc = f[c];
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float x0 = fmaf(s[32 * c + 2 * i], fc, nm), x1 = fmaf(s[32 * c + 2 * i + 1], fc, nm);
+        const float a = ex2(x0), b1 = ex2(x1);
+        rs[i & 3] += a + b1;
+        pk[i] = pack_bf2(a, b1);
+      }
+      // keys [kb0 + 32c, +32) -> bf16 columns [kb0/2 + 16c, +16) of the buffer
+      tmem_st_pair16<32>(tS + 16 * c, pk);
+    }
+    tmem_st_wait();
+    l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+    tc_fence_before();
+    __syncwarp();
+    if (lane_id() == 0) mbar_arrive(p_full + 8 * b);
+  }
+  // O after the last P.V, then O / l of this lane's 64 dims
+  const bool fin = ok && n > 0 && mbar_wait(o_final, 0, p.err, kDevWaitAccFull);
+  if (!__all_sync(0xffffffffu, fin)) return;
+  tc_fence_after();
+  const float lt = l + __shfl_xor_sync(0xffffffffu, l, 16);
+  const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+  __nv_bfloat16* dst = p.out + (long)qi * p.hq * 128 + (long)h * 128 + kb0;
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    uint32_t o[32];
+    tmem_ld_pair32<64>(tO + c * 32, o);
+    tmem_ld_wait();
+    if (qi < p.tq) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        uint4 v;
+        v.x = pack_bf2(__uint_as_float(o[qd * 8 + 0]) * inv, __uint_as_float(o[qd * 8 + 1]) * inv);
+        v.y = pack_bf2(__uint_as_float(o[qd * 8 + 2]) * inv, __uint_as_float(o[qd * 8 + 3]) * inv);
+        v.z = pack_bf2(__uint_as_float(o[qd * 8 + 4]) * inv, __uint_as_float(o[qd * 8 + 5]) * inv);
+        v.w = pack_bf2(__uint_as_float(o[qd * 8 + 6]) * inv, __uint_as_float(o[qd * 8 + 7]) * inv);
+        d4[qd] = v;
+      }
+    }
+  }
+}
+
+
+template <bool SAGE, int kSBuf>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc1_kernel(const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcAttnP p)
+{
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kQBytes1;
+  uint8_t* sV = sK + kStages1 * kKBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages1 * kVBytes);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0;
+  const uint32_t k_full = b0 + 8;                  // [kStages1]
+  const uint32_t v_full = k_full + 8 * kStages1;
+  const uint32_t k_empty = v_full + 8 * kStages1;
+  const uint32_t v_empty = k_empty + 8 * kStages1;
+  const uint32_t s_full = v_empty + 8 * kStages1;  // [kSBuf]
+  const uint32_t p_full = s_full + 8 * kSBuf;      // [kSBuf], one arrival a softmax warp
+  const uint32_t o_done = p_full + 8 * kSBuf;      // [2]: P.V(j) completes slot j & 1
+  const uint32_t o_final = o_done + 16;            // after the last P.V
+  const uint32_t drain = o_final + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages1 + 2 * kSBuf + 2 + 1 + 1);
+
+  const int w = (int)warp_id();
+  const int h = blockIdx.y, hk = h / p.G;
+  const int q0 = (int)blockIdx.x * kTile;
+  const int n = (p.tk + kBlk - 1) / kBlk;
+  const int n_pg = (p.tk + 63) / 64;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages1; ++s) {
+      mbar_init(k_full + 8 * s, 1);
+      mbar_init(v_full + 8 * s, 1);
+      mbar_init(k_empty + 8 * s, 1);
+      mbar_init(v_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < kSBuf; ++b) {
+      mbar_init(s_full + 8 * b, 1);
+      mbar_init(p_full + 8 * b, 8);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_done + 8, 1);
+    mbar_init(o_final, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (w == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // the set-up above overlaps the previous kernel; global memory waits for it
+  griddep_launch();
+  griddep_wait();
+  if (w < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    if (w == 0) {
+      // ------------------------------------------------------------ producer
+      if (lane_id() == 0) {
+        const int qrow = h * p.tq + q0;
+        if constexpr (SAGE) {
+          mbar_arrive_expect_tx(q_full, kTile * 128);
+          tma_load_2d(smem_u32(sQ), &tmQ, 0, qrow, q_full);
+        } else {
+          mbar_arrive_expect_tx(q_full, kTile * 256);
+          for (int d = 0; d < 2; ++d)
+            tma_load_2d(smem_u32(sQ + d * kTile * 128), &tmQ, d * 64, qrow, q_full);
+        }
+        int nk = 0, nv = 0;   // blocks whose K / V loads were issued
+        for (int j = 0; j < n; ++j) {
+          const int s = j % kStages1;
+          const uint32_t ph = (j / kStages1) & 1;
+          // the block's two pages; past the last page the first one is loaded
+          // again (finite data under masked scores)
+          const int pg0 = 2 * j, pg1 = min(2 * j + 1, n_pg - 1);
+          const int page0 = p.page_table ? p.page_table[pg0] : pg0;
+          const int page1 = p.page_table ? p.page_table[pg1] : pg1;
+          if (!mbar_wait(k_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+          uint8_t* k_dst = sK + s * kKBytes;
+          if constexpr (SAGE) {
+            mbar_arrive_expect_tx(k_full + 8 * s, kBlk * 128);
+            const int krow = (int)(hk * p.k8_stride) + j * kBlk;
+            tma_load_2d(smem_u32(k_dst), &tmK, 0, krow, k_full + 8 * s);
+            tma_load_2d(smem_u32(k_dst + 64 * 128), &tmK, 0, krow + 64, k_full + 8 * s);
+          } else {
+            mbar_arrive_expect_tx(k_full + 8 * s, kKBytes);
+            for (int hf = 0; hf < 2; ++hf) {
+              const int krow = ((hf ? page1 : page0) * p.hkv + hk) * 64;
+              for (int d = 0; d < 2; ++d)
+                tma_load_2d(smem_u32(k_dst + d * kBlk * 128 + hf * 64 * 128), &tmK, d * 64, krow,
+                            k_full + 8 * s);
+            }
+          }
+          nk = j + 1;
+          if (!mbar_wait(v_empty + 8 * s, ph ^ 1, p.err, kDevWaitEmpty)) break;
+          mbar_arrive_expect_tx(v_full + 8 * s, kVBytes);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_2d(smem_u32(sV + s * kVBytes + hf * 128 * 128), &tmV, 0,
+                        ((hf ? page1 : page0) * p.hkv + hk) * 128, v_full + 8 * s);
+          nv = j + 1;
+        }
+        // unwinding: every copy issued must land before the CTA may exit
+        mbar_wait(q_full, 0, p.err, kDevWaitDrain);
+        for (int s = 0; s < kStages1; ++s) {
+          if (nk > s) {
+            const int last = ((nk - 1 - s) / kStages1) * kStages1 + s;
+            mbar_wait(k_full + 8 * s, (last / kStages1) & 1, p.err, kDevWaitDrain);
+          }
+          if (nv > s) {
+            const int last = ((nv - 1 - s) / kStages1) * kStages1 + s;
+            mbar_wait(v_full + 8 * s, (last / kStages1) & 1, p.err, kDevWaitDrain);
+          }
+        }
+      }
+    } else if (w == 1) {
+      // ------------------------------------------------------------ MMA
+      // Issue order S(0), S(1), S(2), P.V(0), S(3), P.V(1), S(4), ...:
+      // S(j + 3) overwrites P(j)'s buffer and follows P.V(j) on the tensor
+      // core. A commit arrives when every earlier MMA of this thread has
+      // completed: s_full[b] after S(j), o_done[j & 1] after P.V(j), the
+      // stage releases after the MMAs that read the stage.
+      if (lane_id() == 0) {
+        const uint32_t id_s = SAGE ? idesc_s8(kTile, kBlk) : idesc_bf16(kTile, kBlk);
+        const uint32_t id_o = idesc_bf16(kTile, 128);
+        auto issue_s = [&](int j) {
+          const uint32_t d = tmem + (uint32_t)(j % kSBuf) * 128;
+          const uint32_t kb = smem_u32(sK + (j % kStages1) * kKBytes);
+          const uint32_t a0 = smem_u32(sQ);
+          if constexpr (SAGE) {
+  #pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_i8(d, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(kb + k * 32), id_s, k != 0);
+          } else {
+  #pragma unroll
+            for (int k = 0; k < 8; ++k)
+              mma_bf16(d, smem_desc_sw128(a0 + (k >> 2) * kTile * 128 + (k & 3) * 32),
+                       smem_desc_sw128(kb + (k >> 2) * kBlk * 128 + (k & 3) * 32), id_s, k != 0);
+          }
+        };
+        bool ok = mbar_wait(q_full, 0, p.err, kDevWaitFull);
+        for (int j = 0; j < kSBuf && j < n && ok; ++j) {
+          const int s = j % kStages1;
+          ok = mbar_wait_probe(k_full + 8 * s, (j / kStages1) & 1, p.err, kDevWaitFull);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(j);
+          mma_commit(s_full + 8 * (j % kSBuf));
+          mma_commit(k_empty + 8 * s);
+        }
+        for (int j = 0; j < n && ok; ++j) {
+          const int s = j % kStages1, b = j % kSBuf;
+          if (!mbar_wait_probe(p_full + 8 * b, (j / kSBuf) & 1, p.err, kDevWaitFull) ||
+              !mbar_wait_probe(v_full + 8 * s, (j / kStages1) & 1, p.err, kDevWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t vb = smem_u32(sV + s * kVBytes);
+          const uint32_t d = tmem + kSBuf * 128, a = tmem + (uint32_t)b * 128;
+  #pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16_ts(d, a + k * 8, smem_desc_sw128(vb + (k >> 2) * 128 * 128 + (k & 3) * 32),
+                        id_o, (j | k) != 0);
+          mma_commit(o_done + 8 * (j & 1));
+          if (j == n - 1) mma_commit(o_final);
+          mma_commit(v_empty + 8 * s);
+          if (j + kSBuf < n) {
+            const int s3 = (j + kSBuf) % kStages1;
+            if (!mbar_wait_probe(k_full + 8 * s3, ((j + kSBuf) / kStages1) & 1, p.err,
+                                 kDevWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(j + kSBuf);
+            mma_commit(s_full + 8 * b);
+            mma_commit(k_empty + 8 * s3);
+          }
+        }
+        mma_commit(drain);
+        mbar_wait(drain, 0, p.err, kDevWaitDrain);
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    softmax_single<SAGE, kSBuf>(p, tmem, s_full, p_full, o_done, o_final, h, hk, q0, n);
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (w == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+
 
 }  // namespace
 
@@ -1115,7 +1484,7 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   // The exponentials (U15_ATTN_EXP, read per launch for A/B checks): 0 every
   // one a float ex2 on the MUFU; 1 a quarter of them on the FMA pipe (5-10 %
   // slower for bf16, 4 % for Sage, measured).
-  static std::atomic<uint64_t> set_attr[16];
+  static std::atomic<uint64_t> set_attr[20];
   const int nqblk = (a.tq + 2 * kTile - 1) / (2 * kTile);
   const dim3 grid = a.mode == 0 ? dim3(nqblk, a.hq) : dim3(a.hq, nqblk);
   const char* exp_env = std::getenv("U15_ATTN_EXP");
@@ -1141,13 +1510,25 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
       {{attn_tc_kernel<false, 0, 2, false>, attn_tc_kernel<false, 0, 2, true>},
        {attn_tc_kernel<false, 1, 2, false>, attn_tc_kernel<false, 1, 2, true>}}};
   const int row = sage ? 1 : (a.mode == 0 ? 0 : a.mode + 1);
-  const KFn k = table[row][expm][ks];
-  const int which = (row * 2 + expm) * 2 + ks;
-  const int smem = kSmem;
+  // U15_ATTN_TILES=1 (read per launch, for A/B checks): the bidirectional
+  // pass with one 128-row tile a CTA and two or three S buffers
+  // (U15_ATTN_SBUF=3). Measured in the layer bench against the two-tile
+  // kernel: no faster (attention alone -5 % Sage, +-2 % bf16; the layer
+  // and the denoise loop unchanged or slower).
+  const char* tiles_env = std::getenv("U15_ATTN_TILES");
+  const bool single = a.mode == 0 && tiles_env != nullptr && std::atoi(tiles_env) == 1;
+  const char* sbuf_env = std::getenv("U15_ATTN_SBUF");
+  const int sbuf = sbuf_env != nullptr && std::atoi(sbuf_env) == 3 ? 3 : 2;
+  const KFn k = !single ? table[row][expm][ks]
+                : sbuf == 3 ? (sage ? attn_tc1_kernel<true, 3> : attn_tc1_kernel<false, 3>)
+                            : (sage ? attn_tc1_kernel<true, 2> : attn_tc1_kernel<false, 2>);
+  const int which = single ? 16 + (sage ? 1 : 0) + (sbuf == 3 ? 2 : 0) : (row * 2 + expm) * 2 + ks;
+  const int smem = single ? kSmem1 : kSmem;
+  const dim3 grid_used = single ? dim3((a.tq + kTile - 1) / kTile, a.hq) : grid;
   cudaError_t e = cudaSuccess;
   if (smem_attr_once(k, smem, set_attr[which])) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
+    cfg.gridDim = grid_used;
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
