@@ -370,3 +370,32 @@ def test_tc_one_tile_kernel(ops, monkeypatch, hq, hkv, tq, cap, tk):
         assert rel_l2(got8, O.sage_attention(q, k, v, tk=tk, bq=64, bk=32)) < 1e-2
         outs.append((got, got8))
     assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+
+
+def test_tc_last_round_split(ops, monkeypatch):
+    """The bidirectional pass hands a part-empty last round of two-tile units
+    to a second launch of the one-tile kernel (here 160 units on 148 SMs:
+    the last 12 units, heads 29-31, as 24 one-tile CTAs). bf16 and Sage:
+    within 1e-3 of the single launch (the tail rows sum their softmax in
+    the key-split order) and within the bars of the CPU restatements on
+    heads from both launches."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    hq, hkv, tk = 32, 8, 600
+    tq = 256 * ((sms + 12 + hq - 1) // hq)   # just over one round of units
+    units = tq // 256 * hq
+    assert units % sms and 2 * (units % sms) <= sms
+    q, k, v = qkv(hq, hkv, tq, tk, 29)
+    for sage in (False, True):
+        monkeypatch.setenv("U15_ATTN_SPLIT", "0")
+        one = run_paged(ops, q, k, v, tk, sage=sage)
+        monkeypatch.delenv("U15_ATTN_SPLIT")
+        got = run_paged(ops, q, k, v, tk, sage=sage)
+        assert rel_l2(got, one) < 1e-3
+        for h in (0, hq - 2, hq - 1):
+            hk = h // (hq // hkv)
+            if sage:
+                ref = O.sage_attention(q[h:h + 1], k[hk:hk + 1], v[hk:hk + 1], tk=tk, bq=64, bk=32)
+                assert rel_l2(got[:, h * 128:(h + 1) * 128], ref) < 1e-2
+            else:
+                ref = O.attention(q[h:h + 1], k[hk:hk + 1], v[hk:hk + 1], tk=tk)
+                assert rel_l2(got[:, h * 128:(h + 1) * 128], ref) < BAR

@@ -118,6 +118,8 @@ struct TcAttnP {
   unsigned* err;
   int issuers;       // MMA issuing warps: 1 (warp 1, both tiles) or 2 (warp 1 + t, tile t)
   int release;       // 1: the softmax warps release K/V stages (bidirectional, one issuer)
+  int unit_base;     // bidirectional: the first unit (two-tile: 256-row block of a head;
+                     // one-tile: 128-row block) of this launch's 1-D grid
 };
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
@@ -494,12 +496,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* blk_thi = blk_tlo + kMaxBlk;
 
   const int w = (int)warp_id();
-  // bidirectional: grid (query blocks, heads), the query blocks of a head
-  // side by side (they share its K/V in L2); masked rules: grid (heads,
-  // query blocks) with the last query block first -- the longest CTAs start
-  // first, so the short ones fill the tail
-  const int h = MODE == 0 ? (int)blockIdx.y : (int)blockIdx.x;
-  const int qb = MODE == 0 ? (int)blockIdx.x : (int)(gridDim.y - 1 - blockIdx.y);
+  // bidirectional: a 1-D grid of units u = head * (query blocks) + block
+  // from p.unit_base, the query blocks of a head side by side (they share
+  // its K/V in L2); masked rules: grid (heads, query blocks) with the last
+  // query block first -- the longest CTAs start first, so the short ones
+  // fill the tail
+  const int nqb2 = (p.tq + 2 * kTile - 1) / (2 * kTile);
+  const int u0 = (int)blockIdx.x + p.unit_base;
+  const int h = MODE == 0 ? u0 / nqb2 : (int)blockIdx.x;
+  const int qb = MODE == 0 ? u0 % nqb2 : (int)(gridDim.y - 1 - blockIdx.y);
   const int hk = h / p.G;
   const int q0 = qb * 2 * kTile;
   const int n_all = (p.tk + kBlk - 1) / kBlk;
@@ -1034,8 +1039,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 
 // ---------------------------------------------------------------------
-// The bidirectional pass with ONE 128-row tile a CTA (U15_ATTN_TILES=1, an
-// A/B form; the two-tile kernel above is the default). TMEM holds kSBuf (2
+// The bidirectional pass with ONE 128-row tile a CTA. It runs the
+// part-empty last round of the two-tile kernel's units (a second launch,
+// each unit as two of these CTAs), and the whole pass under
+// U15_ATTN_TILES=1 (an A/B form, no faster than the two-tile kernel for the
+// full rounds). TMEM holds kSBuf (2
 // or 3, U15_ATTN_SBUF) S buffers of 128 columns (block j in buffer
 // j % kSBuf, its P written over the buffer's first 64 columns) and O after
 // them. The MMA issuer runs S(0) .. S(kSBuf - 1), then P.V(j) followed by
@@ -1221,8 +1229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 4 * kStages1 + 2 * kSBuf + 2 + 1 + 1);
 
   const int w = (int)warp_id();
-  const int h = blockIdx.y, hk = h / p.G;
-  const int q0 = (int)blockIdx.x * kTile;
+  // unit t = head * (128-row blocks) + block, from p.unit_base
+  const int nqt = (p.tq + kTile - 1) / kTile;
+  const int t1 = (int)blockIdx.x + p.unit_base;
+  const int h = t1 / nqt, hk = h / p.G;
+  const int q0 = (t1 % nqt) * kTile;
   const int n = (p.tk + kBlk - 1) / kBlk;
   const int n_pg = (p.tk + 63) / 64;
   if (threadIdx.x == 0) {
@@ -1402,6 +1413,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
+// SMs of the current device (cached per device)
+int device_sms()
+{
+  static std::atomic<int> cache[64];
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return 0;
+  int v = cache[d].load(std::memory_order_relaxed);
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d) != cudaSuccess) return 0;
+    cache[d].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
 
 }  // namespace
 
@@ -1486,7 +1511,7 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   // slower for bf16, 4 % for Sage, measured).
   static std::atomic<uint64_t> set_attr[20];
   const int nqblk = (a.tq + 2 * kTile - 1) / (2 * kTile);
-  const dim3 grid = a.mode == 0 ? dim3(nqblk, a.hq) : dim3(a.hq, nqblk);
+  const dim3 grid = a.mode == 0 ? dim3(nqblk * a.hq) : dim3(a.hq, nqblk);
   const char* exp_env = std::getenv("U15_ATTN_EXP");
   int expm = exp_env != nullptr ? std::atoi(exp_env) : kDefaultExp;
   if (expm < 0 || expm > 1) expm = kDefaultExp;
@@ -1519,16 +1544,32 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
   const bool single = a.mode == 0 && tiles_env != nullptr && std::atoi(tiles_env) == 1;
   const char* sbuf_env = std::getenv("U15_ATTN_SBUF");
   const int sbuf = sbuf_env != nullptr && std::atoi(sbuf_env) == 3 ? 3 : 2;
-  const KFn k = !single ? table[row][expm][ks]
-                : sbuf == 3 ? (sage ? attn_tc1_kernel<true, 3> : attn_tc1_kernel<false, 3>)
-                            : (sage ? attn_tc1_kernel<true, 2> : attn_tc1_kernel<false, 2>);
-  const int which = single ? 16 + (sage ? 1 : 0) + (sbuf == 3 ? 2 : 0) : (row * 2 + expm) * 2 + ks;
-  const int smem = single ? kSmem1 : kSmem;
-  const dim3 grid_used = single ? dim3((a.tq + kTile - 1) / kTile, a.hq) : grid;
-  cudaError_t e = cudaSuccess;
-  if (smem_attr_once(k, smem, set_attr[which])) {
+  const KFn k_two = table[row][expm][ks];
+  const KFn k_one = sbuf == 3 ? (sage ? attn_tc1_kernel<true, 3> : attn_tc1_kernel<false, 3>)
+                              : (sage ? attn_tc1_kernel<true, 2> : attn_tc1_kernel<false, 2>);
+  const int which_two = (row * 2 + expm) * 2 + ks;
+  const int which_one = 16 + (sage ? 1 : 0) + (sbuf == 3 ? 2 : 0);
+  // The bidirectional pass's last round: when the two-tile units leave a
+  // last round at most half full (and the query count is whole 256-row
+  // blocks), its units run as twice as many one-tile CTAs in a second
+  // launch, each about 0.58 of a two-tile CTA's time (U15_ATTN_SPLIT=0
+  // keeps one launch).
+  int split_units = 0;   // two-tile units handed to the one-tile launch
+  if (a.mode == 0 && !single && a.tq % (2 * kTile) == 0) {
+    const char* sp_env = std::getenv("U15_ATTN_SPLIT");
+    if (sp_env == nullptr || std::atoi(sp_env) != 0) {
+      const int sms = device_sms();
+      const int units = nqblk * a.hq, r = units % sms;
+      if (sms > 0 && units > sms && r > 0 && 2 * r <= sms) split_units = r;
+    }
+  }
+  auto launch = [&](KFn kf, int which, int smem, dim3 g, const TcAttnP& pp) {
+    if (!smem_attr_once(kf, smem, set_attr[which])) {
+      const cudaError_t e0 = cudaGetLastError();
+      return e0 == cudaSuccess ? cudaErrorInvalidValue : e0;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid_used;
+    cfg.gridDim = g;
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -1537,11 +1578,30 @@ int attention_tc(const TcAttnArgs& a, cudaStream_t st, std::string* err)
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, k, mq, mk, mv, p);
-    if (e == cudaSuccess) e = cudaGetLastError();
+    cudaError_t e1 = cudaLaunchKernelEx(&cfg, kf, mq, mk, mv, pp);
+    if (e1 == cudaSuccess) e1 = cudaGetLastError();
+    return e1;
+  };
+  cudaError_t e = cudaSuccess;
+  KFn k = k_two;
+  int smem = kSmem;
+  p.unit_base = 0;
+  if (single) {
+    k = k_one;
+    smem = kSmem1;
+    e = launch(k_one, which_one, kSmem1, dim3(((a.tq + kTile - 1) / kTile) * a.hq), p);
+  } else if (split_units > 0) {
+    const int units = nqblk * a.hq;
+    e = launch(k_two, which_two, kSmem, dim3(units - split_units), p);
+    if (e == cudaSuccess) {
+      TcAttnP p1 = p;
+      p1.unit_base = 2 * (units - split_units);
+      k = k_one;
+      smem = kSmem1;
+      e = launch(k_one, which_one, kSmem1, dim3(2 * split_units), p1);
+    }
   } else {
-    e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaErrorInvalidValue;
+    e = launch(k_two, which_two, kSmem, grid, p);
   }
   if (e != cudaSuccess) {
     cudaFuncAttributes fa{};
