@@ -485,7 +485,14 @@ def run_ours(args, rank, world, local):
     ops.sync()
     ms_step = total_ms / args.steps
     value = ms_step / world
-    launches_per_layer = 9
+    # rope tables, norm, QKV, qkv_post, attention, O, norm, gate+up, down; the
+    # attention takes a second launch when its last round of 256-row units is
+    # at most half full (the library's rule, U15_ATTN_SPLIT=0 turns it off)
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    units = (M_TOK // 256) * NH
+    split = (os.environ.get("U15_ATTN_SPLIT", "1") != "0" and M_TOK % 256 == 0 and
+             units > sms and 0 < units % sms <= sms // 2)
+    launches_per_layer = 9 + int(split)
 
 
     # ---- W8A8 and Sage variants (same loop, same rules) ----
